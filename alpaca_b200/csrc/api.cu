@@ -1,0 +1,267 @@
+// api.cu — the C ABI (include/alpaca_cuda.h): argument validation, the kernel dispatch policy of alpaca.swift's
+// KernelEncoder.attention (Sources/AlpacaMetal/Backend/KernelEncoder.swift:306-343), workspace sizing
+// (KernelEncoder.decodeScratchBytes, :88-92), status codes mirroring MetalError (MetalContext.swift:7-31) and
+// the device error word that bounded device-side waits report into.
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace alpaca {
+
+// Device error word (one per device that loads this library). Kernels receive its address; host code reads it
+// through alpaca_cuda_device_status.
+__device__ unsigned g_device_error;
+
+namespace {
+
+thread_local std::string t_last_error;
+
+alpaca_cuda_status fail(alpaca_cuda_status st, const std::string& msg) {
+    t_last_error = msg;
+    return st;
+}
+
+alpaca_cuda_status ok() {
+    t_last_error.clear();
+    return ALPACA_CUDA_OK;
+}
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceInfo {
+    unsigned* err = nullptr;
+    int num_sms = 0;
+    bool ready = false;
+};
+DeviceInfo g_devices[kMaxDevices];
+std::mutex g_devices_mu;
+
+// Per-device set-up, done once with that device current: address of the error word and SM count.
+cudaError_t device_info(DeviceInfo* out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(g_devices_mu);
+    DeviceInfo& di = g_devices[dev];
+    if (!di.ready) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_device_error);
+        if (e != cudaSuccess) return e;
+        e = cudaDeviceGetAttribute(&di.num_sms, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return e;
+        di.err = static_cast<unsigned*>(p);
+        di.ready = true;
+    }
+    *out = di;
+    return cudaSuccess;
+}
+
+int env_int(const char* name, int fallback) {
+    const char* v = std::getenv(name);
+    if (!v || !*v) return fallback;
+    char* end = nullptr;
+    long x = std::strtol(v, &end, 10);
+    return (end && *end == '\0') ? static_cast<int>(x) : fallback;
+}
+
+// Tuning knobs with the reference's names and defaults (KernelEncoder.swift:69-85).
+int decode_min_ctx() {
+    static const int v = env_int("ALPACA_DECODE_MINCTX", 64);
+    return v;
+}
+constexpr int kPrefillMinTokens = 8;  // KernelEncoder.prefillAttentionMinTokens (:70)
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+size_t dtype_size(int dt) { return dt == ALPACA_F16 ? 2 : 4; }
+
+std::string shape_str(const alpaca_attn_desc& d) {
+    char buf[256];
+    std::snprintf(buf, sizeof(buf), "seqs=%d T=%d start=%d H=%d/%d d=%d q=%s kv=%s out=%s", d.n_seqs, d.tokens,
+                  d.start_position, d.n_heads, d.n_kv_heads, d.head_dim, d.q_dtype == ALPACA_F16 ? "f16" : "f32",
+                  d.kv_dtype == ALPACA_F16 ? "f16" : "f32", d.out_dtype == ALPACA_F16 ? "f16" : "f32");
+    return buf;
+}
+
+// Shape / pointer / stride checks (MetalOps.swift:179-181 plus what a raw-pointer ABI needs).
+alpaca_cuda_status validate(const alpaca_attn_desc* dp) {
+    if (!dp) return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "attention: null descriptor");
+    const alpaca_attn_desc& d = *dp;
+    const std::string sh = shape_str(d);
+    if (d.n_seqs < 1 || d.n_heads < 1 || d.n_kv_heads < 1 || d.tokens < 1 || d.start_position < 0)
+        return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "attention shapes: " + sh);
+    if (d.n_heads % d.n_kv_heads != 0)
+        return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "attention: heads not a multiple of kvHeads: " + sh);
+    if (d.head_dim < 32 || d.head_dim > 256 || d.head_dim % 32 != 0)
+        return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "attention: headDim must be a multiple of 32 up to 256: " + sh);
+    for (int dt : {d.q_dtype, d.kv_dtype, d.out_dtype})
+        if (dt != ALPACA_F32 && dt != ALPACA_F16)
+            return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "attention: unknown dtype: " + sh);
+    if (!d.q || !d.k || !d.v || !d.out) return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "attention: null tensor pointer");
+    if (!aligned16(d.q) || !aligned16(d.k) || !aligned16(d.v) || !aligned16(d.out))
+        return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "attention: tensor pointers must be 16-byte aligned");
+    const int64_t hq = static_cast<int64_t>(d.n_heads) * d.head_dim, hk = static_cast<int64_t>(d.n_kv_heads) * d.head_dim;
+    if (d.q_token_stride < hq || d.out_token_stride < hq || d.kv_row_stride < hk)
+        return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "attention: row strides smaller than a row: " + sh);
+    if (d.q_seq_stride < 0 || d.kv_seq_stride < 0 || d.out_seq_stride < 0)
+        return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "attention: negative sequence stride");
+    if (d.n_seqs > 1 && (d.q_seq_stride == 0 || d.kv_seq_stride == 0 || d.out_seq_stride == 0))
+        return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "attention: zero sequence stride with several sequences");
+    const int64_t qs = static_cast<int64_t>(dtype_size(d.q_dtype)), ks = dtype_size(d.kv_dtype), os = dtype_size(d.out_dtype);
+    if ((d.q_token_stride * qs) % 16 || (d.q_seq_stride * qs) % 16 || (d.kv_row_stride * ks) % 16 ||
+        (d.kv_seq_stride * ks) % 16 || (d.out_token_stride * os) % 16 || (d.out_seq_stride * os) % 16)
+        return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "attention: strides must be multiples of 16 bytes");
+    if (d.ctx_lens) {
+        if (d.tokens != 1)
+            return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "attention: ctx_lens is only valid for one-token decode");
+        if (d.max_ctx_len < 1)
+            return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "attention: max_ctx_len must bound ctx_lens (>= 1)");
+    }
+    if (d.start_position > (1 << 30) || d.tokens > (1 << 30) - d.start_position)
+        return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "attention: positions out of range: " + sh);
+    if (!(d.scale >= 0.f) || !std::isfinite(d.scale))
+        return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "attention: scale must be finite and >= 0");
+    return ok();
+}
+
+// KernelEncoder.attention's policy (KernelEncoder.swift:309-343).
+alpaca_attn_kernel select_kernel(const alpaca_attn_desc& d) {
+    const int ctx = d.ctx_lens ? d.max_ctx_len : d.start_position + 1;
+    if (d.tokens == 1 && decode_supported(d) && (d.ctx_lens || ctx >= decode_min_ctx())) return ALPACA_ATTN_DECODE_SPLIT;
+    if (d.tokens >= kPrefillMinTokens && prefill_supported(d)) return ALPACA_ATTN_PREFILL_TC;
+    return ALPACA_ATTN_GENERAL;
+}
+
+size_t workspace_for(const alpaca_attn_desc& d, alpaca_attn_kernel k) {
+    switch (k) {
+        case ALPACA_ATTN_DECODE_SPLIT: return decode_workspace_bytes(d);
+        case ALPACA_ATTN_PREFILL_TC: return prefill_workspace_bytes(d);
+        default: return 0;
+    }
+}
+
+alpaca_cuda_status check_kind(const alpaca_attn_desc& d, alpaca_attn_kernel k) {
+    switch (k) {
+        case ALPACA_ATTN_DECODE_SPLIT:
+            if (!decode_supported(d))
+                return fail(ALPACA_CUDA_ERR_UNSUPPORTED,
+                            "split decode needs tokens=1, f16 KV, headDim 64/128 and heads/kvHeads <= 8: " + shape_str(d));
+            return ok();
+        case ALPACA_ATTN_PREFILL_TC:
+            if (!prefill_supported(d))
+                return fail(ALPACA_CUDA_ERR_UNSUPPORTED, "tensor-core prefill needs f16 KV and headDim 64: " + shape_str(d));
+            return ok();
+        case ALPACA_ATTN_GENERAL: return ok();
+        default: return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "attention: unknown kernel kind");
+    }
+}
+
+alpaca_cuda_status run(const alpaca_attn_desc* dp, alpaca_attn_kernel kind, void* ws, size_t ws_bytes,
+                       cudaStream_t stream) {
+    alpaca_cuda_status st = validate(dp);
+    if (st != ALPACA_CUDA_OK) return st;
+    const alpaca_attn_desc& d = *dp;
+    if (kind == ALPACA_ATTN_AUTO) kind = select_kernel(d);
+    st = check_kind(d, kind);
+    if (st != ALPACA_CUDA_OK) return st;
+    const size_t need = workspace_for(d, kind);
+    if (need > 0 && (ws_bytes < need || !ws))
+        return fail(ALPACA_CUDA_ERR_WORKSPACE_TOO_SMALL,
+                    "attention: workspace of " + std::to_string(ws_bytes) + " bytes, " + std::to_string(need) + " needed");
+    if (need > 0 && !aligned16(ws)) return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "attention: workspace must be 16-byte aligned");
+    DeviceInfo di;
+    cudaError_t e = device_info(&di);
+    if (e != cudaSuccess) return fail(ALPACA_CUDA_ERR_CUDA, std::string("attention: device query: ") + cudaGetErrorString(e));
+    Call c{&d, d.scale > 0.f ? d.scale : 1.0f / std::sqrt(static_cast<float>(d.head_dim)), di.err, ws, ws_bytes, di.num_sms};
+    switch (kind) {
+        case ALPACA_ATTN_DECODE_SPLIT: e = launch_decode(c, stream); break;
+        case ALPACA_ATTN_PREFILL_TC: e = launch_prefill(c, stream); break;
+        default: e = launch_general(c, stream); break;
+    }
+    if (e != cudaSuccess)
+        return fail(ALPACA_CUDA_ERR_LAUNCH_FAILED, std::string("attention launch failed: ") + cudaGetErrorString(e));
+    return ok();
+}
+
+}  // namespace
+}  // namespace alpaca
+
+using namespace alpaca;
+
+extern "C" {
+
+alpaca_cuda_status alpaca_attention(const alpaca_attn_desc* desc, alpaca_attn_kernel kind, void* workspace,
+                                    size_t workspace_bytes, alpaca_stream_t stream) {
+    return run(desc, kind, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+alpaca_cuda_status alpaca_attn_prefill(const alpaca_attn_desc* desc, void* workspace, size_t workspace_bytes,
+                                       alpaca_stream_t stream) {
+    return run(desc, ALPACA_ATTN_PREFILL_TC, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+alpaca_cuda_status alpaca_attn_decode(const alpaca_attn_desc* desc, void* workspace, size_t workspace_bytes,
+                                      alpaca_stream_t stream) {
+    return run(desc, ALPACA_ATTN_DECODE_SPLIT, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+alpaca_cuda_status alpaca_attention_workspace_bytes(const alpaca_attn_desc* desc, alpaca_attn_kernel kind,
+                                                    size_t* bytes) {
+    if (!bytes) return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "workspace_bytes: null output");
+    alpaca_cuda_status st = validate(desc);
+    if (st != ALPACA_CUDA_OK) return st;
+    if (kind == ALPACA_ATTN_AUTO) kind = select_kernel(*desc);
+    st = check_kind(*desc, kind);
+    if (st != ALPACA_CUDA_OK) return st;
+    *bytes = workspace_for(*desc, kind);
+    return ok();
+}
+
+alpaca_cuda_status alpaca_attention_select(const alpaca_attn_desc* desc, alpaca_attn_kernel* kind) {
+    if (!kind) return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "select: null output");
+    alpaca_cuda_status st = validate(desc);
+    if (st != ALPACA_CUDA_OK) return st;
+    *kind = select_kernel(*desc);
+    return ok();
+}
+
+alpaca_cuda_status alpaca_cuda_device_status(alpaca_stream_t stream, int clear) {
+    cudaError_t e = cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return fail(ALPACA_CUDA_ERR_CUDA, std::string("device status: ") + cudaGetErrorString(e));
+    unsigned word = 0;
+    e = cudaMemcpyFromSymbol(&word, g_device_error, sizeof(word));
+    if (e != cudaSuccess) return fail(ALPACA_CUDA_ERR_CUDA, std::string("device status: ") + cudaGetErrorString(e));
+    if (clear && word) {
+        const unsigned zero = 0;
+        e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero));
+        if (e != cudaSuccess) return fail(ALPACA_CUDA_ERR_CUDA, std::string("device status: ") + cudaGetErrorString(e));
+    }
+    if (word & kDevErrTimeout) return fail(ALPACA_CUDA_ERR_DEVICE_TIMEOUT, "a bounded device-side wait gave up");
+    if (word) return fail(ALPACA_CUDA_ERR_CUDA, "device error word " + std::to_string(word));
+    return ok();
+}
+
+const char* alpaca_cuda_status_string(alpaca_cuda_status status) {
+    switch (status) {
+        case ALPACA_CUDA_OK: return "ok";
+        case ALPACA_CUDA_ERR_INVALID_ARGUMENT: return "invalid argument";
+        case ALPACA_CUDA_ERR_UNSUPPORTED: return "unsupported";
+        case ALPACA_CUDA_ERR_WORKSPACE_TOO_SMALL: return "workspace too small";
+        case ALPACA_CUDA_ERR_LAUNCH_FAILED: return "kernel launch failed";
+        case ALPACA_CUDA_ERR_DEVICE_TIMEOUT: return "device-side wait timed out";
+        case ALPACA_CUDA_ERR_CUDA: return "CUDA error";
+    }
+    return "unknown status";
+}
+
+const char* alpaca_cuda_last_error(void) { return t_last_error.c_str(); }
+
+int alpaca_cuda_version(void) { return ALPACA_CUDA_VERSION; }
+
+}  // extern "C"

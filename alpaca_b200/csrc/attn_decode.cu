@@ -1,0 +1,373 @@
+// attn_decode.cu — split-KV single-token decode attention over the f16 KV cache, plus the combine kernel.
+//
+// Same job as alpaca.swift's attn_decode_split_* / attn_decode_merge (Sources/AlpacaMetal/Kernels/
+// attention_decode.metal:28-133, dispatched by KernelEncoder.swift:309-326), designed for B200 HBM3e:
+//
+//   split kernel  grid (splits, kv_heads, seqs), 128 threads. One CTA owns SL consecutive cache rows of one KV
+//                 head of one sequence and serves all G query heads of that KV head, so every K/V byte is read
+//                 from HBM exactly once. Each cache row (d halves) is read by d/8 lanes with 128-bit
+//                 non-allocating loads; all of a CTA's K and V loads are issued before any math, so each CTA keeps
+//                 SL*d*4 bytes in flight. Scores are reduced across a row's lanes with a transposing butterfly
+//                 (7 shuffles for 8 rows instead of 24), softmax runs once per (row, head) from shared memory, and
+//                 P·V partial sums are reduced across rows through shared memory.
+//   combine       grid (heads, seqs), d threads: rescales the per-split (m, l, acc) states to the global max and
+//                 normalises. Launched with programmatic dependent launch so its launch overlaps the split tail.
+//                 Sequences with one split are finished by the split kernel itself.
+//
+// Scores are kept in log2 units (q pre-scaled by scale*log2(e)), so every exponential is one ex2.approx.
+// Partial-state layout: [seq][kv_head][split][g][d + 2] f32 = accumulators, then m (log2 units), then l.
+#include "common.cuh"
+#include "internal.h"
+
+namespace alpaca {
+namespace {
+
+constexpr int kThreads = 128;
+constexpr int kSlots = 8;     // cache rows per thread per split
+constexpr int kMaxGroup = 8;  // query heads per KV head (attention_decode.metal:25)
+constexpr float kLog2e = 1.4426950408889634f;
+
+template <int D>
+struct Geo {
+    static constexpr int LPR = D / 8;                    // lanes per cache row (16 B each)
+    static constexpr int RPW = 32 / LPR;                 // rows per warp per slot
+    static constexpr int RPS = RPW * (kThreads / 32);    // rows per CTA per slot
+    static constexpr int SL = RPS * kSlots;              // rows per split: 128 (d=64), 64 (d=128)
+};
+
+struct DecodeArgs {
+    const void* q;
+    int64_t q_seq_stride;
+    int q_f16;
+    const __half* k;
+    const __half* v;
+    int64_t kv_row_stride, kv_seq_stride;
+    void* out;
+    int64_t out_seq_stride;
+    int out_f16;
+    float* partial;
+    const int* ctx_lens;
+    int uniform_len;
+    int n_heads, n_kv_heads, max_splits;
+    float scale_log2;
+};
+
+__device__ __forceinline__ int ctx_len_of(const DecodeArgs& a, int s) {
+    return a.ctx_lens ? a.ctx_lens[s] : a.uniform_len;
+}
+
+__device__ __forceinline__ uint4 ld_stream(const __half* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ void half8_to_float(const uint4& u, float* f) {
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const float2 t = __half22float2(h[i]);
+        f[2 * i] = t.x;
+        f[2 * i + 1] = t.y;
+    }
+}
+
+// Transposing butterfly: on entry every lane of a row group holds partial sums for kSlots rows; on exit lane
+// holds the full sum of one row (slot index returned). LPR lanes form a row group.
+template <int LPR>
+__device__ __forceinline__ float reduce_rows(float (&v)[kSlots], int lane, int& slot) {
+    float w[kSlots];
+#pragma unroll
+    for (int i = 0; i < kSlots; i++) w[i] = v[i];
+    int n = kSlots;
+    int off = LPR / 2;
+    slot = 0;
+#pragma unroll
+    for (int step = 0; step < 3; step++) {  // kSlots = 8 -> 3 halvings
+        const bool up = (lane & off) != 0;
+        const int half = n / 2;
+#pragma unroll
+        for (int i = 0; i < kSlots / 2; i++) {
+            if (i < half) {
+                const float send = up ? w[i] : w[i + half];
+                const float keep = up ? w[i + half] : w[i];
+                w[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+            }
+        }
+        if (up) slot += half;
+        n = half;
+        off >>= 1;
+    }
+    float r = w[0];
+#pragma unroll
+    for (int o = off; o >= 1; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+    return r;
+}
+
+template <int D, int G>
+__global__ void __launch_bounds__(kThreads) decode_split_kernel(const DecodeArgs a) {
+    using Gm = Geo<D>;
+    constexpr int SL = Gm::SL, RPS = Gm::RPS, LPR = Gm::LPR, RPW = Gm::RPW;
+    const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
+    const int L = ctx_len_of(a, seq);
+    const int row0 = split * SL;
+    if (row0 >= L) return;  // uniform for the whole CTA
+    const int row_end = min(L, row0 + SL);
+    const int nsplits = (L + SL - 1) / SL;
+
+    extern __shared__ float smem[];
+    float* s_p = smem;                   // [G][SL]  scores, then probabilities
+    float* s_red = s_p + G * SL;         // [RPS][G][D] per-row-lane partial accumulators
+    float* s_ml = s_red + RPS * G * D;   // [G][2]   split max (log2 units) and denominator
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int lr = lane % LPR;              // this lane's 8 dims: [lr*8, lr*8 + 8)
+    const int rowlane = warp * RPW + lane / LPR;
+
+    // 1. Issue every K and V load of this CTA.
+    const int64_t seq_off = static_cast<int64_t>(seq) * a.kv_seq_stride + static_cast<int64_t>(kvh) * D + lr * 8;
+    uint4 kr[kSlots], vr[kSlots];
+#pragma unroll
+    for (int i = 0; i < kSlots; i++) {
+        const int r = row0 + i * RPS + rowlane;
+        if (r < row_end) {
+            const int64_t off = seq_off + static_cast<int64_t>(r) * a.kv_row_stride;
+            kr[i] = ld_stream(a.k + off);
+            vr[i] = ld_stream(a.v + off);
+        } else {
+            kr[i] = make_uint4(0, 0, 0, 0);
+            vr[i] = make_uint4(0, 0, 0, 0);
+        }
+    }
+
+    // 2. Queries of the G heads (this lane's 8 dims), pre-scaled into log2 units.
+    float qv[G][8];
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        const int64_t qoff = static_cast<int64_t>(seq) * a.q_seq_stride + static_cast<int64_t>(kvh * G + g) * D + lr * 8;
+        if (a.q_f16) {
+            const uint4 u = *reinterpret_cast<const uint4*>(static_cast<const __half*>(a.q) + qoff);
+            half8_to_float(u, qv[g]);
+        } else {
+            const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(a.q) + qoff);
+            const float4 x0 = p[0], x1 = p[1];
+            qv[g][0] = x0.x; qv[g][1] = x0.y; qv[g][2] = x0.z; qv[g][3] = x0.w;
+            qv[g][4] = x1.x; qv[g][5] = x1.y; qv[g][6] = x1.z; qv[g][7] = x1.w;
+        }
+#pragma unroll
+        for (int e = 0; e < 8; e++) qv[g][e] *= a.scale_log2;
+    }
+
+    // 3. Scores: partial dots, then the transposing row reduction; one lane per (row, head) stores it.
+    float part[G][kSlots];
+#pragma unroll
+    for (int i = 0; i < kSlots; i++) {
+        float kf[8];
+        half8_to_float(kr[i], kf);
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            float s = 0.f;
+#pragma unroll
+            for (int e = 0; e < 8; e++) s = fmaf(qv[g][e], kf[e], s);
+            part[g][i] = s;
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        int slot;
+        const float sc = reduce_rows<LPR>(part[g], lane, slot);
+        // lanes that share a slot after the plain-reduce tail hold equal values; the lowest one stores
+        const bool writer = (LPR <= 8) || ((lr & (LPR / 8 - 1)) == 0);
+        if (writer) {
+            const int rl = slot * RPS + rowlane;
+            s_p[g * SL + rl] = (row0 + rl < row_end) ? sc : -INFINITY;
+        }
+    }
+    __syncthreads();
+
+    // 4. Softmax statistics per head over this split (one warp per head).
+    for (int g = warp; g < G; g += kThreads / 32) {
+        float mx = -INFINITY;
+        for (int r = lane; r < SL; r += 32) mx = fmaxf(mx, s_p[g * SL + r]);
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        float sum = 0.f;
+        for (int r = lane; r < SL; r += 32) {
+            const float p = ex2_approx(s_p[g * SL + r] - mx);  // masked rows: 2^-inf = 0
+            s_p[g * SL + r] = p;
+            sum += p;
+        }
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if (lane == 0) {
+            s_ml[2 * g] = mx;
+            s_ml[2 * g + 1] = sum;
+        }
+    }
+    __syncthreads();
+
+    // 5. P·V over this thread's rows and dims.
+    float acc[G][8];
+#pragma unroll
+    for (int g = 0; g < G; g++)
+#pragma unroll
+        for (int e = 0; e < 8; e++) acc[g][e] = 0.f;
+#pragma unroll
+    for (int i = 0; i < kSlots; i++) {
+        float vf[8];
+        half8_to_float(vr[i], vf);
+        const int rl = i * RPS + rowlane;
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            const float p = s_p[g * SL + rl];
+#pragma unroll
+            for (int e = 0; e < 8; e++) acc[g][e] = fmaf(p, vf[e], acc[g][e]);
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        float4* dst = reinterpret_cast<float4*>(s_red + (rowlane * G + g) * D + lr * 8);
+        dst[0] = make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
+        dst[1] = make_float4(acc[g][4], acc[g][5], acc[g][6], acc[g][7]);
+    }
+    __syncthreads();
+    // The combine kernel may start launching now; it waits for this grid's memory before reading.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+    // 6. Reduce across row lanes; finish single-split sequences, else store the partial state.
+    const int64_t part_base =
+        ((static_cast<int64_t>(seq) * a.n_kv_heads + kvh) * a.max_splits + split) * G;
+    for (int o = tid; o < G * D; o += kThreads) {
+        const int g = o / D, col = o - g * D;
+        float s = 0.f;
+#pragma unroll
+        for (int rl = 0; rl < RPS; rl++) s += s_red[(rl * G + g) * D + col];
+        if (nsplits == 1) {
+            const float val = s / s_ml[2 * g + 1];
+            const int64_t oo = static_cast<int64_t>(seq) * a.out_seq_stride + static_cast<int64_t>(kvh * G + g) * D + col;
+            if (a.out_f16) static_cast<__half*>(a.out)[oo] = __float2half_rn(val);
+            else static_cast<float*>(a.out)[oo] = val;
+        } else {
+            float* pp = a.partial + (part_base + g) * (D + 2);
+            pp[col] = s;
+            if (col == 0) {
+                pp[D] = s_ml[2 * g];
+                pp[D + 1] = s_ml[2 * g + 1];
+            }
+        }
+    }
+}
+
+template <int D>
+__global__ void __launch_bounds__(D) decode_combine_kernel(const DecodeArgs a) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // split kernel's writes are visible after this
+    const int h = blockIdx.x, seq = blockIdx.y, col = threadIdx.x;
+    const int G = a.n_heads / a.n_kv_heads, kvh = h / G, g = h - kvh * G;
+    const int L = ctx_len_of(a, seq);
+    const int nsp = (L + Geo<D>::SL - 1) / Geo<D>::SL;
+    if (nsp <= 1) return;
+    const int64_t stride = static_cast<int64_t>(G) * (D + 2);
+    const float* base = a.partial + ((static_cast<int64_t>(seq) * a.n_kv_heads + kvh) * a.max_splits * G + g) * (D + 2);
+    float M = -INFINITY;
+    for (int s = 0; s < nsp; s++) M = fmaxf(M, base[s * stride + D]);
+    float num = 0.f, den = 0.f;
+    for (int s = 0; s < nsp; s++) {
+        const float f = ex2_approx(base[s * stride + D] - M);
+        num = fmaf(base[s * stride + col], f, num);
+        den = fmaf(base[s * stride + D + 1], f, den);
+    }
+    const float val = num / den;
+    const int64_t oo = static_cast<int64_t>(seq) * a.out_seq_stride + static_cast<int64_t>(h) * D + col;
+    if (a.out_f16) static_cast<__half*>(a.out)[oo] = __float2half_rn(val);
+    else static_cast<float*>(a.out)[oo] = val;
+}
+
+template <int D, int G>
+cudaError_t launch_split(const DecodeArgs& a, int n_seqs, cudaStream_t s) {
+    using Gm = Geo<D>;
+    const size_t smem = sizeof(float) * (G * Gm::SL + Gm::RPS * G * D + 2 * G);
+    dim3 grid(a.max_splits, a.n_kv_heads, n_seqs);
+    decode_split_kernel<D, G><<<grid, kThreads, smem, s>>>(a);
+    return cudaGetLastError();
+}
+
+template <int D>
+cudaError_t launch_d(const DecodeArgs& a, int n_seqs, cudaStream_t s) {
+    const int G = a.n_heads / a.n_kv_heads;
+    cudaError_t e;
+    switch (G) {
+        case 1: e = launch_split<D, 1>(a, n_seqs, s); break;
+        case 2: e = launch_split<D, 2>(a, n_seqs, s); break;
+        case 3: e = launch_split<D, 3>(a, n_seqs, s); break;
+        case 4: e = launch_split<D, 4>(a, n_seqs, s); break;
+        case 5: e = launch_split<D, 5>(a, n_seqs, s); break;
+        case 6: e = launch_split<D, 6>(a, n_seqs, s); break;
+        case 7: e = launch_split<D, 7>(a, n_seqs, s); break;
+        case 8: e = launch_split<D, 8>(a, n_seqs, s); break;
+        default: return cudaErrorInvalidValue;
+    }
+    if (e != cudaSuccess) return e;
+    if (a.max_splits <= 1) return cudaSuccess;  // every sequence finished in the split kernel
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.n_heads, n_seqs, 1);
+    cfg.blockDim = dim3(D, 1, 1);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, decode_combine_kernel<D>, a);
+}
+
+}  // namespace
+
+int decode_split_len(int head_dim) { return head_dim == 128 ? Geo<128>::SL : Geo<64>::SL; }
+
+int decode_max_splits(const alpaca_attn_desc& d) {
+    const int L = d.ctx_lens ? d.max_ctx_len : d.start_position + 1;
+    const int sl = decode_split_len(d.head_dim);
+    return (L + sl - 1) / sl;
+}
+
+size_t decode_workspace_bytes(const alpaca_attn_desc& d) {
+    const int ms = decode_max_splits(d);
+    if (ms <= 1) return 0;
+    return sizeof(float) * static_cast<size_t>(d.n_seqs) * d.n_heads * ms * (d.head_dim + 2);
+}
+
+bool decode_supported(const alpaca_attn_desc& d) {
+    if (d.head_dim != 64 && d.head_dim != 128) return false;
+    if (d.n_kv_heads <= 0 || d.n_heads % d.n_kv_heads != 0) return false;
+    const int G = d.n_heads / d.n_kv_heads;
+    return G >= 1 && G <= kMaxGroup && d.kv_dtype == ALPACA_F16 && d.tokens == 1;
+}
+
+cudaError_t launch_decode(const Call& c, cudaStream_t s) {
+    const alpaca_attn_desc& d = *c.d;
+    DecodeArgs a;
+    a.q = d.q;
+    a.q_seq_stride = d.q_seq_stride;
+    a.q_f16 = d.q_dtype == ALPACA_F16;
+    a.k = static_cast<const __half*>(d.k);
+    a.v = static_cast<const __half*>(d.v);
+    a.kv_row_stride = d.kv_row_stride;
+    a.kv_seq_stride = d.kv_seq_stride;
+    a.out = d.out;
+    a.out_seq_stride = d.out_seq_stride;
+    a.out_f16 = d.out_dtype == ALPACA_F16;
+    a.partial = static_cast<float*>(c.ws);
+    a.ctx_lens = d.ctx_lens;
+    a.uniform_len = d.start_position + 1;
+    a.n_heads = d.n_heads;
+    a.n_kv_heads = d.n_kv_heads;
+    a.max_splits = decode_max_splits(d);
+    a.scale_log2 = c.scale * kLog2e;
+    if (a.max_splits < 1) return cudaSuccess;
+    return d.head_dim == 128 ? launch_d<128>(a, d.n_seqs, s) : launch_d<64>(a, d.n_seqs, s);
+}
+
+}  // namespace alpaca

@@ -1,0 +1,528 @@
+// attn_prefill_sm100.cu — causal grouped-query flash attention for prefill on B200 tensor cores (tcgen05).
+//
+// Same computation as alpaca.swift's attn_tensor_* / attn_prefill_* kernels (Sources/AlpacaMetal/Kernels/
+// tensor_attention.metal:29-117, attention_prefill.metal:31-182): f16 Q/K/V, S = Q·Kᵀ with f32 accumulation,
+// online softmax, P rounded to f16, O += P·V with f32 accumulation, causal block skip, mask only on diagonal
+// blocks, final 1/l. The structure is B200-native:
+//
+//   * persistent kernel, one CTA per SM, work items = (sequence, head, pair of 128-row query tiles) handed out
+//     heaviest first (items with more visible KV blocks come first), so causal work is balanced over 148 SMs;
+//   * warp 0: TMA producer. Q tiles and a ring of K/V blocks (128 rows x d) land in shared memory with
+//     128-byte swizzle, no multicast;
+//   * warp 1: one thread issues tcgen05.mma. S tiles (128x128 f32) and O tiles (128xd f32) live in tensor memory
+//     (TMEM: S_A, S_B, O_A, O_B = 384 of 512 columns); completion is signalled with tcgen05.commit;
+//   * warps 4-7 and 8-11: two softmax warpgroups, one per query tile of the pair, one query row per thread. They
+//     read S rows from TMEM, apply the causal mask on diagonal blocks, keep the running max in log2 units (the
+//     max is only moved when it grows by more than 8, so O rarely needs rescaling), write P as f16 into a
+//     swizzled shared-memory tile that is the A operand of the P·V MMA, and finish each tile with O / l.
+//   The tensor pipe alternates S(A, j+1), PV(A, j), S(B, j+1), PV(B, j) so one tile's softmax overlaps the
+//   other tile's MMAs.
+//
+// Every mbarrier wait is bounded (2 s; 2 ms under ALPACA_ATTN_FLAG_DEBUG_FORCE_TIMEOUT). On a timeout the CTA
+// raises its abort flag and the device error word, waits (bounded) for its own TMA loads and MMAs in flight,
+// frees TMEM and returns.
+#include <mutex>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace alpaca {
+namespace {
+
+constexpr int kBM = 128;        // query rows per tile
+constexpr int kBN = 128;        // KV rows per block
+constexpr int kD = 64;          // head dim of this kernel
+constexpr int kStages = 2;      // K/V ring depth
+constexpr int kThreads = 384;   // 12 warps
+constexpr int kTmemCols = 512;
+constexpr uint32_t kTileBytes = kBM * kD * 2;  // 16 KB: one Q, K or V tile
+constexpr float kRescaleThreshold = 8.0f;      // log2 units
+constexpr float kLog2e = 1.4426950408889634f;
+
+// TMEM column map: S_A, S_B (128 f32 columns each), then O_A, O_B (d columns each)
+__host__ __device__ constexpr uint32_t col_s(int tile) { return tile ? 128u : 0u; }
+__host__ __device__ constexpr uint32_t col_o(int tile) { return tile ? 320u : 256u; }
+
+struct PrefillArgs {
+    void* out;
+    int64_t out_token_stride, out_seq_stride;
+    int out_f16;
+    int n_seqs, n_heads, n_kv_heads, tokens, start, kv_len;
+    int n_pairs, total_items;
+    float scale_log2;
+    unsigned* err;
+    unsigned flags;
+};
+
+struct SmemLayout {
+    __half q[2][kBM * kD];
+    __half k[kStages][kBN * kD];
+    __half v[kStages][kBN * kD];
+    __half p[2][kBM * kBN];  // per tile: [2 halves of 64 KV columns][128 rows][64] swizzled
+    uint64_t q_full[2], q_empty[2];
+    uint64_t k_full[kStages], k_empty[kStages], v_full[kStages], v_empty[kStages];
+    uint64_t s_full[2], s_empty[2], p_full[2], o_done[2];
+    uint64_t dbg, fin;
+    uint32_t tmem_base;
+    int abort_flag;
+};
+
+constexpr size_t kSmemBytes = sizeof(SmemLayout) + 1024;  // + alignment slack
+
+struct Item {
+    int seq, head, row0[2], nblk[2];
+};
+
+__device__ __forceinline__ int tile_blocks(const PrefillArgs& a, int row0) {
+    if (row0 >= a.tokens) return 0;
+    const int last_row = min(row0 + kBM, a.tokens);          // exclusive
+    const int visible = a.start + last_row;                  // KV rows visible to the tile's last row
+    return (visible + kBN - 1) / kBN;
+}
+
+__device__ __forceinline__ Item decode_item(const PrefillArgs& a, int it) {
+    const int per_rank = a.n_seqs * a.n_heads;
+    const int rank = it / per_rank, rem = it - rank * per_rank;
+    Item x;
+    const int pair = a.n_pairs - 1 - rank;  // heaviest pairs first
+    x.seq = rem / a.n_heads;
+    x.head = rem - x.seq * a.n_heads;
+    x.row0[0] = pair * 2 * kBM;
+    x.row0[1] = x.row0[0] + kBM;
+    x.nblk[0] = tile_blocks(a, x.row0[0]);
+    x.nblk[1] = tile_blocks(a, x.row0[1]);
+    return x;
+}
+
+// ---------------------------------------------------------------------------------------------- MMA helpers
+
+__device__ __forceinline__ void mma_s(const SmemLayout* sm, int tile, int stage, uint32_t tmem_base) {
+    constexpr uint32_t idesc = idesc_f16_f32(kBM, kBN, false, false);
+    const uint32_t qa = smem_u32(sm->q[tile]), ka = smem_u32(sm->k[stage]);
+#pragma unroll
+    for (int kk = 0; kk < kD / 16; kk++) {
+        const uint64_t ad = smem_desc_sw128(qa + kk * 32, 16, 1024);
+        const uint64_t bd = smem_desc_sw128(ka + kk * 32, 16, 1024);
+        tc_mma_ss(tmem_base + col_s(tile), ad, bd, idesc, kk > 0 ? 1u : 0u);
+    }
+}
+
+__device__ __forceinline__ void mma_pv(const SmemLayout* sm, int tile, int stage, uint32_t tmem_base,
+                                       bool accumulate) {
+    constexpr uint32_t idesc = idesc_f16_f32(kBM, kD, false, true);
+    const uint32_t pa = smem_u32(sm->p[tile]), va = smem_u32(sm->v[stage]);
+#pragma unroll
+    for (int kk = 0; kk < kBN / 16; kk++) {
+        const uint64_t ad = smem_desc_sw128(pa + (kk >> 2) * (kBM * 128) + (kk & 3) * 32, 16, 1024);
+        const uint64_t bd = smem_desc_sw128(va + kk * 16 * 128, kBN * 128, 1024);
+        tc_mma_ss(tmem_base + col_o(tile), ad, bd, idesc, (accumulate || kk > 0) ? 1u : 0u);
+    }
+}
+
+// ---------------------------------------------------------------------------------------------- kernel
+
+__global__ void __launch_bounds__(kThreads, 1)
+    prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                   const __grid_constant__ CUtensorMap tm_v, const PrefillArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    SmemLayout* sm = reinterpret_cast<SmemLayout*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const bool debug_timeout = (a.flags & ALPACA_ATTN_FLAG_DEBUG_FORCE_TIMEOUT) != 0;
+    AbortState ab{&sm->abort_flag, a.err, debug_timeout ? kDebugWaitLimitNs : kWaitLimitNs};
+
+    if (tid == 0) {
+        sm->abort_flag = 0;
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&sm->q_full[i], 1);
+            mbar_init(&sm->q_empty[i], 1);
+            mbar_init(&sm->s_full[i], 1);
+            mbar_init(&sm->s_empty[i], 4);
+            mbar_init(&sm->p_full[i], 4);
+            mbar_init(&sm->o_done[i], 1);
+        }
+        for (int i = 0; i < kStages; i++) {
+            mbar_init(&sm->k_full[i], 1);
+            mbar_init(&sm->k_empty[i], 1);
+            mbar_init(&sm->v_full[i], 1);
+            mbar_init(&sm->v_empty[i], 1);
+        }
+        mbar_init(&sm->dbg, 1);
+        mbar_init(&sm->fin, 1);
+        fence_barrier_init();
+        tma_prefetch_desc(&tm_q);
+        tma_prefetch_desc(&tm_k);
+        tma_prefetch_desc(&tm_v);
+    }
+    if (warp == 2) {
+        tmem_alloc(&sm->tmem_base, kTmemCols);
+        tmem_relinquish();
+        tc_fence_before();
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = sm->tmem_base;
+
+    if (warp == 0 && lane == 0) {
+        // ------------------------------------------------------------------ TMA producer
+        uint32_t kv_it = 0, k_issued = 0, v_issued = 0, q_uses[2] = {0, 0};
+        bool ok = true;
+        for (int it = blockIdx.x; ok && it < a.total_items; it += gridDim.x) {
+            const Item x = decode_item(a, it);
+            const int kvh = x.head / (a.n_heads / a.n_kv_heads);
+            for (int t = 0; t < 2 && ok; t++) {
+                if (x.nblk[t] == 0) continue;
+                ok = mbar_wait(&sm->q_empty[t], (q_uses[t] & 1) ^ 1, ab);
+                if (!ok) break;
+                mbar_arrive_expect_tx(&sm->q_full[t], kTileBytes);
+                tma_load_4d(sm->q[t], &tm_q, 0, x.head, x.row0[t], x.seq, &sm->q_full[t]);
+                q_uses[t]++;
+            }
+            const int nmax = max(x.nblk[0], x.nblk[1]);
+            for (int j = 0; ok && j < nmax; j++, kv_it++) {
+                const int st = kv_it % kStages;
+                const uint32_t ph = (kv_it / kStages) & 1;
+                ok = mbar_wait(&sm->k_empty[st], ph ^ 1, ab);
+                if (!ok) break;
+                mbar_arrive_expect_tx(&sm->k_full[st], kTileBytes);
+                tma_load_4d(sm->k[st], &tm_k, 0, kvh, j * kBN, x.seq, &sm->k_full[st]);
+                k_issued = kv_it + 1;
+                ok = mbar_wait(&sm->v_empty[st], ph ^ 1, ab);
+                if (!ok) break;
+                mbar_arrive_expect_tx(&sm->v_full[st], kTileBytes);
+                tma_load_4d(sm->v[st], &tm_v, 0, kvh, j * kBN, x.seq, &sm->v_full[st]);
+                v_issued = kv_it + 1;
+            }
+        }
+        if (!ok) {
+            // Drain our own loads still in flight before the CTA retires.
+            int dummy = 0;
+            AbortState drain{&dummy, a.err, kWaitLimitNs};
+            for (uint32_t i = (k_issued > kStages ? k_issued - kStages : 0); i < k_issued; i++)
+                mbar_wait(&sm->k_full[i % kStages], (i / kStages) & 1, drain);
+            for (uint32_t i = (v_issued > kStages ? v_issued - kStages : 0); i < v_issued; i++)
+                mbar_wait(&sm->v_full[i % kStages], (i / kStages) & 1, drain);
+            for (int t = 0; t < 2; t++)
+                if (q_uses[t] > 0) mbar_wait(&sm->q_full[t], (q_uses[t] - 1) & 1, drain);
+        }
+    } else if (warp == 1 && lane == 0) {
+        // ------------------------------------------------------------------ MMA issuer
+        uint32_t kv_it = 0, q_uses[2] = {0, 0}, s_uses[2] = {0, 0}, p_uses[2] = {0, 0};
+        bool ok = true;
+        if (debug_timeout) ok = mbar_wait(&sm->dbg, 0, ab);  // nothing arrives: exercises the give-up path
+        for (int it = blockIdx.x; ok && it < a.total_items; it += gridDim.x) {
+            const Item x = decode_item(a, it);
+            const int n[2] = {x.nblk[0], x.nblk[1]};
+            const int nmax = max(n[0], n[1]);
+            for (int t = 0; t < 2 && ok; t++)
+                if (n[t] > 0) ok = mbar_wait(&sm->q_full[t], q_uses[t] & 1, ab);
+            if (!ok) break;
+            // S(0) for both tiles
+            {
+                const int st = kv_it % kStages;
+                ok = mbar_wait(&sm->k_full[st], (kv_it / kStages) & 1, ab);
+                if (!ok) break;
+                tc_fence_after();
+                for (int t = 0; t < 2 && ok; t++) {
+                    if (n[t] == 0) continue;
+                    ok = mbar_wait(&sm->s_empty[t], (s_uses[t] & 1) ^ 1, ab);
+                    if (!ok) break;
+                    tc_fence_after();
+                    mma_s(sm, t, st, tmem_base);
+                    tc_commit(&sm->s_full[t]);
+                    s_uses[t]++;
+                    if (n[t] == 1) tc_commit(&sm->q_empty[t]);
+                }
+                if (!ok) break;
+                tc_commit(&sm->k_empty[st]);
+            }
+            for (int j = 0; ok && j < nmax; j++) {
+                const uint32_t cur = kv_it + j, nxt = cur + 1;
+                const int stc = cur % kStages, stn = nxt % kStages;
+                const bool have_next = j + 1 < nmax;
+                if (have_next) {
+                    ok = mbar_wait(&sm->k_full[stn], (nxt / kStages) & 1, ab);
+                    if (!ok) break;
+                    tc_fence_after();
+                }
+                bool v_ready = false;
+                for (int t = 0; t < 2 && ok; t++) {
+                    if (j + 1 < n[t]) {  // S(t, j+1)
+                        ok = mbar_wait(&sm->s_empty[t], (s_uses[t] & 1) ^ 1, ab);
+                        if (!ok) break;
+                        tc_fence_after();
+                        mma_s(sm, t, stn, tmem_base);
+                        tc_commit(&sm->s_full[t]);
+                        s_uses[t]++;
+                        if (j + 2 == n[t]) tc_commit(&sm->q_empty[t]);
+                    }
+                    if (j < n[t]) {  // PV(t, j)
+                        if (!v_ready) {
+                            ok = mbar_wait(&sm->v_full[stc], (cur / kStages) & 1, ab);
+                            if (!ok) break;
+                            v_ready = true;
+                        }
+                        ok = mbar_wait(&sm->p_full[t], p_uses[t] & 1, ab);
+                        if (!ok) break;
+                        tc_fence_after();
+                        mma_pv(sm, t, stc, tmem_base, j > 0);
+                        tc_commit(&sm->o_done[t]);
+                        p_uses[t]++;
+                    }
+                }
+                if (!ok) break;
+                if (have_next) tc_commit(&sm->k_empty[stn]);
+                tc_commit(&sm->v_empty[stc]);
+            }
+            kv_it += nmax;
+            for (int t = 0; t < 2; t++)
+                if (n[t] > 0) q_uses[t]++;
+        }
+        // Retire every MMA this thread issued before TMEM is freed.
+        int dummy = 0;
+        AbortState drain{&dummy, a.err, kWaitLimitNs};
+        tc_commit(&sm->fin);
+        mbar_wait(&sm->fin, 0, drain);
+    } else if (warp >= 4) {
+        // ------------------------------------------------------------------ softmax warpgroups
+        const int tile = (warp - 4) >> 2;
+        const int quarter = warp & 3;               // TMEM lane quarter this warp may access
+        const int row = quarter * 32 + lane;        // query row within the tile = TMEM lane
+        const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+        const uint32_t s_addr = lane_addr + col_s(tile), o_addr = lane_addr + col_o(tile);
+        uint8_t* p_tile = reinterpret_cast<uint8_t*>(sm->p[tile]);
+        uint32_t s_uses = 0, o_uses = 0;
+        bool ok = true;
+        for (int it = blockIdx.x; ok && it < a.total_items; it += gridDim.x) {
+            const Item x = decode_item(a, it);
+            const int nb = x.nblk[tile];
+            if (nb == 0) continue;
+            const int row0 = x.row0[tile];
+            const int qpos = a.start + row0 + row;  // absolute position of this thread's query
+            float m_used = -INFINITY, l = 0.f;
+            for (int j = 0; j < nb; j++) {
+                ok = mbar_wait(&sm->s_full[tile], s_uses & 1, ab);
+                if (!ok) break;
+                s_uses++;
+                tc_fence_after();
+                float s[kBN];
+#pragma unroll
+                for (int c = 0; c < kBN; c += 32) tmem_ld32(s_addr + c, s + c);
+                tmem_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sm->s_empty[tile]);
+
+                const int kv0 = j * kBN;
+                if (kv0 + kBN - 1 > a.start + row0) {  // block reaches past the tile's first query: mask
+#pragma unroll
+                    for (int c = 0; c < kBN; c++)
+                        if (kv0 + c > qpos) s[c] = -INFINITY;
+                }
+                float mx = s[0];
+#pragma unroll
+                for (int c = 1; c < kBN; c++) mx = fmaxf(mx, s[c]);
+                const float mxs = mx * a.scale_log2;
+                bool rescale = false;
+                float alpha = 1.f;
+                if (j == 0) {
+                    m_used = (mxs == -INFINITY) ? 0.f : mxs;
+                } else if (mxs > m_used + kRescaleThreshold) {
+                    alpha = ex2_approx(m_used - mxs);
+                    l *= alpha;
+                    m_used = mxs;
+                    rescale = true;
+                }
+                uint32_t pk[kBN / 2];
+#pragma unroll
+                for (int c = 0; c < kBN; c += 2) {
+                    const float p0 = ex2_approx(fmaf(s[c], a.scale_log2, -m_used));
+                    const float p1 = ex2_approx(fmaf(s[c + 1], a.scale_log2, -m_used));
+                    l += p0 + p1;
+                    pk[c / 2] = pack_half2(p0, p1);
+                }
+                if (j > 0) {  // PV(j-1) must be done before P is overwritten or O is rescaled
+                    ok = mbar_wait(&sm->o_done[tile], o_uses & 1, ab);
+                    if (!ok) break;
+                    o_uses++;
+                    tc_fence_after();
+                }
+                if (rescale) {
+                    float o[kD];
+#pragma unroll
+                    for (int c = 0; c < kD; c += 32) tmem_ld32(o_addr + c, o + c);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int c = 0; c < kD; c++) o[c] *= alpha;
+#pragma unroll
+                    for (int c = 0; c < kD; c += 32) tmem_st32(o_addr + c, o + c);
+                    tmem_wait_st();
+                }
+                // P row -> swizzled smem: 16 chunks of 8 halves; chunk ch of half hh at
+                // hh*16K + row*128 + ((ch ^ (row & 7)) * 16)
+#pragma unroll
+                for (int ch = 0; ch < kBN / 8; ch++) {
+                    const int hh = ch >> 3, c8 = ch & 7;
+                    uint4 val = make_uint4(pk[ch * 4], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
+                    *reinterpret_cast<uint4*>(p_tile + hh * (kBM * 128) + row * 128 + ((c8 ^ (row & 7)) << 4)) = val;
+                }
+                fence_proxy_async_smem();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sm->p_full[tile]);
+            }
+            if (!ok) break;
+            // epilogue: O / l
+            ok = mbar_wait(&sm->o_done[tile], o_uses & 1, ab);
+            if (!ok) break;
+            o_uses++;
+            tc_fence_after();
+            float o[kD];
+#pragma unroll
+            for (int c = 0; c < kD; c += 32) tmem_ld32(o_addr + c, o + c);
+            tmem_wait_ld();
+            tc_fence_before();
+            const int t = row0 + row;
+            if (t < a.tokens) {
+                const float inv = 1.f / l;
+                const int64_t off = x.seq * a.out_seq_stride + static_cast<int64_t>(t) * a.out_token_stride +
+                                    static_cast<int64_t>(x.head) * kD;
+                if (a.out_f16) {
+                    uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(a.out) + off);
+#pragma unroll
+                    for (int c = 0; c < kD; c += 8)
+                        dst[c / 8] = make_uint4(pack_half2(o[c] * inv, o[c + 1] * inv),
+                                                pack_half2(o[c + 2] * inv, o[c + 3] * inv),
+                                                pack_half2(o[c + 4] * inv, o[c + 5] * inv),
+                                                pack_half2(o[c + 6] * inv, o[c + 7] * inv));
+                } else {
+                    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + off);
+#pragma unroll
+                    for (int c = 0; c < kD; c += 4)
+                        dst[c / 4] = make_float4(o[c] * inv, o[c + 1] * inv, o[c + 2] * inv, o[c + 3] * inv);
+                }
+            }
+        }
+    }
+
+    __syncthreads();
+    if (warp == 2) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, kTmemCols);
+    }
+}
+
+// f32 -> f16 copy of Q into the workspace ([seq][token][head][d], dense), for f32 callers.
+__global__ void q_to_half_kernel(const float* __restrict__ q, int64_t token_stride, int64_t seq_stride,
+                                 __half* __restrict__ dst, int n_seqs, int tokens, int hd_total) {
+    const int64_t n = static_cast<int64_t>(n_seqs) * tokens * hd_total;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t c = i % hd_total, r = i / hd_total;
+        const int64_t t = r % tokens, sq = r / tokens;
+        dst[i] = __float2half_rn(q[sq * seq_stride + t * token_stride + c]);
+    }
+}
+
+// ---------------------------------------------------------------------------------------------- host side
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// 4-D f16 map over [seqs][rows][heads][d] with a 64 x 1 x 128 x 1 box, 128-byte swizzle, zero fill.
+bool make_map(CUtensorMap* map, const void* base, int d, int heads, int rows, int seqs, int64_t row_stride,
+              int64_t seq_stride) {
+    EncodeTiledFn enc = get_encode_fn();
+    if (!enc) return false;
+    if (seqs == 1 || seq_stride == 0) seq_stride = static_cast<int64_t>(rows) * row_stride;
+    cuuint64_t dims[4] = {static_cast<cuuint64_t>(d), static_cast<cuuint64_t>(heads), static_cast<cuuint64_t>(rows),
+                          static_cast<cuuint64_t>(seqs)};
+    cuuint64_t strides[3] = {static_cast<cuuint64_t>(d) * 2, static_cast<cuuint64_t>(row_stride) * 2,
+                             static_cast<cuuint64_t>(seq_stride) * 2};
+    cuuint32_t box[4] = {64, 1, 128, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+bool prefill_supported(const alpaca_attn_desc& d) {
+    return d.head_dim == kD && d.kv_dtype == ALPACA_F16 && d.n_kv_heads > 0 && d.n_heads % d.n_kv_heads == 0 &&
+           d.ctx_lens == nullptr;
+}
+
+size_t prefill_workspace_bytes(const alpaca_attn_desc& d) {
+    if (d.q_dtype != ALPACA_F32) return 0;
+    return sizeof(__half) * static_cast<size_t>(d.n_seqs) * d.tokens * d.n_heads * d.head_dim;
+}
+
+cudaError_t launch_prefill(const Call& c, cudaStream_t s) {
+    const alpaca_attn_desc& d = *c.d;
+    static std::once_flag attr_once;
+    static cudaError_t attr_err = cudaSuccess;
+    std::call_once(attr_once, [] {
+        attr_err = cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(kSmemBytes));
+    });
+    if (attr_err != cudaSuccess) return attr_err;
+
+    const void* qh = d.q;
+    int64_t q_ts = d.q_token_stride, q_ss = d.q_seq_stride;
+    if (d.q_dtype == ALPACA_F32) {
+        __half* dst = static_cast<__half*>(c.ws);
+        const int hd_total = d.n_heads * d.head_dim;
+        const int64_t n = static_cast<int64_t>(d.n_seqs) * d.tokens * hd_total;
+        const int blocks = static_cast<int>(std::min<int64_t>((n + 255) / 256, 4096));
+        q_to_half_kernel<<<blocks, 256, 0, s>>>(static_cast<const float*>(d.q), d.q_token_stride, d.q_seq_stride,
+                                                dst, d.n_seqs, d.tokens, hd_total);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+        qh = dst;
+        q_ts = hd_total;
+        q_ss = static_cast<int64_t>(d.tokens) * hd_total;
+    }
+    const int kv_len = d.start_position + d.tokens;
+    CUtensorMap tq, tk, tv;
+    if (!make_map(&tq, qh, d.head_dim, d.n_heads, d.tokens, d.n_seqs, q_ts, q_ss) ||
+        !make_map(&tk, d.k, d.head_dim, d.n_kv_heads, kv_len, d.n_seqs, d.kv_row_stride, d.kv_seq_stride) ||
+        !make_map(&tv, d.v, d.head_dim, d.n_kv_heads, kv_len, d.n_seqs, d.kv_row_stride, d.kv_seq_stride))
+        return cudaErrorInvalidValue;
+
+    PrefillArgs a;
+    a.out = d.out;
+    a.out_token_stride = d.out_token_stride;
+    a.out_seq_stride = d.out_seq_stride;
+    a.out_f16 = d.out_dtype == ALPACA_F16;
+    a.n_seqs = d.n_seqs;
+    a.n_heads = d.n_heads;
+    a.n_kv_heads = d.n_kv_heads;
+    a.tokens = d.tokens;
+    a.start = d.start_position;
+    a.kv_len = kv_len;
+    a.n_pairs = (d.tokens + 2 * kBM - 1) / (2 * kBM);
+    a.total_items = a.n_pairs * d.n_seqs * d.n_heads;
+    a.scale_log2 = c.scale * kLog2e;
+    a.err = c.err;
+    a.flags = d.flags;
+    const int grid = std::max(1, std::min(a.total_items, c.num_sms));
+    prefill_kernel<<<grid, kThreads, kSmemBytes, s>>>(tq, tk, tv, a);
+    return cudaGetLastError();
+}
+
+}  // namespace alpaca

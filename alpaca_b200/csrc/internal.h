@@ -1,0 +1,37 @@
+// internal.h — launchers shared between the C-ABI front end (api.cu) and the kernel translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/alpaca_cuda.h"
+
+namespace alpaca {
+
+// A validated call: the caller's descriptor plus the values the front end resolved for it.
+struct Call {
+    const alpaca_attn_desc* d;
+    float scale;        // softmax scale (desc.scale or 1/sqrt(d))
+    unsigned* err;      // device error word of the current device
+    void* ws;           // caller workspace (may be null when the kernel needs none)
+    size_t ws_bytes;
+    int num_sms;        // multiprocessors of the current device
+};
+
+// ---- split-KV decode (attn_decode.cu)
+int decode_split_len(int head_dim);                          // KV rows per split CTA
+int decode_max_splits(const alpaca_attn_desc& d);            // splits of the longest sequence
+size_t decode_workspace_bytes(const alpaca_attn_desc& d);    // partial-state bytes
+bool decode_supported(const alpaca_attn_desc& d);            // head_dim / group limits of the kernel
+cudaError_t launch_decode(const Call& c, cudaStream_t s);
+
+// ---- general fp32 SIMT attention (attn_general.cu)
+cudaError_t launch_general(const Call& c, cudaStream_t s);
+
+// ---- tcgen05 prefill (attn_prefill_sm100.cu)
+bool prefill_supported(const alpaca_attn_desc& d);
+size_t prefill_workspace_bytes(const alpaca_attn_desc& d);  // f32 -> f16 Q staging when q_dtype is f32
+cudaError_t launch_prefill(const Call& c, cudaStream_t s);
+
+}  // namespace alpaca

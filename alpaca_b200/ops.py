@@ -1,0 +1,145 @@
+"""Host-side attention interface over libalpaca_cuda.so.
+
+``attention`` mirrors alpaca.swift's test-level boundary ``MetalOps.attention(q:keys:values:startPosition:kv:
+precision:) -> Tensor`` (Sources/AlpacaMetal/Backend/MetalOps.swift:177-206): f32 host arrays in, the KV cache
+rounded to f16 with 32 zero pad rows when ``kv == "f16"`` (MetalOps.swift:182-189), the kernel chosen by the
+dispatch policy of ``KernelEncoder.attention`` (KernelEncoder.swift:306-343), f32 [tokens, heads, head_dim] out.
+
+``attention_device`` is the model-path form (``KernelEncoder.attention`` / ``attentionTensor``): torch CUDA
+tensors already resident in HBM, enqueued on the current stream, no host round trip. PyTorch only supplies device
+memory and streams here; all attention arithmetic runs in the library's own sm_100a kernels.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import torch
+
+from ._lib import AlpacaCUDAError, AttnDesc, DType, Kernel, Status, check, load
+
+KV_PADDING_ROWS = 32  # KernelEncoder.kvPaddingRows (KernelEncoder.swift:73)
+
+_DT = {torch.float32: DType.F32, torch.float16: DType.F16}
+
+
+def _dtype(t: torch.Tensor) -> DType:
+    try:
+        return _DT[t.dtype]
+    except KeyError:
+        raise AlpacaCUDAError(Status.INVALID_ARGUMENT, f"unsupported dtype {t.dtype}") from None
+
+
+def _as4(t: torch.Tensor, name: str) -> torch.Tensor:
+    if t.dim() == 3:
+        t = t.unsqueeze(0)
+    if t.dim() != 4:
+        raise AlpacaCUDAError(Status.INVALID_ARGUMENT, f"{name} must be [seqs, rows, heads, head_dim] or 3-D")
+    if t.stride(-1) != 1 or t.stride(-2) != t.shape[-1]:
+        raise AlpacaCUDAError(Status.INVALID_ARGUMENT, f"{name}: [heads, head_dim] must be contiguous")
+    return t
+
+
+def make_desc(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor, *, start_position: int = 0,
+              ctx_lens: torch.Tensor | None = None, max_ctx_len: int | None = None, scale: float = 0.0,
+              flags: int = 0) -> AttnDesc:
+    """Descriptor for q [S,T,H,d], k/v [S,rows,Hkv,d], out [S,T,H,d] (3-D tensors mean S = 1)."""
+    q4, k4, v4, o4 = _as4(q, "q"), _as4(k, "k"), _as4(v, "v"), _as4(out, "out")
+    if k4.stride() != v4.stride() or k4.shape != v4.shape or k4.dtype != v4.dtype:
+        raise AlpacaCUDAError(Status.INVALID_ARGUMENT, "k and v must share shape, dtype and strides")
+    S, T, H, d = q4.shape
+    d_ = AttnDesc()
+    d_.n_seqs, d_.n_heads, d_.n_kv_heads, d_.head_dim = S, H, k4.shape[2], d
+    d_.tokens, d_.start_position = T, int(start_position)
+    if ctx_lens is not None:
+        if ctx_lens.dtype != torch.int32 or not ctx_lens.is_cuda:
+            raise AlpacaCUDAError(Status.INVALID_ARGUMENT, "ctx_lens must be a CUDA int32 tensor")
+        d_.ctx_lens = ctx_lens.data_ptr()
+        d_.max_ctx_len = int(max_ctx_len if max_ctx_len is not None else k4.shape[1])
+    d_.q_dtype, d_.kv_dtype, d_.out_dtype = _dtype(q4), _dtype(k4), _dtype(o4)
+    d_.q, d_.q_token_stride, d_.q_seq_stride = q4.data_ptr(), q4.stride(1), q4.stride(0) if S > 1 else 0
+    d_.k, d_.v = k4.data_ptr(), v4.data_ptr()
+    d_.kv_row_stride, d_.kv_seq_stride = k4.stride(1), k4.stride(0) if S > 1 else 0
+    d_.out, d_.out_token_stride, d_.out_seq_stride = o4.data_ptr(), o4.stride(1), o4.stride(0) if S > 1 else 0
+    d_.scale, d_.flags = float(scale), int(flags) & 0xFFFFFFFF
+    return d_
+
+
+def workspace_bytes(desc: AttnDesc, kind: Kernel = Kernel.AUTO) -> int:
+    n = ctypes.c_size_t(0)
+    check(load().alpaca_attention_workspace_bytes(ctypes.byref(desc), int(kind), ctypes.byref(n)))
+    return int(n.value)
+
+
+def select_kernel(desc: AttnDesc) -> Kernel:
+    k = ctypes.c_int(0)
+    check(load().alpaca_attention_select(ctypes.byref(desc), ctypes.byref(k)))
+    return Kernel(k.value)
+
+
+def launch(desc: AttnDesc, kind: Kernel = Kernel.AUTO, workspace: torch.Tensor | None = None,
+           stream: torch.cuda.Stream | None = None) -> None:
+    """Enqueue one call of alpaca_attention on `stream` (default: torch's current stream)."""
+    s = stream if stream is not None else torch.cuda.current_stream()
+    ws_ptr = workspace.data_ptr() if workspace is not None else None
+    ws_len = workspace.numel() * workspace.element_size() if workspace is not None else 0
+    check(load().alpaca_attention(ctypes.byref(desc), int(kind), ws_ptr, ws_len, s.cuda_stream))
+
+
+def attention_device(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor, *, start_position: int = 0,
+                     kind: Kernel = Kernel.AUTO, ctx_lens: torch.Tensor | None = None,
+                     max_ctx_len: int | None = None, scale: float = 0.0, flags: int = 0,
+                     workspace: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> AttnDesc:
+    """Enqueue attention on device tensors (KernelEncoder.attention / attentionTensor). Allocates the workspace
+    with torch when none is given (callers on a hot loop pass their own)."""
+    desc = make_desc(q, k, v, out, start_position=start_position, ctx_lens=ctx_lens, max_ctx_len=max_ctx_len,
+                     scale=scale, flags=flags)
+    need = workspace_bytes(desc, kind)
+    if need and (workspace is None or workspace.numel() * workspace.element_size() < need):
+        workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+    launch(desc, kind, workspace, stream)
+    return desc
+
+
+def device_status(stream: torch.cuda.Stream | None = None, clear: bool = True) -> None:
+    """Synchronise and raise AlpacaCUDAError(DEVICE_TIMEOUT) if a bounded device-side wait gave up."""
+    s = stream if stream is not None else torch.cuda.current_stream()
+    check(load().alpaca_cuda_device_status(s.cuda_stream, int(clear)))
+
+
+def to_cache(x: np.ndarray, kv: str, device) -> torch.Tensor:
+    """Upload keys/values [capacity, kvHeads, d] as the GPU cache: f32, or f16 with 32 zero pad rows."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    if kv == "f32":
+        return torch.from_numpy(x).to(device)
+    buf = torch.zeros((x.shape[0] + KV_PADDING_ROWS,) + x.shape[1:], dtype=torch.float16, device=device)
+    buf[: x.shape[0]] = torch.from_numpy(x).to(device).half()
+    return buf
+
+
+def attention(q: np.ndarray, keys: np.ndarray, values: np.ndarray, start_position: int, kv: str = "f16",
+              precision: str = "fast", *, kind: Kernel = Kernel.AUTO, device: str | int = "cuda") -> np.ndarray:
+    """MetalOps.attention (MetalOps.swift:177-206).
+
+    q [tokens, heads, d], keys/values [capacity, kvHeads, d], all f32; the query token t sits at absolute
+    position start_position + t. `kv` is "f16" (cache rounded to half, as the model path stores it) or "f32".
+    `precision` is accepted for signature compatibility: every f16-KV prefill kernel here uses f16 MMA operands
+    and f32 accumulation, as both of the reference's prefill paths do. Returns f32 [tokens, heads, d]."""
+    q = np.asarray(q, dtype=np.float32)
+    keys = np.asarray(keys, dtype=np.float32)
+    values = np.asarray(values, dtype=np.float32)
+    if not (q.ndim == 3 and keys.ndim == 3 and keys.shape == values.shape and keys.shape[2] == q.shape[2]
+            and q.shape[1] % keys.shape[1] == 0 and q.shape[2] % 32 == 0 and q.shape[2] <= 256
+            and start_position + q.shape[0] <= keys.shape[0] and start_position >= 0):
+        raise AlpacaCUDAError(Status.INVALID_ARGUMENT, f"attention shapes q {q.shape} k {keys.shape}")
+    if kv not in ("f16", "f32"):
+        raise AlpacaCUDAError(Status.INVALID_ARGUMENT, f"kv precision {kv!r}")
+    if precision not in ("fast", "exact"):
+        raise AlpacaCUDAError(Status.INVALID_ARGUMENT, f"precision {precision!r}")
+    dev = torch.device(device)
+    kb, vb = to_cache(keys, kv, dev), to_cache(values, kv, dev)
+    qb = torch.from_numpy(np.ascontiguousarray(q)).to(dev)
+    out = torch.empty(q.shape, dtype=torch.float32, device=dev)
+    attention_device(qb, kb, vb, out, start_position=start_position, kind=kind)
+    device_status()
+    return out.cpu().numpy()

@@ -1,0 +1,441 @@
+#!/usr/bin/env python3
+"""Benchmark of the attention hot path on B200 (one process per GPU).
+
+Headline (BASELINE.json config 2 at T=4096): causal GQA prefill attention for the SmolLM2-135M shape (9 query /
+3 KV heads, d=64), 30 independent layers' f16 Q/K/V ~ N(0,1) per step, fp32 accumulate, f32 output. One step =
+one call of the C ABI (alpaca_attention) over the 30 layers, which the library runs as one persistent tcgen05
+kernel. `value` is prefill attention TFLOP/s over all ranks (FLOPs = 2*H*d*T*(T+1) per layer); `tokens_per_s`
+is 30*T / step time per rank, summed over ranks. Inputs (236 MB per step) exceed the 126 MB L2.
+
+Also measured in the same run and reported in the `decode` object: config 3 split-KV decode (batch 64, one token
+each, contexts uniform in [1,4096], 30 layers of distinct f16 KV caches per step), as HBM GB/s.
+
+Multi-GPU (torchrun): every rank runs its own independent sequences (weak scaling; (sequence, KV-head) units
+share nothing), timing is the max over ranks, and NCCL only gathers per-rank output checksums after the timed
+region. `--impl reference` times the CPU restatement of alpaca.swift's reference attention (oracle/) on the host
+cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "prefill attn TFLOP/s + decode attn HBM GB/s; tokens/s at 1/2/4/8 B200"
+H, KVH, D = 9, 3, 64
+LAYERS = 30
+T_PREFILL = 4096
+DEC_BATCH, DEC_CAP = 64, 4096
+
+
+def flops_prefill(T: int, heads: int = H, d: int = D) -> float:
+    return 2.0 * heads * d * T * (T + 1)
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        j = json.loads(p.read_text())
+        return {"hbm_gbs": j["hbm_gbs"], "tflops": j["bf16_tflops"], "tflops_sustained": j["bf16_tflops_sustained"],
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "tflops": 1590.0, "tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def profile_traffic(name: str):
+    """Per-launch DRAM bytes recorded from an ncu capture in profiles/<name>.md ("traffic_bytes_per_launch: N")."""
+    p = ROOT / "profiles" / f"{name}.md"
+    if not p.exists():
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", p.read_text())
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, cuda_index: int):
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+        ids = [x.strip() for x in vis.split(",") if x.strip()]
+        self.idx = ids[cuda_index] if cuda_index < len(ids) else str(cuda_index)
+        self.proc = None
+        self.lines: list[str] = []
+        self.t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, val in zip(names, f[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------------------------- distributed
+
+def dist_setup(gpus: int):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != gpus and world > 1:
+        raise SystemExit(f"--gpus {gpus} but WORLD_SIZE {world}")
+    if torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+        pg = dist
+    return rank, world, local, pg
+
+
+def max_over_ranks(x: float, pg) -> float:
+    if pg is None:
+        return x
+    import torch
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(pg):
+    import torch
+    if pg is not None:
+        pg.barrier()
+    torch.cuda.synchronize()
+
+
+# ---------------------------------------------------------------------------------------------- CPU baseline
+
+def cpu_prefill_sample(seconds_target: float, threads: int, T: int = T_PREFILL):
+    """Times the oracle (C restatement of CPUOps.attentionScores/softmax/attentionApply) on a strided sample of
+    one layer's (head, token) rows of config 2; returns (TFLOP/s, sample description, threads)."""
+    import numpy as np
+
+    import oracle
+    q = oracle.f16_round(oracle.splitmix_normal(7, (T, H, D)))
+    k = oracle.f16_round(oracle.splitmix_normal(8, (T, KVH, D)))
+    v = oracle.f16_round(oracle.splitmix_normal(9, (T, KVH, D)))
+    out = np.zeros((T, H, D), np.float32)
+    # Rows are h*T + t. Blocks of `blk` consecutive rows at evenly spread offsets cover the causal range; each
+    # block runs on all `threads` (the oracle interleaves a block's rows over its POSIX threads). FLOPs are
+    # counted exactly per row (4*d*(t+1)), so the rate is exact for the sample.
+    blk = max(1, threads) * 8
+    done_flops, elapsed, nrows = 0.0, 0.0, 0
+    for nblocks in (4, 16, 64, 256, 1024):
+        if elapsed >= seconds_target:
+            break
+        starts = [int((i + 0.5) * (H * T - blk) / nblocks) for i in range(nblocks)]
+        t0 = time.perf_counter()
+        for r0 in starts:
+            oracle.attention(q, k, v, 0, threads=threads, rows=(r0, r0 + blk), out=out)
+        dt = time.perf_counter() - t0
+        done_flops += sum(4.0 * D * (((r0 + i) % T) + 1) for r0 in starts for i in range(blk))
+        elapsed += dt
+        nrows += nblocks * blk
+    tflops = done_flops / elapsed / 1e12
+    return tflops, f"{nrows} (head, token) rows of one T={T} layer in blocks spread over the causal range, " \
+                   f"{elapsed:.1f} s", threads
+
+
+# ---------------------------------------------------------------------------------------------- our arm
+
+def run_ours(args):
+    import numpy as np
+    import torch
+
+    import alpaca_b200 as ab
+    from alpaca_b200 import Kernel
+    rank, world, local, pg = dist_setup(args.gpus)
+    ab.load()
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream()
+    pk = peaks()
+    T = args.tokens
+
+    # ---- inputs: 30 layers as independent sequences, seeded per rank
+    g = torch.Generator(device=dev)
+    g.manual_seed(20260102 + 1000 * rank)
+    q = torch.randn((LAYERS, T, H, D), generator=g, device=dev).half()
+    k = torch.randn((LAYERS, T, KVH, D), generator=g, device=dev).half()
+    v = torch.randn((LAYERS, T, KVH, D), generator=g, device=dev).half()
+    out = torch.empty((LAYERS, T, H, D), dtype=torch.float32, device=dev)
+    desc = ab.make_desc(q, k, v, out, start_position=0)
+    assert ab.workspace_bytes(desc, Kernel.PREFILL_TC) == 0
+
+    def step():
+        ab.launch(desc, Kernel.PREFILL_TC, None, stream)
+
+    for _ in range(args.warmup):
+        step()
+    ab.device_status()
+    clocks = ClockSampler(local)
+    clocks.start()
+    barrier(pg)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    barrier(pg)
+    clk = clocks.stop()
+    ab.device_status()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    ms_max = max_over_ranks(ms, pg)
+    flops_step = LAYERS * flops_prefill(T)
+    value = world * flops_step / (ms_max * 1e-3) / 1e12
+    tokens_per_s = world * LAYERS * T / (ms_max * 1e-3)
+    kernel_tflops = flops_step / (ms * 1e-3) / 1e12  # one launch per step on this rank
+
+    # ---- correctness spot check of the timed output vs the oracle (rank 0, a few rows of layer 0)
+    spot = None
+    if rank == 0:
+        import oracle
+        q0, k0, v0 = (x[0].float().cpu().numpy() for x in (q, k, v))
+        o0 = out[0].cpu().numpy()
+        ref = np.zeros_like(o0)
+        rows = [0, 1, 129, T - 1, T + 5, 3 * T + 2047, 9 * T - 1]
+        for r in rows:
+            oracle.attention(q0, k0, v0, 0, rows=(r, r + 1), out=ref)
+        sel = np.zeros((T, H), bool)
+        for r in rows:
+            sel[r % T, r // T] = True
+        spot = float(np.abs(o0[sel] - ref[sel]).max())
+
+    # ---- NCCL gather of per-rank output checksums (outside the timed region)
+    gather_ms = None
+    if pg is not None:
+        cs = out.double().sum().reshape(1)
+        allcs = [torch.zeros_like(cs) for _ in range(world)]
+        t0 = time.perf_counter()
+        pg.all_gather(allcs, cs)
+        torch.cuda.synchronize()
+        gather_ms = (time.perf_counter() - t0) * 1e3
+
+    # ---- e2e: host buffers (pinned), H2D of the step's inputs + kernel + D2H of the output, every step
+    hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
+    hout = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv))
+    d2h = hout.numel() * hout.element_size()
+
+    def e2e_step():
+        q.copy_(hq, non_blocking=True)
+        k.copy_(hk, non_blocking=True)
+        v.copy_(hv, non_blocking=True)
+        ab.launch(desc, Kernel.PREFILL_TC, None, stream)
+        hout.copy_(out, non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 10))
+    for _ in range(2):
+        e2e_step()
+    barrier(pg)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    barrier(pg)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps, pg)
+    e2e_value = world * flops_step / (e2e_ms * 1e-3) / 1e12
+    del hq, hk, hv, hout
+
+    # ---- decode (config 3): 30 layers x batch 64, ragged contexts, distinct caches per layer
+    decode = run_decode(args, ab, torch, dev, stream, rank, world, pg, pk) if not args.no_decode else None
+
+    # ---- CPU baseline (rank 0 at N=1 only)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        import oracle
+        thr = oracle.host_threads()
+        tf, sample, cores = cpu_prefill_sample(args.cpu_seconds, thr, T)
+        cpu = {"value": tf, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample}
+
+    if pg is not None:
+        pg.barrier()
+    if rank == 0:
+        traffic = profile_traffic("prefill_sm100_cfg2")
+        roof = {"bound": "tensor", "achieved": kernel_tflops, "peak": pk["tflops"], "unit": "TFLOP/s",
+                "frac": kernel_tflops / pk["tflops"], "traffic": traffic,
+                "peak_source": f"{pk['source']} bf16 dense burst (MEASURED_PEAKS.json bf16_tflops)",
+                "kernel": "alpaca::prefill_kernel (tcgen05)",
+                "algorithmic_flops_per_launch": flops_step}
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic N(0,1) (torch.randn seeded per rank)",
+            "config": {"workload": f"config 2: SmolLM2-135M causal GQA prefill, T={T}, {LAYERS} independent layers "
+                                   f"per step, 9/3 heads, d=64, f16 in / f32 out", "tokens": T, "layers": LAYERS,
+                       "heads": H, "kv_heads": KVH, "head_dim": D, "batch_per_gpu": 1,
+                       "parallelism": f"independent sequences per GPU x{world}",
+                       "l2": "inputs 236 MB per step > 126 MB L2 (no flush)"},
+            "tokens_per_s": tokens_per_s,
+            "roofline": roof,
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": e2e_ms, "api": "alpaca_attention via ctypes, pinned host buffers"},
+            "gpu_launches": args.steps * 1,
+            "clocks": clk,
+            "decode": decode,
+            "spot_check_max_abs": spot,
+            "gather_ms": gather_ms,
+        }
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        pg.destroy_process_group()
+
+
+def run_decode(args, ab, torch, dev, stream, rank, world, pg, pk):
+    from alpaca_b200 import Kernel
+    g = torch.Generator(device=dev)
+    g.manual_seed(20260103 + 1000 * rank)
+    gl = torch.Generator()
+    gl.manual_seed(20260103)
+    lens = torch.randint(1, DEC_CAP + 1, (LAYERS, DEC_BATCH), generator=gl, dtype=torch.int32)
+    lens_d = lens.to(dev)
+    kc = torch.randn((LAYERS, DEC_BATCH, DEC_CAP, KVH, D), generator=g, device=dev).half()
+    vc = torch.randn((LAYERS, DEC_BATCH, DEC_CAP, KVH, D), generator=g, device=dev).half()
+    qd = torch.randn((LAYERS, DEC_BATCH, 1, H, D), generator=g, device=dev)
+    od = torch.empty((LAYERS, DEC_BATCH, 1, H, D), dtype=torch.float32, device=dev)
+    descs = [ab.make_desc(qd[l], kc[l], vc[l], od[l], ctx_lens=lens_d[l], max_ctx_len=DEC_CAP)
+             for l in range(LAYERS)]
+    wsb = max(ab.workspace_bytes(dd, Kernel.DECODE_SPLIT) for dd in descs)
+    ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+
+    def step():
+        for dd in descs:
+            ab.launch(dd, Kernel.DECODE_SPLIT, ws, stream)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    ab.device_status()
+    steps = max(5, args.steps)
+    barrier(pg)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    barrier(pg)
+    ab.device_status()
+    ms = e0.elapsed_time(e1) / steps
+    ms_max = max_over_ranks(ms, pg)
+    kv_bytes = float(lens.sum().item()) * KVH * D * 2 * 2
+    qo_bytes = LAYERS * DEC_BATCH * H * D * 4 * 2
+    byts = kv_bytes + qo_bytes
+    gbs = byts / (ms * 1e-3) / 1e9
+    return {"workload": "config 3: batch 64 one-token decode, contexts U[1,4096], 9/3 heads, d=64, f16 KV, "
+                        f"{LAYERS} layers (distinct caches, {kc.numel() * 4 / 1e9:.1f} GB) per step",
+            "value": world * byts / (ms_max * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms_max,
+            "tokens_per_s": world * DEC_BATCH / (ms_max * 1e-3 / LAYERS) / LAYERS,
+            "bytes_per_step": byts,
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": gbs / pk["hbm_gbs"], "traffic": profile_traffic("decode_split_cfg3"),
+                         "kernel": "alpaca::decode_split_kernel<64,3> + decode_combine_kernel (per layer)"},
+            "gpu_launches": steps * LAYERS * 2}
+
+
+# ---------------------------------------------------------------------------------------------- reference arm
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    import oracle
+    oracle.build()
+    thr = oracle.host_threads()
+    T = args.tokens
+    vals = []
+    for i in range(args.warmup + args.steps):
+        tf, sample, cores = cpu_prefill_sample(args.ref_seconds, thr, T)
+        if i >= args.warmup:
+            vals.append(tf)
+    value = statistics.median(vals)
+    full_step_s = LAYERS * flops_prefill(T) / (value * 1e12)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": full_step_s * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1) (SplitMix64 Box-Muller)",
+        "config": {"workload": f"config 2: SmolLM2-135M causal GQA prefill, T={T}, {LAYERS} independent layers "
+                               f"per step, 9/3 heads, d=64 (CPU reference restatement, sampled rows)",
+                   "tokens": T, "layers": LAYERS},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "alpaca.swift is Swift + Metal (no Swift toolchain or Apple GPU here); the reference's CPU "
+                "attention (CPUOps.swift:162-274) runs as its C restatement in oracle/ on all host threads; ms_per_step "
+                "is the extrapolated time of a full 30-layer step",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--tokens", type=int, default=T_PREFILL)
+    ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--ref-seconds", type=float, default=4.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,150 @@
+/*
+ * alpaca_cuda.h — C ABI of the B200 (sm_100a) attention library for alpaca.swift.
+ *
+ * This library is a drop-in for the attention hot path of alpaca.swift's Metal backend. Each entry point
+ * below names the reference interface it replaces (paths are relative to the alpaca.swift repository):
+ *
+ *   KernelEncoder.attention(q:kCache:vCache:out:heads:kvHeads:headDim:startPosition:tokens:kv:decodeScratch:outputHalf:)
+ *       Sources/AlpacaMetal/Backend/KernelEncoder.swift:306-343        -> alpaca_attention (ALPACA_ATTN_AUTO)
+ *   KernelEncoder.attentionTensor(qHalf:kCache:vCache:out:outputHalf:...)
+ *       Sources/AlpacaMetal/Backend/KernelEncoder.swift:284-292        -> alpaca_attn_prefill
+ *   the split-K decode branch of KernelEncoder.attention (attn_decode_split_* + attn_decode_merge)
+ *       Sources/AlpacaMetal/Backend/KernelEncoder.swift:309-326        -> alpaca_attn_decode
+ *   KernelEncoder.decodeScratchBytes(heads:kvHeads:headDim:capacity:)
+ *       Sources/AlpacaMetal/Backend/KernelEncoder.swift:88-92          -> alpaca_attention_workspace_bytes
+ *   MetalError.invalidArgument / .unsupported / .commandFailed
+ *       Sources/AlpacaMetal/Backend/MetalContext.swift:7-31            -> alpaca_cuda_status + alpaca_cuda_status_string
+ *
+ * Data layout (the hand-off of Sources/AlpacaMetal/Backend/MetalLlamaModel.swift:189-191, 322-337):
+ *   q    [n_seqs][tokens][n_heads][head_dim]     post-RoPE queries (f16 or f32); token t of a sequence sits at
+ *                                                 absolute position start_position + t.
+ *   k, v [n_seqs][rows][n_kv_heads][head_dim]    KV cache rows, row index = absolute position (f16 or f32).
+ *                                                 K holds post-RoPE keys, V raw values. Query head h reads KV
+ *                                                 head h / (n_heads / n_kv_heads).
+ *   out  [n_seqs][tokens][n_heads][head_dim]     context vectors (f32 or f16).
+ * Strides are in elements. The innermost [heads][head_dim] block of one token / row is contiguous.
+ *
+ * Ownership and threading: every pointer in a descriptor is a caller-owned device pointer. Calls only
+ * enqueue work on `stream` and return; the library never allocates device memory on the attention path.
+ * Scratch space is passed in by the caller and sized by alpaca_attention_workspace_bytes. Calls on different
+ * streams may run concurrently; descriptors are read only during the call.
+ */
+#ifndef ALPACA_CUDA_H
+#define ALPACA_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ALPACA_CUDA_VERSION 10000 /* 1.0.0 */
+
+/* Same object as cudaStream_t; NULL is the legacy default stream. */
+typedef struct CUstream_st* alpaca_stream_t;
+
+/* Status codes. Mirrors MetalError (MetalContext.swift:7-16): INVALID_ARGUMENT ~ .invalidArgument,
+ * UNSUPPORTED ~ .unsupported, LAUNCH_FAILED / CUDA_ERROR / DEVICE_TIMEOUT ~ .commandFailed. */
+typedef enum alpaca_cuda_status {
+    ALPACA_CUDA_OK = 0,
+    ALPACA_CUDA_ERR_INVALID_ARGUMENT = 1,    /* bad shape, stride, pointer, alignment or G above the limit */
+    ALPACA_CUDA_ERR_UNSUPPORTED = 2,         /* valid request this build has no kernel for (dtype, head_dim) */
+    ALPACA_CUDA_ERR_WORKSPACE_TOO_SMALL = 3, /* workspace_bytes below alpaca_attention_workspace_bytes() */
+    ALPACA_CUDA_ERR_LAUNCH_FAILED = 4,       /* the kernel launch itself failed */
+    ALPACA_CUDA_ERR_DEVICE_TIMEOUT = 5,      /* a bounded device-side wait gave up (see alpaca_cuda_device_status) */
+    ALPACA_CUDA_ERR_CUDA = 6                 /* any other CUDA runtime / driver error */
+} alpaca_cuda_status;
+
+typedef enum alpaca_dtype {
+    ALPACA_F32 = 0,
+    ALPACA_F16 = 1 /* IEEE binary16 */
+} alpaca_dtype;
+
+/* Kernel selection. ALPACA_ATTN_AUTO applies the dispatch policy of KernelEncoder.attention
+ * (KernelEncoder.swift:306-343): split decode for one f16-KV token with context >= ALPACA_DECODE_MINCTX,
+ * the tensor-core prefill for f16 KV and >= 8 tokens, and the general fp32 kernel otherwise. */
+typedef enum alpaca_attn_kernel {
+    ALPACA_ATTN_AUTO = 0,
+    ALPACA_ATTN_DECODE_SPLIT = 1, /* split-KV decode + combine (attention_decode.metal) */
+    ALPACA_ATTN_PREFILL_TC = 2,   /* tcgen05 causal flash prefill (tensor_attention.metal, attention_prefill.metal) */
+    ALPACA_ATTN_GENERAL = 3       /* fp32 SIMT online-softmax attention, f16 or f32 KV (attention.metal) */
+} alpaca_attn_kernel;
+
+/* Descriptor flags. */
+#define ALPACA_ATTN_FLAG_NONE 0u
+/* Fault-injection hook for tests: the tensor-core prefill kernel waits on a barrier nothing arrives at, with a
+ * ~2 ms limit, so its bounded-wait give-up path runs. The call still returns OK (it only enqueues);
+ * alpaca_cuda_device_status then reports ALPACA_CUDA_ERR_DEVICE_TIMEOUT. The output is unspecified. */
+#define ALPACA_ATTN_FLAG_DEBUG_FORCE_TIMEOUT (1u << 31)
+
+typedef struct alpaca_attn_desc {
+    int32_t n_seqs;          /* independent sequences (or layers) in this call, >= 1 */
+    int32_t n_heads;         /* query heads H */
+    int32_t n_kv_heads;      /* KV heads Hkv; H % Hkv == 0 */
+    int32_t head_dim;        /* d: multiple of 32, <= 256 (64 and 128 have fast kernels) */
+    int32_t tokens;          /* query tokens per sequence, >= 1 */
+    int32_t start_position;  /* absolute position of query token 0; visible KV rows = start_position + tokens */
+    const int32_t* ctx_lens; /* decode only (tokens == 1): optional DEVICE array [n_seqs] of visible KV rows per
+                                sequence (>= 1). When set it overrides start_position (start = ctx_len - 1). */
+    int32_t max_ctx_len;     /* required with ctx_lens: an upper bound of every ctx_lens entry */
+    int32_t q_dtype;         /* alpaca_dtype */
+    int32_t kv_dtype;        /* alpaca_dtype (K and V share it) */
+    int32_t out_dtype;       /* alpaca_dtype */
+    int32_t reserved0;
+    const void* q;
+    int64_t q_token_stride;  /* elements between consecutive tokens (usually n_heads*head_dim) */
+    int64_t q_seq_stride;    /* elements between sequences */
+    const void* k;
+    const void* v;
+    int64_t kv_row_stride;   /* elements between cache rows (usually n_kv_heads*head_dim) */
+    int64_t kv_seq_stride;   /* elements between sequences' caches */
+    void* out;
+    int64_t out_token_stride;
+    int64_t out_seq_stride;
+    float scale;             /* softmax scale; 0 selects 1/sqrt(head_dim) as CPUOps.attentionScores does */
+    uint32_t flags;          /* ALPACA_ATTN_FLAG_* */
+} alpaca_attn_desc;
+
+/* Enqueue attention described by `desc` with the kernel `kind` on `stream`.
+ * Replaces KernelEncoder.attention (KernelEncoder.swift:306-343) when kind == ALPACA_ATTN_AUTO. */
+alpaca_cuda_status alpaca_attention(const alpaca_attn_desc* desc, alpaca_attn_kernel kind, void* workspace,
+                                    size_t workspace_bytes, alpaca_stream_t stream);
+
+/* Tensor-core causal prefill (tcgen05 + TMEM + TMA). f16 KV; f16 or f32 Q (f32 Q is converted into the
+ * workspace first, as MetalLlamaModel.swift:327 converts Q to half). Replaces KernelEncoder.attentionTensor
+ * (KernelEncoder.swift:284-292) and the tiled attn_prefill branch (KernelEncoder.swift:328-335). */
+alpaca_cuda_status alpaca_attn_prefill(const alpaca_attn_desc* desc, void* workspace, size_t workspace_bytes,
+                                       alpaca_stream_t stream);
+
+/* Split-KV single-token decode over the f16 KV cache plus the combine kernel. Replaces the decode-split branch
+ * of KernelEncoder.attention (KernelEncoder.swift:309-326). tokens must be 1. */
+alpaca_cuda_status alpaca_attn_decode(const alpaca_attn_desc* desc, void* workspace, size_t workspace_bytes,
+                                      alpaca_stream_t stream);
+
+/* Bytes of workspace `kind` needs for `desc` (0 when none). Replaces KernelEncoder.decodeScratchBytes
+ * (KernelEncoder.swift:88-92). Host-only; enqueues nothing. */
+alpaca_cuda_status alpaca_attention_workspace_bytes(const alpaca_attn_desc* desc, alpaca_attn_kernel kind,
+                                                    size_t* bytes);
+
+/* Which kernel ALPACA_ATTN_AUTO would run for `desc` (host-only policy query, KernelEncoder.swift:306-343). */
+alpaca_cuda_status alpaca_attention_select(const alpaca_attn_desc* desc, alpaca_attn_kernel* kind);
+
+/* Synchronises `stream`, then reports and (when `clear` != 0) resets the device-side error word of the current
+ * device: ALPACA_CUDA_ERR_DEVICE_TIMEOUT when a bounded wait gave up, ALPACA_CUDA_OK otherwise. */
+alpaca_cuda_status alpaca_cuda_device_status(alpaca_stream_t stream, int clear);
+
+/* Static description of a status code. */
+const char* alpaca_cuda_status_string(alpaca_cuda_status status);
+
+/* Detail message of the last failing call on this host thread ("" when none). */
+const char* alpaca_cuda_last_error(void);
+
+/* ALPACA_CUDA_VERSION of the loaded library. */
+int alpaca_cuda_version(void);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* ALPACA_CUDA_H */

@@ -1,0 +1,168 @@
+"""CPU oracle for the attention hot path — TEST INFRASTRUCTURE ONLY.
+
+ctypes bindings of ``oracle/liboracle.so`` (the C restatement of alpaca.swift's
+``CPUOps.attentionScores / softmax / attentionApply``, Sources/AlpacaCore/Operations/CPUOps.swift:162-274).
+Only ``tests/``, ``__graft_entry__.smoke()`` and the CPU-baseline leg of ``bench.py`` import this module, as the
+checker. The product package ``alpaca_b200`` never imports it.
+
+Parity of this oracle is pinned against the reference's own known-answer fixture
+(Tests/AlpacaCoreTests/Fixtures/ops.json["attention"], committed as tests/golden/attention_kat.json).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+_HERE = Path(__file__).resolve().parent
+_LIB_PATH = _HERE / "liboracle.so"
+_lib = None
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+_f64p = ctypes.POINTER(ctypes.c_double)
+
+
+def build(force: bool = False) -> Path:
+    """Compile liboracle.so with the committed Makefile (gcc, no fast-math, no FMA contraction)."""
+    src = _HERE / "cpu_attention.c"
+    if force or not _LIB_PATH.exists() or _LIB_PATH.stat().st_mtime < src.stat().st_mtime:
+        subprocess.run(["make", "-s", "-C", str(_HERE), "liboracle.so"], check=True)
+    return _LIB_PATH
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not _LIB_PATH.exists():
+            build()
+        L = ctypes.CDLL(str(_LIB_PATH))
+        L.oracle_f16_round.restype = ctypes.c_float
+        L.oracle_f16_round.argtypes = [ctypes.c_float]
+        L.oracle_f16_round_array.argtypes = [_f32p, _f32p, ctypes.c_int64]
+        L.oracle_attention_scores.argtypes = [_f32p, _f32p] + [ctypes.c_int] * 6 + [_f32p]
+        L.oracle_softmax.argtypes = [_f32p, ctypes.c_int64, ctypes.c_int]
+        L.oracle_attention_apply.argtypes = [_f32p, _f32p] + [ctypes.c_int] * 5 + [_f32p]
+        L.oracle_attention.argtypes = ([_f32p, _f32p, _f32p] + [ctypes.c_int] * 6 +
+                                       [ctypes.c_float, _f32p, ctypes.c_int, ctypes.c_int64, ctypes.c_int64])
+        L.oracle_attention_strided.argtypes = ([_f32p, ctypes.c_int64, _f32p, _f32p, ctypes.c_int64] +
+                                               [ctypes.c_int] * 6 +
+                                               [ctypes.c_float, _f32p, ctypes.c_int64, ctypes.c_int,
+                                                ctypes.c_int64, ctypes.c_int64])
+        L.oracle_error_metrics.argtypes = [_f32p, _f64p, ctypes.c_int64, _f64p]
+        L.oracle_error_metrics_f32.argtypes = [_f32p, _f32p, ctypes.c_int64, _f64p]
+        L.oracle_splitmix_uniform.argtypes = [ctypes.c_uint64, ctypes.c_float, _f32p, ctypes.c_int64]
+        L.oracle_splitmix_normal.argtypes = [ctypes.c_uint64, _f32p, ctypes.c_int64]
+        _lib = L
+    return _lib
+
+
+def _p32(a: np.ndarray):
+    assert a.dtype == np.float32 and a.flags.c_contiguous
+    return a.ctypes.data_as(_f32p)
+
+
+def f16_round(x: np.ndarray) -> np.ndarray:
+    """f32 -> binary16 (round to nearest even) -> f32, as Tensor.converted(to: .float16)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty_like(x)
+    lib().oracle_f16_round_array(_p32(x), _p32(out), x.size)
+    return out
+
+
+def attention_scores(q, keys, length: int, start: int) -> np.ndarray:
+    """CPUOps.attentionScores (CPUOps.swift:222-249): [H, T, length] with -inf where masked."""
+    q = np.ascontiguousarray(q, np.float32)
+    keys = np.ascontiguousarray(keys, np.float32)
+    T, H, d = q.shape
+    kvh = keys.shape[1]
+    if keys.ndim != 3 or keys.shape[2] != d or H % kvh != 0:
+        raise ValueError(f"attentionScores: q {q.shape}, keys {keys.shape}")
+    if not (0 <= length <= keys.shape[0] and start + T <= length):
+        raise ValueError(f"attention length {length}, start {start}, tokens {T}, capacity {keys.shape[0]}")
+    s = np.empty((H, T, length), np.float32)
+    lib().oracle_attention_scores(_p32(q), _p32(keys), T, H, kvh, d, length, start, _p32(s))
+    return s
+
+
+def softmax(x) -> np.ndarray:
+    """CPUOps.softmax (CPUOps.swift:162-175) over the last dimension."""
+    x = np.array(x, dtype=np.float32, copy=True, order="C")
+    n = x.shape[-1]
+    lib().oracle_softmax(_p32(x), x.size // n, n)
+    return x
+
+
+def attention_apply(probs, values) -> np.ndarray:
+    """CPUOps.attentionApply (CPUOps.swift:252-274): [T, H, d]."""
+    probs = np.ascontiguousarray(probs, np.float32)
+    values = np.ascontiguousarray(values, np.float32)
+    H, T, L = probs.shape
+    kvh, d = values.shape[1], values.shape[2]
+    out = np.empty((T, H, d), np.float32)
+    lib().oracle_attention_apply(_p32(probs), _p32(values), H, T, L, kvh, d, _p32(out))
+    return out
+
+
+def attention(q, keys, values, start: int, length: int | None = None, scale: float = 0.0, threads: int = 1,
+              rows: tuple[int, int] | None = None, out: np.ndarray | None = None) -> np.ndarray:
+    """Fused row-by-row CPU attention, bit-identical to scores -> softmax -> apply.
+
+    q [T,H,d]; keys/values [capacity,Hkv,d] (first `length` rows read, default start+T). `rows` restricts the
+    computation to rows h*T+t in [rows[0], rows[1]) (others stay as in `out`, default zeros)."""
+    q = np.ascontiguousarray(q, np.float32)
+    keys = np.ascontiguousarray(keys, np.float32)
+    values = np.ascontiguousarray(values, np.float32)
+    T, H, d = q.shape
+    kvh = keys.shape[1]
+    if length is None:
+        length = start + T
+    if not (keys.shape == values.shape and keys.shape[2] == d and H % kvh == 0):
+        raise ValueError(f"attention shapes q {q.shape} k {keys.shape} v {values.shape}")
+    if not (0 <= length <= keys.shape[0] and start + T <= length):
+        raise ValueError(f"attention length {length}, start {start}, tokens {T}, capacity {keys.shape[0]}")
+    if out is None:
+        out = np.zeros((T, H, d), np.float32)
+    r0, r1 = rows if rows is not None else (0, H * T)
+    lib().oracle_attention(_p32(q), _p32(keys), _p32(values), T, H, kvh, d, length, start, float(scale),
+                           _p32(out), int(threads), int(r0), int(r1))
+    return out
+
+
+def error_metrics(actual, expected) -> dict:
+    """ErrorMetrics (ErrorMetrics.swift:15-27)."""
+    a = np.ascontiguousarray(actual, np.float32).reshape(-1)
+    e = np.ascontiguousarray(expected, np.float64).reshape(-1)
+    if a.size != e.size:
+        raise ValueError("length mismatch")
+    o = np.zeros(4, np.float64)
+    lib().oracle_error_metrics(_p32(a), e.ctypes.data_as(_f64p), a.size, o.ctypes.data_as(_f64p))
+    return {"n": int(a.size), "maxAbs": float(o[0]), "meanAbs": float(o[1]), "rms": float(o[2]),
+            "maxRelPeak": float(o[3])}
+
+
+def format_metrics(m: dict) -> str:
+    return (f"n={m['n']} maxAbs={m['maxAbs']:.3e} meanAbs={m['meanAbs']:.3e} rms={m['rms']:.3e} "
+            f"maxRel(peak)={m['maxRelPeak']:.3e}")
+
+
+def splitmix_uniform(seed: int, shape, scale: float = 1.0) -> np.ndarray:
+    """SplitMix.nextFloat() draws of KernelTests.swift:102-114 (uniform [-1,1)), in row-major order."""
+    n = int(np.prod(shape))
+    out = np.empty(n, np.float32)
+    lib().oracle_splitmix_uniform(ctypes.c_uint64(seed & (2**64 - 1)), float(scale), _p32(out), n)
+    return out.reshape(shape)
+
+
+def splitmix_normal(seed: int, shape) -> np.ndarray:
+    """SplitMix64 + Box-Muller N(0,1) draws, row-major."""
+    n = int(np.prod(shape))
+    out = np.empty(max(n, 1), np.float32)
+    lib().oracle_splitmix_normal(ctypes.c_uint64(seed & (2**64 - 1)), _p32(out), n)
+    return out[:n].reshape(shape)
+
+
+def host_threads() -> int:
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)

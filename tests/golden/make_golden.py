@@ -1,0 +1,39 @@
+#!/usr/bin/env python3
+"""Regenerates the golden vectors in tests/golden/ from the alpaca.swift checkout.
+
+Run in a container that has the reference mounted (default path via $ALPACA_REFERENCE):
+
+    python tests/golden/make_golden.py [/path/to/alpaca.swift]
+
+Outputs (committed; nothing reads the reference at test time):
+  attention_kat.json  the reference's own attention known-answer case, Tests/AlpacaCoreTests/Fixtures/ops.json
+                      ["attention"] (generated upstream by Scripts/generate_op_fixtures.py:64-74 as a float64
+                      torch SDPA), copied verbatim, plus the reference tolerances of OperationTests.swift:72-86.
+  softmax_kat.json    ops.json["softmax"] (±30-sigma inputs, float64 expected), OperationTests softmax case.
+"""
+from __future__ import annotations
+
+import json
+import os
+import sys
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+
+
+def main() -> None:
+    ref = Path(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("ALPACA_REFERENCE", "/root/reference"))
+    ops = json.loads((ref / "Tests/AlpacaCoreTests/Fixtures/ops.json").read_text())
+    att = dict(ops["attention"])
+    att["source"] = "alpaca.swift Tests/AlpacaCoreTests/Fixtures/ops.json[\"attention\"]"
+    att["tolerance"] = {"atol": 3e-6, "rtol": 1e-5, "from": "Tests/AlpacaCoreTests/OperationTests.swift:85"}
+    (HERE / "attention_kat.json").write_text(json.dumps(att))
+    sm = dict(ops["softmax"])
+    sm["source"] = "alpaca.swift Tests/AlpacaCoreTests/Fixtures/ops.json[\"softmax\"]"
+    (HERE / "softmax_kat.json").write_text(json.dumps(sm))
+
+    print("wrote", sorted(p.name for p in HERE.iterdir()))
+
+
+if __name__ == "__main__":
+    main()

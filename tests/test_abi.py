@@ -1,0 +1,175 @@
+"""The C ABI without a GPU: the library loads, exports every symbol include/alpaca_cuda.h declares, and its
+host-only entry points (validation, dispatch policy, workspace sizing, status strings) behave as specified.
+No call here launches a kernel."""
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+HEADER = ROOT / "include" / "alpaca_cuda.h"
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from alpaca_b200 import build
+    try:
+        build.build()
+    except (RuntimeError, OSError) as e:  # pragma: no cover - toolchain missing
+        pytest.fail(f"cannot build libalpaca_cuda.so: {e}")
+    import alpaca_b200
+    return alpaca_b200.load()
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?[a-z_]+\s*\*?\s*(alpaca_[a-z_0-9]+)\s*\(", text, re.M)))
+
+
+def test_header_declarations_match_bindings():
+    import alpaca_b200
+    assert declared_functions() == sorted(alpaca_b200.EXPORTED_SYMBOLS)
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+    assert lib.alpaca_cuda_version() == 10000
+
+
+def test_status_strings(lib):
+    from alpaca_b200 import Status
+    for s in Status:
+        assert lib.alpaca_cuda_status_string(int(s))
+    assert lib.alpaca_cuda_status_string(99) == b"unknown status"
+
+
+FAKE = 1 << 20  # a 16-byte aligned fake device address: validation never dereferences pointers
+
+
+def desc(**kw):
+    from alpaca_b200 import AttnDesc, DType
+    d = AttnDesc()
+    d.n_seqs, d.n_heads, d.n_kv_heads, d.head_dim = 1, 9, 3, 64
+    d.tokens, d.start_position = 128, 0
+    d.q_dtype = d.kv_dtype = int(DType.F16)
+    d.out_dtype = int(DType.F32)
+    d.q = d.k = d.v = d.out = FAKE
+    d.q_token_stride = d.out_token_stride = 9 * 64
+    d.kv_row_stride = 3 * 64
+    for k, v in kw.items():
+        setattr(d, k, v)
+    return d
+
+
+def select(lib, d):
+    k = ctypes.c_int(-1)
+    st = lib.alpaca_attention_select(ctypes.byref(d), ctypes.byref(k))
+    return st, k.value
+
+
+def ws(lib, d, kind=0):
+    n = ctypes.c_size_t(0)
+    st = lib.alpaca_attention_workspace_bytes(ctypes.byref(d), kind, ctypes.byref(n))
+    return st, n.value
+
+
+def test_dispatch_policy_mirrors_kernel_encoder(lib):
+    """KernelEncoder.attention (KernelEncoder.swift:309-343): decode split for one f16-KV token with context >= 64,
+    head_dim 64/128 and G <= 8; tensor prefill for f16 KV and >= 8 tokens; the general kernel otherwise."""
+    from alpaca_b200 import DType, Kernel, Status
+    assert select(lib, desc()) == (Status.OK, Kernel.PREFILL_TC)
+    assert select(lib, desc(tokens=7)) == (Status.OK, Kernel.GENERAL)
+    assert select(lib, desc(tokens=8)) == (Status.OK, Kernel.PREFILL_TC)
+    assert select(lib, desc(tokens=1, start_position=63)) == (Status.OK, Kernel.DECODE_SPLIT)
+    assert select(lib, desc(tokens=1, start_position=62)) == (Status.OK, Kernel.GENERAL)
+    assert select(lib, desc(kv_dtype=int(DType.F32))) == (Status.OK, Kernel.GENERAL)
+    assert select(lib, desc(tokens=1, start_position=100, kv_dtype=int(DType.F32))) == (Status.OK, Kernel.GENERAL)
+    assert select(lib, desc(tokens=1, start_position=100, n_heads=18, n_kv_heads=2,
+                            q_token_stride=18 * 64, out_token_stride=18 * 64, kv_row_stride=128)) == \
+        (Status.OK, Kernel.GENERAL)  # G = 9 > 8
+    assert select(lib, desc(head_dim=96, q_token_stride=9 * 96, out_token_stride=9 * 96, kv_row_stride=3 * 96)) == \
+        (Status.OK, Kernel.GENERAL)
+
+
+def test_decode_workspace_matches_split_layout(lib):
+    """Partial state [seq][kvHead][split][G][d+2] f32 with 128-row splits at d=64 (one split needs none)."""
+    from alpaca_b200 import Kernel, Status
+    assert ws(lib, desc(tokens=1, start_position=127), Kernel.DECODE_SPLIT) == (Status.OK, 0)
+    st, n = ws(lib, desc(tokens=1, start_position=128), Kernel.DECODE_SPLIT)
+    assert st == Status.OK and n == 4 * 1 * 9 * 2 * 66
+    st, n = ws(lib, desc(tokens=1, start_position=4095, n_seqs=64, q_seq_stride=576, kv_seq_stride=4128 * 192,
+                         out_seq_stride=576), Kernel.DECODE_SPLIT)
+    assert st == Status.OK and n == 4 * 64 * 9 * 32 * 66
+    assert ws(lib, desc(), Kernel.PREFILL_TC) == (Status.OK, 0)             # f16 Q needs no staging
+    from alpaca_b200 import DType
+    assert ws(lib, desc(q_dtype=int(DType.F32), q_token_stride=576), Kernel.PREFILL_TC) == (Status.OK, 128 * 576 * 2)
+
+
+@pytest.mark.parametrize("bad", [
+    dict(n_heads=10),                 # not a multiple of kv heads
+    dict(head_dim=48),                # not a multiple of 32
+    dict(head_dim=288),               # above 256
+    dict(tokens=0),
+    dict(start_position=-1),
+    dict(q=0),
+    dict(k=FAKE + 8),                 # misaligned
+    dict(kv_row_stride=100),          # smaller than a row
+    dict(q_token_stride=9 * 64 + 4),  # not a multiple of 16 bytes for f16
+    dict(q_dtype=7),
+    dict(scale=-1.0),
+    dict(n_seqs=2),                   # several sequences with zero sequence strides
+])
+def test_invalid_arguments_rejected(lib, bad):
+    from alpaca_b200 import Status
+    d = desc(**bad)
+    st, _ = select(lib, d)
+    assert st == Status.INVALID_ARGUMENT
+    assert lib.alpaca_cuda_last_error()
+    # the launching entry point refuses before touching the device
+    assert lib.alpaca_attention(ctypes.byref(d), 0, None, 0, None) == Status.INVALID_ARGUMENT
+
+
+def test_unsupported_kernel_requests(lib):
+    from alpaca_b200 import DType, Kernel, Status
+    d = desc(kv_dtype=int(DType.F32))
+    assert lib.alpaca_attn_prefill(ctypes.byref(d), None, 0, None) == Status.UNSUPPORTED
+    d = desc(tokens=4)
+    assert lib.alpaca_attn_decode(ctypes.byref(d), None, 0, None) == Status.UNSUPPORTED
+    assert ws(lib, desc(tokens=4), Kernel.DECODE_SPLIT)[0] == Status.UNSUPPORTED
+
+
+def test_workspace_too_small_is_reported(lib):
+    from alpaca_b200 import Kernel, Status
+    d = desc(tokens=1, start_position=1000)
+    assert lib.alpaca_attn_decode(ctypes.byref(d), None, 0, None) == Status.WORKSPACE_TOO_SMALL
+    assert b"needed" in lib.alpaca_cuda_last_error()
+    _ = Kernel
+
+
+def test_ctx_lens_rules(lib):
+    from alpaca_b200 import Kernel, Status
+    d = desc(tokens=2, ctx_lens=FAKE, max_ctx_len=10)
+    assert select(lib, d)[0] == Status.INVALID_ARGUMENT       # ragged lengths are decode-only
+    d = desc(tokens=1, ctx_lens=FAKE, max_ctx_len=0)
+    assert select(lib, d)[0] == Status.INVALID_ARGUMENT       # needs an upper bound
+    d = desc(tokens=1, ctx_lens=FAKE, max_ctx_len=10)
+    assert select(lib, d) == (Status.OK, Kernel.DECODE_SPLIT)  # ragged decode always splits
+
+
+def test_python_mirror_rejects_like_metalops():
+    """MetalOps.attention's guard (MetalOps.swift:179-181) raises invalidArgument before any device work."""
+    import numpy as np
+    from alpaca_b200 import AlpacaCUDAError, Status, attention
+    q = np.zeros((4, 9, 64), np.float32)
+    with pytest.raises(AlpacaCUDAError) as e:
+        attention(q, np.zeros((3, 3, 64), np.float32), np.zeros((3, 3, 64), np.float32), 0)  # capacity < T
+    assert e.value.status == Status.INVALID_ARGUMENT
+    with pytest.raises(AlpacaCUDAError):
+        attention(q, np.zeros((8, 2, 64), np.float32), np.zeros((8, 2, 64), np.float32), 0)  # 9 % 2
+    with pytest.raises(AlpacaCUDAError):
+        attention(np.zeros((4, 9, 48), np.float32), np.zeros((8, 3, 48), np.float32),
+                  np.zeros((8, 3, 48), np.float32), 0)  # head dim % 32

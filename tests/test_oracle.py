@@ -1,0 +1,177 @@
+"""The CPU oracle pinned against the reference's own known answers (CPU only).
+
+Mirrors Tests/AlpacaCoreTests/OperationTests.swift: testCausalGQAAttention (:72-86) and testSoftmax (:55-61),
+on the fixture values committed in tests/golden/ (extracted from the reference's ops.json by
+tests/golden/make_golden.py). Then cross-checks the oracle against float64 SDPA on BASELINE shapes and checks its
+helpers (f16 rounding, generators, error metrics, fused == three-step).
+"""
+from __future__ import annotations
+
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import oracle
+from tests._util import compare
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def _kat():
+    c = json.loads((GOLDEN / "attention_kat.json").read_text())
+    t, h, kv, hd, cap = c["tokens"], c["heads"], c["kvHeads"], c["headDim"], c["capacity"]
+    q = np.array(c["q"], np.float32).reshape(t, h, hd)
+    k = np.array(c["k"], np.float32).reshape(cap, kv, hd)
+    v = np.array(c["v"], np.float32).reshape(cap, kv, hd)
+    return c, q, k, v
+
+
+def test_attention_known_answer():
+    """OperationTests.testCausalGQAAttention: mask pattern and values within 3e-6 abs / 1e-5 rel."""
+    c, q, k, v = _kat()
+    L, start = c["length"], c["start"]
+    s = oracle.attention_scores(q, k, L, start)
+    H, T = c["heads"], c["tokens"]
+    for hh in range(H):
+        for tt in range(T):
+            for p in range(L):
+                assert (s[hh, tt, p] == -np.inf) == (p > start + tt)
+    out = oracle.attention_apply(oracle.softmax(s), v)
+    compare(out, np.array(c["expected"]), 3e-6, 1e-5, "oracle attention KAT")
+
+
+def test_fused_rows_bit_identical_to_three_steps():
+    c, q, k, v = _kat()
+    three = oracle.attention_apply(oracle.softmax(oracle.attention_scores(q, k, c["length"], c["start"])), v)
+    fused = oracle.attention(q, k, v, c["start"], length=c["length"])
+    assert np.array_equal(three, fused)
+    # larger GQA case with a cache longer than `length`
+    rng = np.random.default_rng(5)
+    T, H, kvh, d, start = 13, 9, 3, 64, 20
+    q = rng.standard_normal((T, H, d)).astype(np.float32)
+    k = rng.standard_normal((start + T + 5, kvh, d)).astype(np.float32)
+    v = rng.standard_normal((start + T + 5, kvh, d)).astype(np.float32)
+    three = oracle.attention_apply(oracle.softmax(oracle.attention_scores(q, k, start + T, start)), v)
+    for threads in (1, 3):
+        fused = oracle.attention(q, k, v, start, threads=threads)
+        assert np.array_equal(three, fused)
+
+
+def test_row_subset():
+    rng = np.random.default_rng(6)
+    T, H, kvh, d = 9, 4, 2, 32
+    q = rng.standard_normal((T, H, d)).astype(np.float32)
+    k = rng.standard_normal((T, kvh, d)).astype(np.float32)
+    v = rng.standard_normal((T, kvh, d)).astype(np.float32)
+    full = oracle.attention(q, k, v, 0)
+    part = oracle.attention(q, k, v, 0, rows=(5, 20))
+    rows = np.zeros(H * T, bool)
+    rows[5:20] = True
+    mask = rows.reshape(H, T).T  # [T, H]
+    assert np.array_equal(part[mask], full[mask])
+    assert np.all(part[~mask] == 0)
+
+
+def test_softmax_known_answer():
+    """OperationTests.testSoftmax: ±30-sigma inputs, 1e-6 abs / 1e-5 rel, rows sum to 1."""
+    c = json.loads((GOLDEN / "softmax_kat.json").read_text())
+    x = np.array(c["x"], np.float32).reshape(c["shape"])
+    r = oracle.softmax(x)
+    compare(r, np.array(c["expected"]), 1e-6, 1e-5, "oracle softmax KAT")
+    assert np.allclose(r.sum(-1), 1.0, atol=1e-6)
+
+
+def _sdpa64(q, k, v, start):
+    torch = pytest.importorskip("torch")
+    T, H, d = q.shape
+    g = H // k.shape[1]
+    L = start + T
+    qt = torch.tensor(q, dtype=torch.float64).permute(1, 0, 2)
+    kt = torch.tensor(k[:L], dtype=torch.float64).repeat_interleave(g, 1).permute(1, 0, 2)
+    vt = torch.tensor(v[:L], dtype=torch.float64).repeat_interleave(g, 1).permute(1, 0, 2)
+    mask = torch.tril(torch.ones(L, L, dtype=torch.bool))[start:start + T]
+    return torch.nn.functional.scaled_dot_product_attention(qt, kt, vt, attn_mask=mask).permute(1, 0, 2).numpy()
+
+
+@pytest.mark.parametrize("T,H,kvh,d,start,f16", [
+    (128, 9, 3, 64, 0, False),    # SmolLM2-135M shape, f32 N(0,1)
+    (33, 9, 3, 64, 7, True),
+    (1, 15, 5, 64, 300, True),    # decode row, SmolLM2-360M heads
+    (40, 32, 32, 64, 0, True),    # SmolLM2-1.7B heads
+    (17, 8, 2, 128, 3, True),
+])
+def test_oracle_vs_float64_sdpa(T, H, kvh, d, start, f16):
+    q = oracle.splitmix_normal(20260101 + T, (T, H, d))
+    k = oracle.splitmix_normal(20260201 + T, (start + T, kvh, d))
+    v = oracle.splitmix_normal(20260301 + T, (start + T, kvh, d))
+    if f16:
+        q, k, v = oracle.f16_round(q), oracle.f16_round(k), oracle.f16_round(v)
+    out = oracle.attention(q, k, v, start)
+    exp = _sdpa64(q, k, v, start)
+    m = oracle.error_metrics(out, exp)
+    print(f"[metrics] oracle vs float64 SDPA T={T} H={H}/{kvh} d={d}: {oracle.format_metrics(m)}")
+    assert m["maxAbs"] < 2e-6
+
+
+def test_f16_rounding_matches_ieee():
+    rng = np.random.default_rng(0)
+    x = np.concatenate([
+        rng.standard_normal(20000).astype(np.float32) * 1000,
+        (rng.standard_normal(20000) * 1e-5).astype(np.float32),   # subnormal halves
+        np.array([65504, 65519.99, 65520, 1e9, 6.1e-5, 6.0e-5, 5.96e-8, 2.98e-8, 2.99e-8, 1e-9, 0.0, -0.0,
+                  np.inf, -np.inf], np.float32),
+    ])
+    with np.errstate(over="ignore"):
+        ref = x.astype(np.float16).astype(np.float32)
+    got = oracle.f16_round(x)
+    assert np.array_equal(got, ref)
+    assert np.isnan(oracle.f16_round(np.array([np.nan], np.float32))[0])
+
+
+def _splitmix_py(seed, n):
+    M = (1 << 64) - 1
+    st, out = seed, []
+    for _ in range(n):
+        st = (st + 0x9E3779B97F4A7C15) & M
+        z = st
+        z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & M
+        z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & M
+        out.append(z ^ (z >> 31))
+    return out
+
+
+def test_splitmix_uniform_matches_reference_definition():
+    """SplitMix.nextFloat (KernelTests.swift:105-113) restated independently in Python."""
+    ref = np.array([np.float32(np.float32((x >> 11) / float(1 << 53)) * np.float32(2) - np.float32(1))
+                    for x in _splitmix_py(12, 257)], np.float32)
+    assert np.array_equal(oracle.splitmix_uniform(12, (257,)), ref)
+
+
+def test_normal_generator_moments():
+    x = oracle.splitmix_normal(20260101, (200001,))
+    assert abs(float(x.mean())) < 0.01 and abs(float(x.std()) - 1.0) < 0.01
+    assert np.array_equal(x[:1000], oracle.splitmix_normal(20260101, (1000,)))
+
+
+def test_error_metrics_definition():
+    """ErrorMetrics.swift:15-27."""
+    a = np.array([1.0, -2.0, 3.5], np.float32)
+    e = np.array([1.5, -2.0, 3.0])
+    m = oracle.error_metrics(a, e)
+    d = np.abs(a - e)
+    assert m["maxAbs"] == pytest.approx(d.max())
+    assert m["meanAbs"] == pytest.approx(d.mean())
+    assert m["rms"] == pytest.approx(np.sqrt((d * d).mean()))
+    assert m["maxRelPeak"] == pytest.approx(d.max() / 3.0)
+
+
+def test_oracle_rejects_bad_shapes():
+    q = np.zeros((4, 3, 32), np.float32)
+    k = np.zeros((8, 2, 32), np.float32)
+    with pytest.raises(ValueError):
+        oracle.attention_scores(q, k, 8, 0)          # 3 heads not divisible by 2 KV heads
+    k = np.zeros((8, 1, 32), np.float32)
+    with pytest.raises(ValueError):
+        oracle.attention_scores(q, k, 8, 5)          # start + tokens > length
