@@ -200,55 +200,54 @@ def run_ours(args):
     dev = torch.device("cuda", local)
     stream = torch.cuda.current_stream()
     pk = peaks()
-    T = args.tokens
+    T, L = args.tokens, args.layers
+    flops_step = L * flops_prefill(T)
 
-    # ---- inputs: 30 layers as independent sequences, seeded per rank
+    # ---- inputs: L layers as independent sequences, seeded per rank
     g = torch.Generator(device=dev)
     g.manual_seed(20260102 + 1000 * rank)
-    q = torch.randn((LAYERS, T, H, D), generator=g, device=dev).half()
-    k = torch.randn((LAYERS, T, KVH, D), generator=g, device=dev).half()
-    v = torch.randn((LAYERS, T, KVH, D), generator=g, device=dev).half()
-    out = torch.empty((LAYERS, T, H, D), dtype=torch.float32, device=dev)
+    q = torch.randn((L, T, H, D), generator=g, device=dev).half()
+    k = torch.randn((L, T, KVH, D), generator=g, device=dev).half()
+    v = torch.randn((L, T, KVH, D), generator=g, device=dev).half()
+    out = torch.empty((L, T, H, D), dtype=torch.float32, device=dev)
     desc = ab.make_desc(q, k, v, out, start_position=0)
     assert ab.workspace_bytes(desc, Kernel.PREFILL_TC) == 0
 
     def step():
         ab.launch(desc, Kernel.PREFILL_TC, None, stream)
 
-    for _ in range(args.warmup):
-        step()
-    ab.device_status()
-    clocks = ClockSampler(local)
-    clocks.start()
-    barrier(pg)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record(stream)
-    for _ in range(args.steps):
-        step()
-    ev1.record(stream)
-    barrier(pg)
-    clk = clocks.stop()
-    ab.device_status()
-    ms = ev0.elapsed_time(ev1) / args.steps
-    ms_max = max_over_ranks(ms, pg)
-    flops_step = LAYERS * flops_prefill(T)
+    ms_max = ms = float("nan")
+    clk = None
+    if not args.no_prefill:
+        for _ in range(args.warmup):
+            step()
+        ab.device_status()
+        clocks = ClockSampler(local)
+        clocks.start()
+        barrier(pg)
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        barrier(pg)
+        clk = clocks.stop()
+        ab.device_status()
+        ms = ev0.elapsed_time(ev1) / args.steps
+        ms_max = max_over_ranks(ms, pg)
     value = world * flops_step / (ms_max * 1e-3) / 1e12
-    tokens_per_s = world * LAYERS * T / (ms_max * 1e-3)
+    tokens_per_s = world * L * T / (ms_max * 1e-3)
     kernel_tflops = flops_step / (ms * 1e-3) / 1e12  # one launch per step on this rank
 
     # ---- correctness spot check of the timed output vs the oracle (rank 0, a few rows of layer 0)
     spot = None
-    if rank == 0:
+    if rank == 0 and not args.no_prefill:
         import oracle
         q0, k0, v0 = (x[0].float().cpu().numpy() for x in (q, k, v))
         o0 = out[0].cpu().numpy()
-        ref = np.zeros_like(o0)
-        rows = [0, 1, 129, T - 1, T + 5, 3 * T + 2047, 9 * T - 1]
-        for r in rows:
-            oracle.attention(q0, k0, v0, 0, rows=(r, r + 1), out=ref)
-        sel = np.zeros((T, H), bool)
-        for r in rows:
-            sel[r % T, r // T] = True
+        rows = [0, 1, 129, T - 1, T + 5, 3 * T + T // 2 - 1, H * T - 1]
+        ref = oracle.attention_rows(q0, k0, v0, 0, rows)
+        sel = oracle.rows_mask(rows, T, H)
         spot = float(np.abs(o0[sel] - ref[sel]).max())
 
     # ---- NCCL gather of per-rank output checksums (outside the timed region)
@@ -262,67 +261,69 @@ def run_ours(args):
         gather_ms = (time.perf_counter() - t0) * 1e3
 
     # ---- e2e: host buffers (pinned), H2D of the step's inputs + kernel + D2H of the output, every step
-    hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
-    hout = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
-    h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv))
-    d2h = hout.numel() * hout.element_size()
+    e2e = None
+    if not args.no_e2e:
+        hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
+        hout = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+        h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv))
+        d2h = hout.numel() * hout.element_size()
 
-    def e2e_step():
-        q.copy_(hq, non_blocking=True)
-        k.copy_(hk, non_blocking=True)
-        v.copy_(hv, non_blocking=True)
-        ab.launch(desc, Kernel.PREFILL_TC, None, stream)
-        hout.copy_(out, non_blocking=True)
+        def e2e_step():
+            q.copy_(hq, non_blocking=True)
+            k.copy_(hk, non_blocking=True)
+            v.copy_(hv, non_blocking=True)
+            ab.launch(desc, Kernel.PREFILL_TC, None, stream)
+            hout.copy_(out, non_blocking=True)
 
-    e2e_steps = max(3, min(args.steps, 10))
-    for _ in range(2):
-        e2e_step()
-    barrier(pg)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
-    e1.record(stream)
-    barrier(pg)
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps, pg)
-    e2e_value = world * flops_step / (e2e_ms * 1e-3) / 1e12
-    del hq, hk, hv, hout
+        e2e_steps = max(3, min(args.steps, 10))
+        for _ in range(2):
+            e2e_step()
+        barrier(pg)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        e1.record(stream)
+        barrier(pg)
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps, pg)
+        e2e = {"value": world * flops_step / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+               "api": "alpaca_attention (C ABI via ctypes); pinned host Q/K/V in, f32 context out, every step"}
+        del hq, hk, hv, hout
 
-    # ---- decode (config 3): 30 layers x batch 64, ragged contexts, distinct caches per layer
+    # ---- decode (config 3)
     decode = run_decode(args, ab, torch, dev, stream, rank, world, pg, pk) if not args.no_decode else None
 
     # ---- CPU baseline (rank 0 at N=1 only)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         import oracle
-        thr = oracle.host_threads()
-        tf, sample, cores = cpu_prefill_sample(args.cpu_seconds, thr, T)
+        tf, sample, cores = cpu_prefill_sample(args.cpu_seconds, oracle.host_threads(), T)
         cpu = {"value": tf, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample}
 
     if pg is not None:
         pg.barrier()
     if rank == 0:
-        traffic = profile_traffic("prefill_sm100_cfg2")
         roof = {"bound": "tensor", "achieved": kernel_tflops, "peak": pk["tflops"], "unit": "TFLOP/s",
-                "frac": kernel_tflops / pk["tflops"], "traffic": traffic,
-                "peak_source": f"{pk['source']} bf16 dense burst (MEASURED_PEAKS.json bf16_tflops)",
-                "kernel": "alpaca::prefill_kernel (tcgen05)",
+                "frac": kernel_tflops / pk["tflops"], "traffic": profile_traffic("prefill_sm100_cfg2"),
+                "peak_source": f"{pk['source']}: MEASURED_PEAKS.json bf16_tflops (dense, burst)",
+                "kernel": "alpaca::prefill_kernel (tcgen05, persistent)",
                 "algorithmic_flops_per_launch": flops_step}
+        in_mb = (q.numel() + k.numel() + v.numel()) * 2 / 1e6
         line = {
             "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f16", "data": "synthetic N(0,1) (torch.randn seeded per rank)",
-            "config": {"workload": f"config 2: SmolLM2-135M causal GQA prefill, T={T}, {LAYERS} independent layers "
-                                   f"per step, 9/3 heads, d=64, f16 in / f32 out", "tokens": T, "layers": LAYERS,
+            "config": {"workload": f"config 2: SmolLM2-135M causal GQA prefill, T={T}, {L} independent layers "
+                                   f"per step, 9/3 heads, d=64, f16 in / f32 out", "tokens": T, "layers": L,
                        "heads": H, "kv_heads": KVH, "head_dim": D, "batch_per_gpu": 1,
                        "parallelism": f"independent sequences per GPU x{world}",
-                       "l2": "inputs 236 MB per step > 126 MB L2 (no flush)"},
+                       "l2": f"inputs {in_mb:.0f} MB per step vs 126 MB L2 (no flush)"},
             "tokens_per_s": tokens_per_s,
             "roofline": roof,
             "cpu_baseline": cpu,
-            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "ms_per_step": e2e_ms, "api": "alpaca_attention via ctypes, pinned host buffers"},
-            "gpu_launches": args.steps * 1,
+            "e2e": e2e,
+            "gpu_launches": 0 if args.no_prefill else args.steps,
             "clocks": clk,
             "decode": decode,
             "spot_check_max_abs": spot,
@@ -375,7 +376,7 @@ def run_decode(args, ab, torch, dev, stream, rank, world, pg, pk):
     return {"workload": "config 3: batch 64 one-token decode, contexts U[1,4096], 9/3 heads, d=64, f16 KV, "
                         f"{LAYERS} layers (distinct caches, {kc.numel() * 4 / 1e9:.1f} GB) per step",
             "value": world * byts / (ms_max * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms_max,
-            "tokens_per_s": world * DEC_BATCH / (ms_max * 1e-3 / LAYERS) / LAYERS,
+            "tokens_per_s": world * DEC_BATCH / (ms_max * 1e-3),  # one token per sequence per 30-layer step
             "bytes_per_step": byts,
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": gbs / pk["hbm_gbs"], "traffic": profile_traffic("decode_split_cfg3"),
@@ -426,6 +427,9 @@ def main():
     ap.add_argument("--tokens", type=int, default=T_PREFILL)
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-seconds", type=float, default=4.0)
     args = ap.parse_args()

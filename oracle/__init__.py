@@ -51,6 +51,10 @@ def lib() -> ctypes.CDLL:
                                                [ctypes.c_int] * 6 +
                                                [ctypes.c_float, _f32p, ctypes.c_int64, ctypes.c_int,
                                                 ctypes.c_int64, ctypes.c_int64])
+        L.oracle_attention_rows.argtypes = ([_f32p, ctypes.c_int64, _f32p, _f32p, ctypes.c_int64] +
+                                            [ctypes.c_int] * 6 +
+                                            [ctypes.c_float, _f32p, ctypes.c_int64, ctypes.POINTER(ctypes.c_int64),
+                                             ctypes.c_int64, ctypes.c_int])
         L.oracle_error_metrics.argtypes = [_f32p, _f64p, ctypes.c_int64, _f64p]
         L.oracle_error_metrics_f32.argtypes = [_f32p, _f32p, ctypes.c_int64, _f64p]
         L.oracle_splitmix_uniform.argtypes = [ctypes.c_uint64, ctypes.c_float, _f32p, ctypes.c_int64]
@@ -129,6 +133,37 @@ def attention(q, keys, values, start: int, length: int | None = None, scale: flo
     lib().oracle_attention(_p32(q), _p32(keys), _p32(values), T, H, kvh, d, length, start, float(scale),
                            _p32(out), int(threads), int(r0), int(r1))
     return out
+
+
+def attention_rows(q, keys, values, start: int, rows, length: int | None = None, scale: float = 0.0,
+                   threads: int | None = None, out: np.ndarray | None = None) -> np.ndarray:
+    """oracle attention evaluated only on the listed rows (row = h*T + t), all host threads by default."""
+    q = np.ascontiguousarray(q, np.float32)
+    keys = np.ascontiguousarray(keys, np.float32)
+    values = np.ascontiguousarray(values, np.float32)
+    T, H, d = q.shape
+    kvh = keys.shape[1]
+    if length is None:
+        length = start + T
+    if not (keys.shape == values.shape and keys.shape[2] == d and H % kvh == 0):
+        raise ValueError(f"attention shapes q {q.shape} k {keys.shape} v {values.shape}")
+    if not (0 <= length <= keys.shape[0] and start + T <= length):
+        raise ValueError(f"attention length {length}, start {start}, tokens {T}, capacity {keys.shape[0]}")
+    if out is None:
+        out = np.zeros((T, H, d), np.float32)
+    r = np.ascontiguousarray(rows, np.int64)
+    lib().oracle_attention_rows(_p32(q), H * d, _p32(keys), _p32(values), kvh * d, T, H, kvh, d, length, start,
+                                float(scale), _p32(out), H * d, r.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)),
+                                r.size, int(threads or host_threads()))
+    return out
+
+
+def rows_mask(rows, T: int, H: int) -> np.ndarray:
+    """[T, H] boolean mask of the rows (row = h*T + t)."""
+    m = np.zeros((T, H), bool)
+    r = np.asarray(rows, np.int64)
+    m[r % T, r // T] = True
+    return m
 
 
 def error_metrics(actual, expected) -> dict:

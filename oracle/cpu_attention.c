@@ -135,6 +135,7 @@ typedef struct {
     float* out;
     int64_t row_begin, row_end;
     int tid, nthreads;
+    const int64_t* rows; /* optional explicit row list of length row_end (row_begin unused) */
 } row_job;
 
 /* One (h, t) row: scores over the whole `length` (masked = -inf), softmax, apply; identical operation order to
@@ -167,6 +168,8 @@ static void attention_row(const row_job* j, int h, int t, float* srow) {
     }
 }
 
+static void* list_worker(void* arg);
+
 static void* row_worker(void* arg) {
     const row_job* j = (const row_job*)arg;
     float* srow = (float*)malloc(sizeof(float) * (size_t)(j->length > 0 ? j->length : 1));
@@ -191,7 +194,7 @@ void oracle_attention_strided(const float* q, int64_t q_ts, const float* keys, c
     if (threads < 1) threads = 1;
     if (threads > 256) threads = 256;
     row_job base = {q, keys, values, q_ts, kv_rs, o_ts, tokens, n_heads, n_kv, hd, length, start,
-                    scale > 0.0f ? scale : ref_scale(hd), out, row_begin, row_end, 0, threads};
+                    scale > 0.0f ? scale : ref_scale(hd), out, row_begin, row_end, 0, threads, NULL};
     if (threads == 1) {
         row_worker(&base);
         return;
@@ -213,6 +216,46 @@ void oracle_attention_strided(const float* q, int64_t q_ts, const float* keys, c
     for (int i = 0; i < threads; i++)
         if (tids[i]) pthread_join(tids[i], NULL);
     (void)started;
+}
+
+static void* list_worker(void* arg) {
+    const row_job* j = (const row_job*)arg;
+    float* srow = (float*)malloc(sizeof(float) * (size_t)(j->length > 0 ? j->length : 1));
+    if (!srow) return NULL;
+    const int64_t nrows = (int64_t)j->n_heads * j->tokens;
+    for (int64_t i = j->tid; i < j->row_end; i += j->nthreads) {
+        const int64_t r = j->rows[i];
+        if (r < 0 || r >= nrows) continue;
+        attention_row(j, (int)(r / j->tokens), (int)(r % j->tokens), srow);
+    }
+    free(srow);
+    return NULL;
+}
+
+void oracle_attention_rows(const float* q, int64_t q_ts, const float* keys, const float* values, int64_t kv_rs,
+                           int tokens, int n_heads, int n_kv, int hd, int length, int start, float scale, float* out,
+                           int64_t o_ts, const int64_t* rows, int64_t n_rows, int threads) {
+    if (tokens <= 0 || n_heads <= 0 || n_rows <= 0) return;
+    if (threads < 1) threads = 1;
+    if (threads > 256) threads = 256;
+    row_job base = {q, keys, values, q_ts, kv_rs, o_ts, tokens, n_heads, n_kv, hd, length, start,
+                    scale > 0.0f ? scale : ref_scale(hd), out, 0, n_rows, 0, threads, rows};
+    if (threads == 1) {
+        list_worker(&base);
+        return;
+    }
+    pthread_t tids[256];
+    row_job jobs[256];
+    for (int i = 0; i < threads; i++) {
+        jobs[i] = base;
+        jobs[i].tid = i;
+        if (pthread_create(&tids[i], NULL, list_worker, &jobs[i]) != 0) {
+            list_worker(&jobs[i]);
+            tids[i] = 0;
+        }
+    }
+    for (int i = 0; i < threads; i++)
+        if (tids[i]) pthread_join(tids[i], NULL);
 }
 
 void oracle_attention(const float* q, const float* keys, const float* values, int tokens, int n_heads, int n_kv,

@@ -50,6 +50,13 @@ void oracle_attention_strided(const float* q, int64_t q_token_stride, const floa
                               int start, float scale, float* out, int64_t out_token_stride, int threads,
                               int64_t row_begin, int64_t row_end);
 
+/* Like oracle_attention_strided but over an explicit list of rows (row = h*tokens + t), split over `threads`
+ * POSIX threads: exact sampled parity checks and bounded CPU timing without per-row call overhead. */
+void oracle_attention_rows(const float* q, int64_t q_token_stride, const float* keys, const float* values,
+                           int64_t kv_row_stride, int tokens, int n_heads, int n_kv, int head_dim, int length,
+                           int start, float scale, float* out, int64_t out_token_stride, const int64_t* rows,
+                           int64_t n_rows, int threads);
+
 /* ErrorMetrics (Sources/AlpacaCore/Runtime/ErrorMetrics.swift:15-27):
  * out[0]=maxAbs, out[1]=meanAbs, out[2]=rms, out[3]=maxRelativeToPeak. */
 void oracle_error_metrics(const float* actual, const double* expected, int64_t n, double out[4]);

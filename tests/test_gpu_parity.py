@@ -137,18 +137,10 @@ def test_config2_prefill_135m(cuda_lib, T):
     ks = np.stack([_normal(40 + s, (T, kvh, d)) for s in range(S)])
     vs = np.stack([_normal(50 + s, (T, kvh, d)) for s in range(S)])
     gpu = _device_prefill(qs, ks, vs, 0)
-    nthreads = oracle.host_threads()
     for s in range(S):
-        cpu = np.zeros((T, H, d), np.float32)
-        if T <= 2048:
-            oracle.attention(qs[s], ks[s], vs[s], 0, threads=nthreads, out=cpu)
-            sel = np.ones((T, H), bool)
-        else:
-            sel = np.zeros((T, H), bool)
-            rows = np.arange(0, H * T, 7)
-            sel[rows % T, rows // T] = True
-            for r in rows:  # row index = h*T + t
-                oracle.attention(qs[s], ks[s], vs[s], 0, rows=(int(r), int(r) + 1), out=cpu)
+        rows = np.arange(0, H * T, 1 if T <= 2048 else 7)  # row index = h*T + t
+        cpu = oracle.attention_rows(qs[s], ks[s], vs[s], 0, rows)
+        sel = oracle.rows_mask(rows, T, H)
         max_abs_check(gpu[s][sel], cpu[sel], F16_BOUND, f"config 2 prefill T={T} layer {s}")
 
 
@@ -185,12 +177,9 @@ def test_config4_prefill_360m_batch(cuda_lib):
     vs = np.stack([_normal(90 + s, (T, kvh, d)) for s in range(S)])
     gpu = _device_prefill(qs, ks, vs, 0)
     for s in range(S):
-        cpu = np.zeros((T, H, d), np.float32)
-        sel = np.zeros((T, H), bool)
-        for r in range(s, H * T, 31):
-            t, h = r % T, r // T
-            sel[t, h] = True
-            oracle.attention(qs[s], ks[s], vs[s], 0, rows=(r, r + 1), out=cpu)
+        rows = np.arange(s, H * T, 31)
+        cpu = oracle.attention_rows(qs[s], ks[s], vs[s], 0, rows)
+        sel = oracle.rows_mask(rows, T, H)
         max_abs_check(gpu[s][sel], cpu[sel], F16_BOUND, f"config 4 prefill seq {s}")
 
 
