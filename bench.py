@@ -340,6 +340,7 @@ def run_decode(args, ab, torch, dev, stream, rank, world, pg, pk):
     g.manual_seed(20260103 + 1000 * rank)
     gl = torch.Generator()
     gl.manual_seed(20260103)
+    LAYERS = args.dec_layers
     lens = torch.randint(1, DEC_CAP + 1, (LAYERS, DEC_BATCH), generator=gl, dtype=torch.int32)
     lens_d = lens.to(dev)
     kc = torch.randn((LAYERS, DEC_BATCH, DEC_CAP, KVH, D), generator=g, device=dev).half()
@@ -429,6 +430,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--dec-layers", type=int, default=LAYERS)
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-seconds", type=float, default=4.0)
