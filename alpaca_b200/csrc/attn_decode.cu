@@ -10,12 +10,14 @@
 //                 SL*d*4 bytes in flight. Scores are reduced across a row's lanes with a transposing butterfly
 //                 (7 shuffles for 8 rows instead of 24), softmax runs once per (row, head) from shared memory, and
 //                 P·V partial sums are reduced across rows through shared memory.
-//   combine       grid (heads, seqs), d threads: rescales the per-split (m, l, acc) states to the global max and
-//                 normalises. Launched with programmatic dependent launch so its launch overlaps the split tail.
-//                 Sequences with one split are finished by the split kernel itself.
+//   combine       grid (kv_heads, seqs), 256 threads: rescales the per-split (m, l, acc) states of the G heads to
+//                 the global max and normalises. Launched with programmatic dependent launch so its launch
+//                 overlaps the split tail. Sequences with one split are finished by the split kernel itself.
 //
 // Scores are kept in log2 units (q pre-scaled by scale*log2(e)), so every exponential is one ex2.approx.
 // Partial-state layout: [seq][kv_head][split][g][d + 2] f32 = accumulators, then m (log2 units), then l.
+#include <algorithm>
+
 #include "common.cuh"
 #include "internal.h"
 
@@ -260,28 +262,56 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(const DecodeArgs
     }
 }
 
+constexpr int kCombineThreads = 256;
+
+// One CTA per (KV head, sequence): the G heads' per-split weights 2^(m_s - M) are computed once into shared
+// memory (one warp per head), then every output column sums its accumulators over the splits with independent,
+// coalesced loads.
 template <int D>
-__global__ void __launch_bounds__(D) decode_combine_kernel(const DecodeArgs a) {
+__global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const DecodeArgs a) {
     asm volatile("griddepcontrol.wait;" ::: "memory");  // split kernel's writes are visible after this
-    const int h = blockIdx.x, seq = blockIdx.y, col = threadIdx.x;
-    const int G = a.n_heads / a.n_kv_heads, kvh = h / G, g = h - kvh * G;
+    const int kvh = blockIdx.x, seq = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int G = a.n_heads / a.n_kv_heads;
     const int L = ctx_len_of(a, seq);
     const int nsp = (L + Geo<D>::SL - 1) / Geo<D>::SL;
     if (nsp <= 1) return;
-    const int64_t stride = static_cast<int64_t>(G) * (D + 2);
-    const float* base = a.partial + ((static_cast<int64_t>(seq) * a.n_kv_heads + kvh) * a.max_splits * G + g) * (D + 2);
-    float M = -INFINITY;
-    for (int s = 0; s < nsp; s++) M = fmaxf(M, base[s * stride + D]);
-    float num = 0.f, den = 0.f;
-    for (int s = 0; s < nsp; s++) {
-        const float f = ex2_approx(base[s * stride + D] - M);
-        num = fmaf(base[s * stride + col], f, num);
-        den = fmaf(base[s * stride + D + 1], f, den);
+    extern __shared__ float cs[];
+    float* w = cs;                // [nsp][G] weights
+    float* inv_den = cs + nsp * G; // [G]
+    const int64_t stride = static_cast<int64_t>(G) * (D + 2);  // between splits
+    const float* base = a.partial + (static_cast<int64_t>(seq) * a.n_kv_heads + kvh) * a.max_splits * stride;
+    for (int g = warp; g < G; g += kCombineThreads / 32) {
+        float M = -INFINITY;
+        for (int sp = lane; sp < nsp; sp += 32) M = fmaxf(M, base[sp * stride + g * (D + 2) + D]);
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        float den = 0.f;
+        for (int sp = lane; sp < nsp; sp += 32) {
+            const float* pp = base + sp * stride + g * (D + 2);
+            const float f = ex2_approx(pp[D] - M);
+            w[sp * G + g] = f;
+            den = fmaf(pp[D + 1], f, den);
+        }
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+        if (lane == 0) inv_den[g] = 1.f / den;
     }
-    const float val = num / den;
-    const int64_t oo = static_cast<int64_t>(seq) * a.out_seq_stride + static_cast<int64_t>(h) * D + col;
-    if (a.out_f16) static_cast<__half*>(a.out)[oo] = __float2half_rn(val);
-    else static_cast<float*>(a.out)[oo] = val;
+    __syncthreads();
+    for (int o = tid; o < G * D; o += kCombineThreads) {
+        const int g = o / D, col = o - g * D;
+        const float* pp = base + g * (D + 2) + col;
+        float num0 = 0.f, num1 = 0.f;
+        int sp = 0;
+        for (; sp + 1 < nsp; sp += 2) {
+            num0 = fmaf(pp[sp * stride], w[sp * G + g], num0);
+            num1 = fmaf(pp[(sp + 1) * stride], w[(sp + 1) * G + g], num1);
+        }
+        if (sp < nsp) num0 = fmaf(pp[sp * stride], w[sp * G + g], num0);
+        const float val = (num0 + num1) * inv_den[g];
+        const int64_t oo = static_cast<int64_t>(seq) * a.out_seq_stride + static_cast<int64_t>(kvh * G + g) * D + col;
+        if (a.out_f16) static_cast<__half*>(a.out)[oo] = __float2half_rn(val);
+        else static_cast<float*>(a.out)[oo] = val;
+    }
 }
 
 template <int D, int G>
@@ -295,9 +325,8 @@ cudaError_t launch_split(const DecodeArgs& a, int n_seqs, cudaStream_t s) {
 
 template <int D>
 cudaError_t launch_d(const DecodeArgs& a, int n_seqs, cudaStream_t s) {
-    const int G = a.n_heads / a.n_kv_heads;
     cudaError_t e;
-    switch (G) {
+    switch (a.n_heads / a.n_kv_heads) {
         case 1: e = launch_split<D, 1>(a, n_seqs, s); break;
         case 2: e = launch_split<D, 2>(a, n_seqs, s); break;
         case 3: e = launch_split<D, 3>(a, n_seqs, s); break;
@@ -310,10 +339,17 @@ cudaError_t launch_d(const DecodeArgs& a, int n_seqs, cudaStream_t s) {
     }
     if (e != cudaSuccess) return e;
     if (a.max_splits <= 1) return cudaSuccess;  // every sequence finished in the split kernel
+    const int G = a.n_heads / a.n_kv_heads;
+    const size_t csmem = sizeof(float) * (static_cast<size_t>(a.max_splits) * G + G);
+    if (csmem > 48 * 1024) {
+        cudaError_t ae = cudaFuncSetAttribute(decode_combine_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              static_cast<int>(std::min<size_t>(csmem, 227 * 1024)));
+        if (ae != cudaSuccess) return ae;
+    }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.n_heads, n_seqs, 1);
-    cfg.blockDim = dim3(D, 1, 1);
-    cfg.dynamicSmemBytes = 0;
+    cfg.gridDim = dim3(a.n_kv_heads, n_seqs, 1);
+    cfg.blockDim = dim3(kCombineThreads, 1, 1);
+    cfg.dynamicSmemBytes = csmem;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

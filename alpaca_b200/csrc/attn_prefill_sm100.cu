@@ -13,14 +13,20 @@
 //     (TMEM: S_A, S_B, O_A, O_B = 384 of 512 columns); completion is signalled with tcgen05.commit;
 //   * warps 4-7 and 8-11: two softmax warpgroups, one per query tile of the pair, one query row per thread. They
 //     read S rows from TMEM, apply the causal mask on diagonal blocks, keep the running max in log2 units (the
-//     max is only moved when it grows by more than 8, so O rarely needs rescaling), write P as f16 into a
-//     swizzled shared-memory tile that is the A operand of the P·V MMA, and finish each tile with O / l.
+//     max is only moved when it grows by more than 8, so O rarely needs rescaling), compute P = 2^(s*c - m)
+//     two at a time with ex2.approx.f16x2 (P is an f16 MMA operand anyway), write it into a swizzled
+//     shared-memory tile that is the A operand of the P·V MMA, and finish each tile with O / l;
+//   * the softmax denominator l comes out of the tensor core: the P·V MMA runs with N = d + 16 where the extra
+//     16 columns of B are a constant block of ones, so O's column d accumulates Σ P exactly as the MMA used it
+//     (no per-score FADD, and l matches the rounded P that multiplied V).
 //   The tensor pipe alternates S(A, j+1), PV(A, j), S(B, j+1), PV(B, j) so one tile's softmax overlaps the
 //   other tile's MMAs.
 //
 // Every mbarrier wait is bounded (2 s; 2 ms under ALPACA_ATTN_FLAG_DEBUG_FORCE_TIMEOUT). On a timeout the CTA
 // raises its abort flag and the device error word, waits (bounded) for its own TMA loads and MMAs in flight,
 // frees TMEM and returns.
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -35,13 +41,14 @@ constexpr int kD = 64;          // head dim of this kernel
 constexpr int kStages = 2;      // K/V ring depth
 constexpr int kThreads = 384;   // 12 warps
 constexpr int kTmemCols = 512;
+constexpr int kON = kD + 16;    // O tile columns: d context columns + 16 columns of Σ P (the ones block)
 constexpr uint32_t kTileBytes = kBM * kD * 2;  // 16 KB: one Q, K or V tile
 constexpr float kRescaleThreshold = 8.0f;      // log2 units
 constexpr float kLog2e = 1.4426950408889634f;
 
-// TMEM column map: S_A, S_B (128 f32 columns each), then O_A, O_B (d columns each)
+// TMEM column map: S_A, S_B (128 f32 columns each), then O_A, O_B (kON columns each, 128-aligned)
 __host__ __device__ constexpr uint32_t col_s(int tile) { return tile ? 128u : 0u; }
-__host__ __device__ constexpr uint32_t col_o(int tile) { return tile ? 320u : 256u; }
+__host__ __device__ constexpr uint32_t col_o(int tile) { return tile ? 384u : 256u; }
 
 struct PrefillArgs {
     void* out;
@@ -58,6 +65,7 @@ struct SmemLayout {
     __half q[2][kBM * kD];
     __half k[kStages][kBN * kD];
     __half v[kStages][kBN * kD];
+    __half ones[kBN * 64];   // B-operand block of 1.0 that makes the P·V MMA also produce Σ P
     __half p[2][kBM * kBN];  // per tile: [2 halves of 64 KV columns][128 rows][64] swizzled
     uint64_t q_full[2], q_empty[2];
     uint64_t k_full[kStages], k_empty[kStages], v_full[kStages], v_empty[kStages];
@@ -109,18 +117,22 @@ __device__ __forceinline__ void mma_s(const SmemLayout* sm, int tile, int stage,
 
 __device__ __forceinline__ void mma_pv(const SmemLayout* sm, int tile, int stage, uint32_t tmem_base,
                                        bool accumulate) {
-    constexpr uint32_t idesc = idesc_f16_f32(kBM, kD, false, true);
+    // B = [V | ones]: N = d + 16, MN-major; the second 64-column atom (read for columns d..d+15) is the ones
+    // block, reached through the descriptor's leading-byte offset.
+    constexpr uint32_t idesc = idesc_f16_f32(kBM, kON, false, true);
     const uint32_t pa = smem_u32(sm->p[tile]), va = smem_u32(sm->v[stage]);
+    const uint32_t lbo = smem_u32(sm->ones) - va;
 #pragma unroll
     for (int kk = 0; kk < kBN / 16; kk++) {
         const uint64_t ad = smem_desc_sw128(pa + (kk >> 2) * (kBM * 128) + (kk & 3) * 32, 16, 1024);
-        const uint64_t bd = smem_desc_sw128(va + kk * 16 * 128, kBN * 128, 1024);
+        const uint64_t bd = smem_desc_sw128(va + kk * 16 * 128, lbo, 1024);
         tc_mma_ss(tmem_base + col_o(tile), ad, bd, idesc, (accumulate || kk > 0) ? 1u : 0u);
     }
 }
 
 // ---------------------------------------------------------------------------------------------- kernel
 
+template <bool kF16Exp>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const PrefillArgs a) {
@@ -152,6 +164,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_prefetch_desc(&tm_q);
         tma_prefetch_desc(&tm_k);
         tma_prefetch_desc(&tm_v);
+    }
+    {  // the ones block (16 KB of f16 1.0), written through the generic proxy, read by the tensor core
+        uint4* o4 = reinterpret_cast<uint4*>(sm->ones);
+        for (int i = tid; i < kBN * 64 / 8; i += kThreads) o4[i] = make_uint4(0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u);
+        fence_proxy_async_smem();
     }
     if (warp == 2) {
         tmem_alloc(&sm->tmem_base, kTmemCols);
@@ -298,9 +315,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (nb == 0) continue;
             const int row0 = x.row0[tile];
             const int qpos = a.start + row0 + row;  // absolute position of this thread's query
-            float m_used = -INFINITY, l = 0.f;
+            float m_used = -INFINITY;
             for (int j = 0; j < nb; j++) {
-                ok = mbar_wait(&sm->s_full[tile], s_uses & 1, ab);
+                ok = __all_sync(0xffffffffu, mbar_wait(&sm->s_full[tile], s_uses & 1, ab));
                 if (!ok) break;
                 s_uses++;
                 tc_fence_after();
@@ -318,9 +335,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int c = 0; c < kBN; c++)
                         if (kv0 + c > qpos) s[c] = -INFINITY;
                 }
-                float mx = s[0];
+                // row max as an 8-way tree (no 128-deep dependency chain)
+                float mv[8];
 #pragma unroll
-                for (int c = 1; c < kBN; c++) mx = fmaxf(mx, s[c]);
+                for (int i = 0; i < 8; i++) mv[i] = s[i];
+#pragma unroll
+                for (int c = 8; c < kBN; c += 8)
+#pragma unroll
+                    for (int i = 0; i < 8; i++) mv[i] = fmaxf(mv[i], s[c + i]);
+                const float mx = fmaxf(fmaxf(fmaxf(mv[0], mv[1]), fmaxf(mv[2], mv[3])),
+                                       fmaxf(fmaxf(mv[4], mv[5]), fmaxf(mv[6], mv[7])));
                 const float mxs = mx * a.scale_log2;
                 bool rescale = false;
                 float alpha = 1.f;
@@ -328,33 +352,34 @@ __global__ void __launch_bounds__(kThreads, 1)
                     m_used = (mxs == -INFINITY) ? 0.f : mxs;
                 } else if (mxs > m_used + kRescaleThreshold) {
                     alpha = ex2_approx(m_used - mxs);
-                    l *= alpha;
                     m_used = mxs;
                     rescale = true;
                 }
                 uint32_t pk[kBN / 2];
 #pragma unroll
                 for (int c = 0; c < kBN; c += 2) {
-                    const float p0 = ex2_approx(fmaf(s[c], a.scale_log2, -m_used));
-                    const float p1 = ex2_approx(fmaf(s[c + 1], a.scale_log2, -m_used));
-                    l += p0 + p1;
-                    pk[c / 2] = pack_half2(p0, p1);
+                    const float x0 = fmaf(s[c], a.scale_log2, -m_used);
+                    const float x1 = fmaf(s[c + 1], a.scale_log2, -m_used);
+                    if constexpr (kF16Exp) pk[c / 2] = ex2_approx_f16x2(pack_half2(x0, x1));
+                    else pk[c / 2] = pack_half2(ex2_approx(x0), ex2_approx(x1));
                 }
                 if (j > 0) {  // PV(j-1) must be done before P is overwritten or O is rescaled
-                    ok = mbar_wait(&sm->o_done[tile], o_uses & 1, ab);
+                    ok = __all_sync(0xffffffffu, mbar_wait(&sm->o_done[tile], o_uses & 1, ab));
                     if (!ok) break;
                     o_uses++;
                     tc_fence_after();
                 }
-                if (rescale) {
-                    float o[kD];
+                // tcgen05.ld/st are warp-collective: the whole warp rescales when any of its rows must
+                // (alpha stays 1 for the others). Columns d.. hold Σ P and are rescaled with O.
+                if (__any_sync(0xffffffffu, rescale)) {
+                    float o[96];
 #pragma unroll
-                    for (int c = 0; c < kD; c += 32) tmem_ld32(o_addr + c, o + c);
+                    for (int c = 0; c < 96; c += 32) tmem_ld32(o_addr + c, o + c);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int c = 0; c < kD; c++) o[c] *= alpha;
+                    for (int c = 0; c < 96; c++) o[c] *= alpha;
 #pragma unroll
-                    for (int c = 0; c < kD; c += 32) tmem_st32(o_addr + c, o + c);
+                    for (int c = 0; c < 96; c += 32) tmem_st32(o_addr + c, o + c);
                     tmem_wait_st();
                 }
                 // P row -> swizzled smem: 16 chunks of 8 halves; chunk ch of half hh at
@@ -371,19 +396,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (lane == 0) mbar_arrive(&sm->p_full[tile]);
             }
             if (!ok) break;
-            // epilogue: O / l
-            ok = mbar_wait(&sm->o_done[tile], o_uses & 1, ab);
+            // epilogue: O / l, with l = column d of the O tile
+            ok = __all_sync(0xffffffffu, mbar_wait(&sm->o_done[tile], o_uses & 1, ab));
             if (!ok) break;
             o_uses++;
             tc_fence_after();
-            float o[kD];
+            float o[96];
 #pragma unroll
-            for (int c = 0; c < kD; c += 32) tmem_ld32(o_addr + c, o + c);
+            for (int c = 0; c < 96; c += 32) tmem_ld32(o_addr + c, o + c);
             tmem_wait_ld();
             tc_fence_before();
             const int t = row0 + row;
             if (t < a.tokens) {
-                const float inv = 1.f / l;
+                const float inv = 1.f / o[kD];
                 const int64_t off = x.seq * a.out_seq_stride + static_cast<int64_t>(t) * a.out_token_stride +
                                     static_cast<int64_t>(x.head) * kD;
                 if (a.out_f16) {
@@ -460,6 +485,16 @@ bool make_map(CUtensorMap* map, const void* base, int d, int heads, int rows, in
     return r == CUDA_SUCCESS;
 }
 
+// Exponential unit of the softmax: "f16x2" (default: ex2.approx.f16x2, two scores per MUFU op) or "f32"
+// (ex2.approx.f32 per score, then rounded to f16). Read once from ALPACA_PREFILL_EXP2.
+bool prefill_f16_exp() {
+    static const bool v = [] {
+        const char* e = std::getenv("ALPACA_PREFILL_EXP2");
+        return !(e && std::strcmp(e, "f32") == 0);
+    }();
+    return v;
+}
+
 }  // namespace
 
 bool prefill_supported(const alpaca_attn_desc& d) {
@@ -477,8 +512,11 @@ cudaError_t launch_prefill(const Call& c, cudaStream_t s) {
     static std::once_flag attr_once;
     static cudaError_t attr_err = cudaSuccess;
     std::call_once(attr_once, [] {
-        attr_err = cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        attr_err = cudaFuncSetAttribute(prefill_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         static_cast<int>(kSmemBytes));
+        if (attr_err == cudaSuccess)
+            attr_err = cudaFuncSetAttribute(prefill_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            static_cast<int>(kSmemBytes));
     });
     if (attr_err != cudaSuccess) return attr_err;
 
@@ -521,7 +559,10 @@ cudaError_t launch_prefill(const Call& c, cudaStream_t s) {
     a.err = c.err;
     a.flags = d.flags;
     const int grid = std::max(1, std::min(a.total_items, c.num_sms));
-    prefill_kernel<<<grid, kThreads, kSmemBytes, s>>>(tq, tk, tv, a);
+    if (prefill_f16_exp())
+        prefill_kernel<true><<<grid, kThreads, kSmemBytes, s>>>(tq, tk, tv, a);
+    else
+        prefill_kernel<false><<<grid, kThreads, kSmemBytes, s>>>(tq, tk, tv, a);
     return cudaGetLastError();
 }
 

@@ -34,6 +34,13 @@ __device__ __forceinline__ float ex2_approx(float x) {  // 2^x, MUFU.EX2; -inf -
     return y;
 }
 
+// 2^x for two packed halves (one MUFU op for both lanes of the pair).
+__device__ __forceinline__ uint32_t ex2_approx_f16x2(uint32_t x) {
+    uint32_t y;
+    asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
     __half2 h = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&h);
@@ -94,6 +101,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
             }
         }
     }
+}
+
+// Register reallocation between warpgroups (all warps of a warpgroup execute the same one).
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
 }
 
 // ------------------------------------------------------------------------------------------------ fences

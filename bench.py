@@ -352,24 +352,34 @@ def run_decode(args, ab, torch, dev, stream, rank, world, pg, pk):
     wsb = max(ab.workspace_bytes(dd, Kernel.DECODE_SPLIT) for dd in descs)
     ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
 
-    def step():
+    def step():  # 30 layers x (split + combine), on the current stream
         for dd in descs:
-            ab.launch(dd, Kernel.DECODE_SPLIT, ws, stream)
+            ab.launch(dd, Kernel.DECODE_SPLIT, ws)
 
-    for _ in range(max(3, args.warmup)):
+    # The per-layer launches are captured once in a CUDA graph and replayed (launch-bound otherwise).
+    side = torch.cuda.Stream(device=dev)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
         step()
+    stream.wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(max(3, args.warmup)):
+        graph.replay()
     ab.device_status()
     steps = max(5, args.steps)
     barrier(pg)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(steps):
-        step()
+        graph.replay()
     e1.record(stream)
     barrier(pg)
     ab.device_status()
     ms = e0.elapsed_time(e1) / steps
     ms_max = max_over_ranks(ms, pg)
+    del graph
     kv_bytes = float(lens.sum().item()) * KVH * D * 2 * 2
     qo_bytes = LAYERS * DEC_BATCH * H * D * 4 * 2
     byts = kv_bytes + qo_bytes
@@ -381,7 +391,8 @@ def run_decode(args, ab, torch, dev, stream, rank, world, pg, pk):
             "bytes_per_step": byts,
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": gbs / pk["hbm_gbs"], "traffic": profile_traffic("decode_split_cfg3"),
-                         "kernel": "alpaca::decode_split_kernel<64,3> + decode_combine_kernel (per layer)"},
+                         "kernel": "alpaca::decode_split_kernel<64,3> + decode_combine_kernel per layer, "
+                                   "replayed from a CUDA graph"},
             "gpu_launches": steps * LAYERS * 2}
 
 
