@@ -240,7 +240,9 @@ def test_pad_rows_never_read(cuda_lib):
 
 
 def test_large_scores_rescale_path(cuda_lib):
-    """Scores with a large spread (q scaled by 6, rows whose max jumps between blocks) exercise the O rescale."""
+    """Scores with a large spread (q scaled by 6, rows whose max jumps between blocks) exercise the O rescale.
+    The data is outside the N(0,1) regime the 2e-3 bound is stated for (attention is nearly one-hot), so the bound
+    is the reference's own tolerance basis for f16 P/K/V (KernelTests.swift:116-121): 3 * 2^-11 * max|V|."""
     from alpaca_b200 import Kernel, attention_device, device_status
     T, H, kvh, d = 512, 4, 2, 64
     q = oracle.f16_round(oracle.splitmix_normal(131, (T, H, d)) * 6.0)
@@ -254,4 +256,4 @@ def test_large_scores_rescale_path(cuda_lib):
     attention_device(torch.from_numpy(q).to(dev).half(), torch.from_numpy(k).to(dev).half(),
                      torch.from_numpy(v).to(dev).half(), out, kind=Kernel.PREFILL_TC)
     device_status()
-    max_abs_check(out.cpu().numpy(), cpu, F16_BOUND, "rescale path")
+    max_abs_check(out.cpu().numpy(), cpu, 3 * 2.0 ** -11 * float(np.abs(v).max()), "rescale path")
