@@ -71,6 +71,7 @@ EXPORTED_SYMBOLS = (
     "alpaca_attention",
     "alpaca_attn_prefill",
     "alpaca_attn_decode",
+    "alpaca_attn_decode_noalloc",
     "alpaca_attention_workspace_bytes",
     "alpaca_attention_select",
     "alpaca_cuda_device_status",
@@ -95,6 +96,8 @@ def load() -> ctypes.CDLL:
         f = getattr(L, name)
         f.restype = ctypes.c_int
         f.argtypes = [P, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
+    L.alpaca_attn_decode_noalloc.restype = ctypes.c_int
+    L.alpaca_attn_decode_noalloc.argtypes = [P, ctypes.c_void_p]
     L.alpaca_attention.restype = ctypes.c_int
     L.alpaca_attention.argtypes = [P, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
     L.alpaca_attention_workspace_bytes.restype = ctypes.c_int

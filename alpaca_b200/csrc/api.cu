@@ -211,6 +211,32 @@ alpaca_cuda_status alpaca_attn_decode(const alpaca_attn_desc* desc, void* worksp
     return run(desc, ALPACA_ATTN_DECODE_SPLIT, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
 }
 
+alpaca_cuda_status alpaca_attn_decode_noalloc(const alpaca_attn_desc* desc, alpaca_stream_t stream) {
+    alpaca_cuda_status st = validate(desc);
+    if (st != ALPACA_CUDA_OK) return st;
+    st = check_kind(*desc, ALPACA_ATTN_DECODE_SPLIT);
+    if (st != ALPACA_CUDA_OK) return st;
+    const size_t need = decode_workspace_bytes(*desc);
+    if (need > kDecodeBuiltinScratchBytes)
+        return fail(ALPACA_CUDA_ERR_WORKSPACE_TOO_SMALL,
+                    "decode_noalloc: this call needs " + std::to_string(need) + " bytes of split scratch; the built-in " +
+                        "scratch holds " + std::to_string(kDecodeBuiltinScratchBytes) +
+                        " bytes (use alpaca_attn_decode with a workspace)");
+    DeviceInfo di;
+    cudaError_t e = device_info(&di);
+    if (e != cudaSuccess) return fail(ALPACA_CUDA_ERR_CUDA, std::string("decode_noalloc: device query: ") + cudaGetErrorString(e));
+    void* scratch = nullptr;
+    e = decode_builtin_scratch(&scratch);
+    if (e != cudaSuccess)
+        return fail(ALPACA_CUDA_ERR_CUDA, std::string("decode_noalloc: scratch address: ") + cudaGetErrorString(e));
+    Call c{desc, desc->scale > 0.f ? desc->scale : 1.0f / std::sqrt(static_cast<float>(desc->head_dim)), di.err, scratch,
+           kDecodeBuiltinScratchBytes, di.num_sms};
+    e = launch_decode(c, reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess)
+        return fail(ALPACA_CUDA_ERR_LAUNCH_FAILED, std::string("decode_noalloc launch failed: ") + cudaGetErrorString(e));
+    return ok();
+}
+
 alpaca_cuda_status alpaca_attention_workspace_bytes(const alpaca_attn_desc* desc, alpaca_attn_kernel kind,
                                                     size_t* bytes) {
     if (!bytes) return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "workspace_bytes: null output");

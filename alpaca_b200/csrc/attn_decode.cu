@@ -17,6 +17,7 @@
 // Scores are kept in log2 units (q pre-scaled by scale*log2(e)), so every exponential is one ex2.approx.
 // Partial-state layout: [seq][kv_head][split][g][d + 2] f32 = accumulators, then m (log2 units), then l.
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 #include "internal.h"
@@ -359,7 +360,34 @@ cudaError_t launch_d(const DecodeArgs& a, int n_seqs, cudaStream_t s) {
     return cudaLaunchKernelEx(&cfg, decode_combine_kernel<D>, a);
 }
 
+// Built-in decode scratch for alpaca_attn_decode_noalloc: a file-scope device array, so that entry point never
+// asks for device memory. Every device that loads the library holds these bytes until the process exits; all
+// calls on a device share them.
+static __device__ __align__(256) float g_decode_scratch[kDecodeBuiltinScratchBytes / sizeof(float)];
+
+constexpr int kMaxScratchDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_ptr[kMaxScratchDevices] = {};
+
 }  // namespace
+
+// Device address of the built-in scratch on the current device. The first call on a device looks it up with
+// cudaGetSymbolAddress (with that device current) and caches it; later calls only read the cache.
+cudaError_t decode_builtin_scratch(void** ptr) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kMaxScratchDevices) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    if (!g_scratch_ptr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_decode_scratch);
+        if (e != cudaSuccess) return e;
+        g_scratch_ptr[dev] = p;
+    }
+    *ptr = g_scratch_ptr[dev];
+    return cudaSuccess;
+}
 
 int decode_split_len(int head_dim) { return head_dim == 128 ? Geo<128>::SL : Geo<64>::SL; }
 

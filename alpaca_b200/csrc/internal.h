@@ -25,6 +25,9 @@ int decode_max_splits(const alpaca_attn_desc& d);            // splits of the lo
 size_t decode_workspace_bytes(const alpaca_attn_desc& d);    // partial-state bytes
 bool decode_supported(const alpaca_attn_desc& d);            // head_dim / group limits of the kernel
 cudaError_t launch_decode(const Call& c, cudaStream_t s);
+// Built-in scratch of alpaca_attn_decode_noalloc (file-scope device array in attn_decode.cu).
+constexpr size_t kDecodeBuiltinScratchBytes = size_t(8) << 20;  // 8 MiB
+cudaError_t decode_builtin_scratch(void** ptr);
 
 // ---- general fp32 SIMT attention (attn_general.cu)
 cudaError_t launch_general(const Call& c, cudaStream_t s);

@@ -122,6 +122,23 @@ alpaca_cuda_status alpaca_attn_prefill(const alpaca_attn_desc* desc, void* works
 alpaca_cuda_status alpaca_attn_decode(const alpaca_attn_desc* desc, void* workspace, size_t workspace_bytes,
                                       alpaca_stream_t stream);
 
+/* Split-KV decode that allocates nothing and takes no workspace. No counterpart in alpaca.swift: it is an
+ * addition of this library for callers that cannot call cudaMalloc or hand over a scratch buffer, such as a host
+ * runtime that owns every device allocation through its own fixed memory plan, or code running where allocation is
+ * forbidden. Same computation, kernels and results as alpaca_attn_decode; the caller still passes every input and
+ * output pointer in `desc`.
+ *   - Split scratch lives in a file-scope device array of 8 MiB (8388608 bytes). Every GPU that loads the library
+ *     holds it until the process exits. A call whose split state needs more (n_seqs * n_heads * splits *
+ *     (head_dim + 2) * 4 bytes, see alpaca_attention_workspace_bytes) is rejected with
+ *     ALPACA_CUDA_ERR_WORKSPACE_TOO_SMALL before anything is enqueued.
+ *   - The first call on a device looks up the array's device address (cudaGetSymbolAddress, with that device
+ *     current) and caches it; make that first call before any stream capture.
+ *   - All calls on a device share the array, which keeps the last call's contents. Nothing in it needs to start at
+ *     zero: every split state the combine step reads is written earlier in the same call. Calls that overlap on
+ *     the GPU (different streams without ordering) race on the array; order them on one stream or with events.
+ *   - No cudaMalloc, cudaFree or allocating library routine is called. */
+alpaca_cuda_status alpaca_attn_decode_noalloc(const alpaca_attn_desc* desc, alpaca_stream_t stream);
+
 /* Bytes of workspace `kind` needs for `desc` (0 when none). Replaces KernelEncoder.decodeScratchBytes
  * (KernelEncoder.swift:88-92). Host-only; enqueues nothing. */
 alpaca_cuda_status alpaca_attention_workspace_bytes(const alpaca_attn_desc* desc, alpaca_attn_kernel kind,
