@@ -7,20 +7,21 @@
 //
 //   * persistent kernel, one CTA per SM, work items = (sequence, head, pair of 128-row query tiles) handed out
 //     heaviest first (items with more visible KV blocks come first), so causal work is balanced over 148 SMs;
-//   * warp 0: TMA producer. Q tiles and a ring of K/V blocks (128 rows x d) land in shared memory with
+//   * warp 0: TMA producer. Q tiles and a 3-stage ring of K/V blocks (128 rows x d) land in shared memory with
 //     128-byte swizzle, no multicast;
-//   * warp 1: one thread issues tcgen05.mma. S tiles (128x128 f32) and O tiles (128xd f32) live in tensor memory
+//   * warps 1 and 2: one thread each issues tcgen05.mma for query tile A / B. S tiles (128x128 f32) and O tiles (128xd f32) live in tensor memory
 //     (TMEM: S_A, S_B, O_A, O_B = 384 of 512 columns); completion is signalled with tcgen05.commit;
-//   * warps 4-7 and 8-11: two softmax warpgroups, one per query tile of the pair, one query row per thread. They
-//     read S rows from TMEM, apply the causal mask on diagonal blocks, keep the running max in log2 units (the
+//   * warps 4-11 and 12-19: softmax for query tile A and B, two threads per query row (one per 64-column half
+//     of the 128-column S block; the partial row maxima meet through shared memory and a 64-arrival mbarrier per
+//     pair of warps that share TMEM lanes). They read S from TMEM, apply the causal mask on diagonal blocks, keep the running max in log2 units (the
 //     max is only moved when it grows by more than 8, so O rarely needs rescaling), compute P = 2^(s*c - m)
 //     two at a time with ex2.approx.f16x2 (P is an f16 MMA operand anyway), write it into a swizzled
 //     shared-memory tile that is the A operand of the P·V MMA, and finish each tile with O / l;
 //   * the softmax denominator l comes out of the tensor core: the P·V MMA runs with N = d + 16 where the extra
 //     16 columns of B are a constant block of ones, so O's column d accumulates Σ P exactly as the MMA used it
 //     (no per-score FADD, and l matches the rounded P that multiplied V).
-//   The tensor pipe alternates S(A, j+1), PV(A, j), S(B, j+1), PV(B, j) so one tile's softmax overlaps the
-//   other tile's MMAs.
+//   Each issuer queues S(j+1) before PV(j), so the next S block is ready when the softmax finishes the current
+//   one, and the two tiles' MMAs interleave in the tensor pipe without waiting on each other's softmax.
 //
 // Every mbarrier wait is bounded (2 s; 2 ms under ALPACA_ATTN_FLAG_DEBUG_FORCE_TIMEOUT). On a timeout the CTA
 // raises its abort flag and the device error word, waits (bounded) for its own TMA loads and MMAs in flight,
@@ -38,8 +39,8 @@ namespace {
 constexpr int kBM = 128;        // query rows per tile
 constexpr int kBN = 128;        // KV rows per block
 constexpr int kD = 64;          // head dim of this kernel
-constexpr int kStages = 2;      // K/V ring depth
-constexpr int kThreads = 384;   // 12 warps
+constexpr int kStages = 3;      // K/V ring depth
+constexpr int kThreads = 640;   // 20 warps: TMA, MMA, TMEM allocator, idle, then 16 softmax warps
 constexpr int kTmemCols = 512;
 constexpr int kON = kD + 16;    // O tile columns: d context columns + 16 columns of Σ P (the ones block)
 constexpr uint32_t kTileBytes = kBM * kD * 2;  // 16 KB: one Q, K or V tile
@@ -70,12 +71,15 @@ struct SmemLayout {
     uint64_t q_full[2], q_empty[2];
     uint64_t k_full[kStages], k_empty[kStages], v_full[kStages], v_empty[kStages];
     uint64_t s_full[2], s_empty[2], p_full[2], o_done[2];
-    uint64_t dbg, fin;
+    uint64_t xbar[2][4];       // per (tile, lane quarter): the two half-row warps' partial maxima are in
+    uint64_t dbg, fin[2];
+    float xmax[2][2][2][kBM];  // [tile][block parity][half][row] partial row maxima
     uint32_t tmem_base;
     int abort_flag;
 };
 
 constexpr size_t kSmemBytes = sizeof(SmemLayout) + 1024;  // + alignment slack
+static_assert(kSmemBytes <= 232448, "shared memory layout exceeds the 227 KB a CTA may use");
 
 struct Item {
     int seq, head, row0[2], nblk[2];
@@ -132,7 +136,7 @@ __device__ __forceinline__ void mma_pv(const SmemLayout* sm, int tile, int stage
 
 // ---------------------------------------------------------------------------------------------- kernel
 
-template <bool kF16Exp>
+template <bool kF16Exp, int kEmuPairs>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const PrefillArgs a) {
@@ -148,18 +152,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&sm->q_full[i], 1);
             mbar_init(&sm->q_empty[i], 1);
             mbar_init(&sm->s_full[i], 1);
-            mbar_init(&sm->s_empty[i], 4);
-            mbar_init(&sm->p_full[i], 4);
+            mbar_init(&sm->s_empty[i], 8);
+            mbar_init(&sm->p_full[i], 8);
+            for (int qq = 0; qq < 4; qq++) mbar_init(&sm->xbar[i][qq], 64);
             mbar_init(&sm->o_done[i], 1);
         }
         for (int i = 0; i < kStages; i++) {
             mbar_init(&sm->k_full[i], 1);
-            mbar_init(&sm->k_empty[i], 1);
+            mbar_init(&sm->k_empty[i], 2);  // released by both tiles' MMA issuers
             mbar_init(&sm->v_full[i], 1);
-            mbar_init(&sm->v_empty[i], 1);
+            mbar_init(&sm->v_empty[i], 2);
         }
         mbar_init(&sm->dbg, 1);
-        mbar_init(&sm->fin, 1);
+        mbar_init(&sm->fin[0], 1);
+        mbar_init(&sm->fin[1], 1);
         fence_barrier_init();
         tma_prefetch_desc(&tm_q);
         tma_prefetch_desc(&tm_k);
@@ -221,93 +227,86 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int t = 0; t < 2; t++)
                 if (q_uses[t] > 0) mbar_wait(&sm->q_full[t], (q_uses[t] - 1) & 1, drain);
         }
-    } else if (warp == 1 && lane == 0) {
-        // ------------------------------------------------------------------ MMA issuer
-        uint32_t kv_it = 0, q_uses[2] = {0, 0}, s_uses[2] = {0, 0}, p_uses[2] = {0, 0};
+    } else if ((warp == 1 || warp == 2) && lane == 0) {
+        // ------------------------------------------------------------------ MMA issuers, one thread per tile
+        // Each tile's S and P·V MMAs are issued by its own thread, so one tile's softmax never holds up the other
+        // tile's MMAs. Both threads walk every KV block of every item: a tile with fewer blocks than its partner
+        // still releases the K/V stages it does not use (after they land), so each stage's empty barrier (count 2)
+        // completes once per use.
+        const int t = warp - 1;
+        uint32_t kv_it = 0, q_uses = 0, s_uses = 0, p_uses = 0;
         bool ok = true;
-        if (debug_timeout) ok = mbar_wait(&sm->dbg, 0, ab);  // nothing arrives: exercises the give-up path
+        if (debug_timeout && t == 0) ok = mbar_wait(&sm->dbg, 0, ab);  // nothing arrives: exercises the give-up path
         for (int it = blockIdx.x; ok && it < a.total_items; it += gridDim.x) {
             const Item x = decode_item(a, it);
-            const int n[2] = {x.nblk[0], x.nblk[1]};
-            const int nmax = max(n[0], n[1]);
-            for (int t = 0; t < 2 && ok; t++)
-                if (n[t] > 0) ok = mbar_wait(&sm->q_full[t], q_uses[t] & 1, ab);
-            if (!ok) break;
-            // S(0) for both tiles
-            {
-                const int st = kv_it % kStages;
-                ok = mbar_wait(&sm->k_full[st], (kv_it / kStages) & 1, ab);
+            const int n = x.nblk[t];
+            const int nmax = max(x.nblk[0], x.nblk[1]);
+            if (n > 0) {
+                ok = mbar_wait(&sm->q_full[t], q_uses & 1, ab);
                 if (!ok) break;
-                tc_fence_after();
-                for (int t = 0; t < 2 && ok; t++) {
-                    if (n[t] == 0) continue;
-                    ok = mbar_wait(&sm->s_empty[t], (s_uses[t] & 1) ^ 1, ab);
-                    if (!ok) break;
-                    tc_fence_after();
-                    mma_s(sm, t, st, tmem_base);
-                    tc_commit(&sm->s_full[t]);
-                    s_uses[t]++;
-                    if (n[t] == 1) tc_commit(&sm->q_empty[t]);
-                }
-                if (!ok) break;
-                tc_commit(&sm->k_empty[st]);
             }
-            for (int j = 0; ok && j < nmax; j++) {
-                const uint32_t cur = kv_it + j, nxt = cur + 1;
-                const int stc = cur % kStages, stn = nxt % kStages;
-                const bool have_next = j + 1 < nmax;
-                if (have_next) {
-                    ok = mbar_wait(&sm->k_full[stn], (nxt / kStages) & 1, ab);
+            // Iteration j consumes K(j) (S of block j) and then V(j-1) (P·V of block j-1): the producer's load
+            // order, so every wait here depends only on releases made NS iterations earlier. S(j) is queued
+            // before PV(j-1), so the next S block is ready when the softmax finishes the current one.
+            for (int j = 0; ok && j <= nmax; j++) {
+                if (j < nmax) {
+                    const uint32_t cur = kv_it + j;
+                    const int st = cur % kStages;
+                    ok = mbar_wait(&sm->k_full[st], (cur / kStages) & 1, ab);
                     if (!ok) break;
-                    tc_fence_after();
-                }
-                bool v_ready = false;
-                for (int t = 0; t < 2 && ok; t++) {
-                    if (j + 1 < n[t]) {  // S(t, j+1)
-                        ok = mbar_wait(&sm->s_empty[t], (s_uses[t] & 1) ^ 1, ab);
+                    if (j < n) {
+                        ok = mbar_wait(&sm->s_empty[t], (s_uses & 1) ^ 1, ab);
                         if (!ok) break;
                         tc_fence_after();
-                        mma_s(sm, t, stn, tmem_base);
+                        mma_s(sm, t, st, tmem_base);
                         tc_commit(&sm->s_full[t]);
-                        s_uses[t]++;
-                        if (j + 2 == n[t]) tc_commit(&sm->q_empty[t]);
-                    }
-                    if (j < n[t]) {  // PV(t, j)
-                        if (!v_ready) {
-                            ok = mbar_wait(&sm->v_full[stc], (cur / kStages) & 1, ab);
-                            if (!ok) break;
-                            v_ready = true;
-                        }
-                        ok = mbar_wait(&sm->p_full[t], p_uses[t] & 1, ab);
-                        if (!ok) break;
-                        tc_fence_after();
-                        mma_pv(sm, t, stc, tmem_base, j > 0);
-                        tc_commit(&sm->o_done[t]);
-                        p_uses[t]++;
+                        s_uses++;
+                        if (j + 1 == n) tc_commit(&sm->q_empty[t]);
+                        tc_commit(&sm->k_empty[st]);
+                    } else {
+                        mbar_arrive(&sm->k_empty[st]);  // block this tile does not use
                     }
                 }
-                if (!ok) break;
-                if (have_next) tc_commit(&sm->k_empty[stn]);
-                tc_commit(&sm->v_empty[stc]);
+                if (j > 0) {
+                    const int b = j - 1;
+                    const uint32_t prv = kv_it + b;
+                    const int sp = prv % kStages;
+                    ok = mbar_wait(&sm->v_full[sp], (prv / kStages) & 1, ab);
+                    if (!ok) break;
+                    if (b < n) {
+                        ok = mbar_wait(&sm->p_full[t], p_uses & 1, ab);
+                        if (!ok) break;
+                        tc_fence_after();
+                        mma_pv(sm, t, sp, tmem_base, b > 0);
+                        tc_commit(&sm->o_done[t]);
+                        tc_commit(&sm->v_empty[sp]);
+                        p_uses++;
+                    } else {
+                        mbar_arrive(&sm->v_empty[sp]);
+                    }
+                }
             }
+            if (!ok) break;
             kv_it += nmax;
-            for (int t = 0; t < 2; t++)
-                if (n[t] > 0) q_uses[t]++;
+            if (n > 0) q_uses++;
         }
         // Retire every MMA this thread issued before TMEM is freed.
         int dummy = 0;
         AbortState drain{&dummy, a.err, kWaitLimitNs};
-        tc_commit(&sm->fin);
-        mbar_wait(&sm->fin, 0, drain);
+        tc_commit(&sm->fin[t]);
+        mbar_wait(&sm->fin[t], 0, drain);
     } else if (warp >= 4) {
-        // ------------------------------------------------------------------ softmax warpgroups
-        const int tile = (warp - 4) >> 2;
+        // ------------------------------------------------------------------ softmax warps
+        const int sw = warp - 4;
+        const int tile = sw >> 3;                   // query tile A (0) or B (1)
+        const int half = (sw >> 2) & 1;             // S columns [half*64, half*64 + 64) of each block
         const int quarter = warp & 3;               // TMEM lane quarter this warp may access
         const int row = quarter * 32 + lane;        // query row within the tile = TMEM lane
         const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
-        const uint32_t s_addr = lane_addr + col_s(tile), o_addr = lane_addr + col_o(tile);
-        uint8_t* p_tile = reinterpret_cast<uint8_t*>(sm->p[tile]);
-        uint32_t s_uses = 0, o_uses = 0;
+        const uint32_t s_addr = lane_addr + col_s(tile) + half * 64, o_addr = lane_addr + col_o(tile);
+        uint8_t* p_half = reinterpret_cast<uint8_t*>(sm->p[tile]) + half * (kBM * 128);
+        uint64_t* xbar = &sm->xbar[tile][quarter];
+        uint32_t s_uses = 0, o_uses = 0, x_uses = 0;
         bool ok = true;
         for (int it = blockIdx.x; ok && it < a.total_items; it += gridDim.x) {
             const Item x = decode_item(a, it);
@@ -321,30 +320,39 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!ok) break;
                 s_uses++;
                 tc_fence_after();
-                float s[kBN];
-#pragma unroll
-                for (int c = 0; c < kBN; c += 32) tmem_ld32(s_addr + c, s + c);
+                float s[64];
+                tmem_ld32(s_addr, s);
+                tmem_ld32(s_addr + 32, s + 32);
                 tmem_wait_ld();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&sm->s_empty[tile]);
 
-                const int kv0 = j * kBN;
-                if (kv0 + kBN - 1 > a.start + row0) {  // block reaches past the tile's first query: mask
+                const int kv0 = j * kBN + half * 64;
+                if (kv0 + 63 > a.start + row0) {  // these columns reach past the tile's first query: mask
 #pragma unroll
-                    for (int c = 0; c < kBN; c++)
+                    for (int c = 0; c < 64; c++)
                         if (kv0 + c > qpos) s[c] = -INFINITY;
                 }
-                // row max as an 8-way tree (no 128-deep dependency chain)
+                // partial row max over 64 columns: 8 independent 3-input max chains, then a small tree
                 float mv[8];
 #pragma unroll
-                for (int i = 0; i < 8; i++) mv[i] = s[i];
+                for (int i = 0; i < 8; i++) mv[i] = fmax3(s[i], s[8 + i], s[16 + i]);
 #pragma unroll
-                for (int c = 8; c < kBN; c += 8)
+                for (int i = 0; i < 8; i++) mv[i] = fmax3(mv[i], s[24 + i], s[32 + i]);
 #pragma unroll
-                    for (int i = 0; i < 8; i++) mv[i] = fmaxf(mv[i], s[c + i]);
-                const float mx = fmaxf(fmaxf(fmaxf(mv[0], mv[1]), fmaxf(mv[2], mv[3])),
-                                       fmaxf(fmaxf(mv[4], mv[5]), fmaxf(mv[6], mv[7])));
+                for (int i = 0; i < 8; i++) mv[i] = fmax3(mv[i], s[40 + i], s[48 + i]);
+#pragma unroll
+                for (int i = 0; i < 8; i++) mv[i] = fmaxf(mv[i], s[56 + i]);
+                const float pmax = fmaxf(fmax3(mv[0], mv[1], mv[2]), fmax3(fmax3(mv[3], mv[4], mv[5]), mv[6], mv[7]));
+                // exchange with the warp holding the other half of these rows
+                const int par = x_uses & 1;
+                sm->xmax[tile][par][half][row] = pmax;
+                mbar_arrive(xbar);
+                ok = __all_sync(0xffffffffu, mbar_wait(xbar, par, ab));
+                if (!ok) break;
+                x_uses++;
+                const float mx = fmaxf(pmax, sm->xmax[tile][par][half ^ 1][row]);
                 const float mxs = mx * a.scale_log2;
                 bool rescale = false;
                 float alpha = 1.f;
@@ -355,13 +363,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                     m_used = mxs;
                     rescale = true;
                 }
-                uint32_t pk[kBN / 2];
+                // P = 2^(s*c - m) per column pair; kEmuPairs of every 8 pairs on the FMA pipe, the rest on MUFU
+                const float2 c2 = make_float2(a.scale_log2, a.scale_log2), nm2 = make_float2(-m_used, -m_used);
+                uint32_t pk[32];
 #pragma unroll
-                for (int c = 0; c < kBN; c += 2) {
-                    const float x0 = fmaf(s[c], a.scale_log2, -m_used);
-                    const float x1 = fmaf(s[c + 1], a.scale_log2, -m_used);
-                    if constexpr (kF16Exp) pk[c / 2] = ex2_approx_f16x2(pack_half2(x0, x1));
-                    else pk[c / 2] = pack_half2(ex2_approx(x0), ex2_approx(x1));
+                for (int pr = 0; pr < 32; pr++) {
+                    const float2 xx = __ffma2_rn(make_float2(s[2 * pr], s[2 * pr + 1]), c2, nm2);
+                    if ((pr & 7) < kEmuPairs) {
+                        const float2 e = exp2_poly2(make_float2(fmaxf(xx.x, -125.f), fmaxf(xx.y, -125.f)));
+                        pk[pr] = pack_half2(e.x, e.y);
+                    } else if constexpr (kF16Exp) {
+                        pk[pr] = ex2_approx_f16x2(pack_half2(xx.x, xx.y));
+                    } else {
+                        pk[pr] = pack_half2(ex2_approx(xx.x), ex2_approx(xx.y));
+                    }
                 }
                 if (j > 0) {  // PV(j-1) must be done before P is overwritten or O is rescaled
                     ok = __all_sync(0xffffffffu, mbar_wait(&sm->o_done[tile], o_uses & 1, ab));
@@ -369,26 +384,31 @@ __global__ void __launch_bounds__(kThreads, 1)
                     o_uses++;
                     tc_fence_after();
                 }
-                // tcgen05.ld/st are warp-collective: the whole warp rescales when any of its rows must
-                // (alpha stays 1 for the others). Columns d.. hold Σ P and are rescaled with O.
+                // tcgen05.ld/st are warp-collective: the whole warp rescales when any of its rows must (alpha stays
+                // 1 for the others). Half 0 owns O columns 0-31 and the Σ P columns d..d+15, half 1 columns 32-63.
                 if (__any_sync(0xffffffffu, rescale)) {
-                    float o[96];
-#pragma unroll
-                    for (int c = 0; c < 96; c += 32) tmem_ld32(o_addr + c, o + c);
+                    float o[32];
+                    tmem_ld32(o_addr + half * 32, o);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int c = 0; c < 96; c++) o[c] *= alpha;
+                    for (int c = 0; c < 32; c++) o[c] *= alpha;
+                    tmem_st32(o_addr + half * 32, o);
+                    if (half == 0) {
+                        float lcol[16];
+                        tmem_ld16(o_addr + kD, lcol);
+                        tmem_wait_ld();
 #pragma unroll
-                    for (int c = 0; c < 96; c += 32) tmem_st32(o_addr + c, o + c);
+                        for (int c = 0; c < 16; c++) lcol[c] *= alpha;
+                        tmem_st16(o_addr + kD, lcol);
+                    }
                     tmem_wait_st();
                 }
-                // P row -> swizzled smem: 16 chunks of 8 halves; chunk ch of half hh at
-                // hh*16K + row*128 + ((ch ^ (row & 7)) * 16)
+                // P half-row -> swizzled smem: 8 chunks of 8 halves at row*128 + ((ch ^ (row & 7)) * 16) of this
+                // half's 16 KB K-block
 #pragma unroll
-                for (int ch = 0; ch < kBN / 8; ch++) {
-                    const int hh = ch >> 3, c8 = ch & 7;
-                    uint4 val = make_uint4(pk[ch * 4], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
-                    *reinterpret_cast<uint4*>(p_tile + hh * (kBM * 128) + row * 128 + ((c8 ^ (row & 7)) << 4)) = val;
+                for (int ch = 0; ch < 8; ch++) {
+                    const uint4 val = make_uint4(pk[ch * 4], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
+                    *reinterpret_cast<uint4*>(p_half + row * 128 + ((ch ^ (row & 7)) << 4)) = val;
                 }
                 fence_proxy_async_smem();
                 tc_fence_before();
@@ -401,20 +421,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!ok) break;
             o_uses++;
             tc_fence_after();
-            float o[96];
-#pragma unroll
-            for (int c = 0; c < 96; c += 32) tmem_ld32(o_addr + c, o + c);
+            float o[32];
+            tmem_ld32(o_addr + half * 32, o);
+            const float lsum = tmem_ld1(o_addr + kD);
             tmem_wait_ld();
             tc_fence_before();
             const int t = row0 + row;
             if (t < a.tokens) {
-                const float inv = 1.f / o[kD];
+                const float inv = 1.f / lsum;
                 const int64_t off = x.seq * a.out_seq_stride + static_cast<int64_t>(t) * a.out_token_stride +
-                                    static_cast<int64_t>(x.head) * kD;
+                                    static_cast<int64_t>(x.head) * kD + half * 32;
                 if (a.out_f16) {
                     uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(a.out) + off);
 #pragma unroll
-                    for (int c = 0; c < kD; c += 8)
+                    for (int c = 0; c < 32; c += 8)
                         dst[c / 8] = make_uint4(pack_half2(o[c] * inv, o[c + 1] * inv),
                                                 pack_half2(o[c + 2] * inv, o[c + 3] * inv),
                                                 pack_half2(o[c + 4] * inv, o[c + 5] * inv),
@@ -422,7 +442,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 } else {
                     float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + off);
 #pragma unroll
-                    for (int c = 0; c < kD; c += 4)
+                    for (int c = 0; c < 32; c += 4)
                         dst[c / 4] = make_float4(o[c] * inv, o[c + 1] * inv, o[c + 2] * inv, o[c + 3] * inv);
                 }
             }
@@ -495,6 +515,33 @@ bool prefill_f16_exp() {
     return v;
 }
 
+// Share of exponentials computed on the FMA pipe: ALPACA_PREFILL_EMU column pairs of every 8 (0, 2, 3 or 4;
+// default 3). MUFU gives 16 exp2 per clock per SM, fewer than the tensor pipe consumes at head_dim 64.
+constexpr int kEmuDefault = 3;
+int prefill_emu_pairs() {
+    static const int v = [] {
+        const char* e = std::getenv("ALPACA_PREFILL_EMU");
+        if (!e || !*e) return kEmuDefault;
+        const int x = std::atoi(e);
+        return (x == 0 || x == 2 || x == 3 || x == 4) ? x : kEmuDefault;
+    }();
+    return v;
+}
+
+using PrefillFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, PrefillArgs);
+
+PrefillFn prefill_variant(bool f16exp, int emu) {
+    if (f16exp) {
+        switch (emu) {
+            case 0: return prefill_kernel<true, 0>;
+            case 2: return prefill_kernel<true, 2>;
+            case 4: return prefill_kernel<true, 4>;
+            default: return prefill_kernel<true, 3>;
+        }
+    }
+    return emu == 0 ? prefill_kernel<false, 0> : prefill_kernel<false, 3>;
+}
+
 }  // namespace
 
 bool prefill_supported(const alpaca_attn_desc& d) {
@@ -509,14 +556,12 @@ size_t prefill_workspace_bytes(const alpaca_attn_desc& d) {
 
 cudaError_t launch_prefill(const Call& c, cudaStream_t s) {
     const alpaca_attn_desc& d = *c.d;
+    const PrefillFn fn = prefill_variant(prefill_f16_exp(), prefill_emu_pairs());
     static std::once_flag attr_once;
     static cudaError_t attr_err = cudaSuccess;
-    std::call_once(attr_once, [] {
-        attr_err = cudaFuncSetAttribute(prefill_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    std::call_once(attr_once, [fn] {
+        attr_err = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn), cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         static_cast<int>(kSmemBytes));
-        if (attr_err == cudaSuccess)
-            attr_err = cudaFuncSetAttribute(prefill_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            static_cast<int>(kSmemBytes));
     });
     if (attr_err != cudaSuccess) return attr_err;
 
@@ -559,10 +604,7 @@ cudaError_t launch_prefill(const Call& c, cudaStream_t s) {
     a.err = c.err;
     a.flags = d.flags;
     const int grid = std::max(1, std::min(a.total_items, c.num_sms));
-    if (prefill_f16_exp())
-        prefill_kernel<true><<<grid, kThreads, kSmemBytes, s>>>(tq, tk, tv, a);
-    else
-        prefill_kernel<false><<<grid, kThreads, kSmemBytes, s>>>(tq, tk, tv, a);
+    fn<<<grid, kThreads, kSmemBytes, s>>>(tq, tk, tv, a);
     return cudaGetLastError();
 }
 

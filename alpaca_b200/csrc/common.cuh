@@ -41,6 +41,30 @@ __device__ __forceinline__ uint32_t ex2_approx_f16x2(uint32_t x) {
     return y;
 }
 
+// 3-input maximum (one instruction for two comparisons).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+// 2^x for a pair on the FMA pipe (no MUFU), valid for x >= -125 (callers clamp).
+// Cody-Waite split x = j + f, j = round(x) taken from the low mantissa bits of x + 1.5*2^23, f in [-0.5, 0.5];
+// 2^f from a degree-3 polynomial fitted here for minimax relative error on [-0.5, 0.5] (Lawson iterations,
+// max relative error 7.5e-5, below binary16 rounding); 2^j is applied by adding j to the exponent field.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+    const float2 magic = make_float2(12582912.0f, 12582912.0f);
+    const float2 t = __fadd2_rn(x, magic);
+    const float2 j = __fadd2_rn(t, make_float2(-12582912.0f, -12582912.0f));
+    const float2 f = __ffma2_rn(j, make_float2(-1.f, -1.f), x);
+    float2 p = __ffma2_rn(make_float2(0.055171433836221695f, 0.055171433836221695f), f,
+                          make_float2(0.24261081218719482f, 0.24261081218719482f));
+    p = __ffma2_rn(p, f, make_float2(0.6932609677314758f, 0.6932609677314758f));
+    p = __ffma2_rn(p, f, make_float2(0.9999281167984009f, 0.9999281167984009f));
+    return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
+                       __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
     __half2 h = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&h);
@@ -189,6 +213,32 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
           "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
           "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
         : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+    uint32_t* r = reinterpret_cast<uint32_t*>(v);
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+
+__device__ __forceinline__ float tmem_ld1(uint32_t taddr) {
+    uint32_t r;
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr));
+    return __uint_as_float(r);
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
+    const uint32_t* r = reinterpret_cast<const uint32_t*>(v);
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
 }
 
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
