@@ -5,23 +5,22 @@
 // online softmax, P rounded to f16, O += P·V with f32 accumulation, causal block skip, mask only on diagonal
 // blocks, final 1/l. The structure is B200-native:
 //
-//   * persistent kernel, one CTA per SM, work items = (sequence, head, pair of 128-row query tiles) handed out
-//     heaviest first (items with more visible KV blocks come first), so causal work is balanced over 148 SMs;
-//   * warp 0: TMA producer. Q tiles and a 3-stage ring of K/V blocks (128 rows x d) land in shared memory with
+//   * persistent kernel, one CTA per SM, work items = (sequence, head, pair of 128-row query tiles A and B)
+//     handed out heaviest first (items with more visible KV blocks come first), so the causal triangle is
+//     balanced over the 148 SMs;
+//   * warp 0: TMA producer. Q tiles and a 4-stage ring of K/V blocks (128 rows x d) land in shared memory with
 //     128-byte swizzle, no multicast;
-//   * warps 1 and 2: one thread each issues tcgen05.mma for query tile A / B. S tiles (128x128 f32) and O tiles (128xd f32) live in tensor memory
-//     (TMEM: S_A, S_B, O_A, O_B = 384 of 512 columns); completion is signalled with tcgen05.commit;
-//   * warps 4-11 and 12-19: softmax for query tile A and B, two threads per query row (one per 64-column half
-//     of the 128-column S block; the partial row maxima meet through shared memory and a 64-arrival mbarrier per
-//     pair of warps that share TMEM lanes). They read S from TMEM, apply the causal mask on diagonal blocks, keep the running max in log2 units (the
-//     max is only moved when it grows by more than 8, so O rarely needs rescaling), compute P = 2^(s*c - m)
-//     two at a time with ex2.approx.f16x2 (P is an f16 MMA operand anyway), write it into a swizzled
-//     shared-memory tile that is the A operand of the P·V MMA, and finish each tile with O / l;
-//   * the softmax denominator l comes out of the tensor core: the P·V MMA runs with N = d + 16 where the extra
-//     16 columns of B are a constant block of ones, so O's column d accumulates Σ P exactly as the MMA used it
-//     (no per-score FADD, and l matches the rounded P that multiplied V).
-//   Each issuer queues S(j+1) before PV(j), so the next S block is ready when the softmax finishes the current
-//   one, and the two tiles' MMAs interleave in the tensor pipe without waiting on each other's softmax.
+//   * warps 1 and 2: one thread each issues tcgen05.mma for tile A / B: S = Q·Kᵀ (A and B from shared memory)
+//     into TMEM, and O += P·V with P read from TMEM (A operand in tensor memory, B = V from shared memory), so
+//     P never touches shared memory and the tensor core's shared-memory reads stay within bandwidth. Each issuer
+//     queues S(j+1) before PV(j), so the next S block is ready when the softmax finishes the current one;
+//   * warps 4-11 and 12-19: softmax for tile A and B, two threads per query row (one per 64-column half of the
+//     128-column S block; the two partial row maxima meet through shared memory and a 64-arrival mbarrier per
+//     pair of warps that share TMEM lanes). They read S from TMEM, mask diagonal blocks, keep the running max in
+//     log2 units (it only moves when it grows by more than 8, so O rarely needs rescaling), compute
+//     P = 2^(s*c - m) — most exponentials on MUFU, a fixed share on the FMA pipe with a polynomial — sum the row
+//     in f32, store P to TMEM as f16 pairs and finish each tile with O / l.
+//   TMEM: S_A 0-127, S_B 128-255, O_A 256-319, O_B 320-383, P_A 384-447, P_B 448-511 (all 512 columns).
 //
 // Every mbarrier wait is bounded (2 s; 2 ms under ALPACA_ATTN_FLAG_DEBUG_FORCE_TIMEOUT). On a timeout the CTA
 // raises its abort flag and the device error word, waits (bounded) for its own TMA loads and MMAs in flight,
@@ -39,17 +38,17 @@ namespace {
 constexpr int kBM = 128;        // query rows per tile
 constexpr int kBN = 128;        // KV rows per block
 constexpr int kD = 64;          // head dim of this kernel
-constexpr int kStages = 3;      // K/V ring depth
-constexpr int kThreads = 640;   // 20 warps: TMA, MMA, TMEM allocator, idle, then 16 softmax warps
+constexpr int kStages = 4;      // K/V ring depth
+constexpr int kThreads = 640;   // 20 warps: TMA, MMA A, MMA B (+ TMEM allocator), idle, 16 softmax warps
 constexpr int kTmemCols = 512;
-constexpr int kON = kD + 16;    // O tile columns: d context columns + 16 columns of Σ P (the ones block)
 constexpr uint32_t kTileBytes = kBM * kD * 2;  // 16 KB: one Q, K or V tile
 constexpr float kRescaleThreshold = 8.0f;      // log2 units
 constexpr float kLog2e = 1.4426950408889634f;
 
-// TMEM column map: S_A, S_B (128 f32 columns each), then O_A, O_B (kON columns each, 128-aligned)
-__host__ __device__ constexpr uint32_t col_s(int tile) { return tile ? 128u : 0u; }
-__host__ __device__ constexpr uint32_t col_o(int tile) { return tile ? 384u : 256u; }
+// TMEM column map
+__host__ __device__ constexpr uint32_t col_s(int tile) { return tile ? 128u : 0u; }  // 128 f32 columns
+__host__ __device__ constexpr uint32_t col_o(int tile) { return tile ? 320u : 256u; }  // d f32 columns
+__host__ __device__ constexpr uint32_t col_p(int tile) { return tile ? 448u : 384u; }  // 64 columns of f16 pairs
 
 struct PrefillArgs {
     void* out;
@@ -66,14 +65,13 @@ struct SmemLayout {
     __half q[2][kBM * kD];
     __half k[kStages][kBN * kD];
     __half v[kStages][kBN * kD];
-    __half ones[kBN * 64];   // B-operand block of 1.0 that makes the P·V MMA also produce Σ P
-    __half p[2][kBM * kBN];  // per tile: [2 halves of 64 KV columns][128 rows][64] swizzled
     uint64_t q_full[2], q_empty[2];
     uint64_t k_full[kStages], k_empty[kStages], v_full[kStages], v_empty[kStages];
     uint64_t s_full[2], s_empty[2], p_full[2], o_done[2];
-    uint64_t xbar[2][4];       // per (tile, lane quarter): the two half-row warps' partial maxima are in
+    uint64_t xbar[2][4];       // per (tile, lane quarter): the two half-row warps exchange partial row state
     uint64_t dbg, fin[2];
-    float xmax[2][2][2][kBM];  // [tile][block parity][half][row] partial row maxima
+    float xmax[2][2][2][kBM];  // [tile][exchange parity][half][row] partial row maxima
+    float xl[2][2][kBM];       // [tile][half][row] partial row sums (epilogue)
     uint32_t tmem_base;
     int abort_flag;
 };
@@ -87,8 +85,8 @@ struct Item {
 
 __device__ __forceinline__ int tile_blocks(const PrefillArgs& a, int row0) {
     if (row0 >= a.tokens) return 0;
-    const int last_row = min(row0 + kBM, a.tokens);          // exclusive
-    const int visible = a.start + last_row;                  // KV rows visible to the tile's last row
+    const int last_row = min(row0 + kBM, a.tokens);  // exclusive
+    const int visible = a.start + last_row;          // KV rows visible to the tile's last row
     return (visible + kBN - 1) / kBN;
 }
 
@@ -108,6 +106,7 @@ __device__ __forceinline__ Item decode_item(const PrefillArgs& a, int it) {
 
 // ---------------------------------------------------------------------------------------------- MMA helpers
 
+// S_t = Q_t · K_stageᵀ: M=128, N=128, K=d (4 steps of 16); both operands K-major, 128-byte swizzle.
 __device__ __forceinline__ void mma_s(const SmemLayout* sm, int tile, int stage, uint32_t tmem_base) {
     constexpr uint32_t idesc = idesc_f16_f32(kBM, kBN, false, false);
     const uint32_t qa = smem_u32(sm->q[tile]), ka = smem_u32(sm->k[stage]);
@@ -119,24 +118,23 @@ __device__ __forceinline__ void mma_s(const SmemLayout* sm, int tile, int stage,
     }
 }
 
+// O_t (+)= P_t · V_stage: M=128, N=d, K=128 (8 steps of 16). P in TMEM (8 columns of f16 pairs per step), V
+// MN-major in shared memory (16 KV rows = 2 KB per step).
 __device__ __forceinline__ void mma_pv(const SmemLayout* sm, int tile, int stage, uint32_t tmem_base,
                                        bool accumulate) {
-    // B = [V | ones]: N = d + 16, MN-major; the second 64-column atom (read for columns d..d+15) is the ones
-    // block, reached through the descriptor's leading-byte offset.
-    constexpr uint32_t idesc = idesc_f16_f32(kBM, kON, false, true);
-    const uint32_t pa = smem_u32(sm->p[tile]), va = smem_u32(sm->v[stage]);
-    const uint32_t lbo = smem_u32(sm->ones) - va;
+    constexpr uint32_t idesc = idesc_f16_f32(kBM, kD, false, true);
+    const uint32_t va = smem_u32(sm->v[stage]);
 #pragma unroll
     for (int kk = 0; kk < kBN / 16; kk++) {
-        const uint64_t ad = smem_desc_sw128(pa + (kk >> 2) * (kBM * 128) + (kk & 3) * 32, 16, 1024);
-        const uint64_t bd = smem_desc_sw128(va + kk * 16 * 128, lbo, 1024);
-        tc_mma_ss(tmem_base + col_o(tile), ad, bd, idesc, (accumulate || kk > 0) ? 1u : 0u);
+        const uint64_t bd = smem_desc_sw128(va + kk * 16 * 128, kBN * 128, 1024);
+        tc_mma_ts(tmem_base + col_o(tile), tmem_base + col_p(tile) + kk * 8, bd, idesc,
+                  (accumulate || kk > 0) ? 1u : 0u);
     }
 }
 
 // ---------------------------------------------------------------------------------------------- kernel
 
-template <bool kF16Exp, int kEmuPairs>
+template <int kEmuPairs>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const PrefillArgs a) {
@@ -152,10 +150,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&sm->q_full[i], 1);
             mbar_init(&sm->q_empty[i], 1);
             mbar_init(&sm->s_full[i], 1);
-            mbar_init(&sm->s_empty[i], 8);
+            mbar_init(&sm->s_empty[i], 8);  // one arrival per softmax warp of the tile
             mbar_init(&sm->p_full[i], 8);
-            for (int qq = 0; qq < 4; qq++) mbar_init(&sm->xbar[i][qq], 64);
             mbar_init(&sm->o_done[i], 1);
+            for (int qq = 0; qq < 4; qq++) mbar_init(&sm->xbar[i][qq], 64);
+            mbar_init(&sm->fin[i], 1);
         }
         for (int i = 0; i < kStages; i++) {
             mbar_init(&sm->k_full[i], 1);
@@ -164,17 +163,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&sm->v_empty[i], 2);
         }
         mbar_init(&sm->dbg, 1);
-        mbar_init(&sm->fin[0], 1);
-        mbar_init(&sm->fin[1], 1);
         fence_barrier_init();
         tma_prefetch_desc(&tm_q);
         tma_prefetch_desc(&tm_k);
         tma_prefetch_desc(&tm_v);
-    }
-    {  // the ones block (16 KB of f16 1.0), written through the generic proxy, read by the tensor core
-        uint4* o4 = reinterpret_cast<uint4*>(sm->ones);
-        for (int i = tid; i < kBN * 64 / 8; i += kThreads) o4[i] = make_uint4(0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u);
-        fence_proxy_async_smem();
     }
     if (warp == 2) {
         tmem_alloc(&sm->tmem_base, kTmemCols);
@@ -229,9 +221,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if ((warp == 1 || warp == 2) && lane == 0) {
         // ------------------------------------------------------------------ MMA issuers, one thread per tile
-        // Each tile's S and P·V MMAs are issued by its own thread, so one tile's softmax never holds up the other
-        // tile's MMAs. Both threads walk every KV block of every item: a tile with fewer blocks than its partner
-        // still releases the K/V stages it does not use (after they land), so each stage's empty barrier (count 2)
+        // Both threads walk every KV block of every item: a tile with fewer blocks than its partner still
+        // releases the K/V stages it does not use (after they land), so each stage's empty barrier (count 2)
         // completes once per use.
         const int t = warp - 1;
         uint32_t kv_it = 0, q_uses = 0, s_uses = 0, p_uses = 0;
@@ -246,8 +237,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!ok) break;
             }
             // Iteration j consumes K(j) (S of block j) and then V(j-1) (P·V of block j-1): the producer's load
-            // order, so every wait here depends only on releases made NS iterations earlier. S(j) is queued
-            // before PV(j-1), so the next S block is ready when the softmax finishes the current one.
+            // order, so every wait here depends only on releases made kStages iterations earlier.
             for (int j = 0; ok && j <= nmax; j++) {
                 if (j < nmax) {
                     const uint32_t cur = kv_it + j;
@@ -303,8 +293,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int quarter = warp & 3;               // TMEM lane quarter this warp may access
         const int row = quarter * 32 + lane;        // query row within the tile = TMEM lane
         const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
-        const uint32_t s_addr = lane_addr + col_s(tile) + half * 64, o_addr = lane_addr + col_o(tile);
-        uint8_t* p_half = reinterpret_cast<uint8_t*>(sm->p[tile]) + half * (kBM * 128);
+        const uint32_t s_addr = lane_addr + col_s(tile) + half * 64;
+        const uint32_t o_addr = lane_addr + col_o(tile) + half * 32;  // this thread's 32 context columns
+        const uint32_t p_addr = lane_addr + col_p(tile) + half * 32;  // this thread's 32 columns of P pairs
         uint64_t* xbar = &sm->xbar[tile][quarter];
         uint32_t s_uses = 0, o_uses = 0, x_uses = 0;
         bool ok = true;
@@ -315,6 +306,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int row0 = x.row0[tile];
             const int qpos = a.start + row0 + row;  // absolute position of this thread's query
             float m_used = -INFINITY;
+            float2 lsum = make_float2(0.f, 0.f);    // this thread's half of the row sum (two lanes of a pair)
             for (int j = 0; j < nb; j++) {
                 ok = __all_sync(0xffffffffu, mbar_wait(&sm->s_full[tile], s_uses & 1, ab));
                 if (!ok) break;
@@ -362,21 +354,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                     alpha = ex2_approx(m_used - mxs);
                     m_used = mxs;
                     rescale = true;
+                    lsum.x *= alpha;
+                    lsum.y *= alpha;
                 }
-                // P = 2^(s*c - m) per column pair; kEmuPairs of every 8 pairs on the FMA pipe, the rest on MUFU
+                // P = 2^(s*c - m) per column pair: kEmuPairs of every 8 pairs on the FMA pipe, the rest on MUFU;
+                // the f32 values feed the row sum, the f16 pairs the P·V MMA
                 const float2 c2 = make_float2(a.scale_log2, a.scale_log2), nm2 = make_float2(-m_used, -m_used);
                 uint32_t pk[32];
 #pragma unroll
                 for (int pr = 0; pr < 32; pr++) {
                     const float2 xx = __ffma2_rn(make_float2(s[2 * pr], s[2 * pr + 1]), c2, nm2);
-                    if ((pr & 7) < kEmuPairs) {
-                        const float2 e = exp2_poly2(make_float2(fmaxf(xx.x, -125.f), fmaxf(xx.y, -125.f)));
-                        pk[pr] = pack_half2(e.x, e.y);
-                    } else if constexpr (kF16Exp) {
-                        pk[pr] = ex2_approx_f16x2(pack_half2(xx.x, xx.y));
-                    } else {
-                        pk[pr] = pack_half2(ex2_approx(xx.x), ex2_approx(xx.y));
-                    }
+                    float2 e;
+                    if ((pr & 7) < kEmuPairs) e = exp2_poly2(make_float2(fmaxf(xx.x, -125.f), fmaxf(xx.y, -125.f)));
+                    else e = make_float2(ex2_approx(xx.x), ex2_approx(xx.y));
+                    lsum = __fadd2_rn(lsum, e);
+                    pk[pr] = pack_half2(e.x, e.y);
                 }
                 if (j > 0) {  // PV(j-1) must be done before P is overwritten or O is rescaled
                     ok = __all_sync(0xffffffffu, mbar_wait(&sm->o_done[tile], o_uses & 1, ab));
@@ -384,51 +376,42 @@ __global__ void __launch_bounds__(kThreads, 1)
                     o_uses++;
                     tc_fence_after();
                 }
-                // tcgen05.ld/st are warp-collective: the whole warp rescales when any of its rows must (alpha stays
-                // 1 for the others). Half 0 owns O columns 0-31 and the Σ P columns d..d+15, half 1 columns 32-63.
+                // tcgen05.ld/st are warp-collective: the whole warp rescales when any of its rows must (alpha
+                // stays 1 for the others)
                 if (__any_sync(0xffffffffu, rescale)) {
                     float o[32];
-                    tmem_ld32(o_addr + half * 32, o);
+                    tmem_ld32(o_addr, o);
                     tmem_wait_ld();
 #pragma unroll
                     for (int c = 0; c < 32; c++) o[c] *= alpha;
-                    tmem_st32(o_addr + half * 32, o);
-                    if (half == 0) {
-                        float lcol[16];
-                        tmem_ld16(o_addr + kD, lcol);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int c = 0; c < 16; c++) lcol[c] *= alpha;
-                        tmem_st16(o_addr + kD, lcol);
-                    }
-                    tmem_wait_st();
+                    tmem_st32(o_addr, o);
                 }
-                // P half-row -> swizzled smem: 8 chunks of 8 halves at row*128 + ((ch ^ (row & 7)) * 16) of this
-                // half's 16 KB K-block
-#pragma unroll
-                for (int ch = 0; ch < 8; ch++) {
-                    const uint4 val = make_uint4(pk[ch * 4], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
-                    *reinterpret_cast<uint4*>(p_half + row * 128 + ((ch ^ (row & 7)) << 4)) = val;
-                }
-                fence_proxy_async_smem();
+                tmem_st32(p_addr, reinterpret_cast<const float*>(pk));
+                tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&sm->p_full[tile]);
             }
             if (!ok) break;
-            // epilogue: O / l, with l = column d of the O tile
+            // epilogue: O / l; the two halves of the row sum meet through shared memory
             ok = __all_sync(0xffffffffu, mbar_wait(&sm->o_done[tile], o_uses & 1, ab));
             if (!ok) break;
             o_uses++;
             tc_fence_after();
             float o[32];
-            tmem_ld32(o_addr + half * 32, o);
-            const float lsum = tmem_ld1(o_addr + kD);
+            tmem_ld32(o_addr, o);
+            const float lpart = lsum.x + lsum.y;
+            sm->xl[tile][half][row] = lpart;
+            mbar_arrive(xbar);
             tmem_wait_ld();
             tc_fence_before();
+            ok = __all_sync(0xffffffffu, mbar_wait(xbar, x_uses & 1, ab));
+            if (!ok) break;
+            x_uses++;
+            const float l = lpart + sm->xl[tile][half ^ 1][row];
             const int t = row0 + row;
             if (t < a.tokens) {
-                const float inv = 1.f / lsum;
+                const float inv = 1.f / l;
                 const int64_t off = x.seq * a.out_seq_stride + static_cast<int64_t>(t) * a.out_token_stride +
                                     static_cast<int64_t>(x.head) * kD + half * 32;
                 if (a.out_f16) {
@@ -505,19 +488,9 @@ bool make_map(CUtensorMap* map, const void* base, int d, int heads, int rows, in
     return r == CUDA_SUCCESS;
 }
 
-// Exponential unit of the softmax: "f16x2" (default: ex2.approx.f16x2, two scores per MUFU op) or "f32"
-// (ex2.approx.f32 per score, then rounded to f16). Read once from ALPACA_PREFILL_EXP2.
-bool prefill_f16_exp() {
-    static const bool v = [] {
-        const char* e = std::getenv("ALPACA_PREFILL_EXP2");
-        return !(e && std::strcmp(e, "f32") == 0);
-    }();
-    return v;
-}
-
 // Share of exponentials computed on the FMA pipe: ALPACA_PREFILL_EMU column pairs of every 8 (0, 2, 3 or 4;
-// default 3). MUFU gives 16 exp2 per clock per SM, fewer than the tensor pipe consumes at head_dim 64.
-constexpr int kEmuDefault = 3;
+// default 2). MUFU gives 16 exp2 per clock per SM, fewer than the tensor pipe consumes at head_dim 64.
+constexpr int kEmuDefault = 2;
 int prefill_emu_pairs() {
     static const int v = [] {
         const char* e = std::getenv("ALPACA_PREFILL_EMU");
@@ -530,16 +503,13 @@ int prefill_emu_pairs() {
 
 using PrefillFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, PrefillArgs);
 
-PrefillFn prefill_variant(bool f16exp, int emu) {
-    if (f16exp) {
-        switch (emu) {
-            case 0: return prefill_kernel<true, 0>;
-            case 2: return prefill_kernel<true, 2>;
-            case 4: return prefill_kernel<true, 4>;
-            default: return prefill_kernel<true, 3>;
-        }
+PrefillFn prefill_variant(int emu) {
+    switch (emu) {
+        case 0: return prefill_kernel<0>;
+        case 3: return prefill_kernel<3>;
+        case 4: return prefill_kernel<4>;
+        default: return prefill_kernel<2>;
     }
-    return emu == 0 ? prefill_kernel<false, 0> : prefill_kernel<false, 3>;
 }
 
 }  // namespace
@@ -556,7 +526,7 @@ size_t prefill_workspace_bytes(const alpaca_attn_desc& d) {
 
 cudaError_t launch_prefill(const Call& c, cudaStream_t s) {
     const alpaca_attn_desc& d = *c.d;
-    const PrefillFn fn = prefill_variant(prefill_f16_exp(), prefill_emu_pairs());
+    const PrefillFn fn = prefill_variant(prefill_emu_pairs());
     static std::once_flag attr_once;
     static cudaError_t attr_err = cudaSuccess;
     std::call_once(attr_once, [fn] {
