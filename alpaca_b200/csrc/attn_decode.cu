@@ -5,9 +5,9 @@
 //
 //   split kernel  grid (splits, kv_heads, seqs), 128 threads. One CTA owns SL consecutive cache rows of one KV
 //                 head of one sequence and serves all G query heads of that KV head, so every K/V byte is read
-//                 from HBM exactly once. Each cache row (d halves) is read by d/8 lanes with 128-bit
-//                 non-allocating loads; all of a CTA's K and V loads are issued before any math, so each CTA keeps
-//                 SL*d*4 bytes in flight. Scores are reduced across a row's lanes with a transposing butterfly
+//                 from HBM exactly once. Each cache row (d halves) is copied by d/8 lanes with 16-byte cp.async
+//                 into shared memory (rows past the context are zero-filled), K first then V, so registers stay
+//                 low (six CTAs per SM keep ~190 KB in flight per SM) and the V copy overlaps the score math. Scores are reduced across a row's lanes with a transposing butterfly
 //                 (7 shuffles for 8 rows instead of 24), softmax runs once per (row, head) from shared memory, and
 //                 P·V partial sums are reduced across rows through shared memory.
 //   combine       grid (kv_heads, seqs), 256 threads: rescales the per-split (m, l, acc) states of the G heads to
@@ -109,8 +109,18 @@ __device__ __forceinline__ float reduce_rows(float (&v)[kSlots], int lane, int& 
     return r;
 }
 
+// 16-byte async copy global -> shared (L2 only); src_bytes = 0 fills the 16 bytes with zeros.
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)), "l"(gsrc),
+                 "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 template <int D, int G>
-__global__ void __launch_bounds__(kThreads) decode_split_kernel(const DecodeArgs a) {
+__global__ void __launch_bounds__(kThreads, (G <= 4 ? 6 : 3)) decode_split_kernel(const DecodeArgs a) {
     using Gm = Geo<D>;
     constexpr int SL = Gm::SL, RPS = Gm::RPS, LPR = Gm::LPR, RPW = Gm::RPW;
     const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
@@ -120,30 +130,34 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(const DecodeArgs
     const int row_end = min(L, row0 + SL);
     const int nsplits = (L + SL - 1) / SL;
 
-    extern __shared__ float smem[];
-    float* s_p = smem;                   // [G][SL]  scores, then probabilities
-    float* s_red = s_p + G * SL;         // [RPS][G][D] per-row-lane partial accumulators
-    float* s_ml = s_red + RPS * G * D;   // [G][2]   split max (log2 units) and denominator
+    extern __shared__ __align__(16) uint8_t smem_b[];
+    __half* s_k = reinterpret_cast<__half*>(smem_b);          // [SL][D] this split's K rows
+    __half* s_v = s_k + SL * D;                               // [SL][D] V rows
+    float* s_red = reinterpret_cast<float*>(smem_b);          // [RPS][G][D] partial accumulators (reuses K|V)
+    float* s_p = reinterpret_cast<float*>(s_v + SL * D);      // [G][SL] scores, then probabilities
+    float* s_ml = s_p + G * SL;                               // [G][2] split max (log2 units), denominator
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int lr = lane % LPR;              // this lane's 8 dims: [lr*8, lr*8 + 8)
     const int rowlane = warp * RPW + lane / LPR;
 
-    // 1. Issue every K and V load of this CTA.
+    // 1. Stage this split's K rows, then its V rows, into shared memory with async copies (rows past the
+    //    context are zero-filled, never read). Each thread later reads back only the chunks it copied.
     const int64_t seq_off = static_cast<int64_t>(seq) * a.kv_seq_stride + static_cast<int64_t>(kvh) * D + lr * 8;
-    uint4 kr[kSlots], vr[kSlots];
 #pragma unroll
     for (int i = 0; i < kSlots; i++) {
-        const int r = row0 + i * RPS + rowlane;
-        if (r < row_end) {
-            const int64_t off = seq_off + static_cast<int64_t>(r) * a.kv_row_stride;
-            kr[i] = ld_stream(a.k + off);
-            vr[i] = ld_stream(a.v + off);
-        } else {
-            kr[i] = make_uint4(0, 0, 0, 0);
-            vr[i] = make_uint4(0, 0, 0, 0);
-        }
+        const int rl = i * RPS + rowlane, r = row0 + rl;
+        const bool in = r < row_end;
+        cp_async16(s_k + rl * D + lr * 8, a.k + seq_off + (in ? static_cast<int64_t>(r) * a.kv_row_stride : 0), in ? 16u : 0u);
     }
+    cp_async_commit();
+#pragma unroll
+    for (int i = 0; i < kSlots; i++) {
+        const int rl = i * RPS + rowlane, r = row0 + rl;
+        const bool in = r < row_end;
+        cp_async16(s_v + rl * D + lr * 8, a.v + seq_off + (in ? static_cast<int64_t>(r) * a.kv_row_stride : 0), in ? 16u : 0u);
+    }
+    cp_async_commit();
 
     // 2. Queries of the G heads (this lane's 8 dims), pre-scaled into log2 units.
     float qv[G][8];
@@ -164,17 +178,19 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(const DecodeArgs
     }
 
     // 3. Scores: partial dots, then the transposing row reduction; one lane per (row, head) stores it.
+    cp_async_wait<1>();  // this thread's K chunks have landed
     float part[G][kSlots];
 #pragma unroll
     for (int i = 0; i < kSlots; i++) {
         float kf[8];
-        half8_to_float(kr[i], kf);
+        half8_to_float(*reinterpret_cast<const uint4*>(s_k + (i * RPS + rowlane) * D + lr * 8), kf);
 #pragma unroll
-        for (int g = 0; g < G; g++) {
-            float s = 0.f;
+        for (int g = 0; g < G; g++) {  // packed f32x2 FMAs: two dims per instruction
+            float2 sc = make_float2(0.f, 0.f);
 #pragma unroll
-            for (int e = 0; e < 8; e++) s = fmaf(qv[g][e], kf[e], s);
-            part[g][i] = s;
+            for (int e = 0; e < 8; e += 2)
+                sc = __ffma2_rn(make_float2(qv[g][e], qv[g][e + 1]), make_float2(kf[e], kf[e + 1]), sc);
+            part[g][i] = sc.x + sc.y;
         }
     }
 #pragma unroll
@@ -209,26 +225,37 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(const DecodeArgs
             s_ml[2 * g + 1] = sum;
         }
     }
+    cp_async_wait<0>();  // this thread's V chunks have landed
     __syncthreads();
 
     // 5. P·V over this thread's rows and dims.
+    float2 acc2[G][4];
+#pragma unroll
+    for (int g = 0; g < G; g++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) acc2[g][e] = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int i = 0; i < kSlots; i++) {
+        float vf[8];
+        const int rl = i * RPS + rowlane;
+        half8_to_float(*reinterpret_cast<const uint4*>(s_v + rl * D + lr * 8), vf);
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            const float p = s_p[g * SL + rl];
+            const float2 p2 = make_float2(p, p);
+#pragma unroll
+            for (int e = 0; e < 4; e++) acc2[g][e] = __ffma2_rn(p2, make_float2(vf[2 * e], vf[2 * e + 1]), acc2[g][e]);
+        }
+    }
     float acc[G][8];
 #pragma unroll
     for (int g = 0; g < G; g++)
 #pragma unroll
-        for (int e = 0; e < 8; e++) acc[g][e] = 0.f;
-#pragma unroll
-    for (int i = 0; i < kSlots; i++) {
-        float vf[8];
-        half8_to_float(vr[i], vf);
-        const int rl = i * RPS + rowlane;
-#pragma unroll
-        for (int g = 0; g < G; g++) {
-            const float p = s_p[g * SL + rl];
-#pragma unroll
-            for (int e = 0; e < 8; e++) acc[g][e] = fmaf(p, vf[e], acc[g][e]);
+        for (int e = 0; e < 4; e++) {
+            acc[g][2 * e] = acc2[g][e].x;
+            acc[g][2 * e + 1] = acc2[g][e].y;
         }
-    }
+    __syncthreads();  // every thread is done with K|V: the reduction buffer reuses them
 #pragma unroll
     for (int g = 0; g < G; g++) {
         float4* dst = reinterpret_cast<float4*>(s_red + (rowlane * G + g) * D + lr * 8);
@@ -244,17 +271,17 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(const DecodeArgs
         ((static_cast<int64_t>(seq) * a.n_kv_heads + kvh) * a.max_splits + split) * G;
     for (int o = tid; o < G * D; o += kThreads) {
         const int g = o / D, col = o - g * D;
-        float s = 0.f;
+        float sacc = 0.f;
 #pragma unroll
-        for (int rl = 0; rl < RPS; rl++) s += s_red[(rl * G + g) * D + col];
+        for (int rl = 0; rl < RPS; rl++) sacc += s_red[(rl * G + g) * D + col];
         if (nsplits == 1) {
-            const float val = s / s_ml[2 * g + 1];
+            const float val = sacc / s_ml[2 * g + 1];
             const int64_t oo = static_cast<int64_t>(seq) * a.out_seq_stride + static_cast<int64_t>(kvh * G + g) * D + col;
             if (a.out_f16) static_cast<__half*>(a.out)[oo] = __float2half_rn(val);
             else static_cast<float*>(a.out)[oo] = val;
         } else {
             float* pp = a.partial + (part_base + g) * (D + 2);
-            pp[col] = s;
+            pp[col] = sacc;
             if (col == 0) {
                 pp[D] = s_ml[2 * g];
                 pp[D + 1] = s_ml[2 * g + 1];
@@ -318,7 +345,9 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const D
 template <int D, int G>
 cudaError_t launch_split(const DecodeArgs& a, int n_seqs, cudaStream_t s) {
     using Gm = Geo<D>;
-    const size_t smem = sizeof(float) * (G * Gm::SL + Gm::RPS * G * D + 2 * G);
+    // K and V tiles (2 * SL * D halves; the reduction buffer RPS*G*D floats fits inside them), scores, (m, l)
+    const size_t smem = sizeof(__half) * 2 * Gm::SL * D + sizeof(float) * (G * Gm::SL + 2 * G);
+    static_assert(Gm::RPS * G * D * sizeof(float) <= sizeof(__half) * 2 * Gm::SL * D, "reduction buffer too big");
     dim3 grid(a.max_splits, a.n_kv_heads, n_seqs);
     decode_split_kernel<D, G><<<grid, kThreads, smem, s>>>(a);
     return cudaGetLastError();

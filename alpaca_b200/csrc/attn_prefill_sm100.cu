@@ -361,15 +361,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // the f32 values feed the row sum, the f16 pairs the P·V MMA
                 const float2 c2 = make_float2(a.scale_log2, a.scale_log2), nm2 = make_float2(-m_used, -m_used);
                 uint32_t pk[32];
+                float2 ls[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                                make_float2(0.f, 0.f)};  // four independent partial sums (no serial chain)
 #pragma unroll
                 for (int pr = 0; pr < 32; pr++) {
                     const float2 xx = __ffma2_rn(make_float2(s[2 * pr], s[2 * pr + 1]), c2, nm2);
                     float2 e;
                     if ((pr & 7) < kEmuPairs) e = exp2_poly2(make_float2(fmaxf(xx.x, -125.f), fmaxf(xx.y, -125.f)));
                     else e = make_float2(ex2_approx(xx.x), ex2_approx(xx.y));
-                    lsum = __fadd2_rn(lsum, e);
+                    ls[pr & 3] = __fadd2_rn(ls[pr & 3], e);
                     pk[pr] = pack_half2(e.x, e.y);
                 }
+                lsum = __fadd2_rn(lsum, __fadd2_rn(__fadd2_rn(ls[0], ls[1]), __fadd2_rn(ls[2], ls[3])));
                 if (j > 0) {  // PV(j-1) must be done before P is overwritten or O is rescaled
                     ok = __all_sync(0xffffffffu, mbar_wait(&sm->o_done[tile], o_uses & 1, ab));
                     if (!ok) break;
