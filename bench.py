@@ -135,6 +135,17 @@ def dist_setup(gpus: int):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                 device_id=torch.device("cuda", local))
         pg = dist
+        # Communicator set-up may print a banner on stdout; keep stdout for the one JSON result line.
+        sys.stdout.flush()
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.barrier()
+            torch.cuda.synchronize()
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved, 1)
+            os.close(saved)
     return rank, world, local, pg
 
 
