@@ -3,7 +3,7 @@
 // Same job as alpaca.swift's attn_decode_split_* / attn_decode_merge (Sources/AlpacaMetal/Kernels/
 // attention_decode.metal:28-133, dispatched by KernelEncoder.swift:309-326), designed for B200 HBM3e:
 //
-//   split kernel  grid (splits, kv_heads, seqs), 128 threads. One CTA owns SL consecutive cache rows of one KV
+//   split kernel  grid (splits x kv_heads, seqs), 128 threads, KV heads fastest. One CTA owns SL consecutive cache rows of one KV
 //                 head of one sequence and serves all G query heads of that KV head, so every K/V byte is read
 //                 from HBM exactly once. Each cache row (d halves) is copied by d/8 lanes with 16-byte cp.async
 //                 into shared memory (rows past the context are zero-filled), K first then V, so registers stay
@@ -123,7 +123,9 @@ template <int D, int G>
 __global__ void __launch_bounds__(kThreads, (G <= 4 ? 6 : 3)) decode_split_kernel(const DecodeArgs a) {
     using Gm = Geo<D>;
     constexpr int SL = Gm::SL, RPS = Gm::RPS, LPR = Gm::LPR, RPW = Gm::RPW;
-    const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
+    // KV heads vary fastest across the grid, so the CTAs reading the parts of the same cache rows run together
+    // and DRAM sees whole rows streamed in order.
+    const int split = blockIdx.x / a.n_kv_heads, kvh = blockIdx.x - split * a.n_kv_heads, seq = blockIdx.y;
     const int L = ctx_len_of(a, seq);
     const int row0 = split * SL;
     if (row0 >= L) return;  // uniform for the whole CTA
@@ -348,7 +350,7 @@ cudaError_t launch_split(const DecodeArgs& a, int n_seqs, cudaStream_t s) {
     // K and V tiles (2 * SL * D halves; the reduction buffer RPS*G*D floats fits inside them), scores, (m, l)
     const size_t smem = sizeof(__half) * 2 * Gm::SL * D + sizeof(float) * (G * Gm::SL + 2 * G);
     static_assert(Gm::RPS * G * D * sizeof(float) <= sizeof(__half) * 2 * Gm::SL * D, "reduction buffer too big");
-    dim3 grid(a.max_splits, a.n_kv_heads, n_seqs);
+    dim3 grid(a.max_splits * a.n_kv_heads, n_seqs, 1);
     decode_split_kernel<D, G><<<grid, kThreads, smem, s>>>(a);
     return cudaGetLastError();
 }

@@ -364,6 +364,121 @@ def run_ours(args):
         pg.destroy_process_group()
 
 
+def run_cfg5(args):
+    """Config 5: SmolLM2-1.7B shape (32/32 heads, d=64) ragged mixed batch — 256 prefill sequences with lengths
+    log-uniform in [128, 8192] and 512 one-token decode sequences over f16 caches of 1..8192 rows — whole sequences
+    packed over the ranks longest-processing-time first. Per rank one step = one prefill call per sequence (spread
+    over 4 streams) + one ragged decode call, captured in a CUDA graph and replayed."""
+    import numpy as np
+    import torch
+
+    import alpaca_b200 as ab
+    from alpaca_b200 import Kernel
+    from alpaca_b200.partition import Unit, partition
+    rank, world, local, pg = dist_setup(args.gpus)
+    ab.load()
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream()
+    pk = peaks()
+    NH = NKV = 32
+    rng = np.random.default_rng(20260105)
+    pre_T = np.round(np.exp(rng.uniform(np.log(128), np.log(8192), 256))).astype(int)
+    dec_L = rng.integers(1, 8192 + 1, 512)
+    units = [Unit(i, 0, int(t), 0, NH) for i, t in enumerate(pre_T)] + \
+            [Unit(256 + i, 0, 1, int(l) - 1, NH) for i, l in enumerate(dec_L)]
+    plan = partition(units, world, tflops=pk["tflops"] * 0.4, hbm_gbs=pk["hbm_gbs"] * 0.6)
+    mine = plan.ranks[rank]
+    my_pre = [int(pre_T[u.seq]) for u in mine if u.seq < 256]
+    my_dec = [int(dec_L[u.seq - 256]) for u in mine if u.seq >= 256]
+    g = torch.Generator(device=dev)
+    g.manual_seed(20260105 + 1000 * rank)
+    # prefill: each sequence in its own buffers
+    pre = []
+    for T in my_pre:
+        q = torch.randn((T, NH, D), generator=g, device=dev).half()
+        k = torch.randn((T, NKV, D), generator=g, device=dev).half()
+        v = torch.randn((T, NKV, D), generator=g, device=dev).half()
+        o = torch.empty((T, NH, D), dtype=torch.float32, device=dev)
+        pre.append((q, k, v, o, ab.make_desc(q, k, v, o)))
+    # decode: one ragged batch
+    nd = len(my_dec)
+    cap = max(my_dec) if nd else 1
+    dq = torch.randn((max(nd, 1), 1, NH, D), generator=g, device=dev)
+    dk = torch.randn((max(nd, 1), cap, NKV, D), generator=g, device=dev).half()
+    dv = torch.randn((max(nd, 1), cap, NKV, D), generator=g, device=dev).half()
+    do = torch.empty((max(nd, 1), 1, NH, D), dtype=torch.float32, device=dev)
+    lens = torch.tensor(my_dec if nd else [1], dtype=torch.int32, device=dev)
+    ddesc = ab.make_desc(dq, dk, dv, do, ctx_lens=lens, max_ctx_len=cap)
+    ws = torch.empty(max(16, ab.workspace_bytes(ddesc, Kernel.DECODE_SPLIT)), dtype=torch.uint8, device=dev)
+    streams = [torch.cuda.Stream(device=dev) for _ in range(4)]
+
+    def step():
+        cur = torch.cuda.current_stream()
+        ev = torch.cuda.Event()
+        ev.record(cur)
+        order = sorted(range(len(pre)), key=lambda i: -my_pre[i])  # longest first across the streams
+        for n, i in enumerate(order):
+            st = streams[n % len(streams)]
+            st.wait_event(ev)
+            ab.launch(pre[i][4], Kernel.PREFILL_TC, None, st)
+        if nd:
+            ab.launch(ddesc, Kernel.DECODE_SPLIT, ws, cur)
+        for st in streams:
+            done = torch.cuda.Event()
+            done.record(st)
+            cur.wait_event(done)
+
+    side = torch.cuda.Stream(device=dev)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        step()
+    stream.wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(args.warmup):
+        graph.replay()
+    ab.device_status()
+    clocks = ClockSampler(local)
+    clocks.start()
+    barrier(pg)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        graph.replay()
+    e1.record(stream)
+    barrier(pg)
+    clk = clocks.stop()
+    ab.device_status()
+    ms = e0.elapsed_time(e1) / args.steps
+    ms_max = max_over_ranks(ms, pg)
+    del graph
+    job_flops = float(sum(flops_prefill(int(t), NH) for t in pre_T))
+    job_kv_bytes = float(sum(int(l) * NKV * D * 4 for l in dec_L))
+    tokens = float(pre_T.sum() + len(dec_L))
+    if pg is not None:
+        pg.barrier()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": tokens / (ms_max * 1e-3), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic N(0,1) (torch.randn seeded per rank), lengths seeded",
+            "config": {"workload": "config 5: SmolLM2-1.7B shape (32/32 heads, d=64) ragged mixed batch: 256 prefill "
+                                   "sequences, lengths log-uniform [128, 8192], + 512 decode sequences, contexts "
+                                   "U[1, 8192]; whole sequences LPT-packed over the GPUs",
+                       "prefill_tokens": int(pre_T.sum()), "decode_tokens": len(dec_L),
+                       "parallelism": f"sequence-sharded x{world}", "plan_imbalance": plan.imbalance},
+            "prefill_tflops_if_alone": job_flops / (ms_max * 1e-3) / 1e12,
+            "decode_kv_gbs_if_alone": job_kv_bytes / (ms_max * 1e-3) / 1e9,
+            "gpu_launches": args.steps * (len(pre) + (2 if nd else 0)),
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        pg.destroy_process_group()
+
+
 def run_decode(args, ab, torch, dev, stream, rank, world, pg, pk):
     from alpaca_b200 import Kernel
     g = torch.Generator(device=dev)
@@ -466,8 +581,9 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["cfg2", "cfg4"], default="cfg2",
-                    help="cfg2 (default headline, weak scaling) or cfg4 (8 x 4096 at 15/5 heads, strong scaling)")
+    ap.add_argument("--workload", choices=["cfg2", "cfg4", "cfg5"], default="cfg2",
+                    help="cfg2 (default headline, weak scaling), cfg4 (8 x 4096 at 15/5 heads, strong scaling) or "
+                         "cfg5 (ragged mixed prefill + decode batch at 32/32 heads, strong scaling)")
     ap.add_argument("--tokens", type=int, default=T_PREFILL)
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
@@ -482,6 +598,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "cfg5":
+        run_cfg5(args)
     else:
         run_ours(args)
 
