@@ -59,14 +59,6 @@ __device__ __forceinline__ int ctx_len_of(const DecodeArgs& a, int s) {
     return a.ctx_lens ? a.ctx_lens[s] : a.uniform_len;
 }
 
-__device__ __forceinline__ uint4 ld_stream(const __half* p) {
-    uint4 r;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-                 : "l"(p));
-    return r;
-}
-
 __device__ __forceinline__ void half8_to_float(const uint4& u, float* f) {
     const __half2* h = reinterpret_cast<const __half2*>(&u);
 #pragma unroll
@@ -119,32 +111,12 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-template <int D, int G>
-__global__ void __launch_bounds__(kThreads, (G <= 4 ? 6 : 3)) decode_split_kernel(const DecodeArgs a) {
-    using Gm = Geo<D>;
-    constexpr int SL = Gm::SL, RPS = Gm::RPS, LPR = Gm::LPR, RPW = Gm::RPW;
-    // KV heads vary fastest across the grid, so the CTAs reading the parts of the same cache rows run together
-    // and DRAM sees whole rows streamed in order.
-    const int split = blockIdx.x / a.n_kv_heads, kvh = blockIdx.x - split * a.n_kv_heads, seq = blockIdx.y;
-    const int L = ctx_len_of(a, seq);
-    const int row0 = split * SL;
-    if (row0 >= L) return;  // uniform for the whole CTA
-    const int row_end = min(L, row0 + SL);
-    const int nsplits = (L + SL - 1) / SL;
-
-    extern __shared__ __align__(16) uint8_t smem_b[];
-    __half* s_k = reinterpret_cast<__half*>(smem_b);          // [SL][D] this split's K rows
-    __half* s_v = s_k + SL * D;                               // [SL][D] V rows
-    float* s_red = reinterpret_cast<float*>(smem_b);          // [RPS][G][D] partial accumulators (reuses K|V)
-    float* s_p = reinterpret_cast<float*>(s_v + SL * D);      // [G][SL] scores, then probabilities
-    float* s_ml = s_p + G * SL;                               // [G][2] split max (log2 units), denominator
-
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int lr = lane % LPR;              // this lane's 8 dims: [lr*8, lr*8 + 8)
-    const int rowlane = warp * RPW + lane / LPR;
-
-    // 1. Stage this split's K rows, then its V rows, into shared memory with async copies (rows past the
-    //    context are zero-filled, never read). Each thread later reads back only the chunks it copied.
+// Issue the async copies of one unit's K rows (one commit group) and V rows (a second group) into shared memory.
+// Rows past the context are zero-filled and never read. Each thread later reads back only the chunks it copied.
+template <int D>
+__device__ __forceinline__ void stage_unit(const DecodeArgs& a, int seq, int kvh, int row0, int row_end,
+                                           __half* s_k, __half* s_v, int lr, int rowlane) {
+    constexpr int RPS = Geo<D>::RPS;
     const int64_t seq_off = static_cast<int64_t>(seq) * a.kv_seq_stride + static_cast<int64_t>(kvh) * D + lr * 8;
 #pragma unroll
     for (int i = 0; i < kSlots; i++) {
@@ -160,8 +132,20 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 6 : 3)) decode_split_kerne
         cp_async16(s_v + rl * D + lr * 8, a.v + seq_off + (in ? static_cast<int64_t>(r) * a.kv_row_stride : 0), in ? 16u : 0u);
     }
     cp_async_commit();
+}
 
-    // 2. Queries of the G heads (this lane's 8 dims), pre-scaled into log2 units.
+// One unit = SL cache rows of one KV head of one sequence, for its G query heads. kAfter = commit groups issued
+// after this unit's two (the next unit's prefetch), so the waits below release exactly this unit's K, then V.
+// s_red reuses this unit's K|V buffers after the last read of them.
+template <int D, int G, int kAfter>
+__device__ __forceinline__ void compute_unit(const DecodeArgs& a, int seq, int kvh, int split, int row0, int row_end,
+                                             int nsplits, const __half* s_k, const __half* s_v, float* s_p,
+                                             float* s_ml, int tid, int warp, int lane, int lr, int rowlane) {
+    using Gm = Geo<D>;
+    constexpr int SL = Gm::SL, RPS = Gm::RPS, LPR = Gm::LPR;
+    float* s_red = reinterpret_cast<float*>(const_cast<__half*>(s_k));  // [RPS][G][D] (K|V are contiguous)
+
+    // Queries of the G heads (this lane's 8 dims), pre-scaled into log2 units.
     float qv[G][8];
 #pragma unroll
     for (int g = 0; g < G; g++) {
@@ -179,8 +163,8 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 6 : 3)) decode_split_kerne
         for (int e = 0; e < 8; e++) qv[g][e] *= a.scale_log2;
     }
 
-    // 3. Scores: partial dots, then the transposing row reduction; one lane per (row, head) stores it.
-    cp_async_wait<1>();  // this thread's K chunks have landed
+    // Scores: partial dots, then the transposing row reduction; one lane per (row, head) stores it.
+    cp_async_wait<kAfter + 1>();  // this thread's K chunks have landed
     float part[G][kSlots];
 #pragma unroll
     for (int i = 0; i < kSlots; i++) {
@@ -208,7 +192,7 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 6 : 3)) decode_split_kerne
     }
     __syncthreads();
 
-    // 4. Softmax statistics per head over this split (one warp per head).
+    // Softmax statistics per head over this unit (one warp per head).
     for (int g = warp; g < G; g += kThreads / 32) {
         float mx = -INFINITY;
         for (int r = lane; r < SL; r += 32) mx = fmaxf(mx, s_p[g * SL + r]);
@@ -227,10 +211,10 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 6 : 3)) decode_split_kerne
             s_ml[2 * g + 1] = sum;
         }
     }
-    cp_async_wait<0>();  // this thread's V chunks have landed
+    cp_async_wait<kAfter>();  // this thread's V chunks have landed
     __syncthreads();
 
-    // 5. P·V over this thread's rows and dims.
+    // P·V over this thread's rows and dims.
     float2 acc2[G][4];
 #pragma unroll
     for (int g = 0; g < G; g++)
@@ -249,26 +233,16 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 6 : 3)) decode_split_kerne
             for (int e = 0; e < 4; e++) acc2[g][e] = __ffma2_rn(p2, make_float2(vf[2 * e], vf[2 * e + 1]), acc2[g][e]);
         }
     }
-    float acc[G][8];
-#pragma unroll
-    for (int g = 0; g < G; g++)
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-            acc[g][2 * e] = acc2[g][e].x;
-            acc[g][2 * e + 1] = acc2[g][e].y;
-        }
     __syncthreads();  // every thread is done with K|V: the reduction buffer reuses them
 #pragma unroll
     for (int g = 0; g < G; g++) {
         float4* dst = reinterpret_cast<float4*>(s_red + (rowlane * G + g) * D + lr * 8);
-        dst[0] = make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
-        dst[1] = make_float4(acc[g][4], acc[g][5], acc[g][6], acc[g][7]);
+        dst[0] = make_float4(acc2[g][0].x, acc2[g][0].y, acc2[g][1].x, acc2[g][1].y);
+        dst[1] = make_float4(acc2[g][2].x, acc2[g][2].y, acc2[g][3].x, acc2[g][3].y);
     }
     __syncthreads();
-    // The combine kernel may start launching now; it waits for this grid's memory before reading.
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
-    // 6. Reduce across row lanes; finish single-split sequences, else store the partial state.
+    // Reduce across row lanes; finish single-split sequences, else store the partial state.
     const int64_t part_base =
         ((static_cast<int64_t>(seq) * a.n_kv_heads + kvh) * a.max_splits + split) * G;
     for (int o = tid; o < G * D; o += kThreads) {
@@ -290,6 +264,34 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 6 : 3)) decode_split_kerne
             }
         }
     }
+}
+
+// One CTA per (KV head x split, sequence) grid cell; CTAs past a sequence's context exit at once.
+template <int D, int G>
+__global__ void __launch_bounds__(kThreads, (G <= 4 ? 6 : 3)) decode_split_kernel(const DecodeArgs a) {
+    using Gm = Geo<D>;
+    constexpr int SL = Gm::SL, LPR = Gm::LPR, RPW = Gm::RPW;
+    // KV heads vary fastest across the grid, so the CTAs reading the parts of the same cache rows run together
+    // and DRAM sees whole rows streamed in order.
+    const int split = blockIdx.x / a.n_kv_heads, kvh = blockIdx.x - split * a.n_kv_heads, seq = blockIdx.y;
+    const int L = ctx_len_of(a, seq);
+    const int row0 = split * SL;
+    if (row0 >= L) return;  // uniform for the whole CTA
+    const int row_end = min(L, row0 + SL);
+    const int nsplits = (L + SL - 1) / SL;
+
+    extern __shared__ __align__(16) uint8_t smem_b[];
+    __half* s_k = reinterpret_cast<__half*>(smem_b);       // [SL][D] this unit's K rows
+    __half* s_v = s_k + SL * D;                            // [SL][D] V rows
+    float* s_p = reinterpret_cast<float*>(s_v + SL * D);   // [G][SL] scores, then probabilities
+    float* s_ml = s_p + G * SL;                            // [G][2] unit max (log2 units), denominator
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int lr = lane % LPR, rowlane = warp * RPW + lane / LPR;
+    stage_unit<D>(a, seq, kvh, row0, row_end, s_k, s_v, lr, rowlane);
+    compute_unit<D, G, 0>(a, seq, kvh, split, row0, row_end, nsplits, s_k, s_v, s_p, s_ml, tid, warp, lane, lr, rowlane);
+    // The combine kernel may start launching now; it waits for this grid's memory before reading.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 constexpr int kCombineThreads = 256;
@@ -347,9 +349,9 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const D
 template <int D, int G>
 cudaError_t launch_split(const DecodeArgs& a, int n_seqs, cudaStream_t s) {
     using Gm = Geo<D>;
+    static_assert(Gm::RPS * G * D * sizeof(float) <= sizeof(__half) * 2 * Gm::SL * D, "reduction buffer too big");
     // K and V tiles (2 * SL * D halves; the reduction buffer RPS*G*D floats fits inside them), scores, (m, l)
     const size_t smem = sizeof(__half) * 2 * Gm::SL * D + sizeof(float) * (G * Gm::SL + 2 * G);
-    static_assert(Gm::RPS * G * D * sizeof(float) <= sizeof(__half) * 2 * Gm::SL * D, "reduction buffer too big");
     dim3 grid(a.max_splits * a.n_kv_heads, n_seqs, 1);
     decode_split_kernel<D, G><<<grid, kThreads, smem, s>>>(a);
     return cudaGetLastError();

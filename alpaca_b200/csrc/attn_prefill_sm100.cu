@@ -530,12 +530,9 @@ size_t prefill_workspace_bytes(const alpaca_attn_desc& d) {
 cudaError_t launch_prefill(const Call& c, cudaStream_t s) {
     const alpaca_attn_desc& d = *c.d;
     const PrefillFn fn = prefill_variant(prefill_emu_pairs());
-    static std::once_flag attr_once;
-    static cudaError_t attr_err = cudaSuccess;
-    std::call_once(attr_once, [fn] {
-        attr_err = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        static_cast<int>(kSmemBytes));
-    });
+    // per-device function attribute (host-side, cheap next to the launch itself)
+    cudaError_t attr_err = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
     if (attr_err != cudaSuccess) return attr_err;
 
     const void* qh = d.q;
