@@ -15,11 +15,14 @@
 //     P never touches shared memory and the tensor core's shared-memory reads stay within bandwidth. Each issuer
 //     queues S(j+1) before PV(j), so the next S block is ready when the softmax finishes the current one;
 //   * warps 4-11 and 12-19: softmax for tile A and B, two threads per query row (one per 64-column half of the
-//     128-column S block; the two partial row maxima meet through shared memory and a 64-arrival mbarrier per
-//     pair of warps that share TMEM lanes). They read S from TMEM, mask diagonal blocks, keep the running max in
-//     log2 units (it only moves when it grows by more than 8, so O rarely needs rescaling), compute
-//     P = 2^(s*c - m) — most exponentials on MUFU, a fixed share on the FMA pipe with a polynomial — sum the row
-//     in f32, store P to TMEM as f16 pairs and finish each tile with O / l.
+//     128-column S block). They read S from TMEM, mask diagonal blocks and keep the running max in log2 units
+//     (it only moves when it grows by more than 8, so O rarely needs rescaling). Each half computes its P
+//     against its own candidate max and only then reads the other half's candidate (shared memory, a
+//     two-arrival mbarrier per pair of warps that share TMEM lanes), so the exchange is off the critical path;
+//     the half with the lower candidate scales its f16 P pairs down. P = 2^(s*c - m) — most exponentials on
+//     MUFU, a fixed share on the FMA pipe with a polynomial — is summed per row in f32, stored to TMEM as f16
+//     pairs, and each tile ends with O / l;
+//   * registers: the control warpgroup drops to 56 per thread (setmaxnreg) so the softmax warps get 104.
 //   TMEM: S_A 0-127, S_B 128-255, O_A 256-319, O_B 320-383, P_A 384-447, P_B 448-511 (all 512 columns).
 //
 // Every mbarrier wait is bounded (2 s; 2 ms under ALPACA_ATTN_FLAG_DEBUG_FORCE_TIMEOUT). On a timeout the CTA
@@ -43,6 +46,10 @@ constexpr int kThreads = 640;   // 20 warps: TMA, MMA A, MMA B (+ TMEM allocator
 constexpr int kTmemCols = 512;
 constexpr uint32_t kTileBytes = kBM * kD * 2;  // 16 KB: one Q, K or V tile
 constexpr float kRescaleThreshold = 8.0f;      // log2 units
+// Register split after the role dispatch (setmaxnreg): the control warpgroup (warps 0-3) gives registers to
+// the four softmax warpgroups (128 * 56 + 512 * 104 of the 640 x 96 registers the CTA is launched with).
+constexpr uint32_t kRegsControl = 56, kRegsSoftmax = 104;
+static_assert(128 * kRegsControl + 512 * kRegsSoftmax <= kThreads * 96, "register split exceeds the launch budget");
 constexpr float kLog2e = 1.4426950408889634f;
 
 // TMEM column map
@@ -69,7 +76,7 @@ struct SmemLayout {
     uint64_t k_full[kStages], k_empty[kStages], v_full[kStages], v_empty[kStages];
     uint64_t s_full[2], s_empty[2], p_full[2], o_done[2];
     uint64_t xbar[2][4];       // per (tile, lane quarter): the two half-row warps exchange partial row state
-    uint64_t dbg, fin[2];
+    uint64_t dbg, fin[2], retire;
     float xmax[2][2][2][kBM];  // [tile][exchange parity][half][row] partial row maxima
     float xl[2][2][kBM];       // [tile][half][row] partial row sums (epilogue)
     uint32_t tmem_base;
@@ -153,7 +160,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&sm->s_empty[i], 8);  // one arrival per softmax warp of the tile
             mbar_init(&sm->p_full[i], 8);
             mbar_init(&sm->o_done[i], 1);
-            for (int qq = 0; qq < 4; qq++) mbar_init(&sm->xbar[i][qq], 64);
+            for (int qq = 0; qq < 4; qq++) mbar_init(&sm->xbar[i][qq], 2);  // one arrival per warp of the pair
             mbar_init(&sm->fin[i], 1);
         }
         for (int i = 0; i < kStages; i++) {
@@ -163,6 +170,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&sm->v_empty[i], 2);
         }
         mbar_init(&sm->dbg, 1);
+        mbar_init(&sm->retire, 18);  // 16 softmax warps, the producer and tile A's issuer
         fence_barrier_init();
         tma_prefetch_desc(&tm_q);
         tma_prefetch_desc(&tm_k);
@@ -176,8 +184,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = sm->tmem_base;
-
-    if (warp == 0 && lane == 0) {
+    if (warp == 0) {
+        setmaxnreg_dec<kRegsControl>();
+        if (lane != 0) return;
         // ------------------------------------------------------------------ TMA producer
         uint32_t kv_it = 0, k_issued = 0, v_issued = 0, q_uses[2] = {0, 0};
         bool ok = true;
@@ -219,73 +228,90 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int t = 0; t < 2; t++)
                 if (q_uses[t] > 0) mbar_wait(&sm->q_full[t], (q_uses[t] - 1) & 1, drain);
         }
-    } else if ((warp == 1 || warp == 2) && lane == 0) {
-        // ------------------------------------------------------------------ MMA issuers, one thread per tile
-        // Both threads walk every KV block of every item: a tile with fewer blocks than its partner still
-        // releases the K/V stages it does not use (after they land), so each stage's empty barrier (count 2)
-        // completes once per use.
-        const int t = warp - 1;
-        uint32_t kv_it = 0, q_uses = 0, s_uses = 0, p_uses = 0;
-        bool ok = true;
-        if (debug_timeout && t == 0) ok = mbar_wait(&sm->dbg, 0, ab);  // nothing arrives: exercises the give-up path
-        for (int it = blockIdx.x; ok && it < a.total_items; it += gridDim.x) {
-            const Item x = decode_item(a, it);
-            const int n = x.nblk[t];
-            const int nmax = max(x.nblk[0], x.nblk[1]);
-            if (n > 0) {
-                ok = mbar_wait(&sm->q_full[t], q_uses & 1, ab);
+        mbar_arrive(&sm->retire);
+    } else if (warp == 1 || warp == 2) {
+        setmaxnreg_dec<kRegsControl>();
+        if (lane == 0) {
+            // ------------------------------------------------------------------ MMA issuers, one thread per tile
+            // Both threads walk every KV block of every item: a tile with fewer blocks than its partner still
+            // releases the K/V stages it does not use (after they land), so each stage's empty barrier (count 2)
+            // completes once per use.
+            const int t = warp - 1;
+            uint32_t kv_it = 0, q_uses = 0, s_uses = 0, p_uses = 0;
+            bool ok = true;
+            if (debug_timeout && t == 0) ok = mbar_wait(&sm->dbg, 0, ab);  // nothing arrives: exercises the give-up path
+            for (int it = blockIdx.x; ok && it < a.total_items; it += gridDim.x) {
+                const Item x = decode_item(a, it);
+                const int n = x.nblk[t];
+                const int nmax = max(x.nblk[0], x.nblk[1]);
+                if (n > 0) {
+                    ok = mbar_wait(&sm->q_full[t], q_uses & 1, ab);
+                    if (!ok) break;
+                }
+                // Iteration j consumes K(j) (S of block j) and then V(j-1) (P·V of block j-1): the producer's load
+                // order, so every wait here depends only on releases made kStages iterations earlier.
+                for (int j = 0; ok && j <= nmax; j++) {
+                    if (j < nmax) {
+                        const uint32_t cur = kv_it + j;
+                        const int st = cur % kStages;
+                        ok = mbar_wait(&sm->k_full[st], (cur / kStages) & 1, ab);
+                        if (!ok) break;
+                        if (j < n) {
+                            ok = mbar_wait(&sm->s_empty[t], (s_uses & 1) ^ 1, ab);
+                            if (!ok) break;
+                            tc_fence_after();
+                            mma_s(sm, t, st, tmem_base);
+                            tc_commit(&sm->s_full[t]);
+                            s_uses++;
+                            if (j + 1 == n) tc_commit(&sm->q_empty[t]);
+                            tc_commit(&sm->k_empty[st]);
+                        } else {
+                            mbar_arrive(&sm->k_empty[st]);  // block this tile does not use
+                        }
+                    }
+                    if (j > 0) {
+                        const int b = j - 1;
+                        const uint32_t prv = kv_it + b;
+                        const int sp = prv % kStages;
+                        ok = mbar_wait(&sm->v_full[sp], (prv / kStages) & 1, ab);
+                        if (!ok) break;
+                        if (b < n) {
+                            ok = mbar_wait(&sm->p_full[t], p_uses & 1, ab);
+                            if (!ok) break;
+                            tc_fence_after();
+                            mma_pv(sm, t, sp, tmem_base, b > 0);
+                            tc_commit(&sm->o_done[t]);
+                            tc_commit(&sm->v_empty[sp]);
+                            p_uses++;
+                        } else {
+                            mbar_arrive(&sm->v_empty[sp]);
+                        }
+                    }
+                }
                 if (!ok) break;
+                kv_it += nmax;
+                if (n > 0) q_uses++;
             }
-            // Iteration j consumes K(j) (S of block j) and then V(j-1) (P·V of block j-1): the producer's load
-            // order, so every wait here depends only on releases made kStages iterations earlier.
-            for (int j = 0; ok && j <= nmax; j++) {
-                if (j < nmax) {
-                    const uint32_t cur = kv_it + j;
-                    const int st = cur % kStages;
-                    ok = mbar_wait(&sm->k_full[st], (cur / kStages) & 1, ab);
-                    if (!ok) break;
-                    if (j < n) {
-                        ok = mbar_wait(&sm->s_empty[t], (s_uses & 1) ^ 1, ab);
-                        if (!ok) break;
-                        tc_fence_after();
-                        mma_s(sm, t, st, tmem_base);
-                        tc_commit(&sm->s_full[t]);
-                        s_uses++;
-                        if (j + 1 == n) tc_commit(&sm->q_empty[t]);
-                        tc_commit(&sm->k_empty[st]);
-                    } else {
-                        mbar_arrive(&sm->k_empty[st]);  // block this tile does not use
-                    }
-                }
-                if (j > 0) {
-                    const int b = j - 1;
-                    const uint32_t prv = kv_it + b;
-                    const int sp = prv % kStages;
-                    ok = mbar_wait(&sm->v_full[sp], (prv / kStages) & 1, ab);
-                    if (!ok) break;
-                    if (b < n) {
-                        ok = mbar_wait(&sm->p_full[t], p_uses & 1, ab);
-                        if (!ok) break;
-                        tc_fence_after();
-                        mma_pv(sm, t, sp, tmem_base, b > 0);
-                        tc_commit(&sm->o_done[t]);
-                        tc_commit(&sm->v_empty[sp]);
-                        p_uses++;
-                    } else {
-                        mbar_arrive(&sm->v_empty[sp]);
-                    }
-                }
-            }
-            if (!ok) break;
-            kv_it += nmax;
-            if (n > 0) q_uses++;
+            // Retire every MMA this thread issued before TMEM is freed.
+            int dummy = 0;
+            AbortState drain{&dummy, a.err, kWaitLimitNs};
+            tc_commit(&sm->fin[t]);
+            mbar_wait(&sm->fin[t], 0, drain);
+            if (t == 0) mbar_arrive(&sm->retire);
         }
-        // Retire every MMA this thread issued before TMEM is freed.
-        int dummy = 0;
-        AbortState drain{&dummy, a.err, kWaitLimitNs};
-        tc_commit(&sm->fin[t]);
-        mbar_wait(&sm->fin[t], 0, drain);
-    } else if (warp >= 4) {
+        // Warp 2 frees TMEM once every role has retired (no block-wide barrier after the register split).
+        __syncwarp();
+        if (warp == 2) {
+            int dummy = 0;
+            AbortState drain{&dummy, a.err, 2 * kWaitLimitNs};
+            mbar_wait(&sm->retire, 0, drain);
+            tc_fence_after();
+            tmem_dealloc(tmem_base, kTmemCols);
+        }
+    } else if (warp == 3) {
+        setmaxnreg_dec<kRegsControl>();
+    } else {
+        setmaxnreg_inc<kRegsSoftmax>();
         // ------------------------------------------------------------------ softmax warps
         const int sw = warp - 4;
         const int tile = sw >> 3;                   // query tile A (0) or B (1)
@@ -337,29 +363,22 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int i = 0; i < 8; i++) mv[i] = fmaxf(mv[i], s[56 + i]);
                 const float pmax = fmaxf(fmax3(mv[0], mv[1], mv[2]), fmax3(fmax3(mv[3], mv[4], mv[5]), mv[6], mv[7]));
-                // exchange with the warp holding the other half of these rows
+                // This half's candidate max (log2 units): the running max unless these columns exceed it by more
+                // than the threshold. The two halves publish their candidates and compute P against their own
+                // without waiting; the row max is the larger candidate, and a half whose candidate was lower
+                // scales its P pairs down afterwards (rare: first block of a tile, or a max that jumped).
+                const float pms = pmax * a.scale_log2;
+                const float m_mine = (j == 0 || pms > m_used + kRescaleThreshold) ? pms : m_used;
                 const int par = x_uses & 1;
-                sm->xmax[tile][par][half][row] = pmax;
-                mbar_arrive(xbar);
-                ok = __all_sync(0xffffffffu, mbar_wait(xbar, par, ab));
-                if (!ok) break;
-                x_uses++;
-                const float mx = fmaxf(pmax, sm->xmax[tile][par][half ^ 1][row]);
-                const float mxs = mx * a.scale_log2;
-                bool rescale = false;
-                float alpha = 1.f;
-                if (j == 0) {
-                    m_used = (mxs == -INFINITY) ? 0.f : mxs;
-                } else if (mxs > m_used + kRescaleThreshold) {
-                    alpha = ex2_approx(m_used - mxs);
-                    m_used = mxs;
-                    rescale = true;
-                    lsum.x *= alpha;
-                    lsum.y *= alpha;
-                }
+                sm->xmax[tile][par][half][row] = m_mine;
+                __threadfence_block();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(xbar);
                 // P = 2^(s*c - m) per column pair: kEmuPairs of every 8 pairs on the FMA pipe, the rest on MUFU;
-                // the f32 values feed the row sum, the f16 pairs the P·V MMA
-                const float2 c2 = make_float2(a.scale_log2, a.scale_log2), nm2 = make_float2(-m_used, -m_used);
+                // the f32 values feed the row sum, the f16 pairs the P·V MMA. A fully masked half (m_mine = -inf)
+                // subtracts 0 instead, giving P = 0.
+                const float m_sub = (m_mine == -INFINITY) ? 0.f : m_mine;
+                const float2 c2 = make_float2(a.scale_log2, a.scale_log2), nm2 = make_float2(-m_sub, -m_sub);
                 uint32_t pk[32];
                 float2 ls[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                                 make_float2(0.f, 0.f)};  // four independent partial sums (no serial chain)
@@ -372,7 +391,35 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ls[pr & 3] = __fadd2_rn(ls[pr & 3], e);
                     pk[pr] = pack_half2(e.x, e.y);
                 }
-                lsum = __fadd2_rn(lsum, __fadd2_rn(__fadd2_rn(ls[0], ls[1]), __fadd2_rn(ls[2], ls[3])));
+                float2 lb = __fadd2_rn(__fadd2_rn(ls[0], ls[1]), __fadd2_rn(ls[2], ls[3]));
+                // the partner's candidate (published before its exponentials, so normally already there)
+                ok = __all_sync(0xffffffffu, mbar_wait(xbar, par, ab));
+                if (!ok) break;
+                x_uses++;
+                const float m_row = fmaxf(m_mine, sm->xmax[tile][par][half ^ 1][row]);
+                if (__any_sync(0xffffffffu, m_mine < m_row)) {
+                    // f16 factor, applied identically to the P pairs and to this half's row sum
+                    const __half2 f2 = __float2half2_rn(ex2_approx(m_mine - m_row));  // 1 where m_mine == m_row
+                    const float f = __low2float(f2);
+#pragma unroll
+                    for (int pr = 0; pr < 32; pr++) {
+                        __half2 h = *reinterpret_cast<__half2*>(&pk[pr]);
+                        h = __hmul2(h, f2);
+                        pk[pr] = *reinterpret_cast<uint32_t*>(&h);
+                    }
+                    lb.x *= f;
+                    lb.y *= f;
+                }
+                bool rescale = false;
+                float alpha = 1.f;
+                if (j > 0 && m_row > m_used) {
+                    alpha = ex2_approx(m_used - m_row);
+                    rescale = true;
+                    lsum.x *= alpha;
+                    lsum.y *= alpha;
+                }
+                m_used = m_row;
+                lsum = __fadd2_rn(lsum, lb);
                 if (j > 0) {  // PV(j-1) must be done before P is overwritten or O is rescaled
                     ok = __all_sync(0xffffffffu, mbar_wait(&sm->o_done[tile], o_uses & 1, ab));
                     if (!ok) break;
@@ -405,7 +452,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_ld32(o_addr, o);
             const float lpart = lsum.x + lsum.y;
             sm->xl[tile][half][row] = lpart;
-            mbar_arrive(xbar);
+            __threadfence_block();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(xbar);
             tmem_wait_ld();
             tc_fence_before();
             ok = __all_sync(0xffffffffu, mbar_wait(xbar, x_uses & 1, ab));
@@ -433,13 +482,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm->retire);
     }
 
-    __syncthreads();
-    if (warp == 2) {
-        tc_fence_after();
-        tmem_dealloc(tmem_base, kTmemCols);
-    }
 }
 
 // f32 -> f16 copy of Q into the workspace ([seq][token][head][d], dense), for f32 callers.
