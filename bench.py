@@ -281,35 +281,69 @@ def run_ours(args):
         torch.cuda.synchronize()
         gather_ms = (time.perf_counter() - t0) * 1e3
 
-    # ---- e2e: host buffers (pinned), H2D of the step's inputs + kernel + D2H of the output, every step
+    # ---- e2e: host buffers (pinned), H2D of the step's inputs + kernel + D2H of the output, every step.
+    # The step is pipelined over chunks of sequences (layers): chunk i's H2D (copy-in stream), ABI call (compute
+    # stream) and D2H (copy-out stream) overlap the neighbouring chunks' work, as a caller streaming layers would.
+    # Events order each chunk's copy -> compute -> copy, and guard device-buffer reuse by the next step.
     e2e = None
     if not args.no_e2e:
         hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
         hout = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
         h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv))
         d2h = hout.numel() * hout.element_size()
+        n_units = q.shape[0]
+        chunk = max(1, min(n_units, args.e2e_chunk if args.e2e_chunk > 0 else -(-n_units // 6)))
+        bounds = [(c0, min(n_units, c0 + chunk)) for c0 in range(0, n_units, chunk)]
+        descs = [ab.make_desc(q[a:b], k[a:b], v[a:b], out[a:b], start_position=0) for a, b in bounds]
+        s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        ev_in = [torch.cuda.Event() for _ in bounds]
+        ev_comp = [torch.cuda.Event() for _ in bounds]
+        ev_out = [torch.cuda.Event() for _ in bounds]
+        started = [False]
 
         def e2e_step():
-            q.copy_(hq, non_blocking=True)
-            k.copy_(hk, non_blocking=True)
-            v.copy_(hv, non_blocking=True)
-            ab.launch(desc, Kernel.PREFILL_TC, None, stream)
-            hout.copy_(out, non_blocking=True)
+            for i, ((a, b), dsc) in enumerate(zip(bounds, descs)):
+                with torch.cuda.stream(s_in):
+                    if started[0]:
+                        s_in.wait_event(ev_comp[i])  # previous step's kernel has read these inputs
+                    q[a:b].copy_(hq[a:b], non_blocking=True)
+                    k[a:b].copy_(hk[a:b], non_blocking=True)
+                    v[a:b].copy_(hv[a:b], non_blocking=True)
+                    ev_in[i].record(s_in)
+                stream.wait_event(ev_in[i])
+                if started[0]:
+                    stream.wait_event(ev_out[i])  # previous step's output chunk has been read back
+                ab.launch(dsc, Kernel.PREFILL_TC, None, stream)
+                ev_comp[i].record(stream)
+                with torch.cuda.stream(s_out):
+                    s_out.wait_event(ev_comp[i])
+                    hout[a:b].copy_(out[a:b], non_blocking=True)
+                    ev_out[i].record(s_out)
+            started[0] = True
 
         e2e_steps = max(3, min(args.steps, 10))
         for _ in range(2):
             e2e_step()
+        stream.wait_event(ev_out[-1])
+        torch.cuda.synchronize()
         barrier(pg)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
+        s_in.wait_stream(stream)
         for _ in range(e2e_steps):
             e2e_step()
+        stream.wait_event(ev_out[-1])
         e1.record(stream)
+        torch.cuda.synchronize()
         barrier(pg)
         e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps, pg)
+        # the last step's result must be the device result (checked on one chunk of rows)
+        e2e_ok = bool(torch.equal(hout[-1].to(dev), out[-1]))
         e2e = {"value": job_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
-               "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
-               "api": "alpaca_attention (C ABI via ctypes); pinned host Q/K/V in, f32 context out, every step"}
+               "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms, "chunks_per_step": len(bounds),
+               "readback_matches_device": e2e_ok,
+               "api": "alpaca_attention (C ABI via ctypes), one call per chunk of sequences; pinned host Q/K/V "
+                      "in, f32 context out, every step; copy-in / compute / copy-out on three streams"}
         del hq, hk, hv, hout
 
     # ---- decode (config 3)
@@ -588,6 +622,7 @@ def main():
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-chunk", type=int, default=0, help="sequences per ABI call in the e2e pipeline (0: 1/6 of them)")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--dec-layers", type=int, default=LAYERS)
     ap.add_argument("--layers", type=int, default=LAYERS)
