@@ -295,10 +295,21 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 6 : 3)) decode_split_kerne
 }
 
 constexpr int kCombineThreads = 256;
+constexpr int kCombineSmem = 48 * 1024;  // staging budget per CTA (no opt-in attribute needed)
 
-// One CTA per (KV head, sequence): the G heads' per-split weights 2^(m_s - M) are computed once into shared
-// memory (one warp per head), then every output column sums its accumulators over the splits with independent,
-// coalesced loads.
+// Splits staged per round of the combine: [chunk][G][d + 2] records + [chunk][G] weights in kCombineSmem.
+__host__ __device__ constexpr int combine_chunk(int G, int D) {
+    return (kCombineSmem / 4 - G) / (G * (D + 2) + G);
+}
+
+// 8-byte async copy global -> shared.
+__device__ __forceinline__ void cp_async8(void* smem_dst, const void* gsrc) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+
+// One CTA per (KV head, sequence): the global max per head, then the split states staged into shared memory a
+// chunk of splits at a time (every copy of a chunk in flight at once), weights 2^(m_s - M) once per (split, head),
+// and every output column summed over the staged splits.
 template <int D>
 __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const DecodeArgs a) {
     asm volatile("griddepcontrol.wait;" ::: "memory");  // split kernel's writes are visible after this
@@ -307,42 +318,60 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const D
     const int L = ctx_len_of(a, seq);
     const int nsp = (L + Geo<D>::SL - 1) / Geo<D>::SL;
     if (nsp <= 1) return;
-    extern __shared__ float cs[];
-    float* w = cs;                // [nsp][G] weights
-    float* inv_den = cs + nsp * G; // [G]
-    const int64_t stride = static_cast<int64_t>(G) * (D + 2);  // between splits
-    const float* base = a.partial + (static_cast<int64_t>(seq) * a.n_kv_heads + kvh) * a.max_splits * stride;
+    const int rec = G * (D + 2);                 // floats per split
+    const int chunk = combine_chunk(G, D);
+    extern __shared__ __align__(16) float cs[];
+    float* s_rec = cs;                           // [chunk][G][D + 2]
+    float* s_w = cs + chunk * rec;               // [chunk][G]
+    float* s_max = s_w + chunk * G;              // [G]
+    const float* base = a.partial + (static_cast<int64_t>(seq) * a.n_kv_heads + kvh) * a.max_splits * rec;
     for (int g = warp; g < G; g += kCombineThreads / 32) {
         float M = -INFINITY;
-        for (int sp = lane; sp < nsp; sp += 32) M = fmaxf(M, base[sp * stride + g * (D + 2) + D]);
+        for (int sp = lane; sp < nsp; sp += 32) M = fmaxf(M, __ldcg(base + sp * rec + g * (D + 2) + D));
 #pragma unroll
         for (int o = 16; o >= 1; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-        float den = 0.f;
-        for (int sp = lane; sp < nsp; sp += 32) {
-            const float* pp = base + sp * stride + g * (D + 2);
-            const float f = ex2_approx(pp[D] - M);
-            w[sp * G + g] = f;
-            den = fmaf(pp[D + 1], f, den);
-        }
-#pragma unroll
-        for (int o = 16; o >= 1; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
-        if (lane == 0) inv_den[g] = 1.f / den;
+        if (lane == 0) s_max[g] = M;
     }
-    __syncthreads();
-    for (int o = tid; o < G * D; o += kCombineThreads) {
-        const int g = o / D, col = o - g * D;
-        const float* pp = base + g * (D + 2) + col;
-        float num0 = 0.f, num1 = 0.f;
-        int sp = 0;
-        for (; sp + 1 < nsp; sp += 2) {
-            num0 = fmaf(pp[sp * stride], w[sp * G + g], num0);
-            num1 = fmaf(pp[(sp + 1) * stride], w[(sp + 1) * G + g], num1);
+    constexpr int kMaxCols = (8 * D + kCombineThreads - 1) / kCombineThreads;  // G <= 8
+    float num[kMaxCols], den[kMaxCols];
+#pragma unroll
+    for (int c = 0; c < kMaxCols; c++) num[c] = den[c] = 0.f;
+    for (int c0 = 0; c0 < nsp; c0 += chunk) {
+        const int nc = min(chunk, nsp - c0);
+        const float* src = base + static_cast<int64_t>(c0) * rec;
+        for (int i = tid; i < nc * rec / 2; i += kCombineThreads) cp_async8(s_rec + 2 * i, src + 2 * i);
+        asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+        __syncthreads();  // staged records (and, first time round, s_max) visible
+        for (int i = tid; i < nc * G; i += kCombineThreads) {
+            const int sp = i / G, g = i - sp * G;
+            s_w[i] = ex2_approx(s_rec[sp * rec + g * (D + 2) + D] - s_max[g]);
         }
-        if (sp < nsp) num0 = fmaf(pp[sp * stride], w[sp * G + g], num0);
-        const float val = (num0 + num1) * inv_den[g];
-        const int64_t oo = static_cast<int64_t>(seq) * a.out_seq_stride + static_cast<int64_t>(kvh * G + g) * D + col;
-        if (a.out_f16) static_cast<__half*>(a.out)[oo] = __float2half_rn(val);
-        else static_cast<float*>(a.out)[oo] = val;
+        __syncthreads();
+#pragma unroll
+        for (int c = 0; c < kMaxCols; c++) {
+            const int o = tid + c * kCombineThreads;
+            if (o < G * D) {
+                const int g = o / D, col = o - g * D;
+                const float* r = s_rec + g * (D + 2);
+                for (int sp = 0; sp < nc; sp++) {
+                    const float w = s_w[sp * G + g];
+                    num[c] = fmaf(r[sp * rec + col], w, num[c]);
+                    den[c] = fmaf(r[sp * rec + D + 1], w, den[c]);
+                }
+            }
+        }
+        __syncthreads();  // chunk consumed before the next one is staged
+    }
+#pragma unroll
+    for (int c = 0; c < kMaxCols; c++) {
+        const int o = tid + c * kCombineThreads;
+        if (o < G * D) {
+            const int g = o / D, col = o - g * D;
+            const float val = num[c] / den[c];
+            const int64_t oo = static_cast<int64_t>(seq) * a.out_seq_stride + static_cast<int64_t>(kvh * G + g) * D + col;
+            if (a.out_f16) static_cast<__half*>(a.out)[oo] = __float2half_rn(val);
+            else static_cast<float*>(a.out)[oo] = val;
+        }
     }
 }
 
@@ -374,12 +403,8 @@ cudaError_t launch_d(const DecodeArgs& a, int n_seqs, cudaStream_t s) {
     if (e != cudaSuccess) return e;
     if (a.max_splits <= 1) return cudaSuccess;  // every sequence finished in the split kernel
     const int G = a.n_heads / a.n_kv_heads;
-    const size_t csmem = sizeof(float) * (static_cast<size_t>(a.max_splits) * G + G);
-    if (csmem > 48 * 1024) {
-        cudaError_t ae = cudaFuncSetAttribute(decode_combine_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              static_cast<int>(std::min<size_t>(csmem, 227 * 1024)));
-        if (ae != cudaSuccess) return ae;
-    }
+    const int chunk = combine_chunk(G, D);
+    const size_t csmem = sizeof(float) * (static_cast<size_t>(chunk) * (G * (D + 2) + G) + G);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.n_kv_heads, n_seqs, 1);
     cfg.blockDim = dim3(kCombineThreads, 1, 1);
