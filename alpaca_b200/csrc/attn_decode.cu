@@ -325,9 +325,16 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const D
     float* s_w = cs + chunk * rec;               // [chunk][G]
     float* s_max = s_w + chunk * G;              // [G]
     const float* base = a.partial + (static_cast<int64_t>(seq) * a.n_kv_heads + kvh) * a.max_splits * rec;
+    const bool one_chunk = nsp <= chunk;
+    if (one_chunk) {  // every split state staged in one round trip; the global max is then read from shared memory
+        for (int i = tid; i < nsp * rec / 2; i += kCombineThreads) cp_async8(s_rec + 2 * i, base + 2 * i);
+        asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+        __syncthreads();
+    }
     for (int g = warp; g < G; g += kCombineThreads / 32) {
         float M = -INFINITY;
-        for (int sp = lane; sp < nsp; sp += 32) M = fmaxf(M, __ldcg(base + sp * rec + g * (D + 2) + D));
+        for (int sp = lane; sp < nsp; sp += 32)
+            M = fmaxf(M, one_chunk ? s_rec[sp * rec + g * (D + 2) + D] : __ldcg(base + sp * rec + g * (D + 2) + D));
 #pragma unroll
         for (int o = 16; o >= 1; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
         if (lane == 0) s_max[g] = M;
@@ -338,9 +345,11 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const D
     for (int c = 0; c < kMaxCols; c++) num[c] = den[c] = 0.f;
     for (int c0 = 0; c0 < nsp; c0 += chunk) {
         const int nc = min(chunk, nsp - c0);
-        const float* src = base + static_cast<int64_t>(c0) * rec;
-        for (int i = tid; i < nc * rec / 2; i += kCombineThreads) cp_async8(s_rec + 2 * i, src + 2 * i);
-        asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+        if (!one_chunk) {
+            const float* src = base + static_cast<int64_t>(c0) * rec;
+            for (int i = tid; i < nc * rec / 2; i += kCombineThreads) cp_async8(s_rec + 2 * i, src + 2 * i);
+            asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+        }
         __syncthreads();  // staged records (and, first time round, s_max) visible
         for (int i = tid; i < nc * G; i += kCombineThreads) {
             const int sp = i / G, g = i - sp * G;
