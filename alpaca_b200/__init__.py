@@ -1,17 +1,18 @@
 """alpaca_b200 — B200-native (sm_100a) attention hot path for alpaca.swift.
 
-The product is the C-ABI library ``libalpaca_cuda.so`` (include/alpaca_cuda.h) with three CUDA paths:
-tcgen05 causal flash prefill, split-KV decode + combine, and a general fp32 SIMT kernel. This package holds its
+The product is the C-ABI library ``libalpaca_cuda.so`` (include/alpaca_cuda.h) with three attention paths —
+tcgen05 causal flash prefill, split-KV decode + combine, and a general fp32 SIMT kernel — plus the fused RoPE +
+KV-cache append that produces their input. This package holds its
 sources (``csrc/``), its in-tree build (``build``) and a Python host mirror of alpaca's attention interface
 (``ops``) used by the tests and the benchmark.
 """
 from ._lib import (EXPORTED_SYMBOLS, FLAG_DEBUG_FORCE_TIMEOUT, LIB_PATH, AlpacaCUDAError, AttnDesc, DType, Kernel,
-                   Status, load)
-from .ops import (KV_PADDING_ROWS, attention, attention_device, device_status, launch, make_desc, select_kernel,
-                  workspace_bytes)
+                   RopeDesc, Status, load)
+from .ops import (KV_PADDING_ROWS, attention, attention_device, device_status, launch, make_desc, make_rope_desc,
+                  rope, rope_kv_append, rope_launch, select_kernel, workspace_bytes)
 
 __all__ = [
     "EXPORTED_SYMBOLS", "FLAG_DEBUG_FORCE_TIMEOUT", "LIB_PATH", "AlpacaCUDAError", "AttnDesc", "DType", "Kernel",
     "Status", "load", "KV_PADDING_ROWS", "attention", "attention_device", "device_status", "launch", "make_desc",
-    "select_kernel", "workspace_bytes",
+    "select_kernel", "workspace_bytes", "RopeDesc", "make_rope_desc", "rope", "rope_kv_append", "rope_launch",
 ]

@@ -67,6 +67,35 @@ class AttnDesc(ctypes.Structure):
     ]
 
 
+class RopeDesc(ctypes.Structure):
+    """alpaca_rope_desc (include/alpaca_cuda.h)."""
+    _fields_ = [
+        ("n_seqs", ctypes.c_int32),
+        ("n_heads", ctypes.c_int32),
+        ("n_kv_heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("tokens", ctypes.c_int32),
+        ("start_position", ctypes.c_int32),
+        ("positions", ctypes.c_void_p),
+        ("theta", ctypes.c_float),
+        ("interleaved", ctypes.c_int32),
+        ("q_dtype", ctypes.c_int32),
+        ("cache_dtype", ctypes.c_int32),
+        ("q", ctypes.c_void_p),
+        ("q_token_stride", ctypes.c_int64),
+        ("q_seq_stride", ctypes.c_int64),
+        ("k", ctypes.c_void_p),
+        ("v", ctypes.c_void_p),
+        ("kv_token_stride", ctypes.c_int64),
+        ("kv_seq_stride", ctypes.c_int64),
+        ("k_cache", ctypes.c_void_p),
+        ("v_cache", ctypes.c_void_p),
+        ("cache_row_stride", ctypes.c_int64),
+        ("cache_seq_stride", ctypes.c_int64),
+        ("flags", ctypes.c_uint32),
+    ]
+
+
 EXPORTED_SYMBOLS = (
     "alpaca_attention",
     "alpaca_attn_prefill",
@@ -78,6 +107,7 @@ EXPORTED_SYMBOLS = (
     "alpaca_cuda_status_string",
     "alpaca_cuda_last_error",
     "alpaca_cuda_version",
+    "alpaca_rope_kv_append",
 )
 
 _lib: ctypes.CDLL | None = None
@@ -112,6 +142,8 @@ def load() -> ctypes.CDLL:
     L.alpaca_cuda_last_error.argtypes = []
     L.alpaca_cuda_version.restype = ctypes.c_int
     L.alpaca_cuda_version.argtypes = []
+    L.alpaca_rope_kv_append.restype = ctypes.c_int
+    L.alpaca_rope_kv_append.argtypes = [ctypes.POINTER(RopeDesc), ctypes.c_void_p]
     _lib = L
     return L
 

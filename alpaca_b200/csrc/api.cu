@@ -130,6 +130,50 @@ alpaca_cuda_status validate(const alpaca_attn_desc* dp) {
     return ok();
 }
 
+// RoPE + KV append checks (CPUOps.rope's guards, CPUOps.swift:188-191, plus what a raw-pointer ABI needs).
+alpaca_cuda_status validate_rope(const alpaca_rope_desc* dp) {
+    if (!dp) return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "rope: null descriptor");
+    const alpaca_rope_desc& d = *dp;
+    char sh[200];
+    std::snprintf(sh, sizeof(sh), "seqs=%d T=%d start=%d H=%d/%d d=%d", d.n_seqs, d.tokens, d.start_position,
+                  d.n_heads, d.n_kv_heads, d.head_dim);
+    if (d.n_seqs < 1 || d.n_seqs > 65535 || d.tokens < 1 || d.n_heads < 0 || d.n_kv_heads < 0 ||
+        d.n_heads + d.n_kv_heads < 1 || d.start_position < 0)
+        return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, std::string("rope shapes: ") + sh);
+    if (d.head_dim < 2 || d.head_dim % 2 != 0 || d.head_dim > rope_max_head_dim())
+        return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, std::string("rope: headDim must be even, 2..256: ") + sh);
+    if (!(d.theta > 0.f) || !std::isfinite(d.theta))
+        return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "rope: theta must be finite and > 0");
+    if (d.interleaved != 0 && d.interleaved != 1)
+        return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "rope: interleaved must be 0 or 1");
+    if (d.flags != 0) return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "rope: unknown flags");
+    if (d.start_position > (1 << 30) || d.tokens > (1 << 30) - d.start_position)
+        return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, std::string("rope: positions out of range: ") + sh);
+    auto al8 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7u) == 0; };
+    if (d.n_heads > 0) {
+        if (d.q_dtype != ALPACA_F32 && d.q_dtype != ALPACA_F16)
+            return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "rope: unknown q dtype");
+        if (!d.q || !al8(d.q)) return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "rope: q null or not 8-byte aligned");
+        if (d.q_token_stride < static_cast<int64_t>(d.n_heads) * d.head_dim || d.q_seq_stride < 0 ||
+            (d.n_seqs > 1 && d.q_seq_stride == 0) || d.q_token_stride % 2 || d.q_seq_stride % 2)
+            return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, std::string("rope: q strides: ") + sh);
+    }
+    if (d.n_kv_heads > 0) {
+        if (d.cache_dtype != ALPACA_F32 && d.cache_dtype != ALPACA_F16)
+            return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "rope: unknown cache dtype");
+        if (!d.k || !d.v || !d.k_cache || !d.v_cache)
+            return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "rope: null k / v / cache pointer");
+        if (!al8(d.k) || !al8(d.v) || !al8(d.k_cache) || !al8(d.v_cache))
+            return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "rope: k / v / cache pointers must be 8-byte aligned");
+        const int64_t hk = static_cast<int64_t>(d.n_kv_heads) * d.head_dim;
+        if (d.kv_token_stride < hk || d.cache_row_stride < hk || d.kv_seq_stride < 0 || d.cache_seq_stride < 0 ||
+            (d.n_seqs > 1 && (d.kv_seq_stride == 0 || d.cache_seq_stride == 0)) || d.kv_token_stride % 2 ||
+            d.kv_seq_stride % 2 || d.cache_row_stride % 2 || d.cache_seq_stride % 2)
+            return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, std::string("rope: k / v / cache strides: ") + sh);
+    }
+    return ok();
+}
+
 // KernelEncoder.attention's policy (KernelEncoder.swift:309-343).
 alpaca_attn_kernel select_kernel(const alpaca_attn_desc& d) {
     const int ctx = d.ctx_lens ? d.max_ctx_len : d.start_position + 1;
@@ -234,6 +278,18 @@ alpaca_cuda_status alpaca_attn_decode_noalloc(const alpaca_attn_desc* desc, alpa
     e = launch_decode(c, reinterpret_cast<cudaStream_t>(stream));
     if (e != cudaSuccess)
         return fail(ALPACA_CUDA_ERR_LAUNCH_FAILED, std::string("decode_noalloc launch failed: ") + cudaGetErrorString(e));
+    return ok();
+}
+
+alpaca_cuda_status alpaca_rope_kv_append(const alpaca_rope_desc* desc, alpaca_stream_t stream) {
+    alpaca_cuda_status st = validate_rope(desc);
+    if (st != ALPACA_CUDA_OK) return st;
+    DeviceInfo di;
+    cudaError_t e = device_info(&di);
+    if (e != cudaSuccess) return fail(ALPACA_CUDA_ERR_CUDA, std::string("rope: ") + cudaGetErrorString(e));
+    e = launch_rope_kv(*desc, reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess)
+        return fail(ALPACA_CUDA_ERR_LAUNCH_FAILED, std::string("rope: launch failed: ") + cudaGetErrorString(e));
     return ok();
 }
 

@@ -32,6 +32,10 @@ cudaError_t decode_builtin_scratch(void** ptr);
 // ---- general fp32 SIMT attention (attn_general.cu)
 cudaError_t launch_general(const Call& c, cudaStream_t s);
 
+// ---- RoPE + KV-cache append (rope_kv.cu)
+int rope_max_head_dim();
+cudaError_t launch_rope_kv(const alpaca_rope_desc& d, cudaStream_t s);
+
 // ---- tcgen05 prefill (attn_prefill_sm100.cu)
 bool prefill_supported(const alpaca_attn_desc& d);
 size_t prefill_workspace_bytes(const alpaca_attn_desc& d);  // f32 -> f16 Q staging when q_dtype is f32

@@ -8,6 +8,10 @@ dispatch policy of ``KernelEncoder.attention`` (KernelEncoder.swift:306-343), f3
 ``attention_device`` is the model-path form (``KernelEncoder.attention`` / ``attentionTensor``): torch CUDA
 tensors already resident in HBM, enqueued on the current stream, no host round trip. PyTorch only supplies device
 memory and streams here; all attention arithmetic runs in the library's own sm_100a kernels.
+
+``rope_kv_append`` is the step upstream of attention, ``KernelEncoder.ropeQKVStore`` (KernelEncoder.swift:401-411):
+q rotated in place, rotated k and raw v appended to the cache. ``rope`` mirrors ``MetalOps.rope(_:startPosition:
+theta:)`` (MetalOps.swift:165-171): a host f32 [tokens, heads, head_dim] array rotated through the same kernel.
 """
 from __future__ import annotations
 
@@ -16,7 +20,7 @@ import ctypes
 import numpy as np
 import torch
 
-from ._lib import AlpacaCUDAError, AttnDesc, DType, Kernel, Status, check, load
+from ._lib import AlpacaCUDAError, AttnDesc, DType, Kernel, RopeDesc, Status, check, load
 
 KV_PADDING_ROWS = 32  # KernelEncoder.kvPaddingRows (KernelEncoder.swift:73)
 
@@ -143,3 +147,70 @@ def attention(q: np.ndarray, keys: np.ndarray, values: np.ndarray, start_positio
     attention_device(qb, kb, vb, out, start_position=start_position, kind=kind)
     device_status()
     return out.cpu().numpy()
+
+
+# ---------------------------------------------------------------------------------------------- RoPE + KV append
+
+def make_rope_desc(q: torch.Tensor | None, k: torch.Tensor | None, v: torch.Tensor | None,
+                   k_cache: torch.Tensor | None, v_cache: torch.Tensor | None, *, theta: float,
+                   start_position: int = 0, positions: torch.Tensor | None = None,
+                   interleaved: bool = True) -> RopeDesc:
+    """Descriptor for q [S,T,H,d] (rotated in place), k/v [S,T,Hkv,d] f32 and caches [S,rows,Hkv,d] (3-D tensors
+    mean S = 1). q or (k, v, caches) may be None."""
+    d_ = RopeDesc()
+    ref = q if q is not None else k
+    if ref is None:
+        raise AlpacaCUDAError(Status.INVALID_ARGUMENT, "rope: neither q nor k given")
+    r4 = _as4(ref, "q" if q is not None else "k")
+    S, T, _, D = r4.shape
+    d_.n_seqs, d_.tokens, d_.head_dim = S, T, D
+    d_.start_position = int(start_position)
+    if positions is not None:
+        if positions.dtype != torch.int32 or not positions.is_cuda:
+            raise AlpacaCUDAError(Status.INVALID_ARGUMENT, "positions must be a CUDA int32 tensor")
+        d_.positions = positions.data_ptr()
+    d_.theta = float(theta)
+    d_.interleaved = 1 if interleaved else 0
+    if q is not None:
+        q4 = _as4(q, "q")
+        d_.n_heads, d_.q_dtype = q4.shape[2], _dtype(q4)
+        d_.q, d_.q_token_stride, d_.q_seq_stride = q4.data_ptr(), q4.stride(1), q4.stride(0) if S > 1 else 0
+    if k is not None:
+        k4, v4, kc4, vc4 = _as4(k, "k"), _as4(v, "v"), _as4(k_cache, "k_cache"), _as4(v_cache, "v_cache")
+        if k4.dtype != torch.float32 or v4.dtype != torch.float32 or k4.stride() != v4.stride():
+            raise AlpacaCUDAError(Status.INVALID_ARGUMENT, "rope: k and v must be f32 with equal strides")
+        if kc4.stride() != vc4.stride() or kc4.dtype != vc4.dtype:
+            raise AlpacaCUDAError(Status.INVALID_ARGUMENT, "rope: caches must share dtype and strides")
+        d_.n_kv_heads, d_.cache_dtype = k4.shape[2], _dtype(kc4)
+        d_.k, d_.v, d_.kv_token_stride = k4.data_ptr(), v4.data_ptr(), k4.stride(1)
+        d_.kv_seq_stride = k4.stride(0) if S > 1 else 0
+        d_.k_cache, d_.v_cache, d_.cache_row_stride = kc4.data_ptr(), vc4.data_ptr(), kc4.stride(1)
+        d_.cache_seq_stride = kc4.stride(0) if S > 1 else 0
+    return d_
+
+
+def rope_launch(desc: RopeDesc, stream: torch.cuda.Stream | None = None) -> None:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    check(load().alpaca_rope_kv_append(ctypes.byref(desc), ctypes.c_void_p(s.cuda_stream)))
+
+
+def rope_kv_append(q: torch.Tensor | None, k: torch.Tensor | None, v: torch.Tensor | None,
+                   k_cache: torch.Tensor | None, v_cache: torch.Tensor | None, *, theta: float,
+                   start_position: int = 0, positions: torch.Tensor | None = None, interleaved: bool = True,
+                   stream: torch.cuda.Stream | None = None) -> RopeDesc:
+    """Enqueue RoPE + KV append on device tensors (KernelEncoder.ropeQKVStore, KernelEncoder.swift:401-411)."""
+    d_ = make_rope_desc(q, k, v, k_cache, v_cache, theta=theta, start_position=start_position, positions=positions,
+                        interleaved=interleaved)
+    rope_launch(d_, stream)
+    return d_
+
+
+def rope(x: np.ndarray, start_position: int, theta: float, interleaved: bool = True) -> np.ndarray:
+    """MetalOps.rope(_:startPosition:theta:) (MetalOps.swift:165-171): f32 [tokens, heads, head_dim] in and out."""
+    x = np.asarray(x, dtype=np.float32)
+    if x.ndim != 3 or x.shape[2] % 2:
+        raise AlpacaCUDAError(Status.INVALID_ARGUMENT, f"rope shape {x.shape}")
+    t = torch.from_numpy(np.ascontiguousarray(x)).cuda()
+    rope_kv_append(t, None, None, None, None, theta=theta, start_position=start_position, interleaved=interleaved)
+    torch.cuda.synchronize()
+    return t.cpu().numpy()

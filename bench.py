@@ -349,6 +349,9 @@ def run_ours(args):
     # ---- decode (config 3)
     decode = run_decode(args, ab, torch, dev, stream, rank, world, pg, pk) if not args.no_decode else None
 
+    # ---- RoPE + KV-cache append (the step upstream of attention), config-2 prefill shape
+    rope_kv = run_rope(args, ab, torch, dev, stream, rank, world, pg, pk) if not args.no_rope else None
+
     # ---- CPU baseline (rank 0 at N=1 only)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -390,6 +393,7 @@ def run_ours(args):
             "gpu_launches": 0 if args.no_prefill else args.steps,
             "clocks": clk,
             "decode": decode,
+            "rope_kv_append": rope_kv,
             "spot_check_max_abs": spot,
             "gather_ms": gather_ms,
         }
@@ -513,6 +517,57 @@ def run_cfg5(args):
         pg.destroy_process_group()
 
 
+def run_rope(args, ab, torch, dev, stream, rank, world, pg, pk):
+    """RoPE of q (in place) + rotated K / raw V appended to an f16 cache, for the config-2 prefill shape: 30 layers
+    x T tokens x 9/3 heads x d=64 per step, each layer its own tensors (inputs > L2). HBM-bound; GB/s counts q read
+    + written (f32), k and v read (f32) and the cache rows written (f16)."""
+    LAYERS, T = args.layers, args.tokens
+    g = torch.Generator(device=dev)
+    g.manual_seed(20260105 + 1000 * rank)
+    q = torch.randn((LAYERS, T, H, D), generator=g, device=dev)
+    k = torch.randn((LAYERS, T, KVH, D), generator=g, device=dev)
+    v = torch.randn((LAYERS, T, KVH, D), generator=g, device=dev)
+    kc = torch.zeros((LAYERS, T, KVH, D), dtype=torch.float16, device=dev)
+    vc = torch.zeros_like(kc)
+    descs = [ab.make_rope_desc(q[l], k[l], v[l], kc[l], vc[l], theta=1e5, start_position=0) for l in range(LAYERS)]
+
+    def step():
+        for dd in descs:
+            ab.rope_launch(dd)
+
+    side = torch.cuda.Stream(device=dev)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        step()
+    stream.wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(max(3, args.warmup)):
+        graph.replay()
+    steps = max(5, args.steps)
+    barrier(pg)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        graph.replay()
+    e1.record(stream)
+    barrier(pg)
+    ms = e0.elapsed_time(e1) / steps
+    ms_max = max_over_ranks(ms, pg)
+    del graph
+    byts = LAYERS * T * (H * D * 4 * 2 + KVH * D * 4 * 2 + KVH * D * 2 * 2)
+    gbs = byts / (ms * 1e-3) / 1e9
+    return {"workload": f"RoPE + KV append, config-2 shape: {LAYERS} layers x T={T} tokens, 9/3 heads, d=64, f32 q/k/v "
+                        "in, f16 cache out, one call per layer replayed from a CUDA graph",
+            "value": world * byts / (ms_max * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms_max,
+            "tokens_per_s": world * T / (ms_max * 1e-3),  # prompt tokens through all layers per second
+            "bytes_per_step": byts,
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": gbs / pk["hbm_gbs"], "kernel": "alpaca::rope_kv_kernel per layer"},
+            "gpu_launches": steps * LAYERS}
+
+
 def run_decode(args, ab, torch, dev, stream, rank, world, pg, pk):
     from alpaca_b200 import Kernel
     g = torch.Generator(device=dev)
@@ -620,6 +675,7 @@ def main():
                          "cfg5 (ragged mixed prefill + decode batch at 32/32 heads, strong scaling)")
     ap.add_argument("--tokens", type=int, default=T_PREFILL)
     ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--no-rope", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-chunk", type=int, default=0, help="sequences per ABI call in the e2e pipeline (0: 1/6 of them)")

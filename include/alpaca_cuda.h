@@ -14,6 +14,10 @@
  *       Sources/AlpacaMetal/Backend/KernelEncoder.swift:88-92          -> alpaca_attention_workspace_bytes
  *   MetalError.invalidArgument / .unsupported / .commandFailed
  *       Sources/AlpacaMetal/Backend/MetalContext.swift:7-31            -> alpaca_cuda_status + alpaca_cuda_status_string
+ *   KernelEncoder.ropeQKVStore(q:k:v:kCache:vCache:freqs:heads:kvHeads:headDim:startPosition:tokens:kv:)
+ *       Sources/AlpacaMetal/Backend/KernelEncoder.swift:401-411        -> alpaca_rope_kv_append
+ *       (kernels rope_qkv_store_kv16 / _kv32, Sources/AlpacaMetal/Kernels/decode_fused.metal:126-154; with no K/V
+ *       it is MetalOps.rope, Sources/AlpacaMetal/Backend/MetalOps.swift:165-171)
  *
  * Data layout (the hand-off of Sources/AlpacaMetal/Backend/MetalLlamaModel.swift:189-191, 322-337):
  *   q    [n_seqs][tokens][n_heads][head_dim]     post-RoPE queries (f16 or f32); token t of a sequence sits at
@@ -146,6 +150,48 @@ alpaca_cuda_status alpaca_attention_workspace_bytes(const alpaca_attn_desc* desc
 
 /* Which kernel ALPACA_ATTN_AUTO would run for `desc` (host-only policy query, KernelEncoder.swift:306-343). */
 alpaca_cuda_status alpaca_attention_select(const alpaca_attn_desc* desc, alpaca_attn_kernel* kind);
+
+/* ---- RoPE + KV-cache append: the step that produces the attention hand-off (the next row upstream of it). */
+
+/* Rotates q in place and appends rotated k and raw v to the KV cache, for `tokens` new tokens of each of n_seqs
+ * sequences: token t of sequence s sits at absolute position pos = (positions ? positions[s] : start_position) + t;
+ * its cache row is pos. Pair i of head_dim rotates by angle pos * theta^(-2i/head_dim), computed in double with
+ * cos / sin rounded once to f32 and the rotation in f32, as CPUOps.rope (Sources/AlpacaCore/Operations/
+ * CPUOps.swift:184-210) does; cache values are rounded to the cache type (f16: round to nearest even).
+ *   q        [n_seqs][tokens][n_heads][head_dim]   f32 or f16, rotated in place (n_heads == 0: no queries)
+ *   k, v     [n_seqs][tokens][n_kv_heads][head_dim] f32 projections (n_kv_heads == 0: no append)
+ *   k_cache, v_cache [n_seqs][rows][n_kv_heads][head_dim] f16 or f32; rows > every written position
+ * Pointers 8-byte aligned, strides in elements and even. The caller guarantees every written row exists. */
+typedef struct alpaca_rope_desc {
+    int32_t n_seqs;           /* >= 1 */
+    int32_t n_heads;          /* query heads (0: rotate no queries) */
+    int32_t n_kv_heads;       /* KV heads (0: append nothing) */
+    int32_t head_dim;         /* even, 2 .. 256 */
+    int32_t tokens;           /* new tokens per sequence, >= 1 */
+    int32_t start_position;   /* position of token 0 when positions is NULL, >= 0 */
+    const int32_t* positions; /* optional DEVICE array [n_seqs] of the position of each sequence's token 0 */
+    float theta;              /* RoPE base (LlamaConfig.ropeTheta), > 0 */
+    int32_t interleaved;      /* 1: adjacent pairs (x[2i], x[2i+1]), the layout of GGUF Llama files and of the
+                                 Metal kernel; 0: split halves (x[i], x[i + head_dim/2]), "rotate_half" */
+    int32_t q_dtype;          /* alpaca_dtype of q */
+    int32_t cache_dtype;      /* alpaca_dtype of k_cache / v_cache */
+    void* q;
+    int64_t q_token_stride;
+    int64_t q_seq_stride;
+    const float* k;
+    const float* v;
+    int64_t kv_token_stride;  /* elements between tokens of k / v */
+    int64_t kv_seq_stride;
+    void* k_cache;
+    void* v_cache;
+    int64_t cache_row_stride; /* elements between cache rows */
+    int64_t cache_seq_stride;
+    uint32_t flags;           /* 0 */
+} alpaca_rope_desc;
+
+/* Enqueue the fused RoPE + KV append on `stream`. Replaces KernelEncoder.ropeQKVStore (KernelEncoder.swift:
+ * 401-411) and its rope_qkv_store_kv16 / _kv32 kernels (decode_fused.metal:126-154). */
+alpaca_cuda_status alpaca_rope_kv_append(const alpaca_rope_desc* desc, alpaca_stream_t stream);
 
 /* Synchronises `stream`, then reports and (when `clear` != 0) resets the device-side error word of the current
  * device: ALPACA_CUDA_ERR_DEVICE_TIMEOUT when a bounded wait gave up, ALPACA_CUDA_OK otherwise. */

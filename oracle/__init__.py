@@ -1,12 +1,14 @@
 """CPU oracle for the attention hot path — TEST INFRASTRUCTURE ONLY.
 
 ctypes bindings of ``oracle/liboracle.so`` (the C restatement of alpaca.swift's
-``CPUOps.attentionScores / softmax / attentionApply``, Sources/AlpacaCore/Operations/CPUOps.swift:162-274).
+``CPUOps.attentionScores / softmax / attentionApply``, Sources/AlpacaCore/Operations/CPUOps.swift:162-274, and of
+``CPUOps.rope``, CPUOps.swift:184-210, composed into the RoPE + KV-cache append of decode_fused.metal:126-154).
 Only ``tests/``, ``__graft_entry__.smoke()`` and the CPU-baseline leg of ``bench.py`` import this module, as the
 checker. The product package ``alpaca_b200`` never imports it.
 
 Parity of this oracle is pinned against the reference's own known-answer fixture
-(Tests/AlpacaCoreTests/Fixtures/ops.json["attention"], committed as tests/golden/attention_kat.json).
+(Tests/AlpacaCoreTests/Fixtures/ops.json["attention"] and ["rope"], committed as tests/golden/attention_kat.json
+and tests/golden/rope_kat.json).
 """
 from __future__ import annotations
 
@@ -27,8 +29,8 @@ _f64p = ctypes.POINTER(ctypes.c_double)
 
 def build(force: bool = False) -> Path:
     """Compile liboracle.so with the committed Makefile (gcc, no fast-math, no FMA contraction)."""
-    src = _HERE / "cpu_attention.c"
-    if force or not _LIB_PATH.exists() or _LIB_PATH.stat().st_mtime < src.stat().st_mtime:
+    srcs = [_HERE / n for n in ("cpu_attention.c", "cpu_attention.h", "cpu_rope.c", "cpu_rope.h")]
+    if force or not _LIB_PATH.exists() or any(_LIB_PATH.stat().st_mtime < p.stat().st_mtime for p in srcs):
         subprocess.run(["make", "-s", "-C", str(_HERE), "liboracle.so"], check=True)
     return _LIB_PATH
 
@@ -59,6 +61,9 @@ def lib() -> ctypes.CDLL:
         L.oracle_error_metrics_f32.argtypes = [_f32p, _f32p, ctypes.c_int64, _f64p]
         L.oracle_splitmix_uniform.argtypes = [ctypes.c_uint64, ctypes.c_float, _f32p, ctypes.c_int64]
         L.oracle_splitmix_normal.argtypes = [ctypes.c_uint64, _f32p, ctypes.c_int64]
+        L.oracle_rope.argtypes = [_f32p] + [ctypes.c_int] * 4 + [ctypes.c_double, ctypes.c_int]
+        L.oracle_rope_kv_append.argtypes = ([_f32p, _f32p, _f32p, _f32p, _f32p] + [ctypes.c_int] * 5 +
+                                            [ctypes.c_double, ctypes.c_int, ctypes.c_int])
         _lib = L
     return _lib
 
@@ -156,6 +161,33 @@ def attention_rows(q, keys, values, start: int, rows, length: int | None = None,
                                 float(scale), _p32(out), H * d, r.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)),
                                 r.size, int(threads or host_threads()))
     return out
+
+
+def rope(x, start: int, theta: float, interleaved: bool = True) -> np.ndarray:
+    """CPUOps.rope (CPUOps.swift:184-210) of x [tokens, heads, head_dim]; returns a rotated copy. theta is taken
+    as a Float first, as the reference's `theta: Float` parameter is."""
+    y = np.ascontiguousarray(x, dtype=np.float32).copy()
+    T, H, D = y.shape
+    lib().oracle_rope(_p32(y), T, H, D, int(start), float(np.float32(theta)), int(bool(interleaved)))
+    return y
+
+
+def rope_kv_append(q, k, v, k_cache, v_cache, start: int, theta: float, interleaved: bool = True,
+                   cache_f16: bool = True):
+    """One sequence of the fused step (decode_fused.metal:126-154 on the CPU path). q [T, H, d] is returned
+    rotated; k_cache / v_cache [rows, Hkv, d] (f32 arrays) are returned with rows start..start+T-1 written
+    (rotated k and raw v, binary16-rounded when cache_f16). Inputs are not modified."""
+    q = np.ascontiguousarray(q, dtype=np.float32).copy()
+    k = np.ascontiguousarray(k, dtype=np.float32)
+    v = np.ascontiguousarray(v, dtype=np.float32)
+    kc = np.ascontiguousarray(k_cache, dtype=np.float32).copy()
+    vc = np.ascontiguousarray(v_cache, dtype=np.float32).copy()
+    T, H, D = q.shape
+    Hkv = k.shape[1]
+    assert kc.shape[0] >= start + T and kc.shape[1:] == (Hkv, D) and vc.shape == kc.shape
+    lib().oracle_rope_kv_append(_p32(q), _p32(k), _p32(v), _p32(kc), _p32(vc), T, H, Hkv, D, int(start),
+                                float(np.float32(theta)), int(bool(interleaved)), int(bool(cache_f16)))
+    return q, kc, vc
 
 
 def rows_mask(rows, T: int, H: int) -> np.ndarray:

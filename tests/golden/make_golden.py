@@ -1,15 +1,17 @@
 #!/usr/bin/env python3
 """Regenerates the golden vectors in tests/golden/ from the alpaca.swift checkout.
 
-Run in a container that has the reference mounted (default path via $ALPACA_REFERENCE):
+Run where an alpaca.swift checkout is available (path as the argument or in $ALPACA_REFERENCE):
 
-    python tests/golden/make_golden.py [/path/to/alpaca.swift]
+    python tests/golden/make_golden.py /path/to/alpaca.swift
 
 Outputs (committed; nothing reads the reference at test time):
   attention_kat.json  the reference's own attention known-answer case, Tests/AlpacaCoreTests/Fixtures/ops.json
                       ["attention"] (generated upstream by Scripts/generate_op_fixtures.py:64-74 as a float64
                       torch SDPA), copied verbatim, plus the reference tolerances of OperationTests.swift:72-86.
   softmax_kat.json    ops.json["softmax"] (±30-sigma inputs, float64 expected), OperationTests softmax case.
+  rope_kat.json       ops.json["rope"] (generated upstream by Scripts/generate_op_fixtures.py:50-62 in float64, both
+                      pair conventions), plus the 2e-6 tolerance of OperationTests.swift:63-70.
 """
 from __future__ import annotations
 
@@ -22,7 +24,10 @@ HERE = Path(__file__).resolve().parent
 
 
 def main() -> None:
-    ref = Path(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("ALPACA_REFERENCE", "/root/reference"))
+    src = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("ALPACA_REFERENCE")
+    if not src:
+        sys.exit("usage: make_golden.py /path/to/alpaca.swift  (or set ALPACA_REFERENCE)")
+    ref = Path(src)
     ops = json.loads((ref / "Tests/AlpacaCoreTests/Fixtures/ops.json").read_text())
     att = dict(ops["attention"])
     att["source"] = "alpaca.swift Tests/AlpacaCoreTests/Fixtures/ops.json[\"attention\"]"
@@ -31,6 +36,10 @@ def main() -> None:
     sm = dict(ops["softmax"])
     sm["source"] = "alpaca.swift Tests/AlpacaCoreTests/Fixtures/ops.json[\"softmax\"]"
     (HERE / "softmax_kat.json").write_text(json.dumps(sm))
+    rp = dict(ops["rope"])
+    rp["source"] = "alpaca.swift Tests/AlpacaCoreTests/Fixtures/ops.json[\"rope\"]"
+    rp["tolerance"] = {"atol": 2e-6, "from": "Tests/AlpacaCoreTests/OperationTests.swift:68-69"}
+    (HERE / "rope_kat.json").write_text(json.dumps(rp))
 
     print("wrote", sorted(p.name for p in HERE.iterdir()))
 

@@ -173,3 +173,71 @@ def test_python_mirror_rejects_like_metalops():
     with pytest.raises(AlpacaCUDAError):
         attention(np.zeros((4, 9, 48), np.float32), np.zeros((8, 3, 48), np.float32),
                   np.zeros((8, 3, 48), np.float32), 0)  # head dim % 32
+
+
+# ---------------------------------------------------------------------------------------------- struct layouts
+
+def test_descriptor_layouts_match_the_c_compiler(tmp_path):
+    """The ctypes mirrors have the C structs' size and field offsets (gcc on the header)."""
+    import shutil
+    import subprocess
+
+    from alpaca_b200 import AttnDesc, RopeDesc
+    if not shutil.which("gcc"):
+        pytest.skip("gcc not available")
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "alpaca_cuda.h"', 'int main(void) {']
+    for cname, cls in (("alpaca_attn_desc", AttnDesc), ("alpaca_rope_desc", RopeDesc)):
+        lines.append(f'printf("{cname} size %zu\\n", sizeof({cname}));')
+        for f, _ in cls._fields_:
+            lines.append(f'printf("{cname} {f} %zu\\n", offsetof({cname}, {f}));')
+    lines.append("return 0; }")
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-I", str(HEADER.parent), str(src), "-o", str(exe)], check=True)
+    out = dict((" ".join(l.split()[:2]), int(l.split()[2])) for l in subprocess.run([str(exe)], capture_output=True,
+                                                                                      text=True, check=True).stdout.splitlines())
+    for cname, cls in (("alpaca_attn_desc", AttnDesc), ("alpaca_rope_desc", RopeDesc)):
+        assert out[f"{cname} size"] == ctypes.sizeof(cls), cname
+        for f, _ in cls._fields_:
+            assert out[f"{cname} {f}"] == getattr(cls, f).offset, (cname, f)
+
+
+# ---------------------------------------------------------------------------------------------- RoPE + KV append
+
+def rope_desc(**kw):
+    from alpaca_b200 import DType, RopeDesc
+    d = RopeDesc()
+    d.n_seqs, d.n_heads, d.n_kv_heads, d.head_dim, d.tokens, d.start_position = 1, 9, 3, 64, 4, 10
+    d.theta, d.interleaved = 1e5, 1
+    d.q_dtype, d.cache_dtype = int(DType.F32), int(DType.F16)
+    d.q = d.k = d.v = d.k_cache = d.v_cache = FAKE
+    d.q_token_stride, d.kv_token_stride, d.cache_row_stride = 9 * 64, 3 * 64, 3 * 64
+    for k, v in kw.items():
+        setattr(d, k, v)
+    return d
+
+
+@pytest.mark.parametrize("bad", [
+    dict(head_dim=63),                # odd (CPUOps.rope's guard, CPUOps.swift:188)
+    dict(head_dim=258),               # above the kernel's 256
+    dict(theta=0.0),                  # CPUOps.swift:191
+    dict(theta=float("nan")),
+    dict(start_position=-1),          # CPUOps.swift:191
+    dict(tokens=0),
+    dict(n_heads=0, n_kv_heads=0),    # nothing to do
+    dict(interleaved=2),
+    dict(q=0),
+    dict(k_cache=FAKE + 4),           # not 8-byte aligned
+    dict(q_token_stride=9 * 64 - 2),  # smaller than a token
+    dict(cache_row_stride=3 * 64 + 1),  # odd
+    dict(n_seqs=2),                   # several sequences with zero sequence strides
+    dict(n_seqs=70000),
+    dict(cache_dtype=5),
+    dict(flags=1),
+])
+def test_rope_invalid_arguments_rejected(lib, bad):
+    from alpaca_b200 import Status
+    d = rope_desc(**bad)
+    assert lib.alpaca_rope_kv_append(ctypes.byref(d), None) == Status.INVALID_ARGUMENT
+    assert lib.alpaca_cuda_last_error().startswith(b"rope")

@@ -1,7 +1,7 @@
 """The CPU oracle pinned against the reference's own known answers (CPU only).
 
-Mirrors Tests/AlpacaCoreTests/OperationTests.swift: testCausalGQAAttention (:72-86) and testSoftmax (:55-61),
-on the fixture values committed in tests/golden/ (extracted from the reference's ops.json by
+Mirrors Tests/AlpacaCoreTests/OperationTests.swift: testCausalGQAAttention (:72-86), testSoftmax (:55-61) and
+testRoPEBothConventions (:63-70), on the fixture values committed in tests/golden/ (extracted from the reference's ops.json by
 tests/golden/make_golden.py). Then cross-checks the oracle against float64 SDPA on BASELINE shapes and checks its
 helpers (f16 rounding, generators, error metrics, fused == three-step).
 """
@@ -175,3 +175,49 @@ def test_oracle_rejects_bad_shapes():
     k = np.zeros((8, 1, 32), np.float32)
     with pytest.raises(ValueError):
         oracle.attention_scores(q, k, 8, 5)          # start + tokens > length
+
+
+# ---------------------------------------------------------------------------------------------- RoPE
+
+def _rope_kat():
+    c = json.loads((GOLDEN / "rope_kat.json").read_text())
+    return c, np.array(c["x"], np.float32).reshape(c["shape"])
+
+
+def test_rope_known_answer_both_conventions():
+    """CPUOps.rope restated (CPUOps.swift:184-210) against the reference's own fixture ops.json["rope"] at the
+    tolerance of OperationTests.swift:68-69 (atol 2e-6), adjacent pairs and split halves."""
+    c, x = _rope_kat()
+    for inter, key in ((True, "expected_interleaved"), (False, "expected_split")):
+        got = oracle.rope(x, c["start"], c["theta"], inter)
+        err = float(np.abs(got - np.array(c[key]).reshape(c["shape"])).max())
+        print(f"[metrics] oracle rope {key}: max-abs {err:.2e} (bound {c['tolerance']['atol']})")
+        assert err <= c["tolerance"]["atol"]
+
+
+def test_rope_position_zero_is_identity_and_norms_are_kept():
+    x = oracle.splitmix_normal(5, (3, 4, 32))
+    y = oracle.rope(x, 0, 1e4, True)
+    assert np.array_equal(y[0], x[0])  # angle 0: cos 1, sin 0 exactly
+    n0 = np.linalg.norm(x.reshape(3, 4, 16, 2), axis=-1)
+    n1 = np.linalg.norm(y.reshape(3, 4, 16, 2), axis=-1)
+    assert np.abs(n0 - n1).max() < 1e-5  # a rotation per pair
+
+
+def test_rope_kv_append_composition():
+    """The fused step on the CPU path (decode_fused.metal:126-154): q rotated, cache rows start..start+T-1 get
+    f16(rope(k)) and f16(v), every other cache row unchanged."""
+    T, H, Hkv, d, start, cap = 5, 6, 2, 16, 9, 20
+    q = oracle.splitmix_normal(11, (T, H, d))
+    k = oracle.splitmix_normal(12, (T, Hkv, d))
+    v = oracle.splitmix_normal(13, (T, Hkv, d))
+    kc0 = np.full((cap, Hkv, d), 7.0, np.float32)
+    vc0 = np.full((cap, Hkv, d), -7.0, np.float32)
+    qr, kc, vc = oracle.rope_kv_append(q, k, v, kc0, vc0, start, 1e5, True, True)
+    assert np.array_equal(qr, oracle.rope(q, start, 1e5, True))
+    assert np.array_equal(kc[start:start + T], oracle.f16_round(oracle.rope(k, start, 1e5, True)))
+    assert np.array_equal(vc[start:start + T], oracle.f16_round(v))
+    rest = np.r_[0:start, start + T:cap]
+    assert np.all(kc[rest] == 7.0) and np.all(vc[rest] == -7.0)
+    _, kc32, _ = oracle.rope_kv_append(q, k, v, kc0, vc0, start, 1e5, False, False)
+    assert np.array_equal(kc32[start:start + T], oracle.rope(k, start, 1e5, False))
