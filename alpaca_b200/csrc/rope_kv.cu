@@ -8,12 +8,15 @@
 // KernelEncoder.swift:413-415, without the rounding to f32), the angle position * freq in double, cos and sin in
 // double rounded once to f32, and the rotation a*c - b*s, a*s + b*c as separately rounded f32 operations.
 //
-// One CTA per (token, sequence): its first d/2 threads compute the token's (cos, sin) pairs into shared memory,
-// then all threads rotate / copy the pairs of the token's H query rows and Hkv key and value rows. The step is a
-// few bytes per element and HBM-bound; accesses are per pair (8 bytes f32), coalesced along head_dim.
+// Vector kernel (head_dim % 8 == 0, 16-byte aligned tensors, the usual case): one CTA per 8 tokens of a sequence.
+// Every thread issues its first batch of 16-byte loads (groups of 4 pairs of the tokens' H query rows and Hkv key
+// and value rows), then the CTA computes the tokens' (cos, sin) table into shared memory while those loads are in
+// flight, and the threads rotate / copy and store. Scalar kernel otherwise: one CTA per token, one pair per thread
+// step. The step moves ~20 bytes per f32 element pair and is HBM-bound.
 #include <cuda_fp16.h>
 
 #include <cmath>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "internal.h"
@@ -34,7 +37,8 @@ struct RopeArgs {
     void* v_cache;
     int64_t cache_row_stride, cache_seq_stride;
     const int* positions;
-    int start, n_heads, n_kv_heads, half;
+    int start, n_heads, n_kv_heads, half, tokens;
+    int tpc;  // tokens per CTA of the vector kernel (1 .. kVecTokens)
     double freq[kRopeMaxPairs];  // theta^(-2i/d), host-computed in double
 };
 
@@ -103,17 +107,201 @@ __global__ void __launch_bounds__(kRopeThreads) rope_kv_kernel(const __grid_cons
     }
 }
 
+constexpr int kVecThreads = 256;
+constexpr int kVecTokens = 32;  // most tokens per CTA of the vector kernel
+constexpr int kVecBatch = 4;   // groups of 4 pairs a thread loads before it rotates / stores them
+
+// Four pairs i0..i0+3 of one head row: a[j] = x[ia(i0+j)], b[j] = x[ib(i0+j)].
+template <bool kInterleaved>
+__device__ __forceinline__ void load4(const float* p, int i0, int half, float (&a)[4], float (&b)[4]) {
+    if (kInterleaved) {
+        const float4 u = *reinterpret_cast<const float4*>(p + 2 * i0), w = *reinterpret_cast<const float4*>(p + 2 * i0 + 4);
+        a[0] = u.x; b[0] = u.y; a[1] = u.z; b[1] = u.w; a[2] = w.x; b[2] = w.y; a[3] = w.z; b[3] = w.w;
+    } else {
+        const float4 u = *reinterpret_cast<const float4*>(p + i0), w = *reinterpret_cast<const float4*>(p + half + i0);
+        a[0] = u.x; a[1] = u.y; a[2] = u.z; a[3] = u.w; b[0] = w.x; b[1] = w.y; b[2] = w.z; b[3] = w.w;
+    }
+}
+template <bool kInterleaved>
+__device__ __forceinline__ void load4(const __half* p, int i0, int half, float (&a)[4], float (&b)[4]) {
+    if (kInterleaved) {
+        const uint4 u = *reinterpret_cast<const uint4*>(p + 2 * i0);
+        const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const float2 f = __half22float2(h[j]);
+            a[j] = f.x;
+            b[j] = f.y;
+        }
+    } else {
+        const uint2 u = *reinterpret_cast<const uint2*>(p + i0), w = *reinterpret_cast<const uint2*>(p + half + i0);
+        const __half2* hu = reinterpret_cast<const __half2*>(&u);
+        const __half2* hw = reinterpret_cast<const __half2*>(&w);
+        const float2 u0 = __half22float2(hu[0]), u1 = __half22float2(hu[1]);
+        const float2 w0 = __half22float2(hw[0]), w1 = __half22float2(hw[1]);
+        a[0] = u0.x; a[1] = u0.y; a[2] = u1.x; a[3] = u1.y; b[0] = w0.x; b[1] = w0.y; b[2] = w1.x; b[3] = w1.y;
+    }
+}
+template <bool kInterleaved>
+__device__ __forceinline__ void store4(float* p, int i0, int half, const float (&a)[4], const float (&b)[4]) {
+    if (kInterleaved) {
+        *reinterpret_cast<float4*>(p + 2 * i0) = make_float4(a[0], b[0], a[1], b[1]);
+        *reinterpret_cast<float4*>(p + 2 * i0 + 4) = make_float4(a[2], b[2], a[3], b[3]);
+    } else {
+        *reinterpret_cast<float4*>(p + i0) = make_float4(a[0], a[1], a[2], a[3]);
+        *reinterpret_cast<float4*>(p + half + i0) = make_float4(b[0], b[1], b[2], b[3]);
+    }
+}
+template <bool kInterleaved>
+__device__ __forceinline__ void store4(__half* p, int i0, int half, const float (&a)[4], const float (&b)[4]) {
+    if (kInterleaved) {
+        __half2 h[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) h[j] = __floats2half2_rn(a[j], b[j]);
+        *reinterpret_cast<uint4*>(p + 2 * i0) = *reinterpret_cast<const uint4*>(h);
+    } else {
+        __half2 u[2] = {__floats2half2_rn(a[0], a[1]), __floats2half2_rn(a[2], a[3])};
+        __half2 w[2] = {__floats2half2_rn(b[0], b[1]), __floats2half2_rn(b[2], b[3])};
+        *reinterpret_cast<uint2*>(p + i0) = *reinterpret_cast<const uint2*>(u);
+        *reinterpret_cast<uint2*>(p + half + i0) = *reinterpret_cast<const uint2*>(w);
+    }
+}
+
+// Group `idx` (4 pairs) of the CTA's tokens: which token, row and pairs, and where that row lives.
+template <typename QT, typename CT>
+struct VecItem {
+    bool valid, is_q, is_k;
+    int tt, i0;
+    const float* src;  // k or v row (f32)
+    QT* qrow;          // query row (rotated in place)
+    CT* dst;           // cache row
+};
+
+template <typename QT, typename CT>
+__device__ __forceinline__ VecItem<QT, CT> vec_item(const RopeArgs& a, int seq, int t0, int pos0, int ntok, int idx) {
+    VecItem<QT, CT> it;
+    const int d = 2 * a.half, quads = a.half / 4;
+    const int per_tok = (a.n_heads + 2 * a.n_kv_heads) * quads;
+    it.valid = idx < ntok * per_tok;
+    const int tt = it.valid ? idx / per_tok : 0, rem = it.valid ? idx - tt * per_tok : 0;
+    const int r = rem / quads;
+    it.tt = tt;
+    it.i0 = 4 * (rem - r * quads);
+    const int t = t0 + tt;
+    it.is_q = r < a.n_heads;
+    it.is_k = !it.is_q && r < a.n_heads + a.n_kv_heads;
+    const int h = it.is_q ? 0 : (it.is_k ? r - a.n_heads : r - a.n_heads - a.n_kv_heads);
+    it.qrow = static_cast<QT*>(a.q) + seq * a.q_seq_stride + static_cast<int64_t>(t) * a.q_token_stride + r * d;
+    it.src = (it.is_k ? a.k : a.v) + seq * a.kv_seq_stride + static_cast<int64_t>(t) * a.kv_token_stride + h * d;
+    it.dst = static_cast<CT*>(it.is_k ? a.k_cache : a.v_cache) + seq * a.cache_seq_stride +
+             static_cast<int64_t>(pos0 + tt) * a.cache_row_stride + h * d;
+    return it;
+}
+
+template <bool kInterleaved, typename QT, typename CT>
+__device__ __forceinline__ void vec_load(const RopeArgs& a, int seq, int t0, int pos0, int ntok, int idx,
+                                         float (&x0)[4], float (&x1)[4]) {
+    const VecItem<QT, CT> it = vec_item<QT, CT>(a, seq, t0, pos0, ntok, idx);
+    if (!it.valid) return;
+    if (it.is_q) load4<kInterleaved>(it.qrow, it.i0, a.half, x0, x1);
+    else load4<kInterleaved>(it.src, it.i0, a.half, x0, x1);
+}
+
+template <bool kInterleaved, typename QT, typename CT>
+__device__ __forceinline__ void vec_store(const RopeArgs& a, int seq, int t0, int pos0, int ntok, int idx,
+                                          const float2* cs, float (&x0)[4], float (&x1)[4]) {
+    const VecItem<QT, CT> it = vec_item<QT, CT>(a, seq, t0, pos0, ntok, idx);
+    if (!it.valid) return;
+    if (it.is_q || it.is_k) {
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const float2 w = cs[it.tt * a.half + it.i0 + j];
+            const float y0 = __fsub_rn(__fmul_rn(x0[j], w.x), __fmul_rn(x1[j], w.y));
+            x1[j] = __fadd_rn(__fmul_rn(x0[j], w.y), __fmul_rn(x1[j], w.x));
+            x0[j] = y0;
+        }
+    }
+    if (it.is_q) store4<kInterleaved>(it.qrow, it.i0, a.half, x0, x1);
+    else store4<kInterleaved>(it.dst, it.i0, a.half, x0, x1);
+}
+
+template <bool kInterleaved, typename QT, typename CT>
+__global__ void __launch_bounds__(kVecThreads) rope_kv_vec_kernel(const __grid_constant__ RopeArgs a) {
+    extern __shared__ float2 cs[];  // [tpc][half] (cos, sin)
+    const int t0 = blockIdx.x * a.tpc, seq = blockIdx.y, tid = threadIdx.x;
+    const int ntok = min(a.tpc, a.tokens - t0);
+    const int pos0 = (a.positions ? a.positions[seq] : a.start) + t0;
+    const int total = ntok * (a.n_heads + 2 * a.n_kv_heads) * (a.half / 4);
+    constexpr int kStride = kVecThreads * kVecBatch;
+
+    // every thread's first batch of loads is in flight while the (cos, sin) table is computed
+    float x0[kVecBatch][4], x1[kVecBatch][4];
+#pragma unroll
+    for (int b = 0; b < kVecBatch; b++)
+        vec_load<kInterleaved, QT, CT>(a, seq, t0, pos0, ntok, tid + b * kVecThreads, x0[b], x1[b]);
+    for (int j = tid; j < ntok * a.half; j += kVecThreads) {
+        const int tt = j / a.half, i = j - tt * a.half;
+        double s, c;
+        sincos(static_cast<double>(pos0 + tt) * a.freq[i], &s, &c);
+        cs[j] = make_float2(static_cast<float>(c), static_cast<float>(s));
+    }
+    __syncthreads();  // every thread of the CTA reaches this once
+#pragma unroll
+    for (int b = 0; b < kVecBatch; b++)
+        vec_store<kInterleaved, QT, CT>(a, seq, t0, pos0, ntok, tid + b * kVecThreads, cs, x0[b], x1[b]);
+    for (int base = tid + kStride; base < total; base += kStride) {
+#pragma unroll
+        for (int b = 0; b < kVecBatch; b++)
+            vec_load<kInterleaved, QT, CT>(a, seq, t0, pos0, ntok, base + b * kVecThreads, x0[b], x1[b]);
+#pragma unroll
+        for (int b = 0; b < kVecBatch; b++)
+            vec_store<kInterleaved, QT, CT>(a, seq, t0, pos0, ntok, base + b * kVecThreads, cs, x0[b], x1[b]);
+    }
+}
+
+// 16-byte vectors: head_dim % 8 == 0, tensor pointers 16-byte aligned, every stride a multiple of 8 elements.
+bool vector_ok(const alpaca_rope_desc& d) {
+    auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+    if (d.head_dim % 8) return false;
+    if (d.n_heads > 0 && (!al16(d.q) || d.q_token_stride % 8 || d.q_seq_stride % 8)) return false;
+    if (d.n_kv_heads > 0 && (!al16(d.k) || !al16(d.v) || !al16(d.k_cache) || !al16(d.v_cache) ||
+                             d.kv_token_stride % 8 || d.kv_seq_stride % 8 || d.cache_row_stride % 8 ||
+                             d.cache_seq_stride % 8))
+        return false;
+    return true;
+}
+
+template <bool kInterleaved, typename QT, typename CT>
+cudaError_t launch_qc(const RopeArgs& a, const alpaca_rope_desc& d, cudaStream_t s) {
+    if (vector_ok(d)) {
+        const dim3 grid((d.tokens + a.tpc - 1) / a.tpc, d.n_seqs, 1);
+        const size_t smem = sizeof(float2) * a.tpc * a.half;  // <= 32 KB
+        rope_kv_vec_kernel<kInterleaved, QT, CT><<<grid, kVecThreads, smem, s>>>(a);
+    } else {
+        rope_kv_kernel<kInterleaved, QT, CT><<<dim3(d.tokens, d.n_seqs, 1), kRopeThreads, 0, s>>>(a);
+    }
+    return cudaGetLastError();
+}
+
 template <bool kInterleaved, typename QT>
 cudaError_t launch_q(const RopeArgs& a, const alpaca_rope_desc& d, cudaStream_t s) {
-    const dim3 grid(d.tokens, d.n_seqs, 1);
-    if (d.cache_dtype == ALPACA_F16) rope_kv_kernel<kInterleaved, QT, __half><<<grid, kRopeThreads, 0, s>>>(a);
-    else rope_kv_kernel<kInterleaved, QT, float><<<grid, kRopeThreads, 0, s>>>(a);
-    return cudaGetLastError();
+    return d.cache_dtype == ALPACA_F16 ? launch_qc<kInterleaved, QT, __half>(a, d, s)
+                                       : launch_qc<kInterleaved, QT, float>(a, d, s);
 }
 
 template <bool kInterleaved>
 cudaError_t launch_i(const RopeArgs& a, const alpaca_rope_desc& d, cudaStream_t s) {
     return d.q_dtype == ALPACA_F16 ? launch_q<kInterleaved, __half>(a, d, s) : launch_q<kInterleaved, float>(a, d, s);
+}
+
+// Tokens per CTA of the vector kernel: ALPACA_ROPE_TPC (1 .. 32), default 8.
+int rope_tokens_per_cta() {
+    static const int v = [] {
+        const char* e = std::getenv("ALPACA_ROPE_TPC");
+        const int x = e ? std::atoi(e) : 0;
+        return (x >= 1 && x <= kVecTokens) ? x : kVecTokens;
+    }();
+    return v;
 }
 
 }  // namespace
@@ -138,6 +326,8 @@ cudaError_t launch_rope_kv(const alpaca_rope_desc& d, cudaStream_t s) {
     a.n_heads = d.n_heads;
     a.n_kv_heads = d.n_kv_heads;
     a.half = d.head_dim / 2;
+    a.tokens = d.tokens;
+    a.tpc = rope_tokens_per_cta();
     const double theta = static_cast<double>(d.theta);
     for (int i = 0; i < kRopeMaxPairs; i++)
         a.freq[i] = i < a.half ? std::pow(theta, -2.0 * static_cast<double>(i) / static_cast<double>(d.head_dim)) : 0.0;

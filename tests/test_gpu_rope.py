@@ -2,8 +2,8 @@
 
 Covers the reference's own RoPE fixture through MetalOps.rope's mirror (OperationTests.swift:63-70), the fused
 append of KernelEncoder.ropeQKVStore (decode_fused.metal:126-154) for prefill chunks and ragged decode batches, both
-pair conventions, f16 and f32 caches, f16 queries, head_dim 32 / 64 / 128, untouched cache rows, and the hand-off
-into the decode attention kernel. The rotation is computed exactly as the oracle computes it (double angle, cos /
+pair conventions, f16 and f32 caches, f16 queries, head_dim 6 / 12 / 32 / 64 / 128 (the vector and the scalar
+kernel), unaligned views, untouched cache rows, and the hand-off into the decode attention kernel. The rotation is computed exactly as the oracle computes it (double angle, cos /
 sin rounded once to f32, unfused f32 products), so results are compared for equality; the only allowance is one
 f32 ulp where the device's double cos / sin and the host's differ by an ulp next to an f32 rounding boundary.
 """
@@ -59,6 +59,8 @@ def test_metalops_rope_mirror_on_reference_fixture(cuda_lib):
     (64, True, True, True),     # f16 queries rotated in place
     (128, True, True, False),
     (32, False, False, False),
+    (6, True, True, False),     # head_dim % 8 != 0: the scalar kernel
+    (12, False, False, True),
 ])
 def test_prefill_chunk_append(cuda_lib, d, inter, cache_f16, q_f16):
     """One sequence, a 37-token chunk at position 100 of a 200-row cache pre-filled with a sentinel."""
@@ -90,6 +92,31 @@ def test_prefill_chunk_append(cuda_lib, d, inter, cache_f16, q_f16):
     assert np.array_equal(vg, vcr)  # V is copied (rounded once), bit-exact
     rest = np.r_[0:start, start + T:cap]
     assert np.all(kg[rest] == 3.0) and np.all(vg[rest] == -3.0)
+
+
+def test_unaligned_views_take_the_scalar_kernel(cuda_lib):
+    """Tensors offset by 2 elements (8-byte but not 16-byte aligned) are still handled exactly."""
+    from alpaca_b200 import rope_kv_append
+    T, H, Hkv, d, start, cap, theta = 9, 4, 2, 64, 3, 16, 1e4
+    q = oracle.splitmix_normal(51, (T, H, d))
+    k = oracle.splitmix_normal(52, (T, Hkv, d))
+    v = oracle.splitmix_normal(53, (T, Hkv, d))
+    dev = torch.device("cuda")
+    qb = torch.zeros(T * H * d + 2, device=dev)
+    qb[2:] = torch.from_numpy(q).to(dev).flatten()
+    qd = qb[2:].view(T, H, d)
+    kb = torch.zeros(T * Hkv * d + 2, device=dev)
+    kb[2:] = torch.from_numpy(k).to(dev).flatten()
+    vd = torch.from_numpy(v).to(dev)
+    kc = torch.zeros((cap, Hkv, d), dtype=torch.float16, device=dev)
+    vc = torch.zeros_like(kc)
+    rope_kv_append(qd, kb[2:].view(T, Hkv, d), vd, kc, vc, theta=theta, start_position=start)
+    torch.cuda.synchronize()
+    qr, kcr, vcr = oracle.rope_kv_append(q, k, v, np.zeros((cap, Hkv, d), np.float32),
+                                         np.zeros((cap, Hkv, d), np.float32), start, theta, True, True)
+    assert _ulps(qd.cpu().numpy(), qr) <= 1
+    assert _f16_ulps(kc.float().cpu().numpy(), kcr) <= 1
+    assert np.array_equal(vc.float().cpu().numpy(), vcr)
 
 
 @pytest.mark.parametrize("inter", [True, False])
