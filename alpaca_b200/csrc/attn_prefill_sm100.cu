@@ -8,14 +8,16 @@
 //   * persistent kernel, one CTA per SM, work items = (sequence, head, pair of 128-row query tiles A and B)
 //     handed out heaviest first (items with more visible KV blocks come first), so the causal triangle is
 //     balanced over the 148 SMs;
-//   * warp 0: TMA producer. Q tiles and a 4-stage ring of K/V blocks (128 rows x d) land in shared memory with
-//     128-byte swizzle, no multicast;
+//   * head_dim 64 (128-row KV blocks) and 128 (64-row KV blocks, so S, O and P of both tiles fit TMEM); rows of Q,
+//     K and V are stored as head_dim/64 column blocks of 128 bytes;
+//   * warp 0: TMA producer. Q tiles and a 4-stage ring of K/V blocks land in shared memory with 128-byte swizzle,
+//     no multicast;
 //   * warps 1 and 2: one thread each issues tcgen05.mma for tile A / B: S = Q·Kᵀ (A and B from shared memory)
 //     into TMEM, and O += P·V with P read from TMEM (A operand in tensor memory, B = V from shared memory), so
 //     P never touches shared memory and the tensor core's shared-memory reads stay within bandwidth. Each issuer
 //     queues S(j+1) before PV(j), so the next S block is ready when the softmax finishes the current one;
-//   * warps 4-11 and 12-19: softmax for tile A and B, two threads per query row (one per 64-column half of the
-//     128-column S block). They read S from TMEM, mask diagonal blocks and keep the running max in log2 units
+//   * warps 4-11 and 12-19: softmax for tile A and B, two threads per query row (one per half of the S block
+//     row). They read S from TMEM, mask diagonal blocks and keep the running max in log2 units
 //     (it only moves when it grows by more than 8, so O rarely needs rescaling). Each half computes its P
 //     against its own candidate max and only then reads the other half's candidate (shared memory, a
 //     two-arrival mbarrier per pair of warps that share TMEM lanes), so the exchange is off the critical path;
@@ -23,7 +25,8 @@
 //     MUFU, a fixed share on the FMA pipe with a polynomial — is summed per row in f32, stored to TMEM as f16
 //     pairs, and each tile ends with O / l;
 //   * registers: the control warpgroup drops to 56 per thread (setmaxnreg) so the softmax warps get 104.
-//   TMEM: S_A 0-127, S_B 128-255, O_A 256-319, O_B 320-383, P_A 384-447, P_B 448-511 (all 512 columns).
+//   TMEM (see PG): d=64: S_A 0-127, S_B 128-255, O_A 256-319, O_B 320-383, P_A 384-447, P_B 448-511;
+//                  d=128: S_A 0-63, S_B 64-127, O_A 128-255, O_B 256-383, P_A 384-415, P_B 416-447.
 //
 // Every mbarrier wait is bounded (2 s; 2 ms under ALPACA_ATTN_FLAG_DEBUG_FORCE_TIMEOUT). On a timeout the CTA
 // raises its abort flag and the device error word, waits (bounded) for its own TMA loads and MMAs in flight,
@@ -39,23 +42,35 @@ namespace alpaca {
 namespace {
 
 constexpr int kBM = 128;        // query rows per tile
-constexpr int kBN = 128;        // KV rows per block
-constexpr int kD = 64;          // head dim of this kernel
 constexpr int kStages = 4;      // K/V ring depth
 constexpr int kThreads = 640;   // 20 warps: TMA, MMA A, MMA B (+ TMEM allocator), idle, 16 softmax warps
 constexpr int kTmemCols = 512;
-constexpr uint32_t kTileBytes = kBM * kD * 2;  // 16 KB: one Q, K or V tile
 constexpr float kRescaleThreshold = 8.0f;      // log2 units
+
+// Geometry per head dim. Rows of Q, K and V live in shared memory as D/64 column blocks [rows][64] (128 bytes per
+// row, 128-byte swizzle), the layout a 64 x 1 x rows x 1 TMA box writes. d = 64: 128-row KV blocks; d = 128: 64-row
+// KV blocks, so that S, O and P of both tiles fit the 512 TMEM columns.
+//   TMEM: S_A [0, BN), S_B [BN, 2BN), O_A, O_B (D columns each) from 2BN, P_A, P_B (BN/2 columns each) after them:
+//   d = 64: S 0 / 128, O 256 / 320, P 384 / 448;  d = 128: S 0 / 64, O 128 / 256, P 384 / 416.
+template <int D>
+struct PG {
+    static_assert(D == 64 || D == 128, "head_dim 64 or 128");
+    static constexpr int BN = D == 64 ? 128 : 64;  // KV rows per block
+    static constexpr int CB = D / 64;              // 64-column blocks per row
+    static constexpr int SC = BN / 2;              // S columns per softmax thread (half a block row)
+    static constexpr int OC = D / 2;               // O columns per softmax thread
+    static constexpr uint32_t kQBytes = kBM * D * 2;
+    static constexpr uint32_t kKVBytes = BN * D * 2;
+    __host__ __device__ static constexpr uint32_t col_s(int tile) { return tile * BN; }
+    __host__ __device__ static constexpr uint32_t col_o(int tile) { return 2 * BN + tile * D; }
+    __host__ __device__ static constexpr uint32_t col_p(int tile) { return 2 * BN + 2 * D + tile * (BN / 2); }
+    static_assert(2 * BN + 2 * D + BN <= kTmemCols, "TMEM map exceeds 512 columns");
+};
 // Register split after the role dispatch (setmaxnreg): the control warpgroup (warps 0-3) gives registers to
 // the four softmax warpgroups (128 * 56 + 512 * 104 of the 640 x 96 registers the CTA is launched with).
 constexpr uint32_t kRegsControl = 56, kRegsSoftmax = 104;
 static_assert(128 * kRegsControl + 512 * kRegsSoftmax <= kThreads * 96, "register split exceeds the launch budget");
 constexpr float kLog2e = 1.4426950408889634f;
-
-// TMEM column map
-__host__ __device__ constexpr uint32_t col_s(int tile) { return tile ? 128u : 0u; }  // 128 f32 columns
-__host__ __device__ constexpr uint32_t col_o(int tile) { return tile ? 320u : 256u; }  // d f32 columns
-__host__ __device__ constexpr uint32_t col_p(int tile) { return tile ? 448u : 384u; }  // 64 columns of f16 pairs
 
 struct PrefillArgs {
     void* out;
@@ -68,10 +83,11 @@ struct PrefillArgs {
     unsigned flags;
 };
 
+template <int D>
 struct SmemLayout {
-    __half q[2][kBM * kD];
-    __half k[kStages][kBN * kD];
-    __half v[kStages][kBN * kD];
+    __half q[2][kBM * D];                 // [tile][column block][row][64]
+    __half k[kStages][PG<D>::BN * D];     // [stage][column block][row][64]
+    __half v[kStages][PG<D>::BN * D];
     uint64_t q_full[2], q_empty[2];
     uint64_t k_full[kStages], k_empty[kStages], v_full[kStages], v_empty[kStages];
     uint64_t s_full[2], s_empty[2], p_full[2], o_done[2];
@@ -83,20 +99,23 @@ struct SmemLayout {
     int abort_flag;
 };
 
-constexpr size_t kSmemBytes = sizeof(SmemLayout) + 1024;  // + alignment slack
-static_assert(kSmemBytes <= 232448, "shared memory layout exceeds the 227 KB a CTA may use");
+template <int D>
+constexpr size_t smem_bytes() { return sizeof(SmemLayout<D>) + 1024; }  // + alignment slack
+static_assert(smem_bytes<64>() <= 232448 && smem_bytes<128>() <= 232448, "shared memory exceeds 227 KB per CTA");
 
 struct Item {
     int seq, head, row0[2], nblk[2];
 };
 
+template <int BN>
 __device__ __forceinline__ int tile_blocks(const PrefillArgs& a, int row0) {
     if (row0 >= a.tokens) return 0;
     const int last_row = min(row0 + kBM, a.tokens);  // exclusive
     const int visible = a.start + last_row;          // KV rows visible to the tile's last row
-    return (visible + kBN - 1) / kBN;
+    return (visible + BN - 1) / BN;
 }
 
+template <int BN>
 __device__ __forceinline__ Item decode_item(const PrefillArgs& a, int it) {
     const int per_rank = a.n_seqs * a.n_heads;
     const int rank = it / per_rank, rem = it - rank * per_rank;
@@ -106,47 +125,54 @@ __device__ __forceinline__ Item decode_item(const PrefillArgs& a, int it) {
     x.head = rem - x.seq * a.n_heads;
     x.row0[0] = pair * 2 * kBM;
     x.row0[1] = x.row0[0] + kBM;
-    x.nblk[0] = tile_blocks(a, x.row0[0]);
-    x.nblk[1] = tile_blocks(a, x.row0[1]);
+    x.nblk[0] = tile_blocks<BN>(a, x.row0[0]);
+    x.nblk[1] = tile_blocks<BN>(a, x.row0[1]);
     return x;
 }
 
 // ---------------------------------------------------------------------------------------------- MMA helpers
 
-// S_t = Q_t · K_stageᵀ: M=128, N=128, K=d (4 steps of 16); both operands K-major, 128-byte swizzle.
-__device__ __forceinline__ void mma_s(const SmemLayout* sm, int tile, int stage, uint32_t tmem_base) {
-    constexpr uint32_t idesc = idesc_f16_f32(kBM, kBN, false, false);
+// S_t = Q_t · K_stageᵀ: M=128, N=BN, K=D (D/16 steps of 16); both operands K-major, 128-byte swizzle. K step kk
+// lies in column block kk/4 at byte offset (kk%4)*32 of each 128-byte row.
+template <int D>
+__device__ __forceinline__ void mma_s(const SmemLayout<D>* sm, int tile, int stage, uint32_t tmem_base) {
+    using G = PG<D>;
+    constexpr uint32_t idesc = idesc_f16_f32(kBM, G::BN, false, false);
     const uint32_t qa = smem_u32(sm->q[tile]), ka = smem_u32(sm->k[stage]);
 #pragma unroll
-    for (int kk = 0; kk < kD / 16; kk++) {
-        const uint64_t ad = smem_desc_sw128(qa + kk * 32, 16, 1024);
-        const uint64_t bd = smem_desc_sw128(ka + kk * 32, 16, 1024);
-        tc_mma_ss(tmem_base + col_s(tile), ad, bd, idesc, kk > 0 ? 1u : 0u);
+    for (int kk = 0; kk < D / 16; kk++) {
+        const uint64_t ad = smem_desc_sw128(qa + (kk >> 2) * (kBM * 128) + (kk & 3) * 32, 16, 1024);
+        const uint64_t bd = smem_desc_sw128(ka + (kk >> 2) * (G::BN * 128) + (kk & 3) * 32, 16, 1024);
+        tc_mma_ss(tmem_base + G::col_s(tile), ad, bd, idesc, kk > 0 ? 1u : 0u);
     }
 }
 
-// O_t (+)= P_t · V_stage: M=128, N=d, K=128 (8 steps of 16). P in TMEM (8 columns of f16 pairs per step), V
-// MN-major in shared memory (16 KV rows = 2 KB per step).
-__device__ __forceinline__ void mma_pv(const SmemLayout* sm, int tile, int stage, uint32_t tmem_base,
+// O_t (+)= P_t · V_stage: M=128, N=D, K=BN (BN/16 steps of 16). P in TMEM (8 columns of f16 pairs per step), V
+// MN-major in shared memory: 16 KV rows = 2 KB per step, the next 64-column block BN*128 bytes further (LBO).
+template <int D>
+__device__ __forceinline__ void mma_pv(const SmemLayout<D>* sm, int tile, int stage, uint32_t tmem_base,
                                        bool accumulate) {
-    constexpr uint32_t idesc = idesc_f16_f32(kBM, kD, false, true);
+    using G = PG<D>;
+    constexpr uint32_t idesc = idesc_f16_f32(kBM, D, false, true);
     const uint32_t va = smem_u32(sm->v[stage]);
 #pragma unroll
-    for (int kk = 0; kk < kBN / 16; kk++) {
-        const uint64_t bd = smem_desc_sw128(va + kk * 16 * 128, kBN * 128, 1024);
-        tc_mma_ts(tmem_base + col_o(tile), tmem_base + col_p(tile) + kk * 8, bd, idesc,
+    for (int kk = 0; kk < G::BN / 16; kk++) {
+        const uint64_t bd = smem_desc_sw128(va + kk * 16 * 128, G::BN * 128, 1024);
+        tc_mma_ts(tmem_base + G::col_o(tile), tmem_base + G::col_p(tile) + kk * 8, bd, idesc,
                   (accumulate || kk > 0) ? 1u : 0u);
     }
 }
 
 // ---------------------------------------------------------------------------------------------- kernel
 
-template <int kEmuPairs>
+template <int D, int kEmuPairs>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const PrefillArgs a) {
+    using G = PG<D>;
+    constexpr int kBN = G::BN, SC = G::SC, OC = G::OC;
     extern __shared__ uint8_t smem_raw[];
-    SmemLayout* sm = reinterpret_cast<SmemLayout*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    auto* sm = reinterpret_cast<SmemLayout<D>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const bool debug_timeout = (a.flags & ALPACA_ATTN_FLAG_DEBUG_FORCE_TIMEOUT) != 0;
     AbortState ab{&sm->abort_flag, a.err, debug_timeout ? kDebugWaitLimitNs : kWaitLimitNs};
@@ -191,14 +217,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t kv_it = 0, k_issued = 0, v_issued = 0, q_uses[2] = {0, 0};
         bool ok = true;
         for (int it = blockIdx.x; ok && it < a.total_items; it += gridDim.x) {
-            const Item x = decode_item(a, it);
+            const Item x = decode_item<kBN>(a, it);
             const int kvh = x.head / (a.n_heads / a.n_kv_heads);
             for (int t = 0; t < 2 && ok; t++) {
                 if (x.nblk[t] == 0) continue;
                 ok = mbar_wait(&sm->q_empty[t], (q_uses[t] & 1) ^ 1, ab);
                 if (!ok) break;
-                mbar_arrive_expect_tx(&sm->q_full[t], kTileBytes);
-                tma_load_4d(sm->q[t], &tm_q, 0, x.head, x.row0[t], x.seq, &sm->q_full[t]);
+                mbar_arrive_expect_tx(&sm->q_full[t], G::kQBytes);
+#pragma unroll
+                for (int cb = 0; cb < G::CB; cb++)
+                    tma_load_4d(sm->q[t] + cb * kBM * 64, &tm_q, 64 * cb, x.head, x.row0[t], x.seq, &sm->q_full[t]);
                 q_uses[t]++;
             }
             const int nmax = max(x.nblk[0], x.nblk[1]);
@@ -207,13 +235,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t ph = (kv_it / kStages) & 1;
                 ok = mbar_wait(&sm->k_empty[st], ph ^ 1, ab);
                 if (!ok) break;
-                mbar_arrive_expect_tx(&sm->k_full[st], kTileBytes);
-                tma_load_4d(sm->k[st], &tm_k, 0, kvh, j * kBN, x.seq, &sm->k_full[st]);
+                mbar_arrive_expect_tx(&sm->k_full[st], G::kKVBytes);
+#pragma unroll
+                for (int cb = 0; cb < G::CB; cb++)
+                    tma_load_4d(sm->k[st] + cb * kBN * 64, &tm_k, 64 * cb, kvh, j * kBN, x.seq, &sm->k_full[st]);
                 k_issued = kv_it + 1;
                 ok = mbar_wait(&sm->v_empty[st], ph ^ 1, ab);
                 if (!ok) break;
-                mbar_arrive_expect_tx(&sm->v_full[st], kTileBytes);
-                tma_load_4d(sm->v[st], &tm_v, 0, kvh, j * kBN, x.seq, &sm->v_full[st]);
+                mbar_arrive_expect_tx(&sm->v_full[st], G::kKVBytes);
+#pragma unroll
+                for (int cb = 0; cb < G::CB; cb++)
+                    tma_load_4d(sm->v[st] + cb * kBN * 64, &tm_v, 64 * cb, kvh, j * kBN, x.seq, &sm->v_full[st]);
                 v_issued = kv_it + 1;
             }
         }
@@ -241,7 +273,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = true;
             if (debug_timeout && t == 0) ok = mbar_wait(&sm->dbg, 0, ab);  // nothing arrives: exercises the give-up path
             for (int it = blockIdx.x; ok && it < a.total_items; it += gridDim.x) {
-                const Item x = decode_item(a, it);
+                const Item x = decode_item<kBN>(a, it);
                 const int n = x.nblk[t];
                 const int nmax = max(x.nblk[0], x.nblk[1]);
                 if (n > 0) {
@@ -260,7 +292,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             ok = mbar_wait(&sm->s_empty[t], (s_uses & 1) ^ 1, ab);
                             if (!ok) break;
                             tc_fence_after();
-                            mma_s(sm, t, st, tmem_base);
+                            mma_s<D>(sm, t, st, tmem_base);
                             tc_commit(&sm->s_full[t]);
                             s_uses++;
                             if (j + 1 == n) tc_commit(&sm->q_empty[t]);
@@ -279,7 +311,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             ok = mbar_wait(&sm->p_full[t], p_uses & 1, ab);
                             if (!ok) break;
                             tc_fence_after();
-                            mma_pv(sm, t, sp, tmem_base, b > 0);
+                            mma_pv<D>(sm, t, sp, tmem_base, b > 0);
                             tc_commit(&sm->o_done[t]);
                             tc_commit(&sm->v_empty[sp]);
                             p_uses++;
@@ -315,18 +347,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ------------------------------------------------------------------ softmax warps
         const int sw = warp - 4;
         const int tile = sw >> 3;                   // query tile A (0) or B (1)
-        const int half = (sw >> 2) & 1;             // S columns [half*64, half*64 + 64) of each block
+        const int half = (sw >> 2) & 1;             // S columns [half*SC, half*SC + SC) of each block
         const int quarter = warp & 3;               // TMEM lane quarter this warp may access
         const int row = quarter * 32 + lane;        // query row within the tile = TMEM lane
         const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
-        const uint32_t s_addr = lane_addr + col_s(tile) + half * 64;
-        const uint32_t o_addr = lane_addr + col_o(tile) + half * 32;  // this thread's 32 context columns
-        const uint32_t p_addr = lane_addr + col_p(tile) + half * 32;  // this thread's 32 columns of P pairs
+        const uint32_t s_addr = lane_addr + G::col_s(tile) + half * SC;
+        const uint32_t o_addr = lane_addr + G::col_o(tile) + half * OC;      // this thread's OC context columns
+        const uint32_t p_addr = lane_addr + G::col_p(tile) + half * (SC / 2); // its SC/2 columns of P pairs
         uint64_t* xbar = &sm->xbar[tile][quarter];
         uint32_t s_uses = 0, o_uses = 0, x_uses = 0;
         bool ok = true;
         for (int it = blockIdx.x; ok && it < a.total_items; it += gridDim.x) {
-            const Item x = decode_item(a, it);
+            const Item x = decode_item<kBN>(a, it);
             const int nb = x.nblk[tile];
             if (nb == 0) continue;
             const int row0 = x.row0[tile];
@@ -338,30 +370,31 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!ok) break;
                 s_uses++;
                 tc_fence_after();
-                float s[64];
-                tmem_ld32(s_addr, s);
-                tmem_ld32(s_addr + 32, s + 32);
+                float s[SC];
+#pragma unroll
+                for (int c = 0; c < SC; c += 32) tmem_ld32(s_addr + c, s + c);
                 tmem_wait_ld();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&sm->s_empty[tile]);
 
-                const int kv0 = j * kBN + half * 64;
-                if (kv0 + 63 > a.start + row0) {  // these columns reach past the tile's first query: mask
+                const int kv0 = j * kBN + half * SC;
+                if (kv0 + SC - 1 > a.start + row0) {  // these columns reach past the tile's first query: mask
 #pragma unroll
-                    for (int c = 0; c < 64; c++)
+                    for (int c = 0; c < SC; c++)
                         if (kv0 + c > qpos) s[c] = -INFINITY;
                 }
-                // partial row max over 64 columns: 8 independent 3-input max chains, then a small tree
+                // partial row max over SC columns: 8 independent 3-input max chains, then a small tree
+                static_assert(SC % 16 == 0, "max tree expects SC = 8 + 16k + 8");
                 float mv[8];
 #pragma unroll
-                for (int i = 0; i < 8; i++) mv[i] = fmax3(s[i], s[8 + i], s[16 + i]);
+                for (int i = 0; i < 8; i++) mv[i] = s[i];
 #pragma unroll
-                for (int i = 0; i < 8; i++) mv[i] = fmax3(mv[i], s[24 + i], s[32 + i]);
+                for (int c = 8; c + 16 <= SC; c += 16)
 #pragma unroll
-                for (int i = 0; i < 8; i++) mv[i] = fmax3(mv[i], s[40 + i], s[48 + i]);
+                    for (int i = 0; i < 8; i++) mv[i] = fmax3(mv[i], s[c + i], s[c + 8 + i]);
 #pragma unroll
-                for (int i = 0; i < 8; i++) mv[i] = fmaxf(mv[i], s[56 + i]);
+                for (int i = 0; i < 8; i++) mv[i] = fmaxf(mv[i], s[SC - 8 + i]);
                 const float pmax = fmaxf(fmax3(mv[0], mv[1], mv[2]), fmax3(fmax3(mv[3], mv[4], mv[5]), mv[6], mv[7]));
                 // This half's candidate max (log2 units): the running max unless these columns exceed it by more
                 // than the threshold. The two halves publish their candidates and compute P against their own
@@ -379,11 +412,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // subtracts 0 instead, giving P = 0.
                 const float m_sub = (m_mine == -INFINITY) ? 0.f : m_mine;
                 const float2 c2 = make_float2(a.scale_log2, a.scale_log2), nm2 = make_float2(-m_sub, -m_sub);
-                uint32_t pk[32];
+                uint32_t pk[SC / 2];
                 float2 ls[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                                 make_float2(0.f, 0.f)};  // four independent partial sums (no serial chain)
 #pragma unroll
-                for (int pr = 0; pr < 32; pr++) {
+                for (int pr = 0; pr < SC / 2; pr++) {
                     const float2 xx = __ffma2_rn(make_float2(s[2 * pr], s[2 * pr + 1]), c2, nm2);
                     float2 e;
                     if ((pr & 7) < kEmuPairs) e = exp2_poly2(make_float2(fmaxf(xx.x, -125.f), fmaxf(xx.y, -125.f)));
@@ -402,7 +435,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const __half2 f2 = __float2half2_rn(ex2_approx(m_mine - m_row));  // 1 where m_mine == m_row
                     const float f = __low2float(f2);
 #pragma unroll
-                    for (int pr = 0; pr < 32; pr++) {
+                    for (int pr = 0; pr < SC / 2; pr++) {
                         __half2 h = *reinterpret_cast<__half2*>(&pk[pr]);
                         h = __hmul2(h, f2);
                         pk[pr] = *reinterpret_cast<uint32_t*>(&h);
@@ -429,14 +462,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // tcgen05.ld/st are warp-collective: the whole warp rescales when any of its rows must (alpha
                 // stays 1 for the others)
                 if (__any_sync(0xffffffffu, rescale)) {
-                    float o[32];
-                    tmem_ld32(o_addr, o);
-                    tmem_wait_ld();
 #pragma unroll
-                    for (int c = 0; c < 32; c++) o[c] *= alpha;
-                    tmem_st32(o_addr, o);
+                    for (int c0 = 0; c0 < OC; c0 += 32) {
+                        float o[32];
+                        tmem_ld32(o_addr + c0, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int c = 0; c < 32; c++) o[c] *= alpha;
+                        tmem_st32(o_addr + c0, o);
+                    }
                 }
-                tmem_st32(p_addr, reinterpret_cast<const float*>(pk));
+                if constexpr (SC / 2 == 32) tmem_st32(p_addr, reinterpret_cast<const float*>(pk));
+                else tmem_st16(p_addr, reinterpret_cast<const float*>(pk));
                 tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
@@ -448,8 +485,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!ok) break;
             o_uses++;
             tc_fence_after();
-            float o[32];
-            tmem_ld32(o_addr, o);
+            float o[OC];
+#pragma unroll
+            for (int c0 = 0; c0 < OC; c0 += 32) tmem_ld32(o_addr + c0, o + c0);
             const float lpart = lsum.x + lsum.y;
             sm->xl[tile][half][row] = lpart;
             __threadfence_block();
@@ -465,11 +503,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (t < a.tokens) {
                 const float inv = 1.f / l;
                 const int64_t off = x.seq * a.out_seq_stride + static_cast<int64_t>(t) * a.out_token_stride +
-                                    static_cast<int64_t>(x.head) * kD + half * 32;
+                                    static_cast<int64_t>(x.head) * D + half * OC;
                 if (a.out_f16) {
                     uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(a.out) + off);
 #pragma unroll
-                    for (int c = 0; c < 32; c += 8)
+                    for (int c = 0; c < OC; c += 8)
                         dst[c / 8] = make_uint4(pack_half2(o[c] * inv, o[c + 1] * inv),
                                                 pack_half2(o[c + 2] * inv, o[c + 3] * inv),
                                                 pack_half2(o[c + 4] * inv, o[c + 5] * inv),
@@ -477,7 +515,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 } else {
                     float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + off);
 #pragma unroll
-                    for (int c = 0; c < 32; c += 4)
+                    for (int c = 0; c < OC; c += 4)
                         dst[c / 4] = make_float4(o[c] * inv, o[c + 1] * inv, o[c + 2] * inv, o[c + 3] * inv);
                 }
             }
@@ -520,9 +558,10 @@ EncodeTiledFn get_encode_fn() {
     return fn;
 }
 
-// 4-D f16 map over [seqs][rows][heads][d] with a 64 x 1 x 128 x 1 box, 128-byte swizzle, zero fill.
+// 4-D f16 map over [seqs][rows][heads][d] with a 64 x 1 x box_rows x 1 box (one 128-byte column block of
+// box_rows rows), 128-byte swizzle, zero fill.
 bool make_map(CUtensorMap* map, const void* base, int d, int heads, int rows, int seqs, int64_t row_stride,
-              int64_t seq_stride) {
+              int64_t seq_stride, int box_rows) {
     EncodeTiledFn enc = get_encode_fn();
     if (!enc) return false;
     if (seqs == 1 || seq_stride == 0) seq_stride = static_cast<int64_t>(rows) * row_stride;
@@ -530,7 +569,7 @@ bool make_map(CUtensorMap* map, const void* base, int d, int heads, int rows, in
                           static_cast<cuuint64_t>(seqs)};
     cuuint64_t strides[3] = {static_cast<cuuint64_t>(d) * 2, static_cast<cuuint64_t>(row_stride) * 2,
                              static_cast<cuuint64_t>(seq_stride) * 2};
-    cuuint32_t box[4] = {64, 1, 128, 1};
+    cuuint32_t box[4] = {64, 1, static_cast<cuuint32_t>(box_rows), 1};
     cuuint32_t estr[4] = {1, 1, 1, 1};
     CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -553,19 +592,20 @@ int prefill_emu_pairs() {
 
 using PrefillFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, PrefillArgs);
 
+template <int D>
 PrefillFn prefill_variant(int emu) {
     switch (emu) {
-        case 0: return prefill_kernel<0>;
-        case 3: return prefill_kernel<3>;
-        case 4: return prefill_kernel<4>;
-        default: return prefill_kernel<2>;
+        case 0: return prefill_kernel<D, 0>;
+        case 3: return prefill_kernel<D, 3>;
+        case 4: return prefill_kernel<D, 4>;
+        default: return prefill_kernel<D, 2>;
     }
 }
 
 }  // namespace
 
 bool prefill_supported(const alpaca_attn_desc& d) {
-    return d.head_dim == kD && d.kv_dtype == ALPACA_F16 && d.n_kv_heads > 0 && d.n_heads % d.n_kv_heads == 0 &&
+    return (d.head_dim == 64 || d.head_dim == 128) && d.kv_dtype == ALPACA_F16 && d.n_kv_heads > 0 && d.n_heads % d.n_kv_heads == 0 &&
            d.ctx_lens == nullptr;
 }
 
@@ -576,10 +616,13 @@ size_t prefill_workspace_bytes(const alpaca_attn_desc& d) {
 
 cudaError_t launch_prefill(const Call& c, cudaStream_t s) {
     const alpaca_attn_desc& d = *c.d;
-    const PrefillFn fn = prefill_variant(prefill_emu_pairs());
+    const bool d128 = d.head_dim == 128;
+    const PrefillFn fn = d128 ? prefill_variant<128>(prefill_emu_pairs()) : prefill_variant<64>(prefill_emu_pairs());
+    const size_t smem = d128 ? smem_bytes<128>() : smem_bytes<64>();
+    const int bn = d128 ? PG<128>::BN : PG<64>::BN;
     // per-device function attribute (host-side, cheap next to the launch itself)
     cudaError_t attr_err = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
-                                                cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (attr_err != cudaSuccess) return attr_err;
 
     const void* qh = d.q;
@@ -599,9 +642,9 @@ cudaError_t launch_prefill(const Call& c, cudaStream_t s) {
     }
     const int kv_len = d.start_position + d.tokens;
     CUtensorMap tq, tk, tv;
-    if (!make_map(&tq, qh, d.head_dim, d.n_heads, d.tokens, d.n_seqs, q_ts, q_ss) ||
-        !make_map(&tk, d.k, d.head_dim, d.n_kv_heads, kv_len, d.n_seqs, d.kv_row_stride, d.kv_seq_stride) ||
-        !make_map(&tv, d.v, d.head_dim, d.n_kv_heads, kv_len, d.n_seqs, d.kv_row_stride, d.kv_seq_stride))
+    if (!make_map(&tq, qh, d.head_dim, d.n_heads, d.tokens, d.n_seqs, q_ts, q_ss, kBM) ||
+        !make_map(&tk, d.k, d.head_dim, d.n_kv_heads, kv_len, d.n_seqs, d.kv_row_stride, d.kv_seq_stride, bn) ||
+        !make_map(&tv, d.v, d.head_dim, d.n_kv_heads, kv_len, d.n_seqs, d.kv_row_stride, d.kv_seq_stride, bn))
         return cudaErrorInvalidValue;
 
     PrefillArgs a;
@@ -621,7 +664,7 @@ cudaError_t launch_prefill(const Call& c, cudaStream_t s) {
     a.err = c.err;
     a.flags = d.flags;
     const int grid = std::max(1, std::min(a.total_items, c.num_sms));
-    fn<<<grid, kThreads, kSmemBytes, s>>>(tq, tk, tv, a);
+    fn<<<grid, kThreads, smem, s>>>(tq, tk, tv, a);
     return cudaGetLastError();
 }
 

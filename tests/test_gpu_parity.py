@@ -83,16 +83,17 @@ def test_tiled_attention_matches_cpu_reference(cuda_lib):
 
 
 def test_tensor_core_prefill_on_tiled_cases(cuda_lib):
-    """The tcgen05 kernel forced on every d=64 tiled case and on short prefills (T < 8 go to the general kernel
-    under the dispatch policy)."""
+    """The tcgen05 kernel forced on every tiled case (head_dim 64 and 128) and on short prefills (T < 8 go to the
+    general kernel under the dispatch policy)."""
     from alpaca_b200 import Kernel, attention
-    cases = [c for c in TILED_CASES if c[4] == 64] + [(2, 0, 9, 3, 64), (5, 9, 4, 1, 64), (1, 300, 9, 3, 64)]
+    cases = list(TILED_CASES) + [(2, 0, 9, 3, 64), (5, 9, 4, 1, 64), (1, 300, 9, 3, 64), (3, 70, 8, 2, 128),
+                                 (1, 65, 4, 4, 128)]
     for t, start, heads, kv, hd in cases:
         cap = start + t
         q, k, v = _uniform_stream(t * 131 + start, (t, heads, hd), (cap, kv, hd), (cap, kv, hd))
         cpu = oracle.attention(q, oracle.f16_round(k), oracle.f16_round(v), start)
         gpu = attention(q, k, v, start, kind=Kernel.PREFILL_TC)
-        max_abs_check(gpu, cpu, 1.5e-3, f"tcgen05 prefill T={t} start={start} H={heads}/{kv}")
+        max_abs_check(gpu, cpu, 1.5e-3, f"tcgen05 prefill T={t} start={start} H={heads}/{kv} hd={hd}")
 
 
 # ---------------------------------------------------------------------------------------------- BASELINE configs
@@ -144,6 +145,21 @@ def test_config2_prefill_135m(cuda_lib, T):
         max_abs_check(gpu[s][sel], cpu[sel], F16_BOUND, f"config 2 prefill T={T} layer {s}")
 
 
+def test_prefill_head_dim_128(cuda_lib):
+    """head_dim 128 (the reference's attn_tensor_hd128 / attn_prefill_hd128_kv16): 2 sequences x 2048 tokens, 8/2
+    heads, f16 N(0,1), every 5th (head, token) row against the oracle at the f16 bound."""
+    T, H, kvh, d, S = 2048, 8, 2, 128, 2
+    qs = np.stack([_normal(60 + s, (T, H, d)) for s in range(S)])
+    ks = np.stack([_normal(62 + s, (T, kvh, d)) for s in range(S)])
+    vs = np.stack([_normal(64 + s, (T, kvh, d)) for s in range(S)])
+    gpu = _device_prefill(qs, ks, vs, 0)
+    for s in range(S):
+        rows = np.arange(0, H * T, 5)
+        cpu = oracle.attention_rows(qs[s], ks[s], vs[s], 0, rows)
+        sel = oracle.rows_mask(rows, T, H)
+        max_abs_check(gpu[s][sel], cpu[sel], F16_BOUND, f"prefill d=128 T={T} seq {s}")
+
+
 def test_config3_decode_ragged_batch(cuda_lib):
     """Config 3: batch 64 single-token decode, 9/3 heads, f16 KV with per-sequence lengths uniform in [1,4096]
     (device ctx_lens), N(0,1)."""
@@ -183,10 +199,11 @@ def test_config4_prefill_360m_batch(cuda_lib):
         max_abs_check(gpu[s][sel], cpu[sel], F16_BOUND, f"config 4 prefill seq {s}")
 
 
-def test_prefill_layouts(cuda_lib):
+@pytest.mark.parametrize("d", [64, 128])
+def test_prefill_layouts(cuda_lib, d):
     """Chunked prefill over a longer cache, f32 queries (converted in the workspace), f16 output, strided rows."""
     from alpaca_b200 import Kernel
-    T, start, H, kvh, d = 300, 517, 12, 4, 64
+    T, start, H, kvh = 300, 517, 12, 4
     q = _normal(101, (1, T, H, d))
     k = _normal(102, (1, start + T + 40, kvh, d))
     v = _normal(103, (1, start + T + 40, kvh, d))
@@ -195,7 +212,7 @@ def test_prefill_layouts(cuda_lib):
         for odt in (torch.float32, torch.float16):
             gpu = _device_prefill(q, k, v, start, out_dtype=odt, kind=Kernel.PREFILL_TC, q_dtype=qdt)
             bound = F16_BOUND + (1e-3 if odt == torch.float16 else 0.0)
-            max_abs_check(gpu[0], cpu, bound, f"prefill chunk start={start} q={qdt} out={odt}")
+            max_abs_check(gpu[0], cpu, bound, f"prefill chunk d={d} start={start} q={qdt} out={odt}")
 
 
 def test_strided_cache_views(cuda_lib):
@@ -218,10 +235,11 @@ def test_strided_cache_views(cuda_lib):
         max_abs_check(out.cpu().numpy(), cpu, F16_BOUND, f"strided cache {kind.name}")
 
 
-def test_pad_rows_never_read(cuda_lib):
+@pytest.mark.parametrize("d", [64, 128])
+def test_pad_rows_never_read(cuda_lib, d):
     """Rows past start+tokens may hold anything (here NaN): outputs stay finite and equal the clean run."""
     from alpaca_b200 import Kernel, attention_device, device_status
-    T, start, H, kvh, d = 100, 30, 9, 3, 64
+    T, start, H, kvh = 100, 30, 9, 3
     L = start + T
     q = _normal(121, (T, H, d))
     k = _normal(122, (L, kvh, d))
@@ -236,15 +254,16 @@ def test_pad_rows_never_read(cuda_lib):
         out = torch.empty((T, H, d), dtype=torch.float32, device=dev)
         attention_device(torch.from_numpy(q).to(dev).half(), kd, vd, out, start_position=start, kind=kind)
         device_status()
-        max_abs_check(out.cpu().numpy(), cpu, F16_BOUND, f"NaN tail {kind.name}")
+        max_abs_check(out.cpu().numpy(), cpu, F16_BOUND, f"NaN tail {kind.name} d={d}")
 
 
-def test_large_scores_rescale_path(cuda_lib):
+@pytest.mark.parametrize("d", [64, 128])
+def test_large_scores_rescale_path(cuda_lib, d):
     """Scores with a large spread (q scaled by 6, rows whose max jumps between blocks) exercise the O rescale.
     The data is outside the N(0,1) regime the 2e-3 bound is stated for (attention is nearly one-hot), so the bound
     is the reference's own tolerance basis for f16 P/K/V (KernelTests.swift:116-121): 3 * 2^-11 * max|V|."""
     from alpaca_b200 import Kernel, attention_device, device_status
-    T, H, kvh, d = 512, 4, 2, 64
+    T, H, kvh = 512, 4, 2
     q = oracle.f16_round(oracle.splitmix_normal(131, (T, H, d)) * 6.0)
     k = _normal(132, (T, kvh, d))
     k[300:310] *= 4.0   # late keys with much larger scores than the first blocks
@@ -256,4 +275,4 @@ def test_large_scores_rescale_path(cuda_lib):
     attention_device(torch.from_numpy(q).to(dev).half(), torch.from_numpy(k).to(dev).half(),
                      torch.from_numpy(v).to(dev).half(), out, kind=Kernel.PREFILL_TC)
     device_status()
-    max_abs_check(out.cpu().numpy(), cpu, 3 * 2.0 ** -11 * float(np.abs(v).max()), "rescale path")
+    max_abs_check(out.cpu().numpy(), cpu, 3 * 2.0 ** -11 * float(np.abs(v).max()), f"rescale path d={d}")
