@@ -64,6 +64,12 @@ class AttnDesc(ctypes.Structure):
         ("out_seq_stride", ctypes.c_int64),
         ("scale", ctypes.c_float),
         ("flags", ctypes.c_uint32),
+        ("block_table", ctypes.c_void_p),
+        ("block_rows", ctypes.c_int32),
+        ("max_blocks", ctypes.c_int32),
+        ("block_stride", ctypes.c_int64),
+        ("pool_blocks", ctypes.c_int32),
+        ("reserved1", ctypes.c_int32),
     ]
 
 

@@ -111,7 +111,7 @@ alpaca_cuda_status validate(const alpaca_attn_desc* dp) {
         return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "attention: row strides smaller than a row: " + sh);
     if (d.q_seq_stride < 0 || d.kv_seq_stride < 0 || d.out_seq_stride < 0)
         return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "attention: negative sequence stride");
-    if (d.n_seqs > 1 && (d.q_seq_stride == 0 || d.kv_seq_stride == 0 || d.out_seq_stride == 0))
+    if (d.n_seqs > 1 && (d.q_seq_stride == 0 || (!d.block_table && d.kv_seq_stride == 0) || d.out_seq_stride == 0))
         return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "attention: zero sequence stride with several sequences");
     const int64_t qs = static_cast<int64_t>(dtype_size(d.q_dtype)), ks = dtype_size(d.kv_dtype), os = dtype_size(d.out_dtype);
     if ((d.q_token_stride * qs) % 16 || (d.q_seq_stride * qs) % 16 || (d.kv_row_stride * ks) % 16 ||
@@ -127,6 +127,17 @@ alpaca_cuda_status validate(const alpaca_attn_desc* dp) {
         return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "attention: positions out of range: " + sh);
     if (!(d.scale >= 0.f) || !std::isfinite(d.scale))
         return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "attention: scale must be finite and >= 0");
+    if (d.block_table) {  // paged cache
+        const int64_t rows_needed = d.ctx_lens ? d.max_ctx_len : static_cast<int64_t>(d.start_position) + d.tokens;
+        if (d.block_rows < 128 || d.block_rows % 128 != 0)
+            return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "attention: block_rows must be a positive multiple of 128");
+        if (d.max_blocks < 1 || d.pool_blocks < 1 ||
+            rows_needed > static_cast<int64_t>(d.max_blocks) * d.block_rows)
+            return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "attention: block table too short for the context: " + sh);
+        if (d.block_stride < static_cast<int64_t>(d.block_rows) * d.kv_row_stride || (d.block_stride * ks) % 16)
+            return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT,
+                        "attention: block_stride must cover block_rows rows and be a multiple of 16 bytes");
+    }
     return ok();
 }
 
@@ -176,6 +187,8 @@ alpaca_cuda_status validate_rope(const alpaca_rope_desc* dp) {
 
 // KernelEncoder.attention's policy (KernelEncoder.swift:309-343).
 alpaca_attn_kernel select_kernel(const alpaca_attn_desc& d) {
+    if (d.block_table)  // a paged cache is read by the split decode (any context) and the tensor-core prefill only
+        return (d.tokens == 1 && decode_supported(d)) ? ALPACA_ATTN_DECODE_SPLIT : ALPACA_ATTN_PREFILL_TC;
     const int ctx = d.ctx_lens ? d.max_ctx_len : d.start_position + 1;
     if (d.tokens == 1 && decode_supported(d) && (d.ctx_lens || ctx >= decode_min_ctx())) return ALPACA_ATTN_DECODE_SPLIT;
     if (d.tokens >= kPrefillMinTokens && prefill_supported(d)) return ALPACA_ATTN_PREFILL_TC;
@@ -199,9 +212,13 @@ alpaca_cuda_status check_kind(const alpaca_attn_desc& d, alpaca_attn_kernel k) {
             return ok();
         case ALPACA_ATTN_PREFILL_TC:
             if (!prefill_supported(d))
-                return fail(ALPACA_CUDA_ERR_UNSUPPORTED, "tensor-core prefill needs f16 KV and headDim 64: " + shape_str(d));
+                return fail(ALPACA_CUDA_ERR_UNSUPPORTED,
+                            "tensor-core prefill needs f16 KV and headDim 64/128: " + shape_str(d));
             return ok();
-        case ALPACA_ATTN_GENERAL: return ok();
+        case ALPACA_ATTN_GENERAL:
+            if (d.block_table)
+                return fail(ALPACA_CUDA_ERR_UNSUPPORTED, "the general kernel reads contiguous caches only (paged cache given)");
+            return ok();
         default: return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "attention: unknown kernel kind");
     }
 }
@@ -310,7 +327,7 @@ alpaca_cuda_status alpaca_attention_select(const alpaca_attn_desc* desc, alpaca_
     alpaca_cuda_status st = validate(desc);
     if (st != ALPACA_CUDA_OK) return st;
     *kind = select_kernel(*desc);
-    return ok();
+    return check_kind(*desc, *kind);  // UNSUPPORTED when no kernel can serve it (only possible with a paged cache)
 }
 
 alpaca_cuda_status alpaca_cuda_device_status(alpaca_stream_t stream, int clear) {
@@ -325,6 +342,8 @@ alpaca_cuda_status alpaca_cuda_device_status(alpaca_stream_t stream, int clear) 
         if (e != cudaSuccess) return fail(ALPACA_CUDA_ERR_CUDA, std::string("device status: ") + cudaGetErrorString(e));
     }
     if (word & kDevErrTimeout) return fail(ALPACA_CUDA_ERR_DEVICE_TIMEOUT, "a bounded device-side wait gave up");
+    if (word & kDevErrBadIndex)
+        return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "a block table entry lay outside the KV pool (rows read as zero)");
     if (word) return fail(ALPACA_CUDA_ERR_CUDA, "device error word " + std::to_string(word));
     return ok();
 }

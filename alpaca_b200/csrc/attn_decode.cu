@@ -53,7 +53,30 @@ struct DecodeArgs {
     int uniform_len;
     int n_heads, n_kv_heads, max_splits;
     float scale_log2;
+    const int* block_table;  // paged cache: [seq][max_blocks] block indices (null: contiguous caches)
+    int block_rows, max_blocks, pool_blocks;
+    int64_t block_stride;
+    unsigned* err;
 };
+
+// Element offset of cache row `row0` of KV head `kvh` of sequence `seq` (contiguous, or through the block table;
+// a unit's SL rows never cross a block because block_rows is a multiple of 128). A table entry outside the pool
+// clears `valid` (the unit's rows are then zero-filled, not read) and raises the device error word.
+__device__ __forceinline__ int64_t unit_offset(const DecodeArgs& a, int seq, int kvh, int row0, int D, bool& valid) {
+    valid = true;
+    if (a.block_table) {
+        const int blk = a.block_table[static_cast<int64_t>(seq) * a.max_blocks + row0 / a.block_rows];
+        if (blk < 0 || blk >= a.pool_blocks) {
+            valid = false;
+            atomicOr(a.err, kDevErrBadIndex);
+            return 0;
+        }
+        return static_cast<int64_t>(blk) * a.block_stride + static_cast<int64_t>(row0 % a.block_rows) * a.kv_row_stride +
+               static_cast<int64_t>(kvh) * D;
+    }
+    return static_cast<int64_t>(seq) * a.kv_seq_stride + static_cast<int64_t>(row0) * a.kv_row_stride +
+           static_cast<int64_t>(kvh) * D;
+}
 
 __device__ __forceinline__ int ctx_len_of(const DecodeArgs& a, int s) {
     return a.ctx_lens ? a.ctx_lens[s] : a.uniform_len;
@@ -117,19 +140,20 @@ template <int D>
 __device__ __forceinline__ void stage_unit(const DecodeArgs& a, int seq, int kvh, int row0, int row_end,
                                            __half* s_k, __half* s_v, int lr, int rowlane) {
     constexpr int RPS = Geo<D>::RPS;
-    const int64_t seq_off = static_cast<int64_t>(seq) * a.kv_seq_stride + static_cast<int64_t>(kvh) * D + lr * 8;
+    bool valid;
+    const int64_t base = unit_offset(a, seq, kvh, row0, D, valid) + lr * 8;
 #pragma unroll
     for (int i = 0; i < kSlots; i++) {
         const int rl = i * RPS + rowlane, r = row0 + rl;
-        const bool in = r < row_end;
-        cp_async16(s_k + rl * D + lr * 8, a.k + seq_off + (in ? static_cast<int64_t>(r) * a.kv_row_stride : 0), in ? 16u : 0u);
+        const bool in = valid && r < row_end;
+        cp_async16(s_k + rl * D + lr * 8, a.k + base + (in ? static_cast<int64_t>(rl) * a.kv_row_stride : 0), in ? 16u : 0u);
     }
     cp_async_commit();
 #pragma unroll
     for (int i = 0; i < kSlots; i++) {
         const int rl = i * RPS + rowlane, r = row0 + rl;
-        const bool in = r < row_end;
-        cp_async16(s_v + rl * D + lr * 8, a.v + seq_off + (in ? static_cast<int64_t>(r) * a.kv_row_stride : 0), in ? 16u : 0u);
+        const bool in = valid && r < row_end;
+        cp_async16(s_v + rl * D + lr * 8, a.v + base + (in ? static_cast<int64_t>(rl) * a.kv_row_stride : 0), in ? 16u : 0u);
     }
     cp_async_commit();
 }
@@ -497,6 +521,12 @@ cudaError_t launch_decode(const Call& c, cudaStream_t s) {
     a.n_kv_heads = d.n_kv_heads;
     a.max_splits = decode_max_splits(d);
     a.scale_log2 = c.scale * kLog2e;
+    a.block_table = d.block_table;
+    a.block_rows = d.block_rows;
+    a.max_blocks = d.max_blocks;
+    a.pool_blocks = d.pool_blocks;
+    a.block_stride = d.block_stride;
+    a.err = c.err;
     if (a.max_splits < 1) return cudaSuccess;
     return d.head_dim == 128 ? launch_d<128>(a, d.n_seqs, s) : launch_d<64>(a, d.n_seqs, s);
 }

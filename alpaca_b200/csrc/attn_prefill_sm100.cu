@@ -81,6 +81,8 @@ struct PrefillArgs {
     float scale_log2;
     unsigned* err;
     unsigned flags;
+    const int* block_table;  // paged cache: [seq][max_blocks] (null: contiguous caches)
+    int block_rows, max_blocks, pool_blocks, last_block;  // last_block: block (of a sequence) holding row kv_len - 1
 };
 
 template <int D>
@@ -168,7 +170,8 @@ __device__ __forceinline__ void mma_pv(const SmemLayout<D>* sm, int tile, int st
 template <int D, int kEmuPairs>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                   const __grid_constant__ CUtensorMap tm_v, const PrefillArgs a) {
+                   const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_kt,
+                   const __grid_constant__ CUtensorMap tm_vt, const PrefillArgs a) {
     using G = PG<D>;
     constexpr int kBN = G::BN, SC = G::SC, OC = G::OC;
     extern __shared__ uint8_t smem_raw[];
@@ -201,6 +204,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_prefetch_desc(&tm_q);
         tma_prefetch_desc(&tm_k);
         tma_prefetch_desc(&tm_v);
+        if (a.block_table) {
+            tma_prefetch_desc(&tm_kt);
+            tma_prefetch_desc(&tm_vt);
+        }
     }
     if (warp == 2) {
         tmem_alloc(&sm->tmem_base, kTmemCols);
@@ -233,19 +240,38 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; ok && j < nmax; j++, kv_it++) {
                 const int st = kv_it % kStages;
                 const uint32_t ph = (kv_it / kStages) & 1;
+                // Contiguous caches: coordinates (row, sequence) of the per-sequence map. Paged: (row within the
+                // block, pool block); blocks holding the last visible row use the tail maps, whose row extent ends
+                // at that row, so rows past the context are zero-filled rather than read from the pool.
+                int crow = j * kBN, cseq = x.seq;
+                const CUtensorMap* mk = &tm_k;
+                const CUtensorMap* mv = &tm_v;
+                if (a.block_table) {
+                    const int blk = crow / a.block_rows;
+                    cseq = a.block_table[static_cast<int64_t>(x.seq) * a.max_blocks + blk];
+                    crow -= blk * a.block_rows;
+                    if (cseq < 0 || cseq >= a.pool_blocks) {  // outside the pool: the TMA zero-fills the rows
+                        atomicOr(a.err, kDevErrBadIndex);
+                        cseq = a.pool_blocks;
+                    }
+                    if (blk == a.last_block) {
+                        mk = &tm_kt;
+                        mv = &tm_vt;
+                    }
+                }
                 ok = mbar_wait(&sm->k_empty[st], ph ^ 1, ab);
                 if (!ok) break;
                 mbar_arrive_expect_tx(&sm->k_full[st], G::kKVBytes);
 #pragma unroll
                 for (int cb = 0; cb < G::CB; cb++)
-                    tma_load_4d(sm->k[st] + cb * kBN * 64, &tm_k, 64 * cb, kvh, j * kBN, x.seq, &sm->k_full[st]);
+                    tma_load_4d(sm->k[st] + cb * kBN * 64, mk, 64 * cb, kvh, crow, cseq, &sm->k_full[st]);
                 k_issued = kv_it + 1;
                 ok = mbar_wait(&sm->v_empty[st], ph ^ 1, ab);
                 if (!ok) break;
                 mbar_arrive_expect_tx(&sm->v_full[st], G::kKVBytes);
 #pragma unroll
                 for (int cb = 0; cb < G::CB; cb++)
-                    tma_load_4d(sm->v[st] + cb * kBN * 64, &tm_v, 64 * cb, kvh, j * kBN, x.seq, &sm->v_full[st]);
+                    tma_load_4d(sm->v[st] + cb * kBN * 64, mv, 64 * cb, kvh, crow, cseq, &sm->v_full[st]);
                 v_issued = kv_it + 1;
             }
         }
@@ -590,7 +616,7 @@ int prefill_emu_pairs() {
     return v;
 }
 
-using PrefillFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, PrefillArgs);
+using PrefillFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, PrefillArgs);
 
 template <int D>
 PrefillFn prefill_variant(int emu) {
@@ -641,11 +667,25 @@ cudaError_t launch_prefill(const Call& c, cudaStream_t s) {
         q_ss = static_cast<int64_t>(d.tokens) * hd_total;
     }
     const int kv_len = d.start_position + d.tokens;
-    CUtensorMap tq, tk, tv;
-    if (!make_map(&tq, qh, d.head_dim, d.n_heads, d.tokens, d.n_seqs, q_ts, q_ss, kBM) ||
-        !make_map(&tk, d.k, d.head_dim, d.n_kv_heads, kv_len, d.n_seqs, d.kv_row_stride, d.kv_seq_stride, bn) ||
-        !make_map(&tv, d.v, d.head_dim, d.n_kv_heads, kv_len, d.n_seqs, d.kv_row_stride, d.kv_seq_stride, bn))
-        return cudaErrorInvalidValue;
+    CUtensorMap tq, tk, tv, tkt, tvt;
+    if (!make_map(&tq, qh, d.head_dim, d.n_heads, d.tokens, d.n_seqs, q_ts, q_ss, kBM)) return cudaErrorInvalidValue;
+    int last_block = -1;
+    if (d.block_table) {
+        // pool maps: [pool_blocks][block_rows] rows; tail maps end at the last visible row of its block
+        last_block = (kv_len - 1) / d.block_rows;
+        const int tail_rows = kv_len - last_block * d.block_rows;
+        if (!make_map(&tk, d.k, d.head_dim, d.n_kv_heads, d.block_rows, d.pool_blocks, d.kv_row_stride, d.block_stride, bn) ||
+            !make_map(&tv, d.v, d.head_dim, d.n_kv_heads, d.block_rows, d.pool_blocks, d.kv_row_stride, d.block_stride, bn) ||
+            !make_map(&tkt, d.k, d.head_dim, d.n_kv_heads, tail_rows, d.pool_blocks, d.kv_row_stride, d.block_stride, bn) ||
+            !make_map(&tvt, d.v, d.head_dim, d.n_kv_heads, tail_rows, d.pool_blocks, d.kv_row_stride, d.block_stride, bn))
+            return cudaErrorInvalidValue;
+    } else {
+        if (!make_map(&tk, d.k, d.head_dim, d.n_kv_heads, kv_len, d.n_seqs, d.kv_row_stride, d.kv_seq_stride, bn) ||
+            !make_map(&tv, d.v, d.head_dim, d.n_kv_heads, kv_len, d.n_seqs, d.kv_row_stride, d.kv_seq_stride, bn))
+            return cudaErrorInvalidValue;
+        tkt = tk;
+        tvt = tv;
+    }
 
     PrefillArgs a;
     a.out = d.out;
@@ -663,8 +703,13 @@ cudaError_t launch_prefill(const Call& c, cudaStream_t s) {
     a.scale_log2 = c.scale * kLog2e;
     a.err = c.err;
     a.flags = d.flags;
+    a.block_table = d.block_table;
+    a.block_rows = d.block_rows;
+    a.max_blocks = d.max_blocks;
+    a.pool_blocks = d.pool_blocks;
+    a.last_block = last_block;
     const int grid = std::max(1, std::min(a.total_items, c.num_sms));
-    fn<<<grid, kThreads, smem, s>>>(tq, tk, tv, a);
+    fn<<<grid, kThreads, smem, s>>>(tq, tk, tv, tkt, tvt, a);
     return cudaGetLastError();
 }
 

@@ -46,8 +46,10 @@ def _as4(t: torch.Tensor, name: str) -> torch.Tensor:
 
 def make_desc(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor, *, start_position: int = 0,
               ctx_lens: torch.Tensor | None = None, max_ctx_len: int | None = None, scale: float = 0.0,
-              flags: int = 0) -> AttnDesc:
-    """Descriptor for q [S,T,H,d], k/v [S,rows,Hkv,d], out [S,T,H,d] (3-D tensors mean S = 1)."""
+              flags: int = 0, block_table: torch.Tensor | None = None) -> AttnDesc:
+    """Descriptor for q [S,T,H,d], k/v [S,rows,Hkv,d], out [S,T,H,d] (3-D tensors mean S = 1). With
+    `block_table` (CUDA int32 [S, max_blocks]) k and v are block pools [pool_blocks, block_rows, Hkv, d] and row r
+    of sequence s is row r % block_rows of block block_table[s, r // block_rows]."""
     q4, k4, v4, o4 = _as4(q, "q"), _as4(k, "k"), _as4(v, "v"), _as4(out, "out")
     if k4.stride() != v4.stride() or k4.shape != v4.shape or k4.dtype != v4.dtype:
         raise AlpacaCUDAError(Status.INVALID_ARGUMENT, "k and v must share shape, dtype and strides")
@@ -64,6 +66,14 @@ def make_desc(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tens
     d_.q, d_.q_token_stride, d_.q_seq_stride = q4.data_ptr(), q4.stride(1), q4.stride(0) if S > 1 else 0
     d_.k, d_.v = k4.data_ptr(), v4.data_ptr()
     d_.kv_row_stride, d_.kv_seq_stride = k4.stride(1), k4.stride(0) if S > 1 else 0
+    if block_table is not None:
+        if block_table.dtype != torch.int32 or not block_table.is_cuda or block_table.dim() != 2 or \
+                block_table.shape[0] != S or not block_table.is_contiguous():
+            raise AlpacaCUDAError(Status.INVALID_ARGUMENT, "block_table must be a contiguous CUDA int32 [seqs, blocks]")
+        d_.block_table = block_table.data_ptr()
+        d_.max_blocks = block_table.shape[1]
+        d_.block_rows, d_.pool_blocks, d_.block_stride = k4.shape[1], k4.shape[0], k4.stride(0)
+        d_.kv_seq_stride = 0
     d_.out, d_.out_token_stride, d_.out_seq_stride = o4.data_ptr(), o4.stride(1), o4.stride(0) if S > 1 else 0
     d_.scale, d_.flags = float(scale), int(flags) & 0xFFFFFFFF
     return d_
@@ -93,11 +103,12 @@ def launch(desc: AttnDesc, kind: Kernel = Kernel.AUTO, workspace: torch.Tensor |
 def attention_device(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor, *, start_position: int = 0,
                      kind: Kernel = Kernel.AUTO, ctx_lens: torch.Tensor | None = None,
                      max_ctx_len: int | None = None, scale: float = 0.0, flags: int = 0,
-                     workspace: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> AttnDesc:
+                     workspace: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None,
+                     block_table: torch.Tensor | None = None) -> AttnDesc:
     """Enqueue attention on device tensors (KernelEncoder.attention / attentionTensor). Allocates the workspace
-    with torch when none is given (callers on a hot loop pass their own)."""
+    with torch when none is given (callers on a hot loop pass their own). `block_table`: paged cache (make_desc)."""
     desc = make_desc(q, k, v, out, start_position=start_position, ctx_lens=ctx_lens, max_ctx_len=max_ctx_len,
-                     scale=scale, flags=flags)
+                     scale=scale, flags=flags, block_table=block_table)
     need = workspace_bytes(desc, kind)
     if need and (workspace is None or workspace.numel() * workspace.element_size() < need):
         workspace = torch.empty(need, dtype=torch.uint8, device=q.device)

@@ -108,6 +108,18 @@ typedef struct alpaca_attn_desc {
     int64_t out_seq_stride;
     float scale;             /* softmax scale; 0 selects 1/sqrt(head_dim) as CPUOps.attentionScores does */
     uint32_t flags;          /* ALPACA_ATTN_FLAG_* */
+    /* Paged KV cache (optional; block_table == NULL means one contiguous cache per sequence). k and v then point
+     * at pools of pool_blocks blocks, block_stride elements apart, each holding block_rows consecutive cache rows
+     * (kv_row_stride apart); row r of sequence s lives in block block_table[s * max_blocks + r / block_rows] at
+     * row r % block_rows, and kv_seq_stride is ignored. block_rows is a multiple of 128. Served by the split
+     * decode and the tensor-core prefill kernels (f16 cache); alpaca.swift has no paged cache (README.md:257), so
+     * this extends the layout of KernelEncoder.swift:9-17 for batched serving. */
+    const int32_t* block_table; /* DEVICE array [n_seqs][max_blocks] of block indices into the pools */
+    int32_t block_rows;
+    int32_t max_blocks;
+    int64_t block_stride;       /* elements between blocks of the pool */
+    int32_t pool_blocks;        /* blocks in each pool (bounds of the TMA maps) */
+    int32_t reserved1;
 } alpaca_attn_desc;
 
 /* Enqueue attention described by `desc` with the kernel `kind` on `stream`.
@@ -148,7 +160,8 @@ alpaca_cuda_status alpaca_attn_decode_noalloc(const alpaca_attn_desc* desc, alpa
 alpaca_cuda_status alpaca_attention_workspace_bytes(const alpaca_attn_desc* desc, alpaca_attn_kernel kind,
                                                     size_t* bytes);
 
-/* Which kernel ALPACA_ATTN_AUTO would run for `desc` (host-only policy query, KernelEncoder.swift:306-343). */
+/* Which kernel ALPACA_ATTN_AUTO would run for `desc` (host-only policy query, KernelEncoder.swift:306-343);
+ * ALPACA_CUDA_ERR_UNSUPPORTED when none can (a paged cache of f32 rows, for instance). */
 alpaca_cuda_status alpaca_attention_select(const alpaca_attn_desc* desc, alpaca_attn_kernel* kind);
 
 /* ---- RoPE + KV-cache append: the step that produces the attention hand-off (the next row upstream of it). */

@@ -241,3 +241,41 @@ def test_rope_invalid_arguments_rejected(lib, bad):
     d = rope_desc(**bad)
     assert lib.alpaca_rope_kv_append(ctypes.byref(d), None) == Status.INVALID_ARGUMENT
     assert lib.alpaca_cuda_last_error().startswith(b"rope")
+
+
+# ---------------------------------------------------------------------------------------------- paged KV cache
+
+def paged(**kw):
+    base = dict(block_table=FAKE, block_rows=256, max_blocks=4, block_stride=256 * 3 * 64, pool_blocks=64,
+                kv_seq_stride=0)
+    base.update(kw)
+    return base
+
+
+def test_paged_cache_policy(lib):
+    """A paged cache goes to the split decode at any context and to the tensor-core prefill at any length; the
+    general kernel has no paged form."""
+    from alpaca_b200 import DType, Kernel, Status
+    assert select(lib, desc(tokens=1, start_position=10, **paged())) == (Status.OK, Kernel.DECODE_SPLIT)
+    assert select(lib, desc(tokens=4, start_position=10, **paged())) == (Status.OK, Kernel.PREFILL_TC)
+    assert select(lib, desc(tokens=2, n_seqs=2, q_seq_stride=576, out_seq_stride=576, **paged())) == \
+        (Status.OK, Kernel.PREFILL_TC)  # no sequence stride needed for a paged cache
+    assert select(lib, desc(tokens=4, kv_dtype=int(DType.F32), **paged()))[0] == Status.UNSUPPORTED
+    d = desc(tokens=4, **paged())
+    assert lib.alpaca_attention(ctypes.byref(d), int(Kernel.GENERAL), None, 0, None) == Status.UNSUPPORTED
+
+
+@pytest.mark.parametrize("bad", [
+    dict(block_rows=100),                    # not a multiple of 128
+    dict(block_rows=0),
+    dict(max_blocks=0),
+    dict(pool_blocks=0),
+    dict(max_blocks=1, start_position=200),  # 328 rows > 1 block of 256
+    dict(block_stride=256 * 3 * 64 - 64),    # smaller than a block
+    dict(block_stride=256 * 3 * 64 + 4),     # not a multiple of 16 bytes for f16
+])
+def test_paged_cache_invalid(lib, bad):
+    from alpaca_b200 import Status
+    d = desc(**paged(**bad))
+    assert select(lib, d)[0] == Status.INVALID_ARGUMENT
+    assert lib.alpaca_attention(ctypes.byref(d), 0, None, 0, None) == Status.INVALID_ARGUMENT
