@@ -6,8 +6,8 @@
 // blocks, final 1/l. The structure is B200-native:
 //
 //   * persistent kernel, one CTA per SM, work items = (sequence, head, pair of 128-row query tiles A and B)
-//     handed out heaviest first (items with more visible KV blocks come first), so the causal triangle is
-//     balanced over the 148 SMs;
+//     ordered heaviest first (items with more visible KV blocks come first) and dealt to the CTAs in serpentine
+//     rounds, so the causal triangle is balanced over the 148 SMs even when there are few items per SM;
 //   * head_dim 64 (128-row KV blocks) and 128 (64-row KV blocks, so S, O and P of both tiles fit TMEM); rows of Q,
 //     K and V are stored as head_dim/64 column blocks of 128 bytes;
 //   * warp 0: TMA producer. Q tiles and a 4-stage ring of K/V blocks land in shared memory with 128-byte swizzle,
@@ -179,6 +179,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const bool debug_timeout = (a.flags & ALPACA_ATTN_FLAG_DEBUG_FORCE_TIMEOUT) != 0;
     AbortState ab{&sm->abort_flag, a.err, debug_timeout ? kDebugWaitLimitNs : kWaitLimitNs};
+    // Items are dealt in serpentine rounds (CTA c takes item c of even rounds and item gridDim.x-1-c of odd ones),
+    // so the CTA that draws the heaviest item of one round draws the lightest of the next. Every role of the CTA
+    // walks the same sequence.
+    const auto item_of = [&](int r) {
+        return r * static_cast<int>(gridDim.x) + ((r & 1) ? static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x)
+                                                          : static_cast<int>(blockIdx.x));
+    };
 
     if (tid == 0) {
         sm->abort_flag = 0;
@@ -223,7 +230,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ------------------------------------------------------------------ TMA producer
         uint32_t kv_it = 0, k_issued = 0, v_issued = 0, q_uses[2] = {0, 0};
         bool ok = true;
-        for (int it = blockIdx.x; ok && it < a.total_items; it += gridDim.x) {
+        for (int r = 0, it = item_of(0); ok && it < a.total_items; it = item_of(++r)) {
             const Item x = decode_item<kBN>(a, it);
             const int kvh = x.head / (a.n_heads / a.n_kv_heads);
             for (int t = 0; t < 2 && ok; t++) {
@@ -298,7 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t kv_it = 0, q_uses = 0, s_uses = 0, p_uses = 0;
             bool ok = true;
             if (debug_timeout && t == 0) ok = mbar_wait(&sm->dbg, 0, ab);  // nothing arrives: exercises the give-up path
-            for (int it = blockIdx.x; ok && it < a.total_items; it += gridDim.x) {
+            for (int r = 0, it = item_of(0); ok && it < a.total_items; it = item_of(++r)) {
                 const Item x = decode_item<kBN>(a, it);
                 const int n = x.nblk[t];
                 const int nmax = max(x.nblk[0], x.nblk[1]);
@@ -383,7 +390,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint64_t* xbar = &sm->xbar[tile][quarter];
         uint32_t s_uses = 0, o_uses = 0, x_uses = 0;
         bool ok = true;
-        for (int it = blockIdx.x; ok && it < a.total_items; it += gridDim.x) {
+        for (int r = 0, it = item_of(0); ok && it < a.total_items; it = item_of(++r)) {
             const Item x = decode_item<kBN>(a, it);
             const int nb = x.nblk[tile];
             if (nb == 0) continue;
