@@ -99,6 +99,12 @@ class RopeDesc(ctypes.Structure):
         ("cache_row_stride", ctypes.c_int64),
         ("cache_seq_stride", ctypes.c_int64),
         ("flags", ctypes.c_uint32),
+        ("block_table", ctypes.c_void_p),
+        ("block_rows", ctypes.c_int32),
+        ("max_blocks", ctypes.c_int32),
+        ("block_stride", ctypes.c_int64),
+        ("pool_blocks", ctypes.c_int32),
+        ("reserved0", ctypes.c_int32),
     ]
 
 

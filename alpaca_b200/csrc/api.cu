@@ -178,9 +178,20 @@ alpaca_cuda_status validate_rope(const alpaca_rope_desc* dp) {
             return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "rope: k / v / cache pointers must be 8-byte aligned");
         const int64_t hk = static_cast<int64_t>(d.n_kv_heads) * d.head_dim;
         if (d.kv_token_stride < hk || d.cache_row_stride < hk || d.kv_seq_stride < 0 || d.cache_seq_stride < 0 ||
-            (d.n_seqs > 1 && (d.kv_seq_stride == 0 || d.cache_seq_stride == 0)) || d.kv_token_stride % 2 ||
+            (d.n_seqs > 1 && (d.kv_seq_stride == 0 || (d.cache_seq_stride == 0 && !d.block_table))) ||
+            d.kv_token_stride % 2 ||
             d.kv_seq_stride % 2 || d.cache_row_stride % 2 || d.cache_seq_stride % 2)
             return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, std::string("rope: k / v / cache strides: ") + sh);
+        if (d.block_table) {
+            if (d.block_rows < 128 || d.block_rows % 128 || d.max_blocks < 1 || d.pool_blocks < 1 ||
+                d.block_stride < static_cast<int64_t>(d.block_rows) * d.cache_row_stride || d.block_stride % 2)
+                return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT,
+                            std::string("rope: paged cache needs block_rows a multiple of 128, max_blocks and pool_blocks "
+                                        ">= 1, block_stride covering a block and even: ") + sh);
+            if (!d.positions && static_cast<int64_t>(d.start_position) + d.tokens >
+                                    static_cast<int64_t>(d.max_blocks) * d.block_rows)
+                return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, std::string("rope: block table too short: ") + sh);
+        }
     }
     return ok();
 }
@@ -304,7 +315,7 @@ alpaca_cuda_status alpaca_rope_kv_append(const alpaca_rope_desc* desc, alpaca_st
     DeviceInfo di;
     cudaError_t e = device_info(&di);
     if (e != cudaSuccess) return fail(ALPACA_CUDA_ERR_CUDA, std::string("rope: ") + cudaGetErrorString(e));
-    e = launch_rope_kv(*desc, reinterpret_cast<cudaStream_t>(stream));
+    e = launch_rope_kv(*desc, di.err, reinterpret_cast<cudaStream_t>(stream));
     if (e != cudaSuccess)
         return fail(ALPACA_CUDA_ERR_LAUNCH_FAILED, std::string("rope: launch failed: ") + cudaGetErrorString(e));
     return ok();

@@ -34,7 +34,7 @@ cudaError_t launch_general(const Call& c, cudaStream_t s);
 
 // ---- RoPE + KV-cache append (rope_kv.cu)
 int rope_max_head_dim();
-cudaError_t launch_rope_kv(const alpaca_rope_desc& d, cudaStream_t s);
+cudaError_t launch_rope_kv(const alpaca_rope_desc& d, unsigned* err, cudaStream_t s);
 
 // ---- tcgen05 prefill (attn_prefill_sm100.cu)
 bool prefill_supported(const alpaca_attn_desc& d);

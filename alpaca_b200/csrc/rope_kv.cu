@@ -39,6 +39,10 @@ struct RopeArgs {
     const int* positions;
     int start, n_heads, n_kv_heads, half, tokens;
     int tpc;  // tokens per CTA of the vector kernel (1 .. kVecTokens)
+    const int* block_table;  // paged cache: [seq][max_blocks] (null: contiguous caches)
+    int block_rows, max_blocks, pool_blocks;
+    int64_t block_stride;
+    unsigned* err;
     double freq[kRopeMaxPairs];  // theta^(-2i/d), host-computed in double
 };
 
@@ -63,6 +67,21 @@ __device__ __forceinline__ void pair_index(int i, int half, int& ia, int& ib) {
     ib = kInterleaved ? 2 * i + 1 : i + half;
 }
 
+// Element offset of cache row `pos` of sequence `seq`; a paged table entry outside the pool (or a position past
+// the table) clears `ok` — nothing is written there — and raises the device error word.
+__device__ __forceinline__ int64_t cache_row_offset(const RopeArgs& a, int seq, int pos, bool& ok) {
+    ok = true;
+    if (!a.block_table) return seq * a.cache_seq_stride + static_cast<int64_t>(pos) * a.cache_row_stride;
+    const int b = pos / a.block_rows;
+    const int blk = b < a.max_blocks ? a.block_table[static_cast<int64_t>(seq) * a.max_blocks + b] : -1;
+    if (blk < 0 || blk >= a.pool_blocks) {
+        ok = false;
+        atomicOr(a.err, kDevErrBadIndex);
+        return 0;
+    }
+    return static_cast<int64_t>(blk) * a.block_stride + static_cast<int64_t>(pos % a.block_rows) * a.cache_row_stride;
+}
+
 template <bool kInterleaved, typename QT, typename CT>
 __global__ void __launch_bounds__(kRopeThreads) rope_kv_kernel(const __grid_constant__ RopeArgs a) {
     __shared__ float2 cs[kRopeMaxPairs];
@@ -79,11 +98,13 @@ __global__ void __launch_bounds__(kRopeThreads) rope_kv_kernel(const __grid_cons
     const int rows = a.n_heads + 2 * a.n_kv_heads;
     QT* q = static_cast<QT*>(a.q) + seq * a.q_seq_stride + static_cast<int64_t>(t) * a.q_token_stride;
     const int64_t kv_off = seq * a.kv_seq_stride + static_cast<int64_t>(t) * a.kv_token_stride;
-    const int64_t cache_off = seq * a.cache_seq_stride + static_cast<int64_t>(pos) * a.cache_row_stride;
+    bool row_ok = true;
+    const int64_t cache_off = a.n_kv_heads > 0 ? cache_row_offset(a, seq, pos, row_ok) : 0;
     CT* kc = static_cast<CT*>(a.k_cache) + cache_off;
     CT* vc = static_cast<CT*>(a.v_cache) + cache_off;
     for (int idx = tid; idx < rows * a.half; idx += kRopeThreads) {
         const int r = idx / a.half, i = idx - r * a.half;
+        if (r >= a.n_heads && !row_ok) break;  // k / v rows of an unwritable cache row
         int ia, ib;
         pair_index<kInterleaved>(i, a.half, ia, ib);
         const float2 w = cs[i];
@@ -170,14 +191,14 @@ __device__ __forceinline__ void store4(__half* p, int i0, int half, const float 
 // Group `idx` (4 pairs) of the CTA's tokens: which token, row and pairs, and where that row lives.
 template <typename QT, typename CT>
 struct VecItem {
-    bool valid, is_q, is_k;
+    bool valid, is_q, is_k, dst_ok;
     int tt, i0;
     const float* src;  // k or v row (f32)
     QT* qrow;          // query row (rotated in place)
     CT* dst;           // cache row
 };
 
-template <typename QT, typename CT>
+template <bool kDst, typename QT, typename CT>
 __device__ __forceinline__ VecItem<QT, CT> vec_item(const RopeArgs& a, int seq, int t0, int pos0, int ntok, int idx) {
     VecItem<QT, CT> it;
     const int d = 2 * a.half, quads = a.half / 4;
@@ -193,15 +214,16 @@ __device__ __forceinline__ VecItem<QT, CT> vec_item(const RopeArgs& a, int seq, 
     const int h = it.is_q ? 0 : (it.is_k ? r - a.n_heads : r - a.n_heads - a.n_kv_heads);
     it.qrow = static_cast<QT*>(a.q) + seq * a.q_seq_stride + static_cast<int64_t>(t) * a.q_token_stride + r * d;
     it.src = (it.is_k ? a.k : a.v) + seq * a.kv_seq_stride + static_cast<int64_t>(t) * a.kv_token_stride + h * d;
-    it.dst = static_cast<CT*>(it.is_k ? a.k_cache : a.v_cache) + seq * a.cache_seq_stride +
-             static_cast<int64_t>(pos0 + tt) * a.cache_row_stride + h * d;
+    it.dst_ok = true;
+    it.dst = static_cast<CT*>(it.is_k ? a.k_cache : a.v_cache) + h * d;
+    if (kDst && it.valid && !it.is_q) it.dst += cache_row_offset(a, seq, pos0 + tt, it.dst_ok);
     return it;
 }
 
 template <bool kInterleaved, typename QT, typename CT>
 __device__ __forceinline__ void vec_load(const RopeArgs& a, int seq, int t0, int pos0, int ntok, int idx,
                                          float (&x0)[4], float (&x1)[4]) {
-    const VecItem<QT, CT> it = vec_item<QT, CT>(a, seq, t0, pos0, ntok, idx);
+    const VecItem<QT, CT> it = vec_item<false, QT, CT>(a, seq, t0, pos0, ntok, idx);
     if (!it.valid) return;
     if (it.is_q) load4<kInterleaved>(it.qrow, it.i0, a.half, x0, x1);
     else load4<kInterleaved>(it.src, it.i0, a.half, x0, x1);
@@ -210,7 +232,7 @@ __device__ __forceinline__ void vec_load(const RopeArgs& a, int seq, int t0, int
 template <bool kInterleaved, typename QT, typename CT>
 __device__ __forceinline__ void vec_store(const RopeArgs& a, int seq, int t0, int pos0, int ntok, int idx,
                                           const float2* cs, float (&x0)[4], float (&x1)[4]) {
-    const VecItem<QT, CT> it = vec_item<QT, CT>(a, seq, t0, pos0, ntok, idx);
+    const VecItem<QT, CT> it = vec_item<true, QT, CT>(a, seq, t0, pos0, ntok, idx);
     if (!it.valid) return;
     if (it.is_q || it.is_k) {
 #pragma unroll
@@ -222,7 +244,7 @@ __device__ __forceinline__ void vec_store(const RopeArgs& a, int seq, int t0, in
         }
     }
     if (it.is_q) store4<kInterleaved>(it.qrow, it.i0, a.half, x0, x1);
-    else store4<kInterleaved>(it.dst, it.i0, a.half, x0, x1);
+    else if (it.dst_ok) store4<kInterleaved>(it.dst, it.i0, a.half, x0, x1);
 }
 
 template <bool kInterleaved, typename QT, typename CT>
@@ -266,7 +288,7 @@ bool vector_ok(const alpaca_rope_desc& d) {
     if (d.n_heads > 0 && (!al16(d.q) || d.q_token_stride % 8 || d.q_seq_stride % 8)) return false;
     if (d.n_kv_heads > 0 && (!al16(d.k) || !al16(d.v) || !al16(d.k_cache) || !al16(d.v_cache) ||
                              d.kv_token_stride % 8 || d.kv_seq_stride % 8 || d.cache_row_stride % 8 ||
-                             d.cache_seq_stride % 8))
+                             d.cache_seq_stride % 8 || (d.block_table && d.block_stride % 8)))
         return false;
     return true;
 }
@@ -308,7 +330,7 @@ int rope_tokens_per_cta() {
 
 int rope_max_head_dim() { return 2 * kRopeMaxPairs; }
 
-cudaError_t launch_rope_kv(const alpaca_rope_desc& d, cudaStream_t s) {
+cudaError_t launch_rope_kv(const alpaca_rope_desc& d, unsigned* err, cudaStream_t s) {
     RopeArgs a;
     a.q = d.q;
     a.q_token_stride = d.q_token_stride;
@@ -328,6 +350,12 @@ cudaError_t launch_rope_kv(const alpaca_rope_desc& d, cudaStream_t s) {
     a.half = d.head_dim / 2;
     a.tokens = d.tokens;
     a.tpc = rope_tokens_per_cta();
+    a.block_table = d.block_table;
+    a.block_rows = d.block_rows;
+    a.max_blocks = d.max_blocks;
+    a.pool_blocks = d.pool_blocks;
+    a.block_stride = d.block_stride;
+    a.err = err;
     const double theta = static_cast<double>(d.theta);
     for (int i = 0; i < kRopeMaxPairs; i++)
         a.freq[i] = i < a.half ? std::pow(theta, -2.0 * static_cast<double>(i) / static_cast<double>(d.head_dim)) : 0.0;

@@ -165,9 +165,10 @@ def attention(q: np.ndarray, keys: np.ndarray, values: np.ndarray, start_positio
 def make_rope_desc(q: torch.Tensor | None, k: torch.Tensor | None, v: torch.Tensor | None,
                    k_cache: torch.Tensor | None, v_cache: torch.Tensor | None, *, theta: float,
                    start_position: int = 0, positions: torch.Tensor | None = None,
-                   interleaved: bool = True) -> RopeDesc:
+                   interleaved: bool = True, block_table: torch.Tensor | None = None) -> RopeDesc:
     """Descriptor for q [S,T,H,d] (rotated in place), k/v [S,T,Hkv,d] f32 and caches [S,rows,Hkv,d] (3-D tensors
-    mean S = 1). q or (k, v, caches) may be None."""
+    mean S = 1). q or (k, v, caches) may be None. With `block_table` (CUDA int32 [S, max_blocks]) the caches are
+    block pools [pool_blocks, block_rows, Hkv, d], laid out as for the attention call (make_desc)."""
     d_ = RopeDesc()
     ref = q if q is not None else k
     if ref is None:
@@ -197,6 +198,14 @@ def make_rope_desc(q: torch.Tensor | None, k: torch.Tensor | None, v: torch.Tens
         d_.kv_seq_stride = k4.stride(0) if S > 1 else 0
         d_.k_cache, d_.v_cache, d_.cache_row_stride = kc4.data_ptr(), vc4.data_ptr(), kc4.stride(1)
         d_.cache_seq_stride = kc4.stride(0) if S > 1 else 0
+        if block_table is not None:
+            if block_table.dtype != torch.int32 or not block_table.is_cuda or block_table.dim() != 2 or \
+                    block_table.shape[0] != S or not block_table.is_contiguous():
+                raise AlpacaCUDAError(Status.INVALID_ARGUMENT,
+                                      "block_table must be a contiguous CUDA int32 [seqs, blocks]")
+            d_.block_table, d_.max_blocks = block_table.data_ptr(), block_table.shape[1]
+            d_.block_rows, d_.pool_blocks, d_.block_stride = kc4.shape[1], kc4.shape[0], kc4.stride(0)
+            d_.cache_seq_stride = 0
     return d_
 
 
@@ -208,10 +217,10 @@ def rope_launch(desc: RopeDesc, stream: torch.cuda.Stream | None = None) -> None
 def rope_kv_append(q: torch.Tensor | None, k: torch.Tensor | None, v: torch.Tensor | None,
                    k_cache: torch.Tensor | None, v_cache: torch.Tensor | None, *, theta: float,
                    start_position: int = 0, positions: torch.Tensor | None = None, interleaved: bool = True,
-                   stream: torch.cuda.Stream | None = None) -> RopeDesc:
+                   stream: torch.cuda.Stream | None = None, block_table: torch.Tensor | None = None) -> RopeDesc:
     """Enqueue RoPE + KV append on device tensors (KernelEncoder.ropeQKVStore, KernelEncoder.swift:401-411)."""
     d_ = make_rope_desc(q, k, v, k_cache, v_cache, theta=theta, start_position=start_position, positions=positions,
-                        interleaved=interleaved)
+                        interleaved=interleaved, block_table=block_table)
     rope_launch(d_, stream)
     return d_
 

@@ -200,6 +200,17 @@ typedef struct alpaca_rope_desc {
     int64_t cache_row_stride; /* elements between cache rows */
     int64_t cache_seq_stride;
     uint32_t flags;           /* 0 */
+    /* Paged cache (optional, the layout of alpaca_attn_desc's block_table): k_cache / v_cache are pools of
+     * pool_blocks blocks of block_rows rows (a multiple of 128), block_stride elements apart; cache row pos of
+     * sequence s is row pos % block_rows of block block_table[s * max_blocks + pos / block_rows];
+     * cache_seq_stride is ignored. An entry outside the pool writes nothing and is reported by
+     * alpaca_cuda_device_status. */
+    const int32_t* block_table;
+    int32_t block_rows;
+    int32_t max_blocks;
+    int64_t block_stride;
+    int32_t pool_blocks;
+    int32_t reserved0;
 } alpaca_rope_desc;
 
 /* Enqueue the fused RoPE + KV append on `stream`. Replaces KernelEncoder.ropeQKVStore (KernelEncoder.swift:

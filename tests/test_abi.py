@@ -279,3 +279,34 @@ def test_paged_cache_invalid(lib, bad):
     d = desc(**paged(**bad))
     assert select(lib, d)[0] == Status.INVALID_ARGUMENT
     assert lib.alpaca_attention(ctypes.byref(d), 0, None, 0, None) == Status.INVALID_ARGUMENT
+
+
+def rope_paged(**kw):
+    base = dict(block_table=FAKE, block_rows=128, max_blocks=2, block_stride=128 * 3 * 64, pool_blocks=8)
+    base.update(kw)
+    return base
+
+
+@pytest.mark.parametrize("bad", [
+    dict(block_rows=100),                    # not a multiple of 128 (the attention kernels' block granularity)
+    dict(max_blocks=0),
+    dict(pool_blocks=0),
+    dict(block_stride=127 * 3 * 64),         # smaller than a block
+    dict(block_stride=128 * 3 * 64 + 1),     # odd
+    dict(max_blocks=1, start_position=126),  # rows 126..129 need a second block
+])
+def test_rope_paged_invalid_arguments_rejected(lib, bad):
+    from alpaca_b200 import Status
+    d = rope_desc(**rope_paged(**bad))
+    assert lib.alpaca_rope_kv_append(ctypes.byref(d), None) == Status.INVALID_ARGUMENT
+    assert lib.alpaca_cuda_last_error().startswith(b"rope")
+
+
+def test_rope_paged_cache_needs_no_sequence_stride(lib):
+    """Several sequences appending into one pool: the cache sequence stride is unused (0) and the descriptor passes
+    validation (without a GPU the call then fails at the device query, not on its arguments)."""
+    from alpaca_b200 import Status
+    d = rope_desc(**rope_paged(n_seqs=3, q_seq_stride=4 * 9 * 64, kv_seq_stride=4 * 3 * 64))
+    assert lib.alpaca_rope_kv_append(ctypes.byref(d), None) != Status.INVALID_ARGUMENT
+    d = rope_desc(**rope_paged(n_seqs=3, q_seq_stride=4 * 9 * 64, kv_seq_stride=4 * 3 * 64, block_table=0))
+    assert lib.alpaca_rope_kv_append(ctypes.byref(d), None) == Status.INVALID_ARGUMENT
