@@ -130,6 +130,7 @@ __global__ void __launch_bounds__(kRopeThreads) rope_kv_kernel(const __grid_cons
 
 constexpr int kVecThreads = 256;
 constexpr int kVecTokens = 32;  // most tokens per CTA of the vector kernel
+constexpr int kVecTokensDefault = 8;  // measured best at the config-2 shape (4, 16 and 32 are slower)
 constexpr int kVecBatch = 4;   // groups of 4 pairs a thread loads before it rotates / stores them
 
 // Four pairs i0..i0+3 of one head row: a[j] = x[ia(i0+j)], b[j] = x[ib(i0+j)].
@@ -321,7 +322,7 @@ int rope_tokens_per_cta() {
     static const int v = [] {
         const char* e = std::getenv("ALPACA_ROPE_TPC");
         const int x = e ? std::atoi(e) : 0;
-        return (x >= 1 && x <= kVecTokens) ? x : kVecTokens;
+        return (x >= 1 && x <= kVecTokens) ? x : kVecTokensDefault;
     }();
     return v;
 }
