@@ -17,6 +17,7 @@
 // Scores are kept in log2 units (q pre-scaled by scale*log2(e)), so every exponential is one ex2.approx.
 // Partial-state layout: [seq][kv_head][split][g][d + 2] f32 = accumulators, then m (log2 units), then l.
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -298,6 +299,9 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 6 : 3)) decode_split_kerne
     // KV heads vary fastest across the grid, so the CTAs reading the parts of the same cache rows run together
     // and DRAM sees whole rows streamed in order.
     const int split = blockIdx.x / a.n_kv_heads, kvh = blockIdx.x - split * a.n_kv_heads, seq = blockIdx.y;
+    // Launched with programmatic dependent launch: the CTA may be resident before the previous kernel on the
+    // stream has finished, so it touches no global memory before that kernel's writes are complete and visible.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int L = ctx_len_of(a, seq);
     const int row0 = split * SL;
     if (row0 >= L) return;  // uniform for the whole CTA
@@ -337,6 +341,8 @@ __device__ __forceinline__ void cp_async8(void* smem_dst, const void* gsrc) {
 template <int D>
 __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const DecodeArgs a) {
     asm volatile("griddepcontrol.wait;" ::: "memory");  // split kernel's writes are visible after this
+    // The next stream-ordered kernel may launch now (it waits for this grid to finish before touching memory).
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int kvh = blockIdx.x, seq = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = a.n_heads / a.n_kv_heads;
     const int L = ctx_len_of(a, seq);
@@ -408,15 +414,32 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const D
     }
 }
 
+// Programmatic dependent launch of the split kernel (ALPACA_PDL=0 turns it off).
+bool pdl_enabled() {
+    static const bool v = [] {
+        const char* e = std::getenv("ALPACA_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return v;
+}
+
 template <int D, int G>
 cudaError_t launch_split(const DecodeArgs& a, int n_seqs, cudaStream_t s) {
     using Gm = Geo<D>;
     static_assert(Gm::RPS * G * D * sizeof(float) <= sizeof(__half) * 2 * Gm::SL * D, "reduction buffer too big");
     // K and V tiles (2 * SL * D halves; the reduction buffer RPS*G*D floats fits inside them), scores, (m, l)
     const size_t smem = sizeof(__half) * 2 * Gm::SL * D + sizeof(float) * (G * Gm::SL + 2 * G);
-    dim3 grid(a.max_splits * a.n_kv_heads, n_seqs, 1);
-    decode_split_kernel<D, G><<<grid, kThreads, smem, s>>>(a);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.max_splits * a.n_kv_heads, n_seqs, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, decode_split_kernel<D, G>, a);
 }
 
 template <int D>

@@ -84,6 +84,8 @@ __device__ __forceinline__ int64_t cache_row_offset(const RopeArgs& a, int seq, 
 
 template <bool kInterleaved, typename QT, typename CT>
 __global__ void __launch_bounds__(kRopeThreads) rope_kv_kernel(const __grid_constant__ RopeArgs a) {
+    // The attention call that follows may launch now; it waits for this grid to finish before reading.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     __shared__ float2 cs[kRopeMaxPairs];
     const int t = blockIdx.x, seq = blockIdx.y, tid = threadIdx.x;
     const int pos = (a.positions ? a.positions[seq] : a.start) + t;
@@ -250,6 +252,8 @@ __device__ __forceinline__ void vec_store(const RopeArgs& a, int seq, int t0, in
 
 template <bool kInterleaved, typename QT, typename CT>
 __global__ void __launch_bounds__(kVecThreads) rope_kv_vec_kernel(const __grid_constant__ RopeArgs a) {
+    // The attention call that follows may launch now; it waits for this grid to finish before reading.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     extern __shared__ float2 cs[];  // [tpc][half] (cos, sin)
     const int t0 = blockIdx.x * a.tpc, seq = blockIdx.y, tid = threadIdx.x;
     const int ntok = min(a.tpc, a.tokens - t0);
