@@ -14,6 +14,14 @@
 
 namespace alpaca {
 
+bool pdl_enabled() {
+    static const bool v = [] {
+        const char* e = std::getenv("ALPACA_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return v;
+}
+
 // Device error word (one per device that loads this library). Kernels receive its address; host code reads it
 // through alpaca_cuda_device_status.
 __device__ unsigned g_device_error;

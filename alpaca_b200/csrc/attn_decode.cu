@@ -414,15 +414,6 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const D
     }
 }
 
-// Programmatic dependent launch of the split kernel (ALPACA_PDL=0 turns it off).
-bool pdl_enabled() {
-    static const bool v = [] {
-        const char* e = std::getenv("ALPACA_PDL");
-        return !(e && e[0] == '0');
-    }();
-    return v;
-}
-
 template <int D, int G>
 cudaError_t launch_split(const DecodeArgs& a, int n_seqs, cudaStream_t s) {
     using Gm = Geo<D>;

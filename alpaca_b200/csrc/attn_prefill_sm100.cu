@@ -177,6 +177,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     auto* sm = reinterpret_cast<SmemLayout<D>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // The next stream-ordered kernel may launch now; it waits for this grid to finish before touching memory.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const bool debug_timeout = (a.flags & ALPACA_ATTN_FLAG_DEBUG_FORCE_TIMEOUT) != 0;
     AbortState ab{&sm->abort_flag, a.err, debug_timeout ? kDebugWaitLimitNs : kWaitLimitNs};
     // Items are dealt in serpentine rounds (CTA c takes item c of even rounds and item gridDim.x-1-c of odd ones),
@@ -223,6 +225,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncthreads();
     tc_fence_after();
+    // Launched with programmatic dependent launch: barriers, TMEM and tensor maps are set up while the previous
+    // kernel on the stream drains; no global memory is touched before its writes are complete and visible.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const uint32_t tmem_base = sm->tmem_base;
     if (warp == 0) {
         setmaxnreg_dec<kRegsControl>();
@@ -716,8 +721,17 @@ cudaError_t launch_prefill(const Call& c, cudaStream_t s) {
     a.pool_blocks = d.pool_blocks;
     a.last_block = last_block;
     const int grid = std::max(1, std::min(a.total_items, c.num_sms));
-    fn<<<grid, kThreads, smem, s>>>(tq, tk, tv, tkt, tvt, a);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, fn, tq, tk, tv, tkt, tvt, a);
 }
 
 }  // namespace alpaca

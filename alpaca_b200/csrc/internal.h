@@ -25,6 +25,8 @@ int decode_max_splits(const alpaca_attn_desc& d);            // splits of the lo
 size_t decode_workspace_bytes(const alpaca_attn_desc& d);    // partial-state bytes
 bool decode_supported(const alpaca_attn_desc& d);            // head_dim / group limits of the kernel
 cudaError_t launch_decode(const Call& c, cudaStream_t s);
+// Programmatic dependent launch of the attention kernels (ALPACA_PDL=0 turns it off).
+bool pdl_enabled();
 // Built-in scratch of alpaca_attn_decode_noalloc (file-scope device array in attn_decode.cu).
 constexpr size_t kDecodeBuiltinScratchBytes = size_t(8) << 20;  // 8 MiB
 cudaError_t decode_builtin_scratch(void** ptr);
