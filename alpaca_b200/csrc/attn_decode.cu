@@ -7,9 +7,13 @@
 //                 head of one sequence and serves all G query heads of that KV head, so every K/V byte is read
 //                 from HBM exactly once. Each cache row (d halves) is copied by d/8 lanes with 16-byte cp.async
 //                 into shared memory (rows past the context are zero-filled), K first then V, so registers stay
-//                 low (six CTAs per SM keep ~190 KB in flight per SM) and the V copy overlaps the score math. Scores are reduced across a row's lanes with a transposing butterfly
-//                 (7 shuffles for 8 rows instead of 24), softmax runs once per (row, head) from shared memory, and
-//                 P·V partial sums are reduced across rows through shared memory.
+//                 low (six CTAs per SM keep ~190 KB in flight per SM) and the V copy overlaps the score math.
+//                 head_dim 64: each warp takes a quarter of the rows on mma.sync m16n8k16 with split-precision
+//                 f16 operands (hi / remainder rows of Q and of P in the two halves of the 16-row tile, ~2^-22
+//                 relative error), K and V read with ldmatrix from XOR-swizzled tiles, P kept in registers.
+//                 head_dim 128: packed f32x2 FMAs; scores reduced across a row's lanes with a transposing
+//                 butterfly (7 shuffles for 8 rows instead of 24), softmax once per (row, head) from shared
+//                 memory, P·V partial sums reduced across rows through shared memory.
 //   combine       grid (kv_heads, seqs), 256 threads: rescales the per-split (m, l, acc) states of the G heads to
 //                 the global max and normalises. Launched with programmatic dependent launch so its launch
 //                 overlaps the split tail. Sequences with one split are finished by the split kernel itself.
@@ -137,7 +141,9 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 
 // Issue the async copies of one unit's K rows (one commit group) and V rows (a second group) into shared memory.
 // Rows past the context are zero-filled and never read. Each thread later reads back only the chunks it copied.
-template <int D>
+// kSwz: 16-byte chunk c of row r is stored at chunk c ^ (r & 7), so the eight rows an ldmatrix reads at one chunk
+// index fall in eight different bank groups.
+template <int D, bool kSwz = false>
 __device__ __forceinline__ void stage_unit(const DecodeArgs& a, int seq, int kvh, int row0, int row_end,
                                            __half* s_k, __half* s_v, int lr, int rowlane) {
     constexpr int RPS = Geo<D>::RPS;
@@ -147,16 +153,195 @@ __device__ __forceinline__ void stage_unit(const DecodeArgs& a, int seq, int kvh
     for (int i = 0; i < kSlots; i++) {
         const int rl = i * RPS + rowlane, r = row0 + rl;
         const bool in = valid && r < row_end;
-        cp_async16(s_k + rl * D + lr * 8, a.k + base + (in ? static_cast<int64_t>(rl) * a.kv_row_stride : 0), in ? 16u : 0u);
+        const int c = kSwz ? (lr ^ (rl & 7)) : lr;
+        cp_async16(s_k + rl * D + c * 8, a.k + base + (in ? static_cast<int64_t>(rl) * a.kv_row_stride : 0), in ? 16u : 0u);
     }
     cp_async_commit();
 #pragma unroll
     for (int i = 0; i < kSlots; i++) {
         const int rl = i * RPS + rowlane, r = row0 + rl;
         const bool in = valid && r < row_end;
-        cp_async16(s_v + rl * D + lr * 8, a.v + base + (in ? static_cast<int64_t>(rl) * a.kv_row_stride : 0), in ? 16u : 0u);
+        const int c = kSwz ? (lr ^ (rl & 7)) : lr;
+        cp_async16(s_v + rl * D + c * 8, a.v + base + (in ? static_cast<int64_t>(rl) * a.kv_row_stride : 0), in ? 16u : 0u);
     }
     cp_async_commit();
+}
+
+// ---- tensor-core form of a unit: mma.sync m16n8k16 (f16 operands, f32 accumulators) with split-precision A
+// operands. Q·Kᵀ: A rows 0..7 hold f16(q) of the G heads and rows 8..15 the f16 remainder q - f16(q), so the two
+// accumulator halves a lane holds (rows g and g+8) add up to the f32 score to ~2^-22 relative; K is f16 already.
+// P·V: the same split of P (rows g / g+8), built straight from the score accumulators. Each warp owns SL/4 rows.
+
+__device__ __forceinline__ void ldsm_x4(const void* p, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(const void* p, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// (x0, x1) -> f16 pair hi and the f16 pair of the remainders lo.
+__device__ __forceinline__ void split_f16x2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __floats2half2_rn(x0, x1);
+    const float2 hf = __half22float2(h);
+    const __half2 l = __floats2half2_rn(x0 - hf.x, x1 - hf.y);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+// At head_dim 128 the four warps' P·V rows [4][G][D] are reduced in the K|V tiles (after one more barrier) rather
+// than in a buffer of their own, which would cost a CTA per SM.
+__host__ __device__ constexpr bool tc_red_aliases_kv(int D) { return D == 128; }
+
+template <int D, int G, int kAfter>
+__device__ __forceinline__ void compute_unit_tc(const DecodeArgs& a, int seq, int kvh, int split, int row0,
+                                                int row_end, int nsplits, const __half* s_k, const __half* s_v,
+                                                float* s_red, float* s_stat, int tid, int warp, int lane) {
+    constexpr int SL = Geo<D>::SL, RW = SL / 4, NT = RW / 8, KS = D / 16, DT = D / 8;
+    static_assert(NT % 2 == 0 && KS % 2 == 0 && DT % 2 == 0, "tile shape");
+    const int g = lane >> 2, t4 = lane & 3;
+    const bool act = g < G;
+    const int rbase = warp * RW;
+
+    // A fragments of the scaled query (log2 units): hi rows 0..7, remainder rows 8..15; rows of absent heads are 0.
+    uint32_t qa[KS][4];
+    {
+        const int64_t qoff = static_cast<int64_t>(seq) * a.q_seq_stride + static_cast<int64_t>(kvh * G + (act ? g : 0)) * D;
+#pragma unroll
+        for (int kk = 0; kk < KS; kk++) {
+            float x[4];
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const int col = kk * 16 + h * 8 + t4 * 2;
+                float2 v;
+                if (a.q_f16) v = __half22float2(*reinterpret_cast<const __half2*>(static_cast<const __half*>(a.q) + qoff + col));
+                else v = *reinterpret_cast<const float2*>(static_cast<const float*>(a.q) + qoff + col);
+                x[2 * h] = act ? v.x * a.scale_log2 : 0.f;
+                x[2 * h + 1] = act ? v.y * a.scale_log2 : 0.f;
+            }
+            split_f16x2(x[0], x[1], qa[kk][0], qa[kk][1]);
+            split_f16x2(x[2], x[3], qa[kk][2], qa[kk][3]);
+        }
+    }
+
+    // S = Q·Kᵀ over this warp's RW rows.
+    cp_async_wait<kAfter + 1>();
+    __syncthreads();  // every thread's K chunks have landed
+    float sc[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++) {
+#pragma unroll
+        for (int j = 0; j < 4; j++) sc[nt][j] = 0.f;
+        const int row = rbase + nt * 8 + (lane & 7);
+#pragma unroll
+        for (int q2 = 0; q2 < KS / 2; q2++) {
+            const int chunk = q2 * 4 + (lane >> 3);
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4(s_k + row * D + ((chunk ^ (row & 7)) * 8), b0, b1, b2, b3);
+            mma16816(sc[nt], qa[2 * q2], b0, b1);
+            mma16816(sc[nt], qa[2 * q2 + 1], b2, b3);
+        }
+    }
+    // scores of head g at rows rbase + nt*8 + t4*2 + {0, 1}: hi + remainder halves; rows past the context -> -inf
+    float mloc = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+            const int r = row0 + rbase + nt * 8 + t4 * 2 + j;
+            const float v = (r < row_end) ? sc[nt][j] + sc[nt][j + 2] : -INFINITY;
+            sc[nt][j] = v;
+            mloc = fmaxf(mloc, v);
+        }
+    mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 1));
+    mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 2));
+    float* s_mx = s_stat;          // [4][G] warp maxima
+    float* s_sum = s_stat + 4 * G; // [4][G] warp sums
+    if (act && t4 == 0) s_mx[warp * G + g] = mloc;
+    __syncthreads();
+    float m = -INFINITY;
+    if (act) {
+#pragma unroll
+        for (int w = 0; w < 4; w++) m = fmaxf(m, s_mx[w * G + g]);
+    }
+    float lsum = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+            const float p = act ? ex2_approx(sc[nt][j] - m) : 0.f;  // masked rows: 2^-inf = 0
+            sc[nt][j] = p;
+            lsum += p;
+        }
+    lsum += __shfl_xor_sync(0xffffffffu, lsum, 1);
+    lsum += __shfl_xor_sync(0xffffffffu, lsum, 2);
+    if (act && t4 == 0) s_sum[warp * G + g] = lsum;
+
+    // O += P·V over this warp's rows, all D columns.
+    cp_async_wait<kAfter>();
+    __syncthreads();  // every thread's V chunks have landed (and s_sum is written)
+    float o[DT][4];
+#pragma unroll
+    for (int dt = 0; dt < DT; dt++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) o[dt][j] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < NT / 2; kk++) {
+        uint32_t pa[4];
+        split_f16x2(sc[2 * kk][0], sc[2 * kk][1], pa[0], pa[1]);
+        split_f16x2(sc[2 * kk + 1][0], sc[2 * kk + 1][1], pa[2], pa[3]);
+        const int row = rbase + kk * 16 + ((lane >> 3) & 1) * 8 + (lane & 7);
+#pragma unroll
+        for (int d2 = 0; d2 < DT / 2; d2++) {
+            const int chunk = d2 * 2 + (lane >> 4);
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4_t(s_v + row * D + ((chunk ^ (row & 7)) * 8), b0, b1, b2, b3);
+            mma16816(o[2 * d2], pa, b0, b1);
+            mma16816(o[2 * d2 + 1], pa, b2, b3);
+        }
+    }
+    if (tc_red_aliases_kv(D)) __syncthreads();  // s_red lies over the K|V tiles: every warp is done with V
+    if (act) {
+#pragma unroll
+        for (int dt = 0; dt < DT; dt++)
+            *reinterpret_cast<float2*>(s_red + (warp * G + g) * D + dt * 8 + t4 * 2) =
+                make_float2(o[dt][0] + o[dt][2], o[dt][1] + o[dt][3]);
+    }
+    __syncthreads();
+
+    // Sum the four warps' rows; finish single-split sequences, else store the partial state.
+    const int64_t part_base = ((static_cast<int64_t>(seq) * a.n_kv_heads + kvh) * a.max_splits + split) * G;
+    for (int o2 = tid; o2 < G * D; o2 += kThreads) {
+        const int gg = o2 / D, col = o2 - gg * D;
+        const float sacc = s_red[gg * D + col] + s_red[(G + gg) * D + col] + s_red[(2 * G + gg) * D + col] +
+                           s_red[(3 * G + gg) * D + col];
+        const float l = s_sum[gg] + s_sum[G + gg] + s_sum[2 * G + gg] + s_sum[3 * G + gg];
+        if (nsplits == 1) {
+            store_out_dec(a, seq, kvh * G + gg, D, col, sacc / l);
+        } else {
+            float* pp = a.partial + (part_base + gg) * (D + 2);
+            pp[col] = sacc;
+            if (col == 0) {
+                pp[D] = fmaxf(fmaxf(s_mx[gg], s_mx[G + gg]), fmaxf(s_mx[2 * G + gg], s_mx[3 * G + gg]));
+                pp[D + 1] = l;
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void store_out_dec(const DecodeArgs& a, int seq, int head, int D, int col, float val) {
+    const int64_t oo = static_cast<int64_t>(seq) * a.out_seq_stride + static_cast<int64_t>(head) * D + col;
+    if (a.out_f16) static_cast<__half*>(a.out)[oo] = __float2half_rn(val);
+    else static_cast<float*>(a.out)[oo] = val;
 }
 
 // One unit = SL cache rows of one KV head of one sequence, for its G query heads. kAfter = commit groups issued
@@ -292,7 +477,7 @@ __device__ __forceinline__ void compute_unit(const DecodeArgs& a, int seq, int k
 }
 
 // One CTA per (KV head x split, sequence) grid cell; CTAs past a sequence's context exit at once.
-template <int D, int G>
+template <int D, int G, bool kTc>
 __global__ void __launch_bounds__(kThreads, (G <= 4 ? 6 : 3)) decode_split_kernel(const DecodeArgs a) {
     using Gm = Geo<D>;
     constexpr int SL = Gm::SL, LPR = Gm::LPR, RPW = Gm::RPW;
@@ -316,8 +501,16 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 6 : 3)) decode_split_kerne
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int lr = lane % LPR, rowlane = warp * RPW + lane / LPR;
-    stage_unit<D>(a, seq, kvh, row0, row_end, s_k, s_v, lr, rowlane);
-    compute_unit<D, G, 0>(a, seq, kvh, split, row0, row_end, nsplits, s_k, s_v, s_p, s_ml, tid, warp, lane, lr, rowlane);
+    if (kTc) {
+        stage_unit<D, true>(a, seq, kvh, row0, row_end, s_k, s_v, lr, rowlane);
+        float* s_red = tc_red_aliases_kv(D) ? reinterpret_cast<float*>(s_k) : s_p;
+        float* s_stat = tc_red_aliases_kv(D) ? s_p : s_p + 4 * G * D;
+        compute_unit_tc<D, G, 0>(a, seq, kvh, split, row0, row_end, nsplits, s_k, s_v, s_red, s_stat, tid, warp, lane);
+    } else {
+        stage_unit<D>(a, seq, kvh, row0, row_end, s_k, s_v, lr, rowlane);
+        compute_unit<D, G, 0>(a, seq, kvh, split, row0, row_end, nsplits, s_k, s_v, s_p, s_ml, tid, warp, lane, lr,
+                              rowlane);
+    }
     // The combine kernel may start launching now; it waits for this grid's memory before reading.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
@@ -414,12 +607,27 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const D
     }
 }
 
+// Tensor-core unit compute at head_dim 64 (config-3 layer 26.2 -> 22.4 us); at head_dim 128 the packed-FMA form
+// measured faster (51.1 against 54.0 us on the same batch) and stays. ALPACA_DECODE_MMA=0 / 1 forces either form.
+bool decode_tensor_cores(int head_dim) {
+    static const int v = [] {
+        const char* e = std::getenv("ALPACA_DECODE_MMA");
+        return e ? (e[0] == '0' ? 0 : 1) : -1;
+    }();
+    return v < 0 ? head_dim == 64 : v == 1;
+}
+
 template <int D, int G>
 cudaError_t launch_split(const DecodeArgs& a, int n_seqs, cudaStream_t s) {
     using Gm = Geo<D>;
     static_assert(Gm::RPS * G * D * sizeof(float) <= sizeof(__half) * 2 * Gm::SL * D, "reduction buffer too big");
-    // K and V tiles (2 * SL * D halves; the reduction buffer RPS*G*D floats fits inside them), scores, (m, l)
-    const size_t smem = sizeof(__half) * 2 * Gm::SL * D + sizeof(float) * (G * Gm::SL + 2 * G);
+    const bool tc = decode_tensor_cores(D);
+    // K and V tiles (2 * SL * D halves; the reduction buffer RPS*G*D floats fits inside them), scores, (m, l);
+    // tensor-core form: K and V tiles, the four warps' P·V rows [4][G][D] and their (max, sum) [2][4][G]
+    const size_t smem =
+        tc ? sizeof(__half) * 2 * Gm::SL * D + sizeof(float) * ((tc_red_aliases_kv(D) ? 0 : 4 * G * D) + 8 * G)
+           : sizeof(__half) * 2 * Gm::SL * D + sizeof(float) * (G * Gm::SL + 2 * G);
+    static_assert(4 * G * D * sizeof(float) <= sizeof(__half) * 2 * Gm::SL * D, "P·V rows must fit the K|V tiles");
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.max_splits * a.n_kv_heads, n_seqs, 1);
     cfg.blockDim = dim3(kThreads, 1, 1);
@@ -430,7 +638,13 @@ cudaError_t launch_split(const DecodeArgs& a, int n_seqs, cudaStream_t s) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, decode_split_kernel<D, G>, a);
+    const auto fn = tc ? decode_split_kernel<D, G, true> : decode_split_kernel<D, G, false>;
+    if (smem > 48 * 1024) {
+        const cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+    }
+    return cudaLaunchKernelEx(&cfg, fn, a);
 }
 
 template <int D>
