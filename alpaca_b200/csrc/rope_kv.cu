@@ -251,7 +251,7 @@ __device__ __forceinline__ void vec_store(const RopeArgs& a, int seq, int t0, in
 }
 
 template <bool kInterleaved, typename QT, typename CT>
-__global__ void __launch_bounds__(kVecThreads) rope_kv_vec_kernel(const __grid_constant__ RopeArgs a) {
+__global__ void __launch_bounds__(kVecThreads, 4) rope_kv_vec_kernel(const __grid_constant__ RopeArgs a) {
     // The attention call that follows may launch now; it waits for this grid to finish before reading.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     extern __shared__ float2 cs[];  // [tpc][half] (cos, sin)
