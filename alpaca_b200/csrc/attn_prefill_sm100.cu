@@ -16,8 +16,9 @@
 //     into TMEM, and O += P·V with P read from TMEM (A operand in tensor memory, B = V from shared memory), so
 //     P never touches shared memory and the tensor core's shared-memory reads stay within bandwidth. Each issuer
 //     queues S(j+1) before PV(j), so the next S block is ready when the softmax finishes the current one;
-//   * warps 4-11 and 12-19: softmax for tile A and B, two threads per query row (one per half of the S block
-//     row). They read S from TMEM, mask diagonal blocks and keep the running max in log2 units
+//   * head_dim 64: warps 4-11 and 12-19: softmax for tile A and B, two threads per query row (one per half of the
+//     S block row). head_dim 128: warps 4-7 and 8-11, one thread per query row (the same steps without the
+//     exchange of partial row maxima and sums; 384 threads, registers from the launch bound). They read S from TMEM, mask diagonal blocks and keep the running max in log2 units
 //     (it only moves when it grows by more than 8, so O rarely needs rescaling). Each half computes its P
 //     against its own candidate max and only then reads the other half's candidate (shared memory, a
 //     two-arrival mbarrier per pair of warps that share TMEM lanes), so the exchange is off the critical path;
@@ -43,7 +44,11 @@ namespace {
 
 constexpr int kBM = 128;        // query rows per tile
 constexpr int kStages = 4;      // K/V ring depth
-constexpr int kThreads = 640;   // 20 warps: TMA, MMA A, MMA B (+ TMEM allocator), idle, 16 softmax warps
+// Threads per CTA: warps 0-3 are TMA, MMA A, MMA B (+ TMEM allocator) and idle; then the softmax warps, 16 with
+// two threads per query row (R = 2) or 8 with one (R = 1).
+template <int R>
+__host__ __device__ constexpr int threads_for() { return R == 2 ? 640 : 384; }
+constexpr int kThreads = threads_for<2>();
 constexpr int kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;      // log2 units
 
@@ -167,8 +172,8 @@ __device__ __forceinline__ void mma_pv(const SmemLayout<D>* sm, int tile, int st
 
 // ---------------------------------------------------------------------------------------------- kernel
 
-template <int D, int kEmuPairs>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int D, int kEmuPairs, int R>
+__global__ void __launch_bounds__(threads_for<R>(), 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_kt,
                    const __grid_constant__ CUtensorMap tm_vt, const PrefillArgs a) {
@@ -195,8 +200,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&sm->q_full[i], 1);
             mbar_init(&sm->q_empty[i], 1);
             mbar_init(&sm->s_full[i], 1);
-            mbar_init(&sm->s_empty[i], 8);  // one arrival per softmax warp of the tile
-            mbar_init(&sm->p_full[i], 8);
+            mbar_init(&sm->s_empty[i], 4 * R);  // one arrival per softmax warp of the tile
+            mbar_init(&sm->p_full[i], 4 * R);
             mbar_init(&sm->o_done[i], 1);
             for (int qq = 0; qq < 4; qq++) mbar_init(&sm->xbar[i][qq], 2);  // one arrival per warp of the pair
             mbar_init(&sm->fin[i], 1);
@@ -208,7 +213,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&sm->v_empty[i], 2);
         }
         mbar_init(&sm->dbg, 1);
-        mbar_init(&sm->retire, 18);  // 16 softmax warps, the producer and tile A's issuer
+        mbar_init(&sm->retire, 8 * R + 2);  // the softmax warps, the producer and tile A's issuer
         fence_barrier_init();
         tma_prefetch_desc(&tm_q);
         tma_prefetch_desc(&tm_k);
@@ -230,7 +235,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const uint32_t tmem_base = sm->tmem_base;
     if (warp == 0) {
-        setmaxnreg_dec<kRegsControl>();
+        if constexpr (R == 2) setmaxnreg_dec<kRegsControl>();
         if (lane != 0) return;
         // ------------------------------------------------------------------ TMA producer
         uint32_t kv_it = 0, k_issued = 0, v_issued = 0, q_uses[2] = {0, 0};
@@ -300,7 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mbar_arrive(&sm->retire);
     } else if (warp == 1 || warp == 2) {
-        setmaxnreg_dec<kRegsControl>();
+        if constexpr (R == 2) setmaxnreg_dec<kRegsControl>();
         if (lane == 0) {
             // ------------------------------------------------------------------ MMA issuers, one thread per tile
             // Both threads walk every KV block of every item: a tile with fewer blocks than its partner still
@@ -379,7 +384,146 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_dealloc(tmem_base, kTmemCols);
         }
     } else if (warp == 3) {
-        setmaxnreg_dec<kRegsControl>();
+        if constexpr (R == 2) setmaxnreg_dec<kRegsControl>();
+    } else if constexpr (R == 1) {
+        // ------------------------------------------------------------------ softmax warps, one thread per row
+        // Warp 4 + 4*tile + quarter owns TMEM lane quarter `quarter` of tile `tile`: each thread a whole query row,
+        // so the row max and the row sum need no exchange. Registers come from the launch bound (no split).
+        const int tile = (warp - 4) >> 2;
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;
+        const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+        const uint32_t s_addr = lane_addr + G::col_s(tile);
+        const uint32_t o_addr = lane_addr + G::col_o(tile);
+        const uint32_t p_addr = lane_addr + G::col_p(tile);
+        uint32_t s_uses = 0, o_uses = 0;
+        bool ok = true;
+        for (int r = 0, it = item_of(0); ok && it < a.total_items; it = item_of(++r)) {
+            const Item x = decode_item<kBN>(a, it);
+            const int nb = x.nblk[tile];
+            if (nb == 0) continue;
+            const int row0 = x.row0[tile];
+            const int qpos = a.start + row0 + row;  // absolute position of this thread's query
+            float m_used = -INFINITY;
+            float2 lsum = make_float2(0.f, 0.f);
+            for (int j = 0; j < nb; j++) {
+                ok = __all_sync(0xffffffffu, mbar_wait(&sm->s_full[tile], s_uses & 1, ab));
+                if (!ok) break;
+                s_uses++;
+                tc_fence_after();
+                float s[kBN];
+#pragma unroll
+                for (int c = 0; c < kBN; c += 32) tmem_ld32(s_addr + c, s + c);
+                tmem_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sm->s_empty[tile]);
+
+                const int kv0 = j * kBN;
+                if (kv0 + kBN - 1 > a.start + row0) {  // the block reaches past the tile's first query: mask
+#pragma unroll
+                    for (int c = 0; c < kBN; c++)
+                        if (kv0 + c > qpos) s[c] = -INFINITY;
+                }
+                float mv[8];
+#pragma unroll
+                for (int i = 0; i < 8; i++) mv[i] = s[i];
+#pragma unroll
+                for (int c = 8; c + 16 <= kBN; c += 16)
+#pragma unroll
+                    for (int i = 0; i < 8; i++) mv[i] = fmax3(mv[i], s[c + i], s[c + 8 + i]);
+#pragma unroll
+                for (int i = 0; i < 8; i++) mv[i] = fmaxf(mv[i], s[kBN - 8 + i]);
+                const float pmax = fmaxf(fmax3(mv[0], mv[1], mv[2]), fmax3(fmax3(mv[3], mv[4], mv[5]), mv[6], mv[7]));
+                // running max in log2 units; it moves only when the block exceeds it by more than the threshold
+                const float pms = pmax * a.scale_log2;
+                const float m_new = (j == 0 || pms > m_used + kRescaleThreshold) ? pms : m_used;
+                const float m_sub = (m_new == -INFINITY) ? 0.f : m_new;
+                const float2 c2 = make_float2(a.scale_log2, a.scale_log2), nm2 = make_float2(-m_sub, -m_sub);
+                uint32_t pk[kBN / 2];
+                float2 ls[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                                make_float2(0.f, 0.f)};
+#pragma unroll
+                for (int pr = 0; pr < kBN / 2; pr++) {
+                    const float2 xx = __ffma2_rn(make_float2(s[2 * pr], s[2 * pr + 1]), c2, nm2);
+                    float2 e;
+                    if ((pr & 7) < kEmuPairs) e = exp2_poly2(make_float2(fmaxf(xx.x, -125.f), fmaxf(xx.y, -125.f)));
+                    else e = make_float2(ex2_approx(xx.x), ex2_approx(xx.y));
+                    ls[pr & 3] = __fadd2_rn(ls[pr & 3], e);
+                    pk[pr] = pack_half2(e.x, e.y);
+                }
+                const float2 lb = __fadd2_rn(__fadd2_rn(ls[0], ls[1]), __fadd2_rn(ls[2], ls[3]));
+                bool rescale = false;
+                float alpha = 1.f;
+                if (j > 0 && m_new > m_used) {
+                    alpha = ex2_approx(m_used - m_new);
+                    rescale = true;
+                    lsum.x *= alpha;
+                    lsum.y *= alpha;
+                }
+                m_used = m_new;
+                lsum = __fadd2_rn(lsum, lb);
+                if (j > 0) {  // PV(j-1) must be done before P is overwritten or O is rescaled
+                    ok = __all_sync(0xffffffffu, mbar_wait(&sm->o_done[tile], o_uses & 1, ab));
+                    if (!ok) break;
+                    o_uses++;
+                    tc_fence_after();
+                }
+                if (__any_sync(0xffffffffu, rescale)) {  // warp-collective TMEM access: alpha is 1 for other rows
+#pragma unroll
+                    for (int c0 = 0; c0 < D; c0 += 32) {
+                        float o[32];
+                        tmem_ld32(o_addr + c0, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int c = 0; c < 32; c++) o[c] *= alpha;
+                        tmem_st32(o_addr + c0, o);
+                    }
+                }
+#pragma unroll
+                for (int c = 0; c < kBN / 2; c += 32) tmem_st32(p_addr + c, reinterpret_cast<const float*>(pk + c));
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sm->p_full[tile]);
+            }
+            if (!ok) break;
+            // epilogue: O / l
+            ok = __all_sync(0xffffffffu, mbar_wait(&sm->o_done[tile], o_uses & 1, ab));
+            if (!ok) break;
+            o_uses++;
+            tc_fence_after();
+            const float inv = 1.f / (lsum.x + lsum.y);
+            const int t = row0 + row;
+            const int64_t off = x.seq * a.out_seq_stride + static_cast<int64_t>(t) * a.out_token_stride +
+                                static_cast<int64_t>(x.head) * D;
+#pragma unroll
+            for (int c0 = 0; c0 < D; c0 += 32) {
+                float o[32];
+                tmem_ld32(o_addr + c0, o);
+                tmem_wait_ld();
+                if (t < a.tokens) {
+                    if (a.out_f16) {
+                        uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(a.out) + off + c0);
+#pragma unroll
+                        for (int c = 0; c < 32; c += 8)
+                            dst[c / 8] = make_uint4(pack_half2(o[c] * inv, o[c + 1] * inv),
+                                                    pack_half2(o[c + 2] * inv, o[c + 3] * inv),
+                                                    pack_half2(o[c + 4] * inv, o[c + 5] * inv),
+                                                    pack_half2(o[c + 6] * inv, o[c + 7] * inv));
+                    } else {
+                        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + off + c0);
+#pragma unroll
+                        for (int c = 0; c < 32; c += 4)
+                            dst[c / 4] = make_float4(o[c] * inv, o[c + 1] * inv, o[c + 2] * inv, o[c + 3] * inv);
+                    }
+                }
+            }
+            tc_fence_before();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm->retire);
     } else {
         setmaxnreg_inc<kRegsSoftmax>();
         // ------------------------------------------------------------------ softmax warps
@@ -630,13 +774,32 @@ int prefill_emu_pairs() {
 
 using PrefillFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, PrefillArgs);
 
+// Softmax threads per query row: one at head_dim 128 (822 against 747 TFLOP/s on 30 layers x 4096 tokens), two at
+// head_dim 64 (637 against 612-617: with a whole 128-column row per thread two softmax warps per SMSP hide less
+// latency than four). ALPACA_PREFILL_ROWS = 1 or 2 forces either.
+int prefill_row_threads(int head_dim) {
+    static const int v = [] {
+        const char* e = std::getenv("ALPACA_PREFILL_ROWS");
+        return e ? (e[0] == '1' ? 1 : 2) : 0;
+    }();
+    return v ? v : (head_dim == 128 ? 1 : 2);
+}
+
 template <int D>
-PrefillFn prefill_variant(int emu) {
+PrefillFn prefill_variant(int emu, int rows) {
+    if (rows == 1) {
+        switch (emu) {
+            case 0: return prefill_kernel<D, 0, 1>;
+            case 3: return prefill_kernel<D, 3, 1>;
+            case 4: return prefill_kernel<D, 4, 1>;
+            default: return prefill_kernel<D, 2, 1>;
+        }
+    }
     switch (emu) {
-        case 0: return prefill_kernel<D, 0>;
-        case 3: return prefill_kernel<D, 3>;
-        case 4: return prefill_kernel<D, 4>;
-        default: return prefill_kernel<D, 2>;
+        case 0: return prefill_kernel<D, 0, 2>;
+        case 3: return prefill_kernel<D, 3, 2>;
+        case 4: return prefill_kernel<D, 4, 2>;
+        default: return prefill_kernel<D, 2, 2>;
     }
 }
 
@@ -655,7 +818,9 @@ size_t prefill_workspace_bytes(const alpaca_attn_desc& d) {
 cudaError_t launch_prefill(const Call& c, cudaStream_t s) {
     const alpaca_attn_desc& d = *c.d;
     const bool d128 = d.head_dim == 128;
-    const PrefillFn fn = d128 ? prefill_variant<128>(prefill_emu_pairs()) : prefill_variant<64>(prefill_emu_pairs());
+    const int rows = prefill_row_threads(d.head_dim);
+    const PrefillFn fn = d128 ? prefill_variant<128>(prefill_emu_pairs(), rows)
+                              : prefill_variant<64>(prefill_emu_pairs(), rows);
     const size_t smem = d128 ? smem_bytes<128>() : smem_bytes<64>();
     const int bn = d128 ? PG<128>::BN : PG<64>::BN;
     // per-device function attribute (host-side, cheap next to the launch itself)
@@ -723,7 +888,7 @@ cudaError_t launch_prefill(const Call& c, cudaStream_t s) {
     const int grid = std::max(1, std::min(a.total_items, c.num_sms));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid, 1, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.blockDim = dim3(rows == 1 ? threads_for<1>() : threads_for<2>(), 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
