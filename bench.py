@@ -36,6 +36,7 @@ METRIC = "prefill attn TFLOP/s + decode attn HBM GB/s; tokens/s at 1/2/4/8 B200"
 H, KVH, D = 9, 3, 64
 LAYERS = 30
 T_PREFILL = 4096
+PAGED_BLOCK_ROWS = 256
 DEC_BATCH, DEC_CAP = 64, 4096
 
 
@@ -406,7 +407,9 @@ def run_cfg5(args):
     """Config 5: SmolLM2-1.7B shape (32/32 heads, d=64) ragged mixed batch — 256 prefill sequences with lengths
     log-uniform in [128, 8192] and 512 one-token decode sequences over f16 caches of 1..8192 rows — whole sequences
     packed over the ranks longest-processing-time first. Per rank one step = one prefill call per sequence (spread
-    over 4 streams) + one ragged decode call, captured in a CUDA graph and replayed."""
+    over 4 streams) + one ragged decode call, captured in a CUDA graph and replayed. With --paged every sequence's
+    K/V rows live in one shared pool of 256-row blocks in shuffled order (per-sequence block tables), the serving
+    layout, instead of a buffer per prefill sequence and a decode cache padded to the longest context."""
     import numpy as np
     import torch
 
@@ -430,23 +433,53 @@ def run_cfg5(args):
     my_dec = [int(dec_L[u.seq - 256]) for u in mine if u.seq >= 256]
     g = torch.Generator(device=dev)
     g.manual_seed(20260105 + 1000 * rank)
-    # prefill: each sequence in its own buffers
-    pre = []
-    for T in my_pre:
-        q = torch.randn((T, NH, D), generator=g, device=dev).half()
-        k = torch.randn((T, NKV, D), generator=g, device=dev).half()
-        v = torch.randn((T, NKV, D), generator=g, device=dev).half()
-        o = torch.empty((T, NH, D), dtype=torch.float32, device=dev)
-        pre.append((q, k, v, o, ab.make_desc(q, k, v, o)))
-    # decode: one ragged batch
     nd = len(my_dec)
     cap = max(my_dec) if nd else 1
+    kv_bytes = 0
+    if args.paged:
+        # one pool of R-row blocks for every sequence of this rank, handed out in a shuffled order
+        R = PAGED_BLOCK_ROWS
+        nb_pre = [-(-T // R) for T in my_pre]
+        nb_dec = [-(-L // R) for L in my_dec]
+        total = max(1, sum(nb_pre) + sum(nb_dec))
+        order = torch.randperm(total, generator=torch.Generator().manual_seed(20260106 + rank)).to(torch.int32)
+        kpool = torch.randn((total, R, NKV, D), generator=g, device=dev, dtype=torch.float16)
+        vpool = torch.randn((total, R, NKV, D), generator=g, device=dev, dtype=torch.float16)
+        kv_bytes = 2 * kpool.numel() * 2
+        nxt = 0
+        pre = []
+        for T, nb in zip(my_pre, nb_pre):
+            tab = order[nxt:nxt + nb].reshape(1, nb).to(dev).contiguous()
+            nxt += nb
+            q = torch.randn((T, NH, D), generator=g, device=dev).half()
+            o = torch.empty((T, NH, D), dtype=torch.float32, device=dev)
+            pre.append((q, tab, o, ab.make_desc(q, kpool, vpool, o, block_table=tab)))
+        mb = max(nb_dec) if nd else 1
+        dtab = torch.zeros((max(nd, 1), mb), dtype=torch.int32)
+        for i, nb in enumerate(nb_dec):
+            dtab[i, :nb] = order[nxt:nxt + nb]
+            nxt += nb
+        dtab = dtab.to(dev)
+        dk, dv = kpool, vpool
+    else:
+        # prefill: each sequence in its own buffers
+        pre = []
+        for T in my_pre:
+            q = torch.randn((T, NH, D), generator=g, device=dev).half()
+            k = torch.randn((T, NKV, D), generator=g, device=dev).half()
+            v = torch.randn((T, NKV, D), generator=g, device=dev).half()
+            o = torch.empty((T, NH, D), dtype=torch.float32, device=dev)
+            kv_bytes += 2 * k.numel() * 2
+            pre.append((q, k, v, o, ab.make_desc(q, k, v, o)))
+        # decode: one ragged batch
+        dk = torch.randn((max(nd, 1), cap, NKV, D), generator=g, device=dev).half()
+        dv = torch.randn((max(nd, 1), cap, NKV, D), generator=g, device=dev).half()
+        kv_bytes += 2 * dk.numel() * 2
+        dtab = None
     dq = torch.randn((max(nd, 1), 1, NH, D), generator=g, device=dev)
-    dk = torch.randn((max(nd, 1), cap, NKV, D), generator=g, device=dev).half()
-    dv = torch.randn((max(nd, 1), cap, NKV, D), generator=g, device=dev).half()
     do = torch.empty((max(nd, 1), 1, NH, D), dtype=torch.float32, device=dev)
     lens = torch.tensor(my_dec if nd else [1], dtype=torch.int32, device=dev)
-    ddesc = ab.make_desc(dq, dk, dv, do, ctx_lens=lens, max_ctx_len=cap)
+    ddesc = ab.make_desc(dq, dk, dv, do, ctx_lens=lens, max_ctx_len=cap, block_table=dtab)
     ws = torch.empty(max(16, ab.workspace_bytes(ddesc, Kernel.DECODE_SPLIT)), dtype=torch.uint8, device=dev)
     streams = [torch.cuda.Stream(device=dev) for _ in range(4)]
 
@@ -458,7 +491,7 @@ def run_cfg5(args):
         for n, i in enumerate(order):
             st = streams[n % len(streams)]
             st.wait_event(ev)
-            ab.launch(pre[i][4], Kernel.PREFILL_TC, None, st)
+            ab.launch(pre[i][-1], Kernel.PREFILL_TC, None, st)
         if nd:
             ab.launch(ddesc, Kernel.DECODE_SPLIT, ws, cur)
         for st in streams:
@@ -506,7 +539,12 @@ def run_cfg5(args):
                                    "sequences, lengths log-uniform [128, 8192], + 512 decode sequences, contexts "
                                    "U[1, 8192]; whole sequences LPT-packed over the GPUs",
                        "prefill_tokens": int(pre_T.sum()), "decode_tokens": len(dec_L),
-                       "parallelism": f"sequence-sharded x{world}", "plan_imbalance": plan.imbalance},
+                       "parallelism": f"sequence-sharded x{world}", "plan_imbalance": plan.imbalance,
+                       "kv_layout": (f"paged: one pool of {PAGED_BLOCK_ROWS}-row blocks per GPU, shuffled block "
+                                     f"order, per-sequence block tables" if args.paged else
+                                     "contiguous: a buffer per prefill sequence, decode cache padded to the "
+                                     "longest context"),
+                       "kv_gb_rank0": kv_bytes / 1e9},
             "prefill_tflops_if_alone": job_flops / (ms_max * 1e-3) / 1e12,
             "decode_kv_gbs_if_alone": job_kv_bytes / (ms_max * 1e-3) / 1e9,
             "gpu_launches": args.steps * (len(pre) + (2 if nd else 0)),
@@ -670,6 +708,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--paged", action="store_true",
+                    help="cfg5: K/V of every sequence in one shuffled pool of 256-row blocks (block tables)")
     ap.add_argument("--workload", choices=["cfg2", "cfg4", "cfg5"], default="cfg2",
                     help="cfg2 (default headline, weak scaling), cfg4 (8 x 4096 at 15/5 heads, strong scaling) or "
                          "cfg5 (ragged mixed prefill + decode batch at 32/32 heads, strong scaling)")
