@@ -8,11 +8,12 @@ sources (``csrc/``), its in-tree build (``build``) and a Python host mirror of a
 """
 from ._lib import (EXPORTED_SYMBOLS, FLAG_DEBUG_FORCE_TIMEOUT, LIB_PATH, AlpacaCUDAError, AttnDesc, DType, Kernel,
                    RopeDesc, Status, load)
-from .ops import (KV_PADDING_ROWS, attention, attention_device, device_status, launch, make_desc, make_rope_desc,
-                  rope, rope_kv_append, rope_launch, select_kernel, workspace_bytes)
+from .ops import (KV_PADDING_ROWS, attention, attention_device, decode_rope, device_status, launch, make_desc,
+                  make_rope_desc, rope, rope_kv_append, rope_launch, select_kernel, workspace_bytes)
 
 __all__ = [
     "EXPORTED_SYMBOLS", "FLAG_DEBUG_FORCE_TIMEOUT", "LIB_PATH", "AlpacaCUDAError", "AttnDesc", "DType", "Kernel",
     "Status", "load", "KV_PADDING_ROWS", "attention", "attention_device", "device_status", "launch", "make_desc",
     "select_kernel", "workspace_bytes", "RopeDesc", "make_rope_desc", "rope", "rope_kv_append", "rope_launch",
+    "decode_rope",
 ]

@@ -113,6 +113,7 @@ EXPORTED_SYMBOLS = (
     "alpaca_attn_prefill",
     "alpaca_attn_decode",
     "alpaca_attn_decode_noalloc",
+    "alpaca_attn_decode_rope",
     "alpaca_attention_workspace_bytes",
     "alpaca_attention_select",
     "alpaca_cuda_device_status",
@@ -156,6 +157,9 @@ def load() -> ctypes.CDLL:
     L.alpaca_cuda_version.argtypes = []
     L.alpaca_rope_kv_append.restype = ctypes.c_int
     L.alpaca_rope_kv_append.argtypes = [ctypes.POINTER(RopeDesc), ctypes.c_void_p]
+    L.alpaca_attn_decode_rope.restype = ctypes.c_int
+    L.alpaca_attn_decode_rope.argtypes = [P, ctypes.POINTER(RopeDesc), ctypes.c_void_p, ctypes.c_size_t,
+                                          ctypes.c_void_p]
     _lib = L
     return L
 

@@ -317,6 +317,49 @@ alpaca_cuda_status alpaca_attn_decode_noalloc(const alpaca_attn_desc* desc, alpa
     return ok();
 }
 
+alpaca_cuda_status alpaca_attn_decode_rope(const alpaca_attn_desc* attn, const alpaca_rope_desc* rope,
+                                           void* workspace, size_t workspace_bytes, alpaca_stream_t stream) {
+    alpaca_cuda_status st = validate(attn);
+    if (st != ALPACA_CUDA_OK) return st;
+    st = check_kind(*attn, ALPACA_ATTN_DECODE_SPLIT);
+    if (st != ALPACA_CUDA_OK) return st;
+    st = validate_rope(rope);
+    if (st != ALPACA_CUDA_OK) return st;
+    const alpaca_attn_desc& d = *attn;
+    const alpaca_rope_desc& r = *rope;
+    auto bad = [](const char* what) { return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, std::string("decode_rope: ") + what); };
+    if (r.n_seqs != d.n_seqs || r.tokens != 1 || r.n_heads != d.n_heads || r.n_kv_heads != d.n_kv_heads ||
+        r.head_dim != d.head_dim)
+        return bad("the RoPE descriptor must describe one new token of the attention call's sequences and heads");
+    if (r.q != d.q || r.q_dtype != d.q_dtype || (d.n_seqs > 1 && r.q_seq_stride != d.q_seq_stride))
+        return bad("the RoPE descriptor's q must be the attention call's q");
+    if (r.cache_dtype != ALPACA_F16 || r.k_cache != d.k || r.v_cache != d.v || r.cache_row_stride != d.kv_row_stride)
+        return bad("the RoPE descriptor's caches must be the attention call's f16 K / V caches");
+    if (r.block_table != d.block_table ||
+        (d.block_table ? (r.block_rows != d.block_rows || r.max_blocks != d.max_blocks ||
+                          r.block_stride != d.block_stride || r.pool_blocks != d.pool_blocks)
+                       : (d.n_seqs > 1 && r.cache_seq_stride != d.kv_seq_stride)))
+        return bad("the RoPE descriptor's cache layout must be the attention call's");
+    if (r.positions || (!d.ctx_lens && r.start_position != d.start_position))
+        return bad("the new token's position is the attention call's (ctx_lens - 1, or start_position): positions "
+                   "must be NULL and start_position equal to the attention descriptor's");
+    const size_t need = decode_workspace_bytes(d);
+    if (need > 0 && (workspace_bytes < need || !workspace))
+        return fail(ALPACA_CUDA_ERR_WORKSPACE_TOO_SMALL, "decode_rope: workspace of " + std::to_string(workspace_bytes) +
+                                                             " bytes, " + std::to_string(need) + " needed");
+    if (need > 0 && !aligned16(workspace))
+        return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "decode_rope: workspace must be 16-byte aligned");
+    DeviceInfo di;
+    cudaError_t e = device_info(&di);
+    if (e != cudaSuccess) return fail(ALPACA_CUDA_ERR_CUDA, std::string("decode_rope: device query: ") + cudaGetErrorString(e));
+    Call c{attn, d.scale > 0.f ? d.scale : 1.0f / std::sqrt(static_cast<float>(d.head_dim)), di.err, workspace,
+           workspace_bytes, di.num_sms};
+    c.rope = rope;
+    e = launch_decode(c, reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return fail(ALPACA_CUDA_ERR_LAUNCH_FAILED, std::string("decode_rope launch failed: ") + cudaGetErrorString(e));
+    return ok();
+}
+
 alpaca_cuda_status alpaca_rope_kv_append(const alpaca_rope_desc* desc, alpaca_stream_t stream) {
     alpaca_cuda_status st = validate_rope(desc);
     if (st != ALPACA_CUDA_OK) return st;

@@ -21,6 +21,7 @@
 // Scores are kept in log2 units (q pre-scaled by scale*log2(e)), so every exponential is one ex2.approx.
 // Partial-state layout: [seq][kv_head][split][g][d + 2] f32 = accumulators, then m (log2 units), then l.
 #include <algorithm>
+#include <cmath>
 #include <cstdlib>
 #include <mutex>
 
@@ -62,6 +63,13 @@ struct DecodeArgs {
     int block_rows, max_blocks, pool_blocks;
     int64_t block_stride;
     unsigned* err;
+    // Fused RoPE + KV append (alpaca_attn_decode_rope): each sequence's new token sits at row ctx_len - 1; its
+    // k / v rows (f32 [seq][kv_head][d]) are rotated / copied into the cache there, and q is rotated as it is read.
+    int rope, interleaved;
+    const float* k_new;
+    const float* v_new;
+    int64_t new_seq_stride;
+    double freq[128];  // theta^(-2i/d), host-computed in double as for alpaca_rope_kv_append
 };
 
 // Element offset of cache row `row0` of KV head `kvh` of sequence `seq` (contiguous, or through the block table;
@@ -143,9 +151,10 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 // Rows past the context are zero-filled and never read. Each thread later reads back only the chunks it copied.
 // kSwz: 16-byte chunk c of row r is stored at chunk c ^ (r & 7), so the eight rows an ldmatrix reads at one chunk
 // index fall in eight different bank groups.
-template <int D, bool kSwz = false>
+// kSkip: row skip_row (absolute) is not copied at all because the CTA writes it into the tiles itself.
+template <int D, bool kSwz = false, bool kSkip = false>
 __device__ __forceinline__ void stage_unit(const DecodeArgs& a, int seq, int kvh, int row0, int row_end,
-                                           __half* s_k, __half* s_v, int lr, int rowlane) {
+                                           __half* s_k, __half* s_v, int lr, int rowlane, int skip_row = -1) {
     constexpr int RPS = Geo<D>::RPS;
     bool valid;
     const int64_t base = unit_offset(a, seq, kvh, row0, D, valid) + lr * 8;
@@ -154,7 +163,9 @@ __device__ __forceinline__ void stage_unit(const DecodeArgs& a, int seq, int kvh
         const int rl = i * RPS + rowlane, r = row0 + rl;
         const bool in = valid && r < row_end;
         const int c = kSwz ? (lr ^ (rl & 7)) : lr;
-        cp_async16(s_k + rl * D + c * 8, a.k + base + (in ? static_cast<int64_t>(rl) * a.kv_row_stride : 0), in ? 16u : 0u);
+        if (!kSkip || r != skip_row)
+            cp_async16(s_k + rl * D + c * 8, a.k + base + (in ? static_cast<int64_t>(rl) * a.kv_row_stride : 0),
+                       in ? 16u : 0u);
     }
     cp_async_commit();
 #pragma unroll
@@ -162,9 +173,127 @@ __device__ __forceinline__ void stage_unit(const DecodeArgs& a, int seq, int kvh
         const int rl = i * RPS + rowlane, r = row0 + rl;
         const bool in = valid && r < row_end;
         const int c = kSwz ? (lr ^ (rl & 7)) : lr;
-        cp_async16(s_v + rl * D + c * 8, a.v + base + (in ? static_cast<int64_t>(rl) * a.kv_row_stride : 0), in ? 16u : 0u);
+        if (!kSkip || r != skip_row)
+            cp_async16(s_v + rl * D + c * 8, a.v + base + (in ? static_cast<int64_t>(rl) * a.kv_row_stride : 0),
+                       in ? 16u : 0u);
     }
     cp_async_commit();
+}
+
+// ---- fused RoPE + KV append: the same arithmetic as alpaca_rope_kv_append (rope_kv.cu), so the fused call gives
+// the results of the two calls bit for bit: angle position * freq and cos / sin in double, rounded once to f32,
+// rotation as separately rounded f32 products, f16 values rounded once.
+
+// (cos, sin) of position pos for the D/2 pairs.
+template <int D>
+__device__ __forceinline__ void rope_table(const DecodeArgs& a, int pos, float2* s_cs, int tid) {
+    for (int i = tid; i < D / 2; i += kThreads) {
+        double sn, cs;
+        sincos(static_cast<double>(pos) * a.freq[i], &sn, &cs);
+        s_cs[i] = make_float2(static_cast<float>(cs), static_cast<float>(sn));
+    }
+}
+
+// Pair partner of element dim (D elements per row) and whether dim is the pair's first element.
+__device__ __forceinline__ int rope_partner(int dim, int D, int interleaved, bool& first) {
+    const int h = D / 2;
+    first = interleaved ? (dim & 1) == 0 : dim < h;
+    return interleaved ? dim ^ 1 : (first ? dim + h : dim - h);
+}
+// Rotated element from the element x and its partner xp: a' = a c - b s for the first, b' = a s + b c for the
+// second element of a pair (a, b), as separately rounded f32 operations.
+__device__ __forceinline__ float rope_rotate(float x, float xp, int dim, int D, int interleaved, const float2* cs) {
+    const int h = D / 2;
+    const bool first = interleaved ? (dim & 1) == 0 : dim < h;
+    const float2 w = cs[interleaved ? dim >> 1 : (first ? dim : dim - h)];
+    const float a0 = first ? x : xp, b0 = first ? xp : x;
+    return first ? __fsub_rn(__fmul_rn(a0, w.x), __fmul_rn(b0, w.y)) : __fadd_rn(__fmul_rn(a0, w.y), __fmul_rn(b0, w.x));
+}
+
+// Fused-call prologue, part 1 (before the (cos, sin) table): this thread's query elements of the G heads and their
+// partners, and for the CTA holding the new row its k / v elements, loaded while the table is computed.
+template <int D, int G>
+struct RopeRegs {
+    static constexpr int QE = (G * D + kThreads - 1) / kThreads;  // query elements per thread
+    float qx[QE], qp[QE];
+    float nx[8], np[8];  // new row: 8 elements of one 16-byte chunk of k or v, and (k) their partners
+};
+
+template <int D, int G>
+__device__ __forceinline__ void rope_load(const DecodeArgs& a, int seq, int kvh, bool has_new_row, int tid,
+                                          RopeRegs<D, G>& r) {
+    const int64_t qbase = static_cast<int64_t>(seq) * a.q_seq_stride + static_cast<int64_t>(kvh * G) * D;
+#pragma unroll
+    for (int k = 0; k < RopeRegs<D, G>::QE; k++) {
+        const int i = tid + k * kThreads;
+        r.qx[k] = r.qp[k] = 0.f;
+        if (i < G * D) {
+            const int g = i / D, dim = i - g * D;
+            bool first;
+            const int pd = rope_partner(dim, D, a.interleaved, first);
+            const int64_t o = qbase + static_cast<int64_t>(g) * D;
+            if (a.q_f16) {
+                r.qx[k] = __half2float(static_cast<const __half*>(a.q)[o + dim]);
+                r.qp[k] = __half2float(static_cast<const __half*>(a.q)[o + pd]);
+            } else {
+                r.qx[k] = static_cast<const float*>(a.q)[o + dim];
+                r.qp[k] = static_cast<const float*>(a.q)[o + pd];
+            }
+        }
+    }
+    constexpr int CH = D / 8;
+    if (has_new_row && tid < 2 * CH) {
+        const bool is_k = tid < CH;
+        const int c = is_k ? tid : tid - CH;
+        const float* src = (is_k ? a.k_new : a.v_new) + static_cast<int64_t>(seq) * a.new_seq_stride +
+                           static_cast<int64_t>(kvh) * D;
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            const int dim = c * 8 + e;
+            bool first;
+            r.nx[e] = src[dim];
+            r.np[e] = is_k ? src[rope_partner(dim, D, a.interleaved, first)] : 0.f;
+        }
+    }
+}
+
+// Part 2 (after the table): the rotated queries into s_q [G][D] (rounded to f16 when q is f16, as the in-place
+// rotation stores them), and the new row — rotated k and raw v rounded to f16 — into the cache in global memory and
+// straight into the unit's tiles (local row row - row0; swizzled chunks when kSwz).
+template <int D, int G, bool kSwz>
+__device__ __forceinline__ void rope_store(const DecodeArgs& a, int seq, int kvh, int row, int row0, __half* s_k,
+                                           __half* s_v, float* s_q, const float2* cs, int tid,
+                                           const RopeRegs<D, G>& r) {
+#pragma unroll
+    for (int k = 0; k < RopeRegs<D, G>::QE; k++) {
+        const int i = tid + k * kThreads;
+        if (i < G * D) {
+            const int dim = i % D;
+            float x = rope_rotate(r.qx[k], r.qp[k], dim, D, a.interleaved, cs);
+            if (a.q_f16) x = __half2float(__float2half_rn(x));
+            s_q[i] = x;
+        }
+    }
+    constexpr int CH = D / 8;
+    if (row < 0 || tid >= 2 * CH) return;
+    const bool is_k = tid < CH;
+    const int c = is_k ? tid : tid - CH;
+    uint32_t w[4];
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+        const int dim = c * 8 + e;
+        const float x0 = is_k ? rope_rotate(r.nx[e], r.np[e], dim, D, a.interleaved, cs) : r.nx[e];
+        const float x1 = is_k ? rope_rotate(r.nx[e + 1], r.np[e + 1], dim + 1, D, a.interleaved, cs) : r.nx[e + 1];
+        const __half2 h = __floats2half2_rn(x0, x1);
+        w[e / 2] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    const uint4 u = make_uint4(w[0], w[1], w[2], w[3]);
+    const int rl = row - row0;
+    const int cc = kSwz ? (c ^ (rl & 7)) : c;
+    *reinterpret_cast<uint4*>((is_k ? s_k : s_v) + rl * D + cc * 8) = u;
+    bool valid;
+    const int64_t off = unit_offset(a, seq, kvh, row, D, valid);
+    if (valid) *reinterpret_cast<uint4*>(const_cast<__half*>(is_k ? a.k : a.v) + off + c * 8) = u;
 }
 
 // ---- tensor-core form of a unit: mma.sync m16n8k16 (f16 operands, f32 accumulators) with split-precision A
@@ -202,10 +331,12 @@ __device__ __forceinline__ void split_f16x2(float x0, float x1, uint32_t& hi, ui
 // than in a buffer of their own, which would cost a CTA per SM.
 __host__ __device__ constexpr bool tc_red_aliases_kv(int D) { return D == 128; }
 
-template <int D, int G, int kAfter>
+// kRope: the rotated queries of the G heads are in shared memory (s_q [G][D] f32) instead of global memory.
+template <int D, int G, int kAfter, bool kRope = false>
 __device__ __forceinline__ void compute_unit_tc(const DecodeArgs& a, int seq, int kvh, int split, int row0,
                                                 int row_end, int nsplits, const __half* s_k, const __half* s_v,
-                                                float* s_red, float* s_stat, int tid, int warp, int lane) {
+                                                float* s_red, float* s_stat, const float* s_q, int tid, int warp,
+                                                int lane) {
     constexpr int SL = Geo<D>::SL, RW = SL / 4, NT = RW / 8, KS = D / 16, DT = D / 8;
     static_assert(NT % 2 == 0 && KS % 2 == 0 && DT % 2 == 0, "tile shape");
     const int g = lane >> 2, t4 = lane & 3;
@@ -223,7 +354,8 @@ __device__ __forceinline__ void compute_unit_tc(const DecodeArgs& a, int seq, in
             for (int h = 0; h < 2; h++) {
                 const int col = kk * 16 + h * 8 + t4 * 2;
                 float2 v;
-                if (a.q_f16) v = __half22float2(*reinterpret_cast<const __half2*>(static_cast<const __half*>(a.q) + qoff + col));
+                if (kRope) v = *reinterpret_cast<const float2*>(s_q + (act ? g : 0) * D + col);
+                else if (a.q_f16) v = __half22float2(*reinterpret_cast<const __half2*>(static_cast<const __half*>(a.q) + qoff + col));
                 else v = *reinterpret_cast<const float2*>(static_cast<const float*>(a.q) + qoff + col);
                 x[2 * h] = act ? v.x * a.scale_log2 : 0.f;
                 x[2 * h + 1] = act ? v.y * a.scale_log2 : 0.f;
@@ -347,10 +479,11 @@ __device__ __forceinline__ void store_out_dec(const DecodeArgs& a, int seq, int 
 // One unit = SL cache rows of one KV head of one sequence, for its G query heads. kAfter = commit groups issued
 // after this unit's two (the next unit's prefetch), so the waits below release exactly this unit's K, then V.
 // s_red reuses this unit's K|V buffers after the last read of them.
-template <int D, int G, int kAfter>
+template <int D, int G, int kAfter, bool kRope = false>
 __device__ __forceinline__ void compute_unit(const DecodeArgs& a, int seq, int kvh, int split, int row0, int row_end,
                                              int nsplits, const __half* s_k, const __half* s_v, float* s_p,
-                                             float* s_ml, int tid, int warp, int lane, int lr, int rowlane) {
+                                             float* s_ml, const float* s_q, int tid, int warp, int lane, int lr,
+                                             int rowlane) {
     using Gm = Geo<D>;
     constexpr int SL = Gm::SL, RPS = Gm::RPS, LPR = Gm::LPR;
     float* s_red = reinterpret_cast<float*>(const_cast<__half*>(s_k));  // [RPS][G][D] (K|V are contiguous)
@@ -360,7 +493,10 @@ __device__ __forceinline__ void compute_unit(const DecodeArgs& a, int seq, int k
 #pragma unroll
     for (int g = 0; g < G; g++) {
         const int64_t qoff = static_cast<int64_t>(seq) * a.q_seq_stride + static_cast<int64_t>(kvh * G + g) * D + lr * 8;
-        if (a.q_f16) {
+        if (kRope) {
+#pragma unroll
+            for (int e = 0; e < 8; e++) qv[g][e] = s_q[g * D + lr * 8 + e];
+        } else if (a.q_f16) {
             const uint4 u = *reinterpret_cast<const uint4*>(static_cast<const __half*>(a.q) + qoff);
             half8_to_float(u, qv[g]);
         } else {
@@ -477,7 +613,7 @@ __device__ __forceinline__ void compute_unit(const DecodeArgs& a, int seq, int k
 }
 
 // One CTA per (KV head x split, sequence) grid cell; CTAs past a sequence's context exit at once.
-template <int D, int G, bool kTc>
+template <int D, int G, bool kTc, bool kRope>
 __global__ void __launch_bounds__(kThreads, (G <= 4 ? 6 : 3)) decode_split_kernel(const DecodeArgs a) {
     using Gm = Geo<D>;
     constexpr int SL = Gm::SL, LPR = Gm::LPR, RPW = Gm::RPW;
@@ -501,16 +637,32 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 6 : 3)) decode_split_kerne
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int lr = lane % LPR, rowlane = warp * RPW + lane / LPR;
-    if (kTc) {
-        stage_unit<D, true>(a, seq, kvh, row0, row_end, s_k, s_v, lr, rowlane);
-        float* s_red = tc_red_aliases_kv(D) ? reinterpret_cast<float*>(s_k) : s_p;
-        float* s_stat = tc_red_aliases_kv(D) ? s_p : s_p + 4 * G * D;
-        compute_unit_tc<D, G, 0>(a, seq, kvh, split, row0, row_end, nsplits, s_k, s_v, s_red, s_stat, tid, warp, lane);
+    float* s_red = tc_red_aliases_kv(D) ? reinterpret_cast<float*>(s_k) : s_p;  // tensor-core form
+    float* s_stat = tc_red_aliases_kv(D) ? s_p : s_p + 4 * G * D;
+    // Fused RoPE + append (kRope): [D/2] (cos, sin) after the statistics, and the G rotated query rows [G][D] f32 —
+    // over the P·V reduction rows in the tensor-core form at head_dim 64 (read into registers before those are
+    // written), after the table otherwise.
+    float2* s_cs = reinterpret_cast<float2*>(kTc ? s_stat + 8 * G : s_ml + 2 * G);
+    float* s_q = (kTc && !tc_red_aliases_kv(D)) ? s_red : reinterpret_cast<float*>(s_cs + D / 2);
+    if constexpr (kRope) {
+        // The sequence's new token is row L - 1; the CTA whose unit holds it writes that row itself.
+        const int new_row = row_end == L ? L - 1 : -1;
+        stage_unit<D, kTc, true>(a, seq, kvh, row0, row_end, s_k, s_v, lr, rowlane, new_row);
+        RopeRegs<D, G> rr;
+        rope_load<D, G>(a, seq, kvh, new_row >= 0, tid, rr);  // loads in flight with the unit's copies
+        rope_table<D>(a, L - 1, s_cs, tid);
+        __syncthreads();
+        rope_store<D, G, kTc>(a, seq, kvh, new_row, row0, s_k, s_v, s_q, s_cs, tid, rr);
+        __syncthreads();  // rotated queries and the new row are in shared memory before any thread reads them
     } else {
-        stage_unit<D>(a, seq, kvh, row0, row_end, s_k, s_v, lr, rowlane);
-        compute_unit<D, G, 0>(a, seq, kvh, split, row0, row_end, nsplits, s_k, s_v, s_p, s_ml, tid, warp, lane, lr,
-                              rowlane);
+        stage_unit<D, kTc>(a, seq, kvh, row0, row_end, s_k, s_v, lr, rowlane);
     }
+    if (kTc)
+        compute_unit_tc<D, G, 0, kRope>(a, seq, kvh, split, row0, row_end, nsplits, s_k, s_v, s_red, s_stat, s_q, tid,
+                                        warp, lane);
+    else
+        compute_unit<D, G, 0, kRope>(a, seq, kvh, split, row0, row_end, nsplits, s_k, s_v, s_p, s_ml, s_q, tid, warp,
+                                     lane, lr, rowlane);
     // The combine kernel may start launching now; it waits for this grid's memory before reading.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
@@ -625,8 +777,9 @@ cudaError_t launch_split(const DecodeArgs& a, int n_seqs, cudaStream_t s) {
     // K and V tiles (2 * SL * D halves; the reduction buffer RPS*G*D floats fits inside them), scores, (m, l);
     // tensor-core form: K and V tiles, the four warps' P·V rows [4][G][D] and their (max, sum) [2][4][G]
     const size_t smem =
-        tc ? sizeof(__half) * 2 * Gm::SL * D + sizeof(float) * ((tc_red_aliases_kv(D) ? 0 : 4 * G * D) + 8 * G)
-           : sizeof(__half) * 2 * Gm::SL * D + sizeof(float) * (G * Gm::SL + 2 * G);
+        (tc ? sizeof(__half) * 2 * Gm::SL * D + sizeof(float) * ((tc_red_aliases_kv(D) ? 0 : 4 * G * D) + 8 * G)
+            : sizeof(__half) * 2 * Gm::SL * D + sizeof(float) * (G * Gm::SL + 2 * G)) +
+        (a.rope ? sizeof(float2) * (D / 2) + ((tc && !tc_red_aliases_kv(D)) ? 0 : sizeof(float) * G * D) : 0);
     static_assert(4 * G * D * sizeof(float) <= sizeof(__half) * 2 * Gm::SL * D, "P·V rows must fit the K|V tiles");
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.max_splits * a.n_kv_heads, n_seqs, 1);
@@ -638,12 +791,19 @@ cudaError_t launch_split(const DecodeArgs& a, int n_seqs, cudaStream_t s) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() ? 1 : 0;
-    const auto fn = tc ? decode_split_kernel<D, G, true> : decode_split_kernel<D, G, false>;
+    const auto fn = tc ? (a.rope ? decode_split_kernel<D, G, true, true> : decode_split_kernel<D, G, true, false>)
+                       : (a.rope ? decode_split_kernel<D, G, false, true> : decode_split_kernel<D, G, false, false>);
     if (smem > 48 * 1024) {
         const cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
                                                    cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return e;
     }
+    // Six CTAs of ~37 KB per SM need the whole shared-memory carve-out; without a preference the driver may pick a
+    // smaller one (more L1) for a kernel with a stack frame, and fewer CTAs fit.
+    const cudaError_t ce = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
+                                                cudaFuncAttributePreferredSharedMemoryCarveout,
+                                                static_cast<int>(cudaSharedmemCarveoutMaxShared));
+    if (ce != cudaSuccess) return ce;
     return cudaLaunchKernelEx(&cfg, fn, a);
 }
 
@@ -755,6 +915,21 @@ cudaError_t launch_decode(const Call& c, cudaStream_t s) {
     a.pool_blocks = d.pool_blocks;
     a.block_stride = d.block_stride;
     a.err = c.err;
+    a.rope = c.rope ? 1 : 0;
+    a.interleaved = 0;
+    a.k_new = a.v_new = nullptr;
+    a.new_seq_stride = 0;
+    for (int i = 0; i < 128; i++) a.freq[i] = 0.0;
+    if (c.rope) {  // frequencies exactly as alpaca_rope_kv_append computes them
+        const alpaca_rope_desc& r = *c.rope;
+        a.interleaved = r.interleaved;
+        a.k_new = r.k;
+        a.v_new = r.v;
+        a.new_seq_stride = r.kv_seq_stride;
+        const double theta = static_cast<double>(r.theta);
+        for (int i = 0; i < d.head_dim / 2; i++)
+            a.freq[i] = std::pow(theta, -2.0 * static_cast<double>(i) / static_cast<double>(d.head_dim));
+    }
     if (a.max_splits < 1) return cudaSuccess;
     return d.head_dim == 128 ? launch_d<128>(a, d.n_seqs, s) : launch_d<64>(a, d.n_seqs, s);
 }

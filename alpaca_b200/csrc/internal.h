@@ -17,6 +17,7 @@ struct Call {
     void* ws;           // caller workspace (may be null when the kernel needs none)
     size_t ws_bytes;
     int num_sms;        // multiprocessors of the current device
+    const alpaca_rope_desc* rope = nullptr;  // decode with the RoPE + KV append fused in (alpaca_attn_decode_rope)
 };
 
 // ---- split-KV decode (attn_decode.cu)

@@ -225,6 +225,27 @@ def rope_kv_append(q: torch.Tensor | None, k: torch.Tensor | None, v: torch.Tens
     return d_
 
 
+def decode_rope(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, k_cache: torch.Tensor,
+                v_cache: torch.Tensor, out: torch.Tensor, *, theta: float, start_position: int = 0,
+                ctx_lens: torch.Tensor | None = None, max_ctx_len: int | None = None, interleaved: bool = True,
+                block_table: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
+                stream: torch.cuda.Stream | None = None) -> None:
+    """One decode step with the RoPE + KV append fused into the attention launch (alpaca_attn_decode_rope): the
+    results of rope_kv_append(q, k_new, v_new, caches, positions = context length - 1) followed by the split decode
+    over the caches, except that q is not rotated in place. q [S,1,H,d], k_new / v_new f32 [S,1,Hkv,d], caches as
+    for attention_device (contiguous [S,rows,Hkv,d] f16, or pools with `block_table`), out [S,1,H,d]."""
+    ad = make_desc(q, k_cache, v_cache, out, start_position=start_position, ctx_lens=ctx_lens,
+                   max_ctx_len=max_ctx_len, block_table=block_table)
+    rd = make_rope_desc(q, k_new, v_new, k_cache, v_cache, theta=theta, start_position=start_position,
+                        interleaved=interleaved, block_table=block_table)
+    if workspace is None:
+        n = workspace_bytes(ad, Kernel.DECODE_SPLIT)
+        workspace = torch.empty(max(n, 16), dtype=torch.uint8, device=q.device)
+    s = stream if stream is not None else torch.cuda.current_stream()
+    check(load().alpaca_attn_decode_rope(ctypes.byref(ad), ctypes.byref(rd), workspace.data_ptr(),
+                                         workspace.numel() * workspace.element_size(), s.cuda_stream))
+
+
 def rope(x: np.ndarray, start_position: int, theta: float, interleaved: bool = True) -> np.ndarray:
     """MetalOps.rope(_:startPosition:theta:) (MetalOps.swift:165-171): f32 [tokens, heads, head_dim] in and out."""
     x = np.asarray(x, dtype=np.float32)

@@ -656,6 +656,53 @@ def run_decode(args, ab, torch, dev, stream, rank, world, pg, pk):
     qo_bytes = LAYERS * DEC_BATCH * H * D * 4 * 2
     byts = kv_bytes + qo_bytes
     gbs = byts / (ms * 1e-3) / 1e9
+
+    # The decode step of each layer: RoPE + KV append of the new token at row ctx_len - 1, then the attention, as
+    # two calls (alpaca_rope_kv_append + alpaca_attention) and fused (alpaca_attn_decode_rope).
+    kn = torch.randn((LAYERS, DEC_BATCH, 1, KVH, D), generator=g, device=dev)
+    vn = torch.randn((LAYERS, DEC_BATCH, 1, KVH, D), generator=g, device=dev)
+    pos_d = (lens_d - 1).contiguous()
+    rdescs = [ab.make_rope_desc(qd[l], kn[l], vn[l], kc[l], vc[l], theta=1e5, positions=pos_d[l])
+              for l in range(LAYERS)]
+
+    def step_two_calls():
+        for l in range(LAYERS):
+            ab.rope_launch(rdescs[l])
+            ab.launch(descs[l], Kernel.DECODE_SPLIT, ws)
+
+    def step_fused():
+        for l in range(LAYERS):
+            ab.decode_rope(qd[l], kn[l], vn[l], kc[l], vc[l], od[l], theta=1e5, ctx_lens=lens_d[l],
+                           max_ctx_len=DEC_CAP, workspace=ws)
+
+    step_ms = {}
+    for name, fn in (("two_calls", step_two_calls), ("fused", step_fused)):
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            fn()
+        stream.wait_stream(side)
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            fn()
+        for _ in range(max(3, args.warmup)):
+            gr.replay()
+        barrier(pg)
+        e0.record(stream)
+        for _ in range(steps):
+            gr.replay()
+        e1.record(stream)
+        barrier(pg)
+        ab.device_status()
+        step_ms[name] = max_over_ranks(e0.elapsed_time(e1) / steps, pg)
+        del gr
+    decode_step = {
+        "workload": f"config 3 decode step of {LAYERS} layers: per layer the RoPE + f16 KV append of each sequence's "
+                    "new token (row ctx_len - 1), then the split-KV attention",
+        "two_calls_ms_per_step": step_ms["two_calls"], "fused_ms_per_step": step_ms["fused"],
+        "value": world * DEC_BATCH / (step_ms["fused"] * 1e-3), "unit": "tokens/s",
+        "two_calls_tokens_per_s": world * DEC_BATCH / (step_ms["two_calls"] * 1e-3),
+        "gpu_launches": steps * LAYERS * 2,
+    }
     return {"workload": "config 3: batch 64 one-token decode, contexts U[1,4096], 9/3 heads, d=64, f16 KV, "
                         f"{LAYERS} layers (distinct caches, {kc.numel() * 4 / 1e9:.1f} GB) per step",
             "value": world * byts / (ms_max * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms_max,
@@ -665,7 +712,8 @@ def run_decode(args, ab, torch, dev, stream, rank, world, pg, pk):
                          "frac": gbs / pk["hbm_gbs"], "traffic": profile_traffic("decode_split_cfg3"),
                          "kernel": "alpaca::decode_split_kernel<64,3> + decode_combine_kernel per layer, "
                                    "replayed from a CUDA graph"},
-            "gpu_launches": steps * LAYERS * 2}
+            "gpu_launches": steps * LAYERS * 2,
+            "decode_step": decode_step}
 
 
 # ---------------------------------------------------------------------------------------------- reference arm

@@ -217,6 +217,17 @@ typedef struct alpaca_rope_desc {
  * 401-411) and its rope_qkv_store_kv16 / _kv32 kernels (decode_fused.metal:126-154). */
 alpaca_cuda_status alpaca_rope_kv_append(const alpaca_rope_desc* desc, alpaca_stream_t stream);
 
+/* One decode step with the RoPE + KV append fused into the split-KV attention launch: the results of
+ * alpaca_rope_kv_append(rope) followed by alpaca_attention(attn, ALPACA_ATTN_DECODE_SPLIT, ...) bit for bit, with
+ * one kernel launch fewer (the pair MetalLlamaSession.encodeChunk issues per layer for a one-token chunk,
+ * MetalLlamaModel.swift:347-351). Each sequence's new token is at position ctx_lens[s] - 1 (start_position when
+ * ctx_lens is NULL): rope->positions must be NULL and rope->start_position equal attn->start_position. The RoPE
+ * descriptor must describe that one token (tokens 1) of the same sequences, heads, q and f16 caches (same layout,
+ * block table included). q is read and rotated as it is read, not rotated in place. Workspace as for the decode
+ * call (alpaca_attention_workspace_bytes with ALPACA_ATTN_DECODE_SPLIT). */
+alpaca_cuda_status alpaca_attn_decode_rope(const alpaca_attn_desc* attn, const alpaca_rope_desc* rope,
+                                           void* workspace, size_t workspace_bytes, alpaca_stream_t stream);
+
 /* Synchronises `stream`, then reports and (when `clear` != 0) resets the device-side error word of the current
  * device: ALPACA_CUDA_ERR_DEVICE_TIMEOUT when a bounded wait gave up, ALPACA_CUDA_OK otherwise. */
 alpaca_cuda_status alpaca_cuda_device_status(alpaca_stream_t stream, int clear);

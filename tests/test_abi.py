@@ -310,3 +310,33 @@ def test_rope_paged_cache_needs_no_sequence_stride(lib):
     assert lib.alpaca_rope_kv_append(ctypes.byref(d), None) != Status.INVALID_ARGUMENT
     d = rope_desc(**rope_paged(n_seqs=3, q_seq_stride=4 * 9 * 64, kv_seq_stride=4 * 3 * 64, block_table=0))
     assert lib.alpaca_rope_kv_append(ctypes.byref(d), None) == Status.INVALID_ARGUMENT
+
+
+# ---------------------------------------------------------------------------------------------- fused RoPE + decode
+
+def test_decode_rope_validation(lib):
+    """alpaca_attn_decode_rope takes the new token's position from the attention descriptor and needs the RoPE
+    descriptor to describe that one token of the same sequences, heads, q and f16 caches; anything else is an
+    invalid argument before any device work (a valid pair fails only at the device query without a GPU)."""
+    from alpaca_b200 import DType, Status
+
+    def attn(**kw):
+        base = dict(tokens=1, start_position=300, q_dtype=int(DType.F32), q_token_stride=576)
+        base.update(kw)
+        return desc(**base)
+
+    def call(a, r):
+        return lib.alpaca_attn_decode_rope(ctypes.byref(a), ctypes.byref(r), FAKE, 1 << 20, None)
+
+    st = call(attn(), rope_desc(tokens=1, start_position=300))
+    assert st not in (Status.OK, Status.INVALID_ARGUMENT, Status.UNSUPPORTED, Status.WORKSPACE_TOO_SMALL)
+    for bad in (dict(positions=FAKE), dict(tokens=2), dict(start_position=299), dict(k_cache=FAKE + 4096),
+                dict(cache_dtype=int(DType.F32)), dict(n_heads=8), dict(interleaved=2)):
+        kw = dict(tokens=1, start_position=300)
+        kw.update(bad)
+        assert call(attn(), rope_desc(**kw)) == Status.INVALID_ARGUMENT, bad
+        msg = lib.alpaca_cuda_last_error()
+        assert msg.startswith(b"decode_rope") or msg.startswith(b"rope"), msg
+    assert call(attn(tokens=2), rope_desc(tokens=1, start_position=300)) == Status.UNSUPPORTED
+    assert lib.alpaca_attn_decode_rope(ctypes.byref(attn()), ctypes.byref(rope_desc(tokens=1, start_position=300)),
+                                       FAKE, 16, None) == Status.WORKSPACE_TOO_SMALL
