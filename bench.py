@@ -602,7 +602,8 @@ def run_rope(args, ab, torch, dev, stream, rank, world, pg, pk):
             "tokens_per_s": world * T / (ms_max * 1e-3),  # prompt tokens through all layers per second
             "bytes_per_step": byts,
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                         "frac": gbs / pk["hbm_gbs"], "kernel": "alpaca::rope_kv_kernel per layer"},
+                         "frac": gbs / pk["hbm_gbs"], "traffic": profile_traffic("rope_kv_cfg2"),
+                         "kernel": "alpaca::rope_kv_vec_kernel per layer"},
             "gpu_launches": steps * LAYERS}
 
 
