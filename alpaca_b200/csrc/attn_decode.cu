@@ -69,6 +69,7 @@ struct DecodeArgs {
     const float* k_new;
     const float* v_new;
     int64_t new_seq_stride;
+    int early_release;  // split CTAs release the combine launch at their start (else at their end)
     double freq[128];  // theta^(-2i/d), host-computed in double as for alpaca_rope_kv_append
 };
 
@@ -623,6 +624,9 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 6 : 3)) decode_split_kerne
     // Launched with programmatic dependent launch: the CTA may be resident before the previous kernel on the
     // stream has finished, so it touches no global memory before that kernel's writes are complete and visible.
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    // The combine kernel may launch as soon as every CTA of this grid has started: its CTAs then wait in
+    // griddepcontrol.wait for this grid's memory, already resident when the last split ends.
+    if (a.early_release) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int L = ctx_len_of(a, seq);
     const int row0 = split * SL;
     if (row0 >= L) return;  // uniform for the whole CTA
@@ -664,7 +668,7 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 6 : 3)) decode_split_kerne
         compute_unit<D, G, 0, kRope>(a, seq, kvh, split, row0, row_end, nsplits, s_k, s_v, s_p, s_ml, s_q, tid, warp,
                                      lane, lr, rowlane);
     // The combine kernel may start launching now; it waits for this grid's memory before reading.
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    if (!a.early_release) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 constexpr int kCombineThreads = 256;
@@ -915,6 +919,11 @@ cudaError_t launch_decode(const Call& c, cudaStream_t s) {
     a.pool_blocks = d.pool_blocks;
     a.block_stride = d.block_stride;
     a.err = c.err;
+    static const int early = [] {
+        const char* e = std::getenv("ALPACA_DECODE_EARLY");
+        return (e && e[0] == '1') ? 1 : 0;
+    }();
+    a.early_release = early;
     a.rope = c.rope ? 1 : 0;
     a.interleaved = 0;
     a.k_new = a.v_new = nullptr;
