@@ -624,8 +624,10 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 6 : 3)) decode_split_kerne
     // Launched with programmatic dependent launch: the CTA may be resident before the previous kernel on the
     // stream has finished, so it touches no global memory before that kernel's writes are complete and visible.
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    // The combine kernel may launch as soon as every CTA of this grid has started: its CTAs then wait in
-    // griddepcontrol.wait for this grid's memory, already resident when the last split ends.
+    // When the whole grid is resident at once, the combine kernel may launch as soon as every CTA has started: its
+    // CTAs then wait in griddepcontrol.wait for this grid's memory, already resident when the last split ends
+    // (two-split batches: 8.7 -> 7.6 us per layer). With several waves the release stays at the CTAs' end (early
+    // release measured 23.5 against 22.7 us per config-3 layer).
     if (a.early_release) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int L = ctx_len_of(a, seq);
     const int row0 = split * SL;
@@ -774,7 +776,7 @@ bool decode_tensor_cores(int head_dim) {
 }
 
 template <int D, int G>
-cudaError_t launch_split(const DecodeArgs& a, int n_seqs, cudaStream_t s) {
+cudaError_t launch_split(const DecodeArgs& a, int n_seqs, int num_sms, cudaStream_t s) {
     using Gm = Geo<D>;
     static_assert(Gm::RPS * G * D * sizeof(float) <= sizeof(__half) * 2 * Gm::SL * D, "reduction buffer too big");
     const bool tc = decode_tensor_cores(D);
@@ -797,6 +799,17 @@ cudaError_t launch_split(const DecodeArgs& a, int n_seqs, cudaStream_t s) {
     cfg.numAttrs = pdl_enabled() ? 1 : 0;
     const auto fn = tc ? (a.rope ? decode_split_kernel<D, G, true, true> : decode_split_kernel<D, G, true, false>)
                        : (a.rope ? decode_split_kernel<D, G, false, true> : decode_split_kernel<D, G, false, false>);
+    // CTAs of this kernel form one SM holds (depends only on the form and its shared memory): one query per form.
+    const int fidx = (tc ? 2 : 0) + (a.rope ? 1 : 0);
+    static int occ[4] = {0, 0, 0, 0};
+    static std::once_flag occ_once[4];
+    std::call_once(occ_once[fidx], [&] {
+        int n = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, kThreads, smem) == cudaSuccess) occ[fidx] = n;
+    });
+    DecodeArgs la = a;
+    la.early_release = static_cast<int64_t>(a.max_splits) * a.n_kv_heads * n_seqs <=
+                       static_cast<int64_t>(occ[fidx]) * num_sms;
     if (smem > 48 * 1024) {
         const cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
                                                    cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
@@ -808,21 +821,21 @@ cudaError_t launch_split(const DecodeArgs& a, int n_seqs, cudaStream_t s) {
                                                 cudaFuncAttributePreferredSharedMemoryCarveout,
                                                 static_cast<int>(cudaSharedmemCarveoutMaxShared));
     if (ce != cudaSuccess) return ce;
-    return cudaLaunchKernelEx(&cfg, fn, a);
+    return cudaLaunchKernelEx(&cfg, fn, la);
 }
 
 template <int D>
-cudaError_t launch_d(const DecodeArgs& a, int n_seqs, cudaStream_t s) {
+cudaError_t launch_d(const DecodeArgs& a, int n_seqs, int num_sms, cudaStream_t s) {
     cudaError_t e;
     switch (a.n_heads / a.n_kv_heads) {
-        case 1: e = launch_split<D, 1>(a, n_seqs, s); break;
-        case 2: e = launch_split<D, 2>(a, n_seqs, s); break;
-        case 3: e = launch_split<D, 3>(a, n_seqs, s); break;
-        case 4: e = launch_split<D, 4>(a, n_seqs, s); break;
-        case 5: e = launch_split<D, 5>(a, n_seqs, s); break;
-        case 6: e = launch_split<D, 6>(a, n_seqs, s); break;
-        case 7: e = launch_split<D, 7>(a, n_seqs, s); break;
-        case 8: e = launch_split<D, 8>(a, n_seqs, s); break;
+        case 1: e = launch_split<D, 1>(a, n_seqs, num_sms, s); break;
+        case 2: e = launch_split<D, 2>(a, n_seqs, num_sms, s); break;
+        case 3: e = launch_split<D, 3>(a, n_seqs, num_sms, s); break;
+        case 4: e = launch_split<D, 4>(a, n_seqs, num_sms, s); break;
+        case 5: e = launch_split<D, 5>(a, n_seqs, num_sms, s); break;
+        case 6: e = launch_split<D, 6>(a, n_seqs, num_sms, s); break;
+        case 7: e = launch_split<D, 7>(a, n_seqs, num_sms, s); break;
+        case 8: e = launch_split<D, 8>(a, n_seqs, num_sms, s); break;
         default: return cudaErrorInvalidValue;
     }
     if (e != cudaSuccess) return e;
@@ -919,11 +932,7 @@ cudaError_t launch_decode(const Call& c, cudaStream_t s) {
     a.pool_blocks = d.pool_blocks;
     a.block_stride = d.block_stride;
     a.err = c.err;
-    static const int early = [] {
-        const char* e = std::getenv("ALPACA_DECODE_EARLY");
-        return (e && e[0] == '1') ? 1 : 0;
-    }();
-    a.early_release = early;
+    a.early_release = 0;  // set per launch in launch_split
     a.rope = c.rope ? 1 : 0;
     a.interleaved = 0;
     a.k_new = a.v_new = nullptr;
@@ -940,7 +949,7 @@ cudaError_t launch_decode(const Call& c, cudaStream_t s) {
             a.freq[i] = std::pow(theta, -2.0 * static_cast<double>(i) / static_cast<double>(d.head_dim));
     }
     if (a.max_splits < 1) return cudaSuccess;
-    return d.head_dim == 128 ? launch_d<128>(a, d.n_seqs, s) : launch_d<64>(a, d.n_seqs, s);
+    return d.head_dim == 128 ? launch_d<128>(a, d.n_seqs, c.num_sms, s) : launch_d<64>(a, d.n_seqs, c.num_sms, s);
 }
 
 }  // namespace alpaca
