@@ -104,7 +104,7 @@ class RopeDesc(ctypes.Structure):
         ("max_blocks", ctypes.c_int32),
         ("block_stride", ctypes.c_int64),
         ("pool_blocks", ctypes.c_int32),
-        ("reserved0", ctypes.c_int32),
+        ("cache_rows", ctypes.c_int32),
     ]
 
 

@@ -190,6 +190,10 @@ alpaca_cuda_status validate_rope(const alpaca_rope_desc* dp) {
             d.kv_token_stride % 2 ||
             d.kv_seq_stride % 2 || d.cache_row_stride % 2 || d.cache_seq_stride % 2)
             return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, std::string("rope: k / v / cache strides: ") + sh);
+        if (d.cache_rows < 0) return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, std::string("rope: cache_rows < 0: ") + sh);
+        if (!d.block_table && d.cache_rows > 0 && !d.positions &&
+            static_cast<int64_t>(d.start_position) + d.tokens > d.cache_rows)
+            return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, std::string("rope: rows past cache_rows: ") + sh);
         if (d.block_table) {
             if (d.block_rows < 128 || d.block_rows % 128 || d.max_blocks < 1 || d.pool_blocks < 1 ||
                 d.block_stride < static_cast<int64_t>(d.block_rows) * d.cache_row_stride || d.block_stride % 2)

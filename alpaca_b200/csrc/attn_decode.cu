@@ -57,6 +57,7 @@ struct DecodeArgs {
     float* partial;
     const int* ctx_lens;
     int uniform_len;
+    int max_len;  // upper bound of every context length (desc.max_ctx_len, or uniform_len)
     int n_heads, n_kv_heads, max_splits;
     float scale_log2;
     const int* block_table;  // paged cache: [seq][max_blocks] block indices (null: contiguous caches)
@@ -92,8 +93,17 @@ __device__ __forceinline__ int64_t unit_offset(const DecodeArgs& a, int seq, int
            static_cast<int64_t>(kvh) * D;
 }
 
+// Context length of sequence s. A device entry outside [1, max_len] breaks the caller's contract (the grid and the
+// workspace were sized for max_len): it is clamped, so no CTA reads or writes past the sequence's records, and the
+// device error word reports it (INVALID_ARGUMENT from alpaca_cuda_device_status).
 __device__ __forceinline__ int ctx_len_of(const DecodeArgs& a, int s) {
-    return a.ctx_lens ? a.ctx_lens[s] : a.uniform_len;
+    if (!a.ctx_lens) return a.uniform_len;
+    const int L = a.ctx_lens[s];
+    if (L < 1 || L > a.max_len) {
+        atomicOr(a.err, kDevErrBadIndex);
+        return L < 1 ? 0 : a.max_len;
+    }
+    return L;
 }
 
 __device__ __forceinline__ void half8_to_float(const uint4& u, float* f) {
@@ -922,6 +932,7 @@ cudaError_t launch_decode(const Call& c, cudaStream_t s) {
     a.partial = static_cast<float*>(c.ws);
     a.ctx_lens = d.ctx_lens;
     a.uniform_len = d.start_position + 1;
+    a.max_len = d.ctx_lens ? d.max_ctx_len : a.uniform_len;
     a.n_heads = d.n_heads;
     a.n_kv_heads = d.n_kv_heads;
     a.max_splits = decode_max_splits(d);

@@ -42,6 +42,7 @@ struct RopeArgs {
     const int* block_table;  // paged cache: [seq][max_blocks] (null: contiguous caches)
     int block_rows, max_blocks, pool_blocks;
     int64_t block_stride;
+    int cache_rows;  // contiguous caches: rows per sequence, or 0 (unchecked)
     unsigned* err;
     double freq[kRopeMaxPairs];  // theta^(-2i/d), host-computed in double
 };
@@ -67,13 +68,21 @@ __device__ __forceinline__ void pair_index(int i, int half, int& ia, int& ib) {
     ib = kInterleaved ? 2 * i + 1 : i + half;
 }
 
-// Element offset of cache row `pos` of sequence `seq`; a paged table entry outside the pool (or a position past
-// the table) clears `ok` — nothing is written there — and raises the device error word.
+// Element offset of cache row `pos` of sequence `seq`; a position outside the cache (negative, past cache_rows, or
+// past the block table) or a table entry outside the pool clears `ok` — nothing is written there — and raises the
+// device error word.
 __device__ __forceinline__ int64_t cache_row_offset(const RopeArgs& a, int seq, int pos, bool& ok) {
     ok = true;
-    if (!a.block_table) return seq * a.cache_seq_stride + static_cast<int64_t>(pos) * a.cache_row_stride;
+    if (!a.block_table) {
+        if (pos < 0 || (a.cache_rows > 0 && pos >= a.cache_rows)) {  // past the cache: write nothing, report it
+            ok = false;
+            atomicOr(a.err, kDevErrBadIndex);
+            return 0;
+        }
+        return seq * a.cache_seq_stride + static_cast<int64_t>(pos) * a.cache_row_stride;
+    }
     const int b = pos / a.block_rows;
-    const int blk = b < a.max_blocks ? a.block_table[static_cast<int64_t>(seq) * a.max_blocks + b] : -1;
+    const int blk = (pos >= 0 && b < a.max_blocks) ? a.block_table[static_cast<int64_t>(seq) * a.max_blocks + b] : -1;
     if (blk < 0 || blk >= a.pool_blocks) {
         ok = false;
         atomicOr(a.err, kDevErrBadIndex);
@@ -360,6 +369,7 @@ cudaError_t launch_rope_kv(const alpaca_rope_desc& d, unsigned* err, cudaStream_
     a.max_blocks = d.max_blocks;
     a.pool_blocks = d.pool_blocks;
     a.block_stride = d.block_stride;
+    a.cache_rows = d.cache_rows;
     a.err = err;
     const double theta = static_cast<double>(d.theta);
     for (int i = 0; i < kRopeMaxPairs; i++)

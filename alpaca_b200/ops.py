@@ -198,6 +198,7 @@ def make_rope_desc(q: torch.Tensor | None, k: torch.Tensor | None, v: torch.Tens
         d_.kv_seq_stride = k4.stride(0) if S > 1 else 0
         d_.k_cache, d_.v_cache, d_.cache_row_stride = kc4.data_ptr(), vc4.data_ptr(), kc4.stride(1)
         d_.cache_seq_stride = kc4.stride(0) if S > 1 else 0
+        d_.cache_rows = kc4.shape[1]  # contiguous caches: positions past the cache are reported, not written
         if block_table is not None:
             if block_table.dtype != torch.int32 or not block_table.is_cuda or block_table.dim() != 2 or \
                     block_table.shape[0] != S or not block_table.is_contiguous():
@@ -206,6 +207,7 @@ def make_rope_desc(q: torch.Tensor | None, k: torch.Tensor | None, v: torch.Tens
             d_.block_table, d_.max_blocks = block_table.data_ptr(), block_table.shape[1]
             d_.block_rows, d_.pool_blocks, d_.block_stride = kc4.shape[1], kc4.shape[0], kc4.stride(0)
             d_.cache_seq_stride = 0
+            d_.cache_rows = 0
     return d_
 
 

@@ -210,7 +210,8 @@ typedef struct alpaca_rope_desc {
     int32_t max_blocks;
     int64_t block_stride;
     int32_t pool_blocks;
-    int32_t reserved0;
+    int32_t cache_rows;       /* rows of each contiguous cache, or 0 (unchecked); a token whose position is outside
+                                 [0, cache_rows) writes no cache row and is reported by alpaca_cuda_device_status */
 } alpaca_rope_desc;
 
 /* Enqueue the fused RoPE + KV append on `stream`. Replaces KernelEncoder.ropeQKVStore (KernelEncoder.swift:

@@ -340,3 +340,14 @@ def test_decode_rope_validation(lib):
     assert call(attn(tokens=2), rope_desc(tokens=1, start_position=300)) == Status.UNSUPPORTED
     assert lib.alpaca_attn_decode_rope(ctypes.byref(attn()), ctypes.byref(rope_desc(tokens=1, start_position=300)),
                                        FAKE, 16, None) == Status.WORKSPACE_TOO_SMALL
+
+
+@pytest.mark.parametrize("bad", [
+    dict(cache_rows=-1),
+    dict(cache_rows=12, start_position=10, tokens=4),  # rows 10..13 past a 12-row cache
+])
+def test_rope_cache_rows_checked(lib, bad):
+    from alpaca_b200 import Status
+    d = rope_desc(**bad)
+    assert lib.alpaca_rope_kv_append(ctypes.byref(d), None) == Status.INVALID_ARGUMENT
+    assert lib.alpaca_cuda_last_error().startswith(b"rope")

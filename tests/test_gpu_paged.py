@@ -251,3 +251,56 @@ def test_paged_rope_block_outside_pool_is_reported(cuda_lib):
     rope_kv_append(q, k, v, kp, vp, theta=1e4, block_table=table)
     device_status()
     assert torch.all(vp[3, :T - R] == 1)
+
+
+def test_ctx_len_past_max_is_reported_and_clamped(cuda_lib):
+    """A ctx_lens entry above max_ctx_len breaks the caller's contract (the grid and the workspace are sized for
+    max_ctx_len): the kernels clamp it, so nothing is read or written past the sequence's records, and
+    alpaca_cuda_device_status reports INVALID_ARGUMENT; the other sequences are unaffected. The caches hold the
+    longer context, so even an unclamped read would stay inside them."""
+    from alpaca_b200 import AlpacaCUDAError, Kernel, Status, attention_device, device_status
+    S, H, Hkv, d, cap, mx = 3, 9, 3, 64, 600, 300
+    lens = np.array([100, 550, 200], np.int32)
+    q = oracle.splitmix_normal(701, (S, 1, H, d))
+    k = oracle.f16_round(oracle.splitmix_normal(702, (S, cap, Hkv, d)))
+    v = oracle.f16_round(oracle.splitmix_normal(703, (S, cap, Hkv, d)))
+    dev = torch.device("cuda")
+    out = torch.empty((S, 1, H, d), dtype=torch.float32, device=dev)
+    device_status()
+    attention_device(torch.from_numpy(q).to(dev), torch.from_numpy(k).to(dev).half(),
+                     torch.from_numpy(v).to(dev).half(), out, ctx_lens=torch.from_numpy(lens).to(dev),
+                     max_ctx_len=mx, kind=Kernel.DECODE_SPLIT)
+    with pytest.raises(AlpacaCUDAError) as e:
+        device_status()
+    assert e.value.status == Status.INVALID_ARGUMENT
+    got = out.cpu().numpy()
+    assert np.isfinite(got).all()
+    for s in (0, 2):
+        L = int(lens[s])
+        ref = oracle.attention(q[s], k[s], v[s], L - 1, length=L)
+        max_abs_check(got[s], ref, DECODE_TOL, f"ctx_len clamp, unaffected seq {s}")
+    ref1 = oracle.attention(q[1], k[1], v[1], mx - 1, length=mx)  # the offending sequence: clamped to max_ctx_len
+    max_abs_check(got[1], ref1, DECODE_TOL, "ctx_len clamp, clamped seq")
+
+
+def test_rope_position_past_cache_is_reported(cuda_lib):
+    """A device position at or past the contiguous cache's rows writes no cache row and is reported; the rows of the
+    in-range sequence are written. The caches are 16-row views of 64-row buffers, so the row an unchecked kernel
+    would write exists and can be checked untouched."""
+    from alpaca_b200 import AlpacaCUDAError, Status, device_status, rope_kv_append
+    S, H, Hkv, d = 2, 4, 2, 64
+    dev = torch.device("cuda")
+    kb = torch.full((S, 64, Hkv, d), 7.0, dtype=torch.float16, device=dev)
+    vb = torch.full_like(kb, 7.0)
+    kc, vc = kb[:, :16], vb[:, :16]
+    q = torch.ones((S, 1, H, d), device=dev)
+    k = torch.ones((S, 1, Hkv, d), device=dev)
+    v = torch.ones((S, 1, Hkv, d), device=dev)
+    pos = torch.tensor([3, 40], dtype=torch.int32, device=dev)
+    device_status()
+    rope_kv_append(q, k, v, kc, vc, theta=1e4, positions=pos)
+    with pytest.raises(AlpacaCUDAError) as e:
+        device_status()
+    assert e.value.status == Status.INVALID_ARGUMENT
+    assert torch.all(vb[0, 3] == 1) and torch.all(vb[1, 40] == 7) and torch.all(kb[1, 40] == 7)
+    assert not torch.equal(q[1], torch.ones_like(q[1]))  # q is rotated regardless
