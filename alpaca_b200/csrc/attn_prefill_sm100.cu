@@ -43,7 +43,12 @@ namespace alpaca {
 namespace {
 
 constexpr int kBM = 128;        // query rows per tile
-constexpr int kStages = 4;      // K/V ring depth
+// K/V ring depth: 3 at head_dim 64 (as fast as 4, and it leaves room for the output staging tiles), 4 at 128.
+template <int D>
+__host__ __device__ constexpr int stages_for() { return D == 64 ? 3 : 4; }
+// head_dim 64, two softmax threads per row: the output leaves through shared memory and TMA stores.
+template <int D, int R>
+__host__ __device__ constexpr bool tma_out() { return D == 64 && R != 1; }
 // Threads per CTA: warps 0-3 are TMA, MMA A, MMA B (+ TMEM allocator) and idle; then the softmax warps, 16 with
 // two threads per query row (R = 2) or 8 with one (R = 1).
 template <int R>
@@ -92,7 +97,11 @@ struct PrefillArgs {
 
 template <int D>
 struct SmemLayout {
+    static constexpr int kStages = stages_for<D>();
     __half q[2][kBM * D];                 // [tile][column block][row][64]
+    // head_dim 64: each tile's normalised output [128 rows][64] as TMA store boxes of 128-byte rows with the
+    // 128-byte swizzle (f32: two boxes of 32 columns; f16: one box of 64)
+    float o_stage[D == 64 ? 2 * kBM * 64 : 256];
     __half k[kStages][PG<D>::BN * D];     // [stage][column block][row][64]
     __half v[kStages][PG<D>::BN * D];
     uint64_t q_full[2], q_empty[2];
@@ -100,6 +109,7 @@ struct SmemLayout {
     uint64_t s_full[2], s_empty[2], p_full[2], o_done[2];
     uint64_t xbar[2][4];       // per (tile, lane quarter): the two half-row warps exchange partial row state
     uint64_t dbg, fin[2], retire;
+    uint64_t o_staged[2], o_free[2];  // head_dim 64 output: rows staged (8 warps), staging free again (issuer)
     float xmax[2][2][2][kBM];  // [tile][exchange parity][half][row] partial row maxima
     float xl[2][2][kBM];       // [tile][half][row] partial row sums (epilogue)
     uint32_t tmem_base;
@@ -176,8 +186,11 @@ template <int D, int kEmuPairs, int R>
 __global__ void __launch_bounds__(threads_for<R>(), 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_kt,
-                   const __grid_constant__ CUtensorMap tm_vt, const PrefillArgs a) {
+                   const __grid_constant__ CUtensorMap tm_vt, const __grid_constant__ CUtensorMap tm_o,
+                   const PrefillArgs a) {
     using G = PG<D>;
+    constexpr int kStages = stages_for<D>();
+    constexpr bool kTmaOut = tma_out<D, R>();
     constexpr int kBN = G::BN, SC = G::SC, OC = G::OC;
     extern __shared__ uint8_t smem_raw[];
     auto* sm = reinterpret_cast<SmemLayout<D>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -205,6 +218,8 @@ __global__ void __launch_bounds__(threads_for<R>(), 1)
             mbar_init(&sm->o_done[i], 1);
             for (int qq = 0; qq < 4; qq++) mbar_init(&sm->xbar[i][qq], 2);  // one arrival per warp of the pair
             mbar_init(&sm->fin[i], 1);
+            mbar_init(&sm->o_staged[i], 8);  // the tile's 8 softmax warps (head_dim 64 form)
+            mbar_init(&sm->o_free[i], 1);
         }
         for (int i = 0; i < kStages; i++) {
             mbar_init(&sm->k_full[i], 1);
@@ -218,6 +233,7 @@ __global__ void __launch_bounds__(threads_for<R>(), 1)
         tma_prefetch_desc(&tm_q);
         tma_prefetch_desc(&tm_k);
         tma_prefetch_desc(&tm_v);
+        if (kTmaOut) tma_prefetch_desc(&tm_o);
         if (a.block_table) {
             tma_prefetch_desc(&tm_kt);
             tma_prefetch_desc(&tm_vt);
@@ -537,7 +553,8 @@ __global__ void __launch_bounds__(threads_for<R>(), 1)
         const uint32_t o_addr = lane_addr + G::col_o(tile) + half * OC;      // this thread's OC context columns
         const uint32_t p_addr = lane_addr + G::col_p(tile) + half * (SC / 2); // its SC/2 columns of P pairs
         uint64_t* xbar = &sm->xbar[tile][quarter];
-        uint32_t s_uses = 0, o_uses = 0, x_uses = 0;
+        uint32_t s_uses = 0, o_uses = 0, x_uses = 0, ep_uses = 0;
+        const bool issuer = kTmaOut && ((warp - 4) & 7) == 0 && lane == 0;  // the tile's output TMA thread
         bool ok = true;
         for (int r = 0, it = item_of(0); ok && it < a.total_items; it = item_of(++r)) {
             const Item x = decode_item<kBN>(a, it);
@@ -682,7 +699,59 @@ __global__ void __launch_bounds__(threads_for<R>(), 1)
             x_uses++;
             const float l = lpart + sm->xl[tile][half ^ 1][row];
             const int t = row0 + row;
-            if (t < a.tokens) {
+            if constexpr (kTmaOut) {
+                // The rows go through the tile's staging box and one thread's TMA stores (rows past the tokens are
+                // clipped by the tensor map). Hand-offs on mbarriers with bounded waits: o_free (the previous
+                // store has read the box) and o_staged (all 8 warps have written their rows).
+                const float inv = 1.f / l;
+                if (ep_uses > 0) {
+                    if (issuer) {
+                        bulk_wait_read_all();
+                        mbar_arrive(&sm->o_free[tile]);
+                    }
+                    ok = __all_sync(0xffffffffu, mbar_wait(&sm->o_free[tile], (ep_uses - 1) & 1, ab));
+                    if (!ok) break;
+                }
+                float* stage = sm->o_stage + tile * (kBM * 64);
+                if (a.out_f16) {
+                    __half* rowp = reinterpret_cast<__half*>(stage) + row * 64;  // one box, 128-byte rows of 64
+#pragma unroll
+                    for (int c = 0; c < 4; c++) {
+                        const int ch = (half * 4 + c) ^ (row & 7);
+                        const float* v = o + 8 * c;
+                        *reinterpret_cast<uint4*>(rowp + ch * 8) =
+                            make_uint4(pack_half2(v[0] * inv, v[1] * inv), pack_half2(v[2] * inv, v[3] * inv),
+                                       pack_half2(v[4] * inv, v[5] * inv), pack_half2(v[6] * inv, v[7] * inv));
+                    }
+                } else {
+                    float* rowp = stage + half * (kBM * 32) + row * 32;  // this half's box, 128-byte rows of 32
+#pragma unroll
+                    for (int c = 0; c < 8; c++) {
+                        const int ch = c ^ (row & 7);
+                        *reinterpret_cast<float4*>(rowp + ch * 4) =
+                            make_float4(o[4 * c] * inv, o[4 * c + 1] * inv, o[4 * c + 2] * inv, o[4 * c + 3] * inv);
+                    }
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sm->o_staged[tile]);
+                bool sent = true;
+                if (issuer) {
+                    sent = mbar_wait(&sm->o_staged[tile], ep_uses & 1, ab);
+                    if (sent) {
+                        if (a.out_f16) {
+                            tma_store_4d(&tm_o, stage, 0, x.head, row0, x.seq);
+                        } else {
+                            tma_store_4d(&tm_o, stage, 0, x.head, row0, x.seq);
+                            tma_store_4d(&tm_o, stage + kBM * 32, 32, x.head, row0, x.seq);
+                        }
+                        bulk_commit();
+                    }
+                }
+                ok = __all_sync(0xffffffffu, sent);
+                if (!ok) break;
+                ep_uses++;
+            } else if (t < a.tokens) {
                 const float inv = 1.f / l;
                 const int64_t off = x.seq * a.out_seq_stride + static_cast<int64_t>(t) * a.out_token_stride +
                                     static_cast<int64_t>(x.head) * D + half * OC;
@@ -702,6 +771,7 @@ __global__ void __launch_bounds__(threads_for<R>(), 1)
                 }
             }
         }
+        if (issuer) bulk_wait_all();  // the tile's last output stores are done before the CTA retires
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm->retire);
@@ -772,7 +842,27 @@ int prefill_emu_pairs() {
     return v;
 }
 
-using PrefillFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, PrefillArgs);
+using PrefillFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, PrefillArgs);
+
+// 4-D map of the output [seqs][tokens][heads][d] (f32 or f16) for TMA stores: boxes of one 128-byte row segment
+// (32 f32 or 64 f16 columns) x 128 tokens, 128-byte swizzle; rows past `tokens` are clipped.
+bool make_out_map(CUtensorMap* map, void* base, bool f16, int d, int heads, int tokens, int seqs, int64_t token_stride,
+                  int64_t seq_stride) {
+    EncodeTiledFn enc = get_encode_fn();
+    if (!enc) return false;
+    const int es = f16 ? 2 : 4;
+    if (seqs == 1 || seq_stride == 0) seq_stride = static_cast<int64_t>(tokens) * token_stride;
+    cuuint64_t dims[4] = {static_cast<cuuint64_t>(d), static_cast<cuuint64_t>(heads), static_cast<cuuint64_t>(tokens),
+                          static_cast<cuuint64_t>(seqs)};
+    cuuint64_t strides[3] = {static_cast<cuuint64_t>(d) * es, static_cast<cuuint64_t>(token_stride) * es,
+                             static_cast<cuuint64_t>(seq_stride) * es};
+    cuuint32_t box[4] = {static_cast<cuuint32_t>(128 / es), 1, static_cast<cuuint32_t>(kBM), 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = enc(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, dims, strides,
+                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
 
 // Softmax threads per query row: one at head_dim 128 (822 against 747 TFLOP/s on 30 layers x 4096 tokens), two at
 // head_dim 64 (637 against 612-617: with a whole 128-column row per thread two softmax warps per SMSP hide less
@@ -864,6 +954,12 @@ cudaError_t launch_prefill(const Call& c, cudaStream_t s) {
         tvt = tv;
     }
 
+    CUtensorMap to = tq;  // unused by the forms that store the output directly
+    if (!d128 && rows != 1 &&
+        !make_out_map(&to, d.out, d.out_dtype == ALPACA_F16, d.head_dim, d.n_heads, d.tokens, d.n_seqs,
+                      d.out_token_stride, d.out_seq_stride))
+        return cudaErrorInvalidValue;
+
     PrefillArgs a;
     a.out = d.out;
     a.out_token_stride = d.out_token_stride;
@@ -896,7 +992,7 @@ cudaError_t launch_prefill(const Call& c, cudaStream_t s) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, fn, tq, tk, tv, tkt, tvt, a);
+    return cudaLaunchKernelEx(&cfg, fn, tq, tk, tv, tkt, tvt, to, a);
 }
 
 }  // namespace alpaca
