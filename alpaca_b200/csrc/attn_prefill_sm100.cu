@@ -830,8 +830,9 @@ bool make_map(CUtensorMap* map, const void* base, int d, int heads, int rows, in
 }
 
 // Share of exponentials computed on the FMA pipe: ALPACA_PREFILL_EMU column pairs of every 8 (0, 2, 3 or 4;
-// default 2). MUFU gives 16 exp2 per clock per SM, fewer than the tensor pipe consumes at head_dim 64.
-constexpr int kEmuDefault = 2;
+// default 0). MUFU gives 16 exp2 per clock per SM; with the output leaving through TMA stores, all exponentials on
+// MUFU measured fastest (0.806 against 0.820 ms with 2 of 8 pairs on the FMA pipe, 30 layers x 4096 tokens).
+constexpr int kEmuDefault = 0;
 int prefill_emu_pairs() {
     static const int v = [] {
         const char* e = std::getenv("ALPACA_PREFILL_EMU");
