@@ -43,12 +43,13 @@ namespace alpaca {
 namespace {
 
 constexpr int kBM = 128;        // query rows per tile
-// K/V ring depth: 3 at head_dim 64 (as fast as 4, and it leaves room for the output staging tiles), 4 at 128.
+// K/V ring depth: 3 (as fast as 4 at head_dim 64, and it leaves room for the output staging tiles).
 template <int D>
-__host__ __device__ constexpr int stages_for() { return D == 64 ? 3 : 4; }
-// head_dim 64, two softmax threads per row: the output leaves through shared memory and TMA stores.
+__host__ __device__ constexpr int stages_for() { return 3; }
+// The default forms (head_dim 64 with two softmax threads per row, head_dim 128 with one) write the output through
+// shared-memory staging tiles and TMA stores.
 template <int D, int R>
-__host__ __device__ constexpr bool tma_out() { return D == 64 && R != 1; }
+__host__ __device__ constexpr bool tma_out() { return (D == 64 && R == 2) || (D == 128 && R == 1); }
 // Threads per CTA: warps 0-3 are TMA, MMA A, MMA B (+ TMEM allocator) and idle; then the softmax warps, 16 with
 // two threads per query row (R = 2) or 8 with one (R = 1).
 template <int R>
@@ -99,9 +100,9 @@ template <int D>
 struct SmemLayout {
     static constexpr int kStages = stages_for<D>();
     __half q[2][kBM * D];                 // [tile][column block][row][64]
-    // head_dim 64: each tile's normalised output [128 rows][64] as TMA store boxes of 128-byte rows with the
-    // 128-byte swizzle (f32: two boxes of 32 columns; f16: one box of 64)
-    float o_stage[D == 64 ? 2 * kBM * 64 : 256];
+    // per tile, 64 columns of the normalised output [128 rows][64] as TMA store boxes of 128-byte rows with the
+    // 128-byte swizzle (f32: two boxes of 32 columns; f16: one box of 64); head_dim 128 stages it in two rounds
+    float o_stage[2 * kBM * 64];
     __half k[kStages][PG<D>::BN * D];     // [stage][column block][row][64]
     __half v[kStages][PG<D>::BN * D];
     uint64_t q_full[2], q_empty[2];
@@ -110,8 +111,10 @@ struct SmemLayout {
     uint64_t xbar[2][4];       // per (tile, lane quarter): the two half-row warps exchange partial row state
     uint64_t dbg, fin[2], retire;
     uint64_t o_staged[2], o_free[2];  // head_dim 64 output: rows staged (8 warps), staging free again (issuer)
-    float xmax[2][2][2][kBM];  // [tile][exchange parity][half][row] partial row maxima
-    float xl[2][2][kBM];       // [tile][half][row] partial row sums (epilogue)
+    // two-thread form (head_dim 64 only): exchanged partial row maxima and sums
+    static constexpr int kXR = D == 64 ? kBM : 1;
+    float xmax[2][2][2][kXR];  // [tile][exchange parity][half][row]
+    float xl[2][2][kXR];       // [tile][half][row] (epilogue)
     uint32_t tmem_base;
     int abort_flag;
 };
@@ -191,6 +194,7 @@ __global__ void __launch_bounds__(threads_for<R>(), 1)
     using G = PG<D>;
     constexpr int kStages = stages_for<D>();
     constexpr bool kTmaOut = tma_out<D, R>();
+    static_assert(D == 64 || R == 1, "head_dim 128 is built in the one-thread-per-row form only");
     constexpr int kBN = G::BN, SC = G::SC, OC = G::OC;
     extern __shared__ uint8_t smem_raw[];
     auto* sm = reinterpret_cast<SmemLayout<D>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -218,7 +222,7 @@ __global__ void __launch_bounds__(threads_for<R>(), 1)
             mbar_init(&sm->o_done[i], 1);
             for (int qq = 0; qq < 4; qq++) mbar_init(&sm->xbar[i][qq], 2);  // one arrival per warp of the pair
             mbar_init(&sm->fin[i], 1);
-            mbar_init(&sm->o_staged[i], 8);  // the tile's 8 softmax warps (head_dim 64 form)
+            mbar_init(&sm->o_staged[i], 4 * R);  // the tile's softmax warps
             mbar_init(&sm->o_free[i], 1);
         }
         for (int i = 0; i < kStages; i++) {
@@ -412,7 +416,8 @@ __global__ void __launch_bounds__(threads_for<R>(), 1)
         const uint32_t s_addr = lane_addr + G::col_s(tile);
         const uint32_t o_addr = lane_addr + G::col_o(tile);
         const uint32_t p_addr = lane_addr + G::col_p(tile);
-        uint32_t s_uses = 0, o_uses = 0;
+        uint32_t s_uses = 0, o_uses = 0, ep_uses = 0;
+        const bool issuer = kTmaOut && ((warp - 4) & 3) == 0 && lane == 0;  // the tile's output TMA thread
         bool ok = true;
         for (int r = 0, it = item_of(0); ok && it < a.total_items; it = item_of(++r)) {
             const Item x = decode_item<kBN>(a, it);
@@ -511,6 +516,71 @@ __global__ void __launch_bounds__(threads_for<R>(), 1)
             tc_fence_after();
             const float inv = 1.f / (lsum.x + lsum.y);
             const int t = row0 + row;
+            if constexpr (kTmaOut) {
+                // Two rounds of 64 columns through the tile's staging boxes and one thread's TMA stores, with the
+                // same o_free / o_staged hand-offs as the two-thread form.
+                float* stage = sm->o_stage + tile * (kBM * 64);
+#pragma unroll 1
+                for (int r64 = 0; r64 < D / 64; r64++) {
+                    float o[64];
+                    tmem_ld32(o_addr + r64 * 64, o);
+                    tmem_ld32(o_addr + r64 * 64 + 32, o + 32);
+                    tmem_wait_ld();
+                    if (ep_uses > 0) {
+                        if (issuer) {
+                            bulk_wait_read_all();
+                            mbar_arrive(&sm->o_free[tile]);
+                        }
+                        ok = __all_sync(0xffffffffu, mbar_wait(&sm->o_free[tile], (ep_uses - 1) & 1, ab));
+                        if (!ok) break;
+                    }
+                    if (a.out_f16) {
+                        __half* rowp = reinterpret_cast<__half*>(stage) + row * 64;
+#pragma unroll
+                        for (int c = 0; c < 8; c++) {
+                            const int ch = c ^ (row & 7);
+                            const float* v = o + 8 * c;
+                            *reinterpret_cast<uint4*>(rowp + ch * 8) =
+                                make_uint4(pack_half2(v[0] * inv, v[1] * inv), pack_half2(v[2] * inv, v[3] * inv),
+                                           pack_half2(v[4] * inv, v[5] * inv), pack_half2(v[6] * inv, v[7] * inv));
+                        }
+                    } else {
+#pragma unroll
+                        for (int b = 0; b < 2; b++) {
+                            float* rowp = stage + b * (kBM * 32) + row * 32;
+#pragma unroll
+                            for (int c = 0; c < 8; c++) {
+                                const int ch = c ^ (row & 7);
+                                const float* v = o + 32 * b + 4 * c;
+                                *reinterpret_cast<float4*>(rowp + ch * 4) =
+                                    make_float4(v[0] * inv, v[1] * inv, v[2] * inv, v[3] * inv);
+                            }
+                        }
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&sm->o_staged[tile]);
+                    bool sent = true;
+                    if (issuer) {
+                        sent = mbar_wait(&sm->o_staged[tile], ep_uses & 1, ab);
+                        if (sent) {
+                            if (a.out_f16) {
+                                tma_store_4d(&tm_o, stage, r64 * 64, x.head, row0, x.seq);
+                            } else {
+                                tma_store_4d(&tm_o, stage, r64 * 64, x.head, row0, x.seq);
+                                tma_store_4d(&tm_o, stage + kBM * 32, r64 * 64 + 32, x.head, row0, x.seq);
+                            }
+                            bulk_commit();
+                        }
+                    }
+                    ok = __all_sync(0xffffffffu, sent);
+                    if (!ok) break;
+                    ep_uses++;
+                }
+                if (!ok) break;
+                tc_fence_before();
+                continue;
+            }
             const int64_t off = x.seq * a.out_seq_stride + static_cast<int64_t>(t) * a.out_token_stride +
                                 static_cast<int64_t>(x.head) * D;
 #pragma unroll
@@ -537,6 +607,7 @@ __global__ void __launch_bounds__(threads_for<R>(), 1)
             }
             tc_fence_before();
         }
+        if (issuer) bulk_wait_all();  // the tile's last output stores are done before the CTA retires
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm->retire);
@@ -867,7 +938,8 @@ bool make_out_map(CUtensorMap* map, void* base, bool f16, int d, int heads, int 
 
 // Softmax threads per query row: one at head_dim 128 (822 against 747 TFLOP/s on 30 layers x 4096 tokens), two at
 // head_dim 64 (637 against 612-617: with a whole 128-column row per thread two softmax warps per SMSP hide less
-// latency than four). ALPACA_PREFILL_ROWS = 1 or 2 forces either.
+// latency than four). ALPACA_PREFILL_ROWS = 1 or 2 forces a form at head_dim 64; head_dim 128 has only the
+// one-thread form.
 int prefill_row_threads(int head_dim) {
     static const int v = [] {
         const char* e = std::getenv("ALPACA_PREFILL_ROWS");
@@ -878,19 +950,21 @@ int prefill_row_threads(int head_dim) {
 
 template <int D>
 PrefillFn prefill_variant(int emu, int rows) {
-    if (rows == 1) {
-        switch (emu) {
-            case 0: return prefill_kernel<D, 0, 1>;
-            case 3: return prefill_kernel<D, 3, 1>;
-            case 4: return prefill_kernel<D, 4, 1>;
-            default: return prefill_kernel<D, 2, 1>;
+    if constexpr (D == 64) {  // head_dim 128 is built in the one-thread form only
+        if (rows != 1) {
+            switch (emu) {
+                case 0: return prefill_kernel<D, 0, 2>;
+                case 3: return prefill_kernel<D, 3, 2>;
+                case 4: return prefill_kernel<D, 4, 2>;
+                default: return prefill_kernel<D, 2, 2>;
+            }
         }
     }
     switch (emu) {
-        case 0: return prefill_kernel<D, 0, 2>;
-        case 3: return prefill_kernel<D, 3, 2>;
-        case 4: return prefill_kernel<D, 4, 2>;
-        default: return prefill_kernel<D, 2, 2>;
+        case 0: return prefill_kernel<D, 0, 1>;
+        case 3: return prefill_kernel<D, 3, 1>;
+        case 4: return prefill_kernel<D, 4, 1>;
+        default: return prefill_kernel<D, 2, 1>;
     }
 }
 
@@ -909,7 +983,7 @@ size_t prefill_workspace_bytes(const alpaca_attn_desc& d) {
 cudaError_t launch_prefill(const Call& c, cudaStream_t s) {
     const alpaca_attn_desc& d = *c.d;
     const bool d128 = d.head_dim == 128;
-    const int rows = prefill_row_threads(d.head_dim);
+    const int rows = d128 ? 1 : prefill_row_threads(d.head_dim);
     const PrefillFn fn = d128 ? prefill_variant<128>(prefill_emu_pairs(), rows)
                               : prefill_variant<64>(prefill_emu_pairs(), rows);
     const size_t smem = d128 ? smem_bytes<128>() : smem_bytes<64>();
@@ -956,7 +1030,7 @@ cudaError_t launch_prefill(const Call& c, cudaStream_t s) {
     }
 
     CUtensorMap to = tq;  // unused by the forms that store the output directly
-    if (!d128 && rows != 1 &&
+    if ((d128 || rows != 1) &&
         !make_out_map(&to, d.out, d.out_dtype == ALPACA_F16, d.head_dim, d.n_heads, d.tokens, d.n_seqs,
                       d.out_token_stride, d.out_seq_stride))
         return cudaErrorInvalidValue;
