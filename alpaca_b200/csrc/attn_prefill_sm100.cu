@@ -10,7 +10,7 @@
 //     rounds, so the causal triangle is balanced over the 148 SMs even when there are few items per SM;
 //   * head_dim 64 (128-row KV blocks) and 128 (64-row KV blocks, so S, O and P of both tiles fit TMEM); rows of Q,
 //     K and V are stored as head_dim/64 column blocks of 128 bytes;
-//   * warp 0: TMA producer. Q tiles and a 4-stage ring of K/V blocks land in shared memory with 128-byte swizzle,
+//   * warp 0: TMA producer. Q tiles and a 3-stage ring of K/V blocks land in shared memory with 128-byte swizzle,
 //     no multicast;
 //   * warps 1 and 2: one thread each issues tcgen05.mma for tile A / B: S = Q·Kᵀ (A and B from shared memory)
 //     into TMEM, and O += P·V with P read from TMEM (A operand in tensor memory, B = V from shared memory), so
@@ -24,8 +24,11 @@
 //     two-arrival mbarrier per pair of warps that share TMEM lanes), so the exchange is off the critical path;
 //     the half with the lower candidate scales its f16 P pairs down. P = 2^(s*c - m) — most exponentials on
 //     MUFU, a fixed share on the FMA pipe with a polynomial — is summed per row in f32, stored to TMEM as f16
-//     pairs, and each tile ends with O / l;
-//   * registers: the control warpgroup drops to 56 per thread (setmaxnreg) so the softmax warps get 104.
+//     pairs, and each tile ends with O / l, written into a shared-memory staging tile (128-byte swizzle) and sent
+//     to global memory by one thread's TMA stores (mbarrier hand-offs with bounded waits; rows past the tokens are
+//     clipped by the tensor map);
+//   * registers (two-thread form): the control warpgroup drops to 56 per thread (setmaxnreg) so the softmax warps
+//     get 104; the one-thread form takes up to 168 per thread from its launch bound.
 //   TMEM (see PG): d=64: S_A 0-127, S_B 128-255, O_A 256-319, O_B 320-383, P_A 384-447, P_B 448-511;
 //                  d=128: S_A 0-63, S_B 64-127, O_A 128-255, O_B 256-383, P_A 384-415, P_B 416-447.
 //
