@@ -276,3 +276,28 @@ def test_large_scores_rescale_path(cuda_lib, d):
                      torch.from_numpy(v).to(dev).half(), out, kind=Kernel.PREFILL_TC)
     device_status()
     max_abs_check(out.cpu().numpy(), cpu, 3 * 2.0 ** -11 * float(np.abs(v).max()), f"rescale path d={d}")
+
+
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("odt", [torch.float32, torch.float16])
+def test_prefill_output_views(cuda_lib, d, odt):
+    """The prefill output written through its tensor map (TMA stores): into views of wider buffers (padded token and
+    sequence strides, two sequences, a last tile that ends mid-tile) it equals the contiguous output bit for bit, and
+    the padding around the view is left untouched."""
+    from alpaca_b200 import Kernel, attention_device, device_status
+    S, T, start, H, kvh = 2, 200, 60, 6, 2
+    L = start + T
+    dev = torch.device("cuda")
+    q = torch.from_numpy(_normal(121, (S, T, H, d))).to(dev).half()
+    k = torch.from_numpy(_normal(122, (S, L, kvh, d))).to(dev).half()
+    v = torch.from_numpy(_normal(123, (S, L, kvh, d))).to(dev).half()
+    ref = torch.empty((S, T, H, d), dtype=odt, device=dev)
+    attention_device(q, k, v, ref, start_position=start, kind=Kernel.PREFILL_TC)
+    big = torch.full((S, T + 8, H + 2, d), 7.0, dtype=odt, device=dev)  # token stride (H+2)*d, seq stride (T+8)*...
+    view = big[:, 3:3 + T, 1:1 + H]
+    attention_device(q, k, v, view, start_position=start, kind=Kernel.PREFILL_TC)
+    device_status()
+    assert torch.equal(view, ref)
+    pad = torch.ones_like(big, dtype=torch.bool)
+    pad[:, 3:3 + T, 1:1 + H] = False
+    assert torch.all(big[pad] == 7.0)
