@@ -149,7 +149,6 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// 4-D tiled load (no multicast) completing `bytes` on `bar`.
 // Tiled TMA store of a shared-memory box to global memory (bulk-group completion), the group commit, and the waits:
 // .read returns once the source shared memory has been read (the box may be overwritten), the plain form once the
 // global writes are done.
@@ -164,6 +163,7 @@ __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.comm
 __device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
+// 4-D tiled load (no multicast) completing `bytes` on `bar`.
 __device__ __forceinline__ void tma_load_4d(void* smem_dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
                                             uint64_t* bar) {
     asm volatile(
