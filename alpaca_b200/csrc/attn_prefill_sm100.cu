@@ -47,43 +47,49 @@ namespace {
 
 constexpr int kBM = 128;        // query rows per tile
 // K/V ring depth: 3 (as fast as 4 at head_dim 64, and it leaves room for the output staging tiles).
-template <int D>
-__host__ __device__ constexpr int stages_for() { return 3; }
+template <int D, int NT>
+__host__ __device__ constexpr int stages_for() { return NT == 3 ? 4 : 3; }
 // The default forms (head_dim 64 with two softmax threads per row, head_dim 128 with one) write the output through
 // shared-memory staging tiles and TMA stores.
-template <int D, int R>
-__host__ __device__ constexpr bool tma_out() { return (D == 64 && R == 2) || (D == 128 && R == 1); }
-// Threads per CTA: warps 0-3 are TMA, MMA A, MMA B (+ TMEM allocator) and idle; then the softmax warps, 16 with
-// two threads per query row (R = 2) or 8 with one (R = 1).
-template <int R>
-__host__ __device__ constexpr int threads_for() { return R == 2 ? 640 : 384; }
-constexpr int kThreads = threads_for<2>();
+template <int D, int R, int NT>
+__host__ __device__ constexpr bool tma_out() { return (D == 64 && R == 2) || (D == 128 && R == 1) || NT == 3; }
+// Threads per CTA: warps 0-3 are the TMA producer, the MMA issuers of the NT query tiles (warp 2 also allocates
+// TMEM) and, with two tiles, an idle warp; then 4 R softmax warps per tile (R threads per query row).
+template <int R, int NT>
+__host__ __device__ constexpr int threads_for() { return 32 * (4 + 4 * R * NT); }
+constexpr int kThreads = threads_for<2, 2>();
 constexpr int kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;      // log2 units
 
-// Geometry per head dim. Rows of Q, K and V live in shared memory as D/64 column blocks [rows][64] (128 bytes per
-// row, 128-byte swizzle), the layout a 64 x 1 x rows x 1 TMA box writes. d = 64: 128-row KV blocks; d = 128: 64-row
-// KV blocks, so that S, O and P of both tiles fit the 512 TMEM columns.
-//   TMEM: S_A [0, BN), S_B [BN, 2BN), O_A, O_B (D columns each) from 2BN, P_A, P_B (BN/2 columns each) after them:
-//   d = 64: S 0 / 128, O 256 / 320, P 384 / 448;  d = 128: S 0 / 64, O 128 / 256, P 384 / 416.
-template <int D>
+// Geometry per head dim and number of query tiles per work item (NT). Rows of Q, K and V live in shared memory as
+// D/64 column blocks [rows][64] (128 bytes per row, 128-byte swizzle), the layout a 64 x 1 x rows x 1 TMA box
+// writes. d = 64 with two tiles: 128-row KV blocks; d = 128, and d = 64 with three tiles: 64-row KV blocks, so that
+// S, O and P of every tile fit the 512 TMEM columns.
+//   TMEM: S_t at t BN, O_t (D columns) at NT BN + t D, P_t (BN/2 columns of f16 pairs) at NT (BN + D) + t BN/2:
+//   d = 64, two tiles: S 0 / 128, O 256 / 320, P 384 / 448;  d = 128: S 0 / 64, O 128 / 256, P 384 / 416;
+//   d = 64, three tiles: S 0 / 64 / 128, O 192 / 256 / 320, P 384 / 416 / 448.
+template <int D, int NT = 2>
 struct PG {
     static_assert(D == 64 || D == 128, "head_dim 64 or 128");
-    static constexpr int BN = D == 64 ? 128 : 64;  // KV rows per block
+    static_assert(NT == 2 || (NT == 3 && D == 64), "three query tiles at head_dim 64 only");
+    static constexpr int BN = (D == 64 && NT == 2) ? 128 : 64;  // KV rows per block
     static constexpr int CB = D / 64;              // 64-column blocks per row
     static constexpr int SC = BN / 2;              // S columns per softmax thread (half a block row)
     static constexpr int OC = D / 2;               // O columns per softmax thread
     static constexpr uint32_t kQBytes = kBM * D * 2;
     static constexpr uint32_t kKVBytes = BN * D * 2;
     __host__ __device__ static constexpr uint32_t col_s(int tile) { return tile * BN; }
-    __host__ __device__ static constexpr uint32_t col_o(int tile) { return 2 * BN + tile * D; }
-    __host__ __device__ static constexpr uint32_t col_p(int tile) { return 2 * BN + 2 * D + tile * (BN / 2); }
-    static_assert(2 * BN + 2 * D + BN <= kTmemCols, "TMEM map exceeds 512 columns");
+    __host__ __device__ static constexpr uint32_t col_o(int tile) { return NT * BN + tile * D; }
+    __host__ __device__ static constexpr uint32_t col_p(int tile) { return NT * (BN + D) + tile * (BN / 2); }
+    static_assert(NT * (BN + D + BN / 2) <= kTmemCols, "TMEM map exceeds 512 columns");
 };
 // Register split after the role dispatch (setmaxnreg): the control warpgroup (warps 0-3) gives registers to
 // the four softmax warpgroups (128 * 56 + 512 * 104 of the 640 x 96 registers the CTA is launched with).
 constexpr uint32_t kRegsControl = 56, kRegsSoftmax = 104;
 static_assert(128 * kRegsControl + 512 * kRegsSoftmax <= kThreads * 96, "register split exceeds the launch budget");
+// Three-tile form: 512 threads launched at 128 registers; the three softmax warpgroups take 152.
+constexpr uint32_t kRegsSoftmax3 = 152;
+static_assert(128 * kRegsControl + 384 * kRegsSoftmax3 <= 512 * 128, "register split exceeds the launch budget");
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct PrefillArgs {
@@ -91,7 +97,7 @@ struct PrefillArgs {
     int64_t out_token_stride, out_seq_stride;
     int out_f16;
     int n_seqs, n_heads, n_kv_heads, tokens, start, kv_len;
-    int n_pairs, total_items;
+    int n_groups, total_items;  // groups of NT query tiles per (sequence, head); work items
     float scale_log2;
     unsigned* err;
     unsigned flags;
@@ -99,35 +105,36 @@ struct PrefillArgs {
     int block_rows, max_blocks, pool_blocks, last_block;  // last_block: block (of a sequence) holding row kv_len - 1
 };
 
-template <int D>
+template <int D, int NT = 2>
 struct SmemLayout {
-    static constexpr int kStages = stages_for<D>();
-    __half q[2][kBM * D];                 // [tile][column block][row][64]
+    static constexpr int kStages = stages_for<D, NT>();
+    __half q[NT][kBM * D];                // [tile][column block][row][64]
     // per tile, 64 columns of the normalised output [128 rows][64] as TMA store boxes of 128-byte rows with the
     // 128-byte swizzle (f32: two boxes of 32 columns; f16: one box of 64); head_dim 128 stages it in two rounds
-    float o_stage[2 * kBM * 64];
-    __half k[kStages][PG<D>::BN * D];     // [stage][column block][row][64]
-    __half v[kStages][PG<D>::BN * D];
-    uint64_t q_full[2], q_empty[2];
+    float o_stage[NT * kBM * 64];
+    __half k[kStages][PG<D, NT>::BN * D];  // [stage][column block][row][64]
+    __half v[kStages][PG<D, NT>::BN * D];
+    uint64_t q_full[NT], q_empty[NT];
     uint64_t k_full[kStages], k_empty[kStages], v_full[kStages], v_empty[kStages];
-    uint64_t s_full[2], s_empty[2], p_full[2], o_done[2];
+    uint64_t s_full[NT], s_empty[NT], p_full[NT], o_done[NT];
     uint64_t xbar[2][4];       // per (tile, lane quarter): the two half-row warps exchange partial row state
-    uint64_t dbg, fin[2], retire;
-    uint64_t o_staged[2], o_free[2];  // head_dim 64 output: rows staged (8 warps), staging free again (issuer)
+    uint64_t dbg, fin[NT], retire;
+    uint64_t o_staged[NT], o_free[NT];  // output: rows staged (the tile's softmax warps), staging free again (issuer)
     // two-thread form (head_dim 64 only): exchanged partial row maxima and sums
-    static constexpr int kXR = D == 64 ? kBM : 1;
+    static constexpr int kXR = (D == 64 && NT == 2) ? kBM : 1;
     float xmax[2][2][2][kXR];  // [tile][exchange parity][half][row]
     float xl[2][2][kXR];       // [tile][half][row] (epilogue)
     uint32_t tmem_base;
     int abort_flag;
 };
 
-template <int D>
-constexpr size_t smem_bytes() { return sizeof(SmemLayout<D>) + 1024; }  // + alignment slack
-static_assert(smem_bytes<64>() <= 232448 && smem_bytes<128>() <= 232448, "shared memory exceeds 227 KB per CTA");
+template <int D, int NT = 2>
+constexpr size_t smem_bytes() { return sizeof(SmemLayout<D, NT>) + 1024; }  // + alignment slack
+static_assert(smem_bytes<64>() <= 232448 && smem_bytes<128>() <= 232448 && smem_bytes<64, 3>() <= 232448,
+              "shared memory exceeds 227 KB per CTA");
 
 struct Item {
-    int seq, head, row0[2], nblk[2];
+    int seq, head, row0[3], nblk[3];  // first NT entries used
 };
 
 template <int BN>
@@ -138,28 +145,37 @@ __device__ __forceinline__ int tile_blocks(const PrefillArgs& a, int row0) {
     return (visible + BN - 1) / BN;
 }
 
-template <int BN>
+template <int BN, int NT>
 __device__ __forceinline__ Item decode_item(const PrefillArgs& a, int it) {
     const int per_rank = a.n_seqs * a.n_heads;
     const int rank = it / per_rank, rem = it - rank * per_rank;
     Item x;
-    const int pair = a.n_pairs - 1 - rank;  // heaviest pairs first
+    const int group = a.n_groups - 1 - rank;  // heaviest groups first
     x.seq = rem / a.n_heads;
     x.head = rem - x.seq * a.n_heads;
-    x.row0[0] = pair * 2 * kBM;
-    x.row0[1] = x.row0[0] + kBM;
-    x.nblk[0] = tile_blocks<BN>(a, x.row0[0]);
-    x.nblk[1] = tile_blocks<BN>(a, x.row0[1]);
+#pragma unroll
+    for (int t = 0; t < NT; t++) {
+        x.row0[t] = (group * NT + t) * kBM;
+        x.nblk[t] = tile_blocks<BN>(a, x.row0[t]);
+    }
     return x;
+}
+
+template <int NT>
+__device__ __forceinline__ int item_blocks(const Item& x) {
+    int n = x.nblk[0];
+#pragma unroll
+    for (int t = 1; t < NT; t++) n = max(n, x.nblk[t]);
+    return n;
 }
 
 // ---------------------------------------------------------------------------------------------- MMA helpers
 
 // S_t = Q_t · K_stageᵀ: M=128, N=BN, K=D (D/16 steps of 16); both operands K-major, 128-byte swizzle. K step kk
 // lies in column block kk/4 at byte offset (kk%4)*32 of each 128-byte row.
-template <int D>
-__device__ __forceinline__ void mma_s(const SmemLayout<D>* sm, int tile, int stage, uint32_t tmem_base) {
-    using G = PG<D>;
+template <int D, int NT>
+__device__ __forceinline__ void mma_s(const SmemLayout<D, NT>* sm, int tile, int stage, uint32_t tmem_base) {
+    using G = PG<D, NT>;
     constexpr uint32_t idesc = idesc_f16_f32(kBM, G::BN, false, false);
     const uint32_t qa = smem_u32(sm->q[tile]), ka = smem_u32(sm->k[stage]);
 #pragma unroll
@@ -172,10 +188,10 @@ __device__ __forceinline__ void mma_s(const SmemLayout<D>* sm, int tile, int sta
 
 // O_t (+)= P_t · V_stage: M=128, N=D, K=BN (BN/16 steps of 16). P in TMEM (8 columns of f16 pairs per step), V
 // MN-major in shared memory: 16 KV rows = 2 KB per step, the next 64-column block BN*128 bytes further (LBO).
-template <int D>
-__device__ __forceinline__ void mma_pv(const SmemLayout<D>* sm, int tile, int stage, uint32_t tmem_base,
+template <int D, int NT>
+__device__ __forceinline__ void mma_pv(const SmemLayout<D, NT>* sm, int tile, int stage, uint32_t tmem_base,
                                        bool accumulate) {
-    using G = PG<D>;
+    using G = PG<D, NT>;
     constexpr uint32_t idesc = idesc_f16_f32(kBM, D, false, true);
     const uint32_t va = smem_u32(sm->v[stage]);
 #pragma unroll
@@ -188,19 +204,20 @@ __device__ __forceinline__ void mma_pv(const SmemLayout<D>* sm, int tile, int st
 
 // ---------------------------------------------------------------------------------------------- kernel
 
-template <int D, int kEmuPairs, int R>
-__global__ void __launch_bounds__(threads_for<R>(), 1)
+template <int D, int kEmuPairs, int R, int NT>
+__global__ void __launch_bounds__(threads_for<R, NT>(), 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_kt,
                    const __grid_constant__ CUtensorMap tm_vt, const __grid_constant__ CUtensorMap tm_o,
                    const PrefillArgs a) {
-    using G = PG<D>;
-    constexpr int kStages = stages_for<D>();
-    constexpr bool kTmaOut = tma_out<D, R>();
+    using G = PG<D, NT>;
+    constexpr int kStages = stages_for<D, NT>();
+    constexpr bool kTmaOut = tma_out<D, R, NT>();
     static_assert(D == 64 || R == 1, "head_dim 128 is built in the one-thread-per-row form only");
+    static_assert(NT == 2 || R == 1, "three query tiles in the one-thread-per-row form only");
     constexpr int kBN = G::BN, SC = G::SC, OC = G::OC;
     extern __shared__ uint8_t smem_raw[];
-    auto* sm = reinterpret_cast<SmemLayout<D>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    auto* sm = reinterpret_cast<SmemLayout<D, NT>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // The next stream-ordered kernel may launch now; it waits for this grid to finish before touching memory.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -216,26 +233,27 @@ __global__ void __launch_bounds__(threads_for<R>(), 1)
 
     if (tid == 0) {
         sm->abort_flag = 0;
-        for (int i = 0; i < 2; i++) {
+        for (int i = 0; i < NT; i++) {
             mbar_init(&sm->q_full[i], 1);
             mbar_init(&sm->q_empty[i], 1);
             mbar_init(&sm->s_full[i], 1);
             mbar_init(&sm->s_empty[i], 4 * R);  // one arrival per softmax warp of the tile
             mbar_init(&sm->p_full[i], 4 * R);
             mbar_init(&sm->o_done[i], 1);
-            for (int qq = 0; qq < 4; qq++) mbar_init(&sm->xbar[i][qq], 2);  // one arrival per warp of the pair
             mbar_init(&sm->fin[i], 1);
             mbar_init(&sm->o_staged[i], 4 * R);  // the tile's softmax warps
             mbar_init(&sm->o_free[i], 1);
         }
+        for (int i = 0; i < 2; i++)
+            for (int qq = 0; qq < 4; qq++) mbar_init(&sm->xbar[i][qq], 2);  // one arrival per warp of the pair
         for (int i = 0; i < kStages; i++) {
             mbar_init(&sm->k_full[i], 1);
-            mbar_init(&sm->k_empty[i], 2);  // released by both tiles' MMA issuers
+            mbar_init(&sm->k_empty[i], NT);  // released by every tile's MMA issuer
             mbar_init(&sm->v_full[i], 1);
-            mbar_init(&sm->v_empty[i], 2);
+            mbar_init(&sm->v_empty[i], NT);
         }
         mbar_init(&sm->dbg, 1);
-        mbar_init(&sm->retire, 8 * R + 2);  // the softmax warps, the producer and tile A's issuer
+        mbar_init(&sm->retire, 4 * R * NT + 2);  // the softmax warps, the producer and tile 0's issuer
         fence_barrier_init();
         tma_prefetch_desc(&tm_q);
         tma_prefetch_desc(&tm_k);
@@ -258,15 +276,15 @@ __global__ void __launch_bounds__(threads_for<R>(), 1)
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const uint32_t tmem_base = sm->tmem_base;
     if (warp == 0) {
-        if constexpr (R == 2) setmaxnreg_dec<kRegsControl>();
+        if constexpr (R == 2 || NT == 3) setmaxnreg_dec<kRegsControl>();
         if (lane != 0) return;
         // ------------------------------------------------------------------ TMA producer
-        uint32_t kv_it = 0, k_issued = 0, v_issued = 0, q_uses[2] = {0, 0};
+        uint32_t kv_it = 0, k_issued = 0, v_issued = 0, q_uses[NT] = {};
         bool ok = true;
         for (int r = 0, it = item_of(0); ok && it < a.total_items; it = item_of(++r)) {
-            const Item x = decode_item<kBN>(a, it);
+            const Item x = decode_item<kBN, NT>(a, it);
             const int kvh = x.head / (a.n_heads / a.n_kv_heads);
-            for (int t = 0; t < 2 && ok; t++) {
+            for (int t = 0; t < NT && ok; t++) {
                 if (x.nblk[t] == 0) continue;
                 ok = mbar_wait(&sm->q_empty[t], (q_uses[t] & 1) ^ 1, ab);
                 if (!ok) break;
@@ -276,7 +294,7 @@ __global__ void __launch_bounds__(threads_for<R>(), 1)
                     tma_load_4d(sm->q[t] + cb * kBM * 64, &tm_q, 64 * cb, x.head, x.row0[t], x.seq, &sm->q_full[t]);
                 q_uses[t]++;
             }
-            const int nmax = max(x.nblk[0], x.nblk[1]);
+            const int nmax = item_blocks<NT>(x);
             for (int j = 0; ok && j < nmax; j++, kv_it++) {
                 const int st = kv_it % kStages;
                 const uint32_t ph = (kv_it / kStages) & 1;
@@ -323,25 +341,25 @@ __global__ void __launch_bounds__(threads_for<R>(), 1)
                 mbar_wait(&sm->k_full[i % kStages], (i / kStages) & 1, drain);
             for (uint32_t i = (v_issued > kStages ? v_issued - kStages : 0); i < v_issued; i++)
                 mbar_wait(&sm->v_full[i % kStages], (i / kStages) & 1, drain);
-            for (int t = 0; t < 2; t++)
+            for (int t = 0; t < NT; t++)
                 if (q_uses[t] > 0) mbar_wait(&sm->q_full[t], (q_uses[t] - 1) & 1, drain);
         }
         mbar_arrive(&sm->retire);
-    } else if (warp == 1 || warp == 2) {
-        if constexpr (R == 2) setmaxnreg_dec<kRegsControl>();
+    } else if (warp >= 1 && warp <= NT) {
+        if constexpr (R == 2 || NT == 3) setmaxnreg_dec<kRegsControl>();
         if (lane == 0) {
             // ------------------------------------------------------------------ MMA issuers, one thread per tile
-            // Both threads walk every KV block of every item: a tile with fewer blocks than its partner still
-            // releases the K/V stages it does not use (after they land), so each stage's empty barrier (count 2)
+            // Every issuer walks every KV block of every item: a tile with fewer blocks than the others still
+            // releases the K/V stages it does not use (after they land), so each stage's empty barrier (count NT)
             // completes once per use.
             const int t = warp - 1;
             uint32_t kv_it = 0, q_uses = 0, s_uses = 0, p_uses = 0;
             bool ok = true;
             if (debug_timeout && t == 0) ok = mbar_wait(&sm->dbg, 0, ab);  // nothing arrives: exercises the give-up path
             for (int r = 0, it = item_of(0); ok && it < a.total_items; it = item_of(++r)) {
-                const Item x = decode_item<kBN>(a, it);
+                const Item x = decode_item<kBN, NT>(a, it);
                 const int n = x.nblk[t];
-                const int nmax = max(x.nblk[0], x.nblk[1]);
+                const int nmax = item_blocks<NT>(x);
                 if (n > 0) {
                     ok = mbar_wait(&sm->q_full[t], q_uses & 1, ab);
                     if (!ok) break;
@@ -358,7 +376,7 @@ __global__ void __launch_bounds__(threads_for<R>(), 1)
                             ok = mbar_wait(&sm->s_empty[t], (s_uses & 1) ^ 1, ab);
                             if (!ok) break;
                             tc_fence_after();
-                            mma_s<D>(sm, t, st, tmem_base);
+                            mma_s<D, NT>(sm, t, st, tmem_base);
                             tc_commit(&sm->s_full[t]);
                             s_uses++;
                             if (j + 1 == n) tc_commit(&sm->q_empty[t]);
@@ -377,7 +395,7 @@ __global__ void __launch_bounds__(threads_for<R>(), 1)
                             ok = mbar_wait(&sm->p_full[t], p_uses & 1, ab);
                             if (!ok) break;
                             tc_fence_after();
-                            mma_pv<D>(sm, t, sp, tmem_base, b > 0);
+                            mma_pv<D, NT>(sm, t, sp, tmem_base, b > 0);
                             tc_commit(&sm->o_done[t]);
                             tc_commit(&sm->v_empty[sp]);
                             p_uses++;
@@ -407,8 +425,9 @@ __global__ void __launch_bounds__(threads_for<R>(), 1)
             tmem_dealloc(tmem_base, kTmemCols);
         }
     } else if (warp == 3) {
-        if constexpr (R == 2) setmaxnreg_dec<kRegsControl>();
+        if constexpr (R == 2 || NT == 3) setmaxnreg_dec<kRegsControl>();
     } else if constexpr (R == 1) {
+        if constexpr (NT == 3) setmaxnreg_inc<kRegsSoftmax3>();
         // ------------------------------------------------------------------ softmax warps, one thread per row
         // Warp 4 + 4*tile + quarter owns TMEM lane quarter `quarter` of tile `tile`: each thread a whole query row,
         // so the row max and the row sum need no exchange. Registers come from the launch bound (no split).
@@ -423,7 +442,7 @@ __global__ void __launch_bounds__(threads_for<R>(), 1)
         const bool issuer = kTmaOut && ((warp - 4) & 3) == 0 && lane == 0;  // the tile's output TMA thread
         bool ok = true;
         for (int r = 0, it = item_of(0); ok && it < a.total_items; it = item_of(++r)) {
-            const Item x = decode_item<kBN>(a, it);
+            const Item x = decode_item<kBN, NT>(a, it);
             const int nb = x.nblk[tile];
             if (nb == 0) continue;
             const int row0 = x.row0[tile];
@@ -631,7 +650,7 @@ __global__ void __launch_bounds__(threads_for<R>(), 1)
         const bool issuer = kTmaOut && ((warp - 4) & 7) == 0 && lane == 0;  // the tile's output TMA thread
         bool ok = true;
         for (int r = 0, it = item_of(0); ok && it < a.total_items; it = item_of(++r)) {
-            const Item x = decode_item<kBN>(a, it);
+            const Item x = decode_item<kBN, NT>(a, it);
             const int nb = x.nblk[tile];
             if (nb == 0) continue;
             const int row0 = x.row0[tile];
@@ -903,18 +922,19 @@ bool make_map(CUtensorMap* map, const void* base, int d, int heads, int rows, in
     return r == CUDA_SUCCESS;
 }
 
-// Share of exponentials computed on the FMA pipe: ALPACA_PREFILL_EMU column pairs of every 8 (0, 2, 3 or 4;
-// default 0). MUFU gives 16 exp2 per clock per SM; with the output leaving through TMA stores, all exponentials on
-// MUFU measured fastest (0.806 against 0.820 ms with 2 of 8 pairs on the FMA pipe, 30 layers x 4096 tokens).
-constexpr int kEmuDefault = 0;
-int prefill_emu_pairs() {
+// Share of exponentials computed on the FMA pipe: ALPACA_PREFILL_EMU column pairs of every 8 (0, 2, 3 or 4).
+// MUFU gives 16 exp2 per clock per SM. Defaults, measured on 30 layers x 4096 tokens: the two-tile forms keep every
+// exponential on MUFU (0.806 against 0.820 ms with 2 of 8 pairs on the FMA pipe, now that the output leaves through
+// TMA stores); the three-tile form, whose three softmax phase groups keep MUFU busier, moves 2 of 8 (0.831 against
+// 0.924 ms; 3 of 8: 0.839, 4 of 8: 0.951).
+int prefill_emu_pairs(int tiles) {
     static const int v = [] {
         const char* e = std::getenv("ALPACA_PREFILL_EMU");
-        if (!e || !*e) return kEmuDefault;
+        if (!e || !*e) return -1;
         const int x = std::atoi(e);
-        return (x == 0 || x == 2 || x == 3 || x == 4) ? x : kEmuDefault;
+        return (x == 0 || x == 2 || x == 3 || x == 4) ? x : -1;
     }();
-    return v;
+    return v >= 0 ? v : (tiles == 3 ? 2 : 0);
 }
 
 using PrefillFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, PrefillArgs);
@@ -951,23 +971,42 @@ int prefill_row_threads(int head_dim) {
     return v ? v : (head_dim == 128 ? 1 : 2);
 }
 
+// Query tiles per work item at head_dim 64: 2 (128-row KV blocks; default) or 3 (64-row KV blocks, one softmax
+// thread per row, three softmax phase groups per SMSP instead of two): 0.831 against 0.807 ms on 30 layers x 4096
+// tokens. ALPACA_PREFILL_TILES = 3 selects the three-tile form.
+int prefill_tiles(int head_dim) {
+    static const int v = [] {
+        const char* e = std::getenv("ALPACA_PREFILL_TILES");
+        return e ? (e[0] == '3' ? 3 : 2) : 0;
+    }();
+    return head_dim != 64 ? 2 : (v ? v : 2);
+}
+
 template <int D>
-PrefillFn prefill_variant(int emu, int rows) {
-    if constexpr (D == 64) {  // head_dim 128 is built in the one-thread form only
+PrefillFn prefill_variant(int emu, int rows, int tiles) {
+    if constexpr (D == 64) {  // head_dim 128 is built in the one-thread two-tile form only
+        if (tiles == 3) {
+            switch (emu) {
+                case 0: return prefill_kernel<D, 0, 1, 3>;
+                case 3: return prefill_kernel<D, 3, 1, 3>;
+                case 4: return prefill_kernel<D, 4, 1, 3>;
+                default: return prefill_kernel<D, 2, 1, 3>;
+            }
+        }
         if (rows != 1) {
             switch (emu) {
-                case 0: return prefill_kernel<D, 0, 2>;
-                case 3: return prefill_kernel<D, 3, 2>;
-                case 4: return prefill_kernel<D, 4, 2>;
-                default: return prefill_kernel<D, 2, 2>;
+                case 0: return prefill_kernel<D, 0, 2, 2>;
+                case 3: return prefill_kernel<D, 3, 2, 2>;
+                case 4: return prefill_kernel<D, 4, 2, 2>;
+                default: return prefill_kernel<D, 2, 2, 2>;
             }
         }
     }
     switch (emu) {
-        case 0: return prefill_kernel<D, 0, 1>;
-        case 3: return prefill_kernel<D, 3, 1>;
-        case 4: return prefill_kernel<D, 4, 1>;
-        default: return prefill_kernel<D, 2, 1>;
+        case 0: return prefill_kernel<D, 0, 1, 2>;
+        case 3: return prefill_kernel<D, 3, 1, 2>;
+        case 4: return prefill_kernel<D, 4, 1, 2>;
+        default: return prefill_kernel<D, 2, 1, 2>;
     }
 }
 
@@ -986,11 +1025,12 @@ size_t prefill_workspace_bytes(const alpaca_attn_desc& d) {
 cudaError_t launch_prefill(const Call& c, cudaStream_t s) {
     const alpaca_attn_desc& d = *c.d;
     const bool d128 = d.head_dim == 128;
-    const int rows = d128 ? 1 : prefill_row_threads(d.head_dim);
-    const PrefillFn fn = d128 ? prefill_variant<128>(prefill_emu_pairs(), rows)
-                              : prefill_variant<64>(prefill_emu_pairs(), rows);
-    const size_t smem = d128 ? smem_bytes<128>() : smem_bytes<64>();
-    const int bn = d128 ? PG<128>::BN : PG<64>::BN;
+    const int tiles = prefill_tiles(d.head_dim);
+    const int rows = (d128 || tiles == 3) ? 1 : prefill_row_threads(d.head_dim);
+    const int emu = prefill_emu_pairs(tiles);
+    const PrefillFn fn = d128 ? prefill_variant<128>(emu, rows, tiles) : prefill_variant<64>(emu, rows, tiles);
+    const size_t smem = d128 ? smem_bytes<128>() : (tiles == 3 ? smem_bytes<64, 3>() : smem_bytes<64>());
+    const int bn = d128 ? PG<128>::BN : (tiles == 3 ? PG<64, 3>::BN : PG<64>::BN);
     // per-device function attribute (host-side, cheap next to the launch itself)
     cudaError_t attr_err = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
@@ -1033,7 +1073,7 @@ cudaError_t launch_prefill(const Call& c, cudaStream_t s) {
     }
 
     CUtensorMap to = tq;  // unused by the forms that store the output directly
-    if ((d128 || rows != 1) &&
+    if ((d128 || rows != 1 || tiles == 3) &&
         !make_out_map(&to, d.out, d.out_dtype == ALPACA_F16, d.head_dim, d.n_heads, d.tokens, d.n_seqs,
                       d.out_token_stride, d.out_seq_stride))
         return cudaErrorInvalidValue;
@@ -1049,8 +1089,8 @@ cudaError_t launch_prefill(const Call& c, cudaStream_t s) {
     a.tokens = d.tokens;
     a.start = d.start_position;
     a.kv_len = kv_len;
-    a.n_pairs = (d.tokens + 2 * kBM - 1) / (2 * kBM);
-    a.total_items = a.n_pairs * d.n_seqs * d.n_heads;
+    a.n_groups = (d.tokens + tiles * kBM - 1) / (tiles * kBM);
+    a.total_items = a.n_groups * d.n_seqs * d.n_heads;
     a.scale_log2 = c.scale * kLog2e;
     a.err = c.err;
     a.flags = d.flags;
@@ -1062,7 +1102,7 @@ cudaError_t launch_prefill(const Call& c, cudaStream_t s) {
     const int grid = std::max(1, std::min(a.total_items, c.num_sms));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid, 1, 1);
-    cfg.blockDim = dim3(rows == 1 ? threads_for<1>() : threads_for<2>(), 1, 1);
+    cfg.blockDim = dim3(32 * (4 + 4 * rows * tiles), 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
