@@ -95,6 +95,9 @@ template <bool kInterleaved, typename QT, typename CT>
 __global__ void __launch_bounds__(kRopeThreads) rope_kv_kernel(const __grid_constant__ RopeArgs a) {
     // The attention call that follows may launch now; it waits for this grid to finish before reading.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    // Launched with programmatic dependent launch: no global access before the previous kernel's writes are
+    // complete and visible.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     __shared__ float2 cs[kRopeMaxPairs];
     const int t = blockIdx.x, seq = blockIdx.y, tid = threadIdx.x;
     const int pos = (a.positions ? a.positions[seq] : a.start) + t;
@@ -266,21 +269,30 @@ __global__ void __launch_bounds__(kVecThreads, 4) rope_kv_vec_kernel(const __gri
     extern __shared__ float2 cs[];  // [tpc][half] (cos, sin)
     const int t0 = blockIdx.x * a.tpc, seq = blockIdx.y, tid = threadIdx.x;
     const int ntok = min(a.tpc, a.tokens - t0);
-    const int pos0 = (a.positions ? a.positions[seq] : a.start) + t0;
     const int total = ntok * (a.n_heads + 2 * a.n_kv_heads) * (a.half / 4);
     constexpr int kStride = kVecThreads * kVecBatch;
+    const auto table = [&](int pos0) {
+        for (int j = tid; j < ntok * a.half; j += kVecThreads) {
+            const int tt = j / a.half, i = j - tt * a.half;
+            double s, c;
+            sincos(static_cast<double>(pos0 + tt) * a.freq[i], &s, &c);
+            cs[j] = make_float2(static_cast<float>(c), static_cast<float>(s));
+        }
+    };
+    // A uniform start position needs no global data: the (cos, sin) table is computed while the previous kernel
+    // drains. Launched with programmatic dependent launch, the CTA then waits for that kernel's writes before its
+    // first global access.
+    const bool uniform = a.positions == nullptr;
+    if (uniform) table(a.start + t0);
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int pos0 = (uniform ? a.start : a.positions[seq]) + t0;
 
-    // every thread's first batch of loads is in flight while the (cos, sin) table is computed
+    // every thread's first batch of loads is in flight while a per-sequence (cos, sin) table is computed
     float x0[kVecBatch][4], x1[kVecBatch][4];
 #pragma unroll
     for (int b = 0; b < kVecBatch; b++)
         vec_load<kInterleaved, QT, CT>(a, seq, t0, pos0, ntok, tid + b * kVecThreads, x0[b], x1[b]);
-    for (int j = tid; j < ntok * a.half; j += kVecThreads) {
-        const int tt = j / a.half, i = j - tt * a.half;
-        double s, c;
-        sincos(static_cast<double>(pos0 + tt) * a.freq[i], &s, &c);
-        cs[j] = make_float2(static_cast<float>(c), static_cast<float>(s));
-    }
+    if (!uniform) table(pos0);
     __syncthreads();  // every thread of the CTA reaches this once
 #pragma unroll
     for (int b = 0; b < kVecBatch; b++)
@@ -309,14 +321,24 @@ bool vector_ok(const alpaca_rope_desc& d) {
 
 template <bool kInterleaved, typename QT, typename CT>
 cudaError_t launch_qc(const RopeArgs& a, const alpaca_rope_desc& d, cudaStream_t s) {
+    // Programmatic dependent launch: the CTAs may become resident while the previous kernel on the stream drains
+    // (both kernels wait in griddepcontrol.wait before touching global memory).
+    cudaLaunchConfig_t cfg = {};
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
     if (vector_ok(d)) {
-        const dim3 grid((d.tokens + a.tpc - 1) / a.tpc, d.n_seqs, 1);
-        const size_t smem = sizeof(float2) * a.tpc * a.half;  // <= 32 KB
-        rope_kv_vec_kernel<kInterleaved, QT, CT><<<grid, kVecThreads, smem, s>>>(a);
-    } else {
-        rope_kv_kernel<kInterleaved, QT, CT><<<dim3(d.tokens, d.n_seqs, 1), kRopeThreads, 0, s>>>(a);
+        cfg.gridDim = dim3((d.tokens + a.tpc - 1) / a.tpc, d.n_seqs, 1);
+        cfg.blockDim = dim3(kVecThreads, 1, 1);
+        cfg.dynamicSmemBytes = sizeof(float2) * a.tpc * a.half;  // <= 32 KB
+        return cudaLaunchKernelEx(&cfg, rope_kv_vec_kernel<kInterleaved, QT, CT>, a);
     }
-    return cudaGetLastError();
+    cfg.gridDim = dim3(d.tokens, d.n_seqs, 1);
+    cfg.blockDim = dim3(kRopeThreads, 1, 1);
+    return cudaLaunchKernelEx(&cfg, rope_kv_kernel<kInterleaved, QT, CT>, a);
 }
 
 template <bool kInterleaved, typename QT>
