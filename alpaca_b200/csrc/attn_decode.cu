@@ -701,14 +701,18 @@ __device__ __forceinline__ void cp_async8(void* smem_dst, const void* gsrc) {
 // and every output column summed over the staged splits.
 template <int D>
 __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const DecodeArgs a) {
-    asm volatile("griddepcontrol.wait;" ::: "memory");  // split kernel's writes are visible after this
-    // The next stream-ordered kernel may launch now (it waits for this grid to finish before touching memory).
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int kvh = blockIdx.x, seq = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = a.n_heads / a.n_kv_heads;
+    // The context lengths are read before the wait for the split kernel: that kernel does not write them, and this
+    // grid launches only once every split CTA has passed its own griddepcontrol.wait, so whatever wrote them
+    // before the split kernel is complete and visible. The length read then overlaps the split grid's drain, and
+    // single-split units leave without waiting.
     const int L = ctx_len_of(a, seq);
     const int nsp = (L + Geo<D>::SL - 1) / Geo<D>::SL;
     if (nsp <= 1) return;
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // split kernel's writes are visible after this
+    // The next stream-ordered kernel may launch now (it waits for this grid to finish before touching memory).
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int rec = G * (D + 2);                 // floats per split
     const int chunk = combine_chunk(G, D);
     extern __shared__ __align__(16) float cs[];
