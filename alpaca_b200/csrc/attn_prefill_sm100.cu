@@ -29,6 +29,9 @@
 //     clipped by the tensor map);
 //   * registers (two-thread form): the control warpgroup drops to 56 per thread (setmaxnreg) so the softmax warps
 //     get 104; the one-thread form takes up to 168 per thread from its launch bound.
+//   * an alternative head_dim-64 form (template parameter NT = 3, switch ALPACA_PREFILL_TILES=3): work items of
+//     three query tiles with 64-row KV blocks and one softmax thread per row (warps 4-15, issuers in warps 1-3),
+//     so each SMSP holds three independent softmax phase groups; 2 of 8 exponential pairs on the FMA pipe.
 //   TMEM (see PG): d=64: S_A 0-127, S_B 128-255, O_A 256-319, O_B 320-383, P_A 384-447, P_B 448-511;
 //                  d=128: S_A 0-63, S_B 64-127, O_A 128-255, O_B 256-383, P_A 384-415, P_B 416-447.
 //
