@@ -35,6 +35,7 @@ class Kernel(IntEnum):
 
 
 FLAG_DEBUG_FORCE_TIMEOUT = 1 << 31
+FLAG_VARLEN = 1 << 0
 
 
 class AttnDesc(ctypes.Structure):
@@ -70,6 +71,10 @@ class AttnDesc(ctypes.Structure):
         ("block_stride", ctypes.c_int64),
         ("pool_blocks", ctypes.c_int32),
         ("reserved1", ctypes.c_int32),
+        ("q_offsets", ctypes.c_void_p),
+        ("start_positions", ctypes.c_void_p),
+        ("total_tokens", ctypes.c_int32),
+        ("reserved2", ctypes.c_int32),
     ]
 
 

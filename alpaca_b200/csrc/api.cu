@@ -1,13 +1,14 @@
 // api.cu — the C ABI (include/alpaca_cuda.h): argument validation, the kernel dispatch policy of alpaca.swift's
 // KernelEncoder.attention (Sources/AlpacaMetal/Backend/KernelEncoder.swift:306-343), workspace sizing
 // (KernelEncoder.decodeScratchBytes, :88-92), status codes mirroring MetalError (MetalContext.swift:7-31) and
-// the device error word that bounded device-side waits report into.
+// the per-stream device error words that bounded device-side waits and contract checks report into.
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <unordered_map>
 
 #include "common.cuh"
 #include "internal.h"
@@ -22,9 +23,13 @@ bool pdl_enabled() {
     return v;
 }
 
-// Device error word (one per device that loads this library). Kernels receive its address; host code reads it
-// through alpaca_cuda_device_status.
-__device__ unsigned g_device_error;
+// Device error words. Each stream that calls into the library on a device gets its own word (a slot of this
+// array), so a bounded wait that gives up or a bad index met by one call is reported to the caller that synchronises
+// that stream, not to whichever caller reads first. Slot 0 is shared by the streams beyond the first
+// kErrorSlots - 1 on a device. Kernels receive the address of their call's slot; host code reads it through
+// alpaca_cuda_device_status.
+constexpr int kErrorSlots = 1024;
+__device__ unsigned g_error_slots[kErrorSlots];
 
 namespace {
 
@@ -42,32 +47,53 @@ alpaca_cuda_status ok() {
 
 constexpr int kMaxDevices = 64;
 
+struct DeviceState {
+    unsigned* slots = nullptr;  // device address of g_error_slots on this device
+    int num_sms = 0;
+    bool ready = false;
+    std::unordered_map<uintptr_t, int> slot_of;  // stream handle -> error slot
+    int next_slot = 1;
+};
+DeviceState g_devices[kMaxDevices];
+std::mutex g_devices_mu;
+
+// What a launch needs from the current device: its SM count and the error word of `stream`.
 struct DeviceInfo {
     unsigned* err = nullptr;
     int num_sms = 0;
-    bool ready = false;
 };
-DeviceInfo g_devices[kMaxDevices];
-std::mutex g_devices_mu;
 
-// Per-device set-up, done once with that device current: address of the error word and SM count.
-cudaError_t device_info(DeviceInfo* out) {
+// Per-device set-up, done once with that device current (address of the error slots, SM count), then the slot of
+// `stream` (assigned on the stream's first call). The addresses are those of the context current at set-up, the
+// runtime's primary context, and stay valid until the process exits or the device is reset.
+cudaError_t device_info(cudaStream_t stream, DeviceInfo* out, bool assign = true, int* slot_out = nullptr) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
     std::lock_guard<std::mutex> lock(g_devices_mu);
-    DeviceInfo& di = g_devices[dev];
-    if (!di.ready) {
+    DeviceState& ds = g_devices[dev];
+    if (!ds.ready) {
         void* p = nullptr;
-        e = cudaGetSymbolAddress(&p, g_device_error);
+        e = cudaGetSymbolAddress(&p, g_error_slots);
         if (e != cudaSuccess) return e;
-        e = cudaDeviceGetAttribute(&di.num_sms, cudaDevAttrMultiProcessorCount, dev);
+        e = cudaDeviceGetAttribute(&ds.num_sms, cudaDevAttrMultiProcessorCount, dev);
         if (e != cudaSuccess) return e;
-        di.err = static_cast<unsigned*>(p);
-        di.ready = true;
+        ds.slots = static_cast<unsigned*>(p);
+        ds.ready = true;
     }
-    *out = di;
+    const uintptr_t key = reinterpret_cast<uintptr_t>(stream);
+    int slot = -1;
+    auto it = ds.slot_of.find(key);
+    if (it != ds.slot_of.end()) {
+        slot = it->second;
+    } else if (assign) {
+        slot = ds.next_slot < kErrorSlots ? ds.next_slot++ : 0;
+        ds.slot_of.emplace(key, slot);
+    }
+    if (slot_out) *slot_out = slot;
+    out->err = slot >= 0 ? ds.slots + slot : nullptr;
+    out->num_sms = ds.num_sms;
     return cudaSuccess;
 }
 
@@ -119,8 +145,21 @@ alpaca_cuda_status validate(const alpaca_attn_desc* dp) {
         return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "attention: row strides smaller than a row: " + sh);
     if (d.q_seq_stride < 0 || d.kv_seq_stride < 0 || d.out_seq_stride < 0)
         return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "attention: negative sequence stride");
-    if (d.n_seqs > 1 && (d.q_seq_stride == 0 || (!d.block_table && d.kv_seq_stride == 0) || d.out_seq_stride == 0))
+    const bool varlen = (d.flags & ALPACA_ATTN_FLAG_VARLEN) != 0;
+    if (d.n_seqs > 1 && ((!varlen && (d.q_seq_stride == 0 || d.out_seq_stride == 0)) ||
+                         (!d.block_table && d.kv_seq_stride == 0)))
         return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "attention: zero sequence stride with several sequences");
+    if (varlen) {  // ragged prefill: packed queries, per-sequence offsets and start positions on the device
+        if (d.ctx_lens)
+            return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "attention: ctx_lens and the ragged prefill flag together");
+        if (!d.q_offsets || !d.start_positions)
+            return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "attention: ragged prefill needs q_offsets and start_positions");
+        if (d.total_tokens < 1 || d.max_ctx_len < 1)
+            return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT,
+                        "attention: ragged prefill needs total_tokens >= 1 and max_ctx_len >= 1: " + sh);
+        if (d.n_seqs > (1 << 24) || static_cast<int64_t>(d.n_seqs) * ((d.tokens + 255) / 256) > (1 << 26))
+            return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "attention: ragged prefill has too many sequences: " + sh);
+    }
     const int64_t qs = static_cast<int64_t>(dtype_size(d.q_dtype)), ks = dtype_size(d.kv_dtype), os = dtype_size(d.out_dtype);
     if ((d.q_token_stride * qs) % 16 || (d.q_seq_stride * qs) % 16 || (d.kv_row_stride * ks) % 16 ||
         (d.kv_seq_stride * ks) % 16 || (d.out_token_stride * os) % 16 || (d.out_seq_stride * os) % 16)
@@ -136,7 +175,8 @@ alpaca_cuda_status validate(const alpaca_attn_desc* dp) {
     if (!(d.scale >= 0.f) || !std::isfinite(d.scale))
         return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "attention: scale must be finite and >= 0");
     if (d.block_table) {  // paged cache
-        const int64_t rows_needed = d.ctx_lens ? d.max_ctx_len : static_cast<int64_t>(d.start_position) + d.tokens;
+        const int64_t rows_needed =
+            (d.ctx_lens || varlen) ? d.max_ctx_len : static_cast<int64_t>(d.start_position) + d.tokens;
         if (d.block_rows < 128 || d.block_rows % 128 != 0)
             return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "attention: block_rows must be a positive multiple of 128");
         if (d.max_blocks < 1 || d.pool_blocks < 1 ||
@@ -210,6 +250,7 @@ alpaca_cuda_status validate_rope(const alpaca_rope_desc* dp) {
 
 // KernelEncoder.attention's policy (KernelEncoder.swift:309-343).
 alpaca_attn_kernel select_kernel(const alpaca_attn_desc& d) {
+    if (d.flags & ALPACA_ATTN_FLAG_VARLEN) return ALPACA_ATTN_PREFILL_TC;  // the only kernel with the ragged form
     if (d.block_table)  // a paged cache is read by the split decode (any context) and the tensor-core prefill only
         return (d.tokens == 1 && decode_supported(d)) ? ALPACA_ATTN_DECODE_SPLIT : ALPACA_ATTN_PREFILL_TC;
     const int ctx = d.ctx_lens ? d.max_ctx_len : d.start_position + 1;
@@ -227,6 +268,8 @@ size_t workspace_for(const alpaca_attn_desc& d, alpaca_attn_kernel k) {
 }
 
 alpaca_cuda_status check_kind(const alpaca_attn_desc& d, alpaca_attn_kernel k) {
+    if ((d.flags & ALPACA_ATTN_FLAG_VARLEN) && k != ALPACA_ATTN_PREFILL_TC && k != ALPACA_ATTN_AUTO)
+        return fail(ALPACA_CUDA_ERR_UNSUPPORTED, "the ragged prefill form is served by the tensor-core prefill only");
     switch (k) {
         case ALPACA_ATTN_DECODE_SPLIT:
             if (!decode_supported(d))
@@ -246,31 +289,62 @@ alpaca_cuda_status check_kind(const alpaca_attn_desc& d, alpaca_attn_kernel k) {
     }
 }
 
-alpaca_cuda_status run(const alpaca_attn_desc* dp, alpaca_attn_kernel kind, void* ws, size_t ws_bytes,
-                       cudaStream_t stream) {
+float call_scale(const alpaca_attn_desc& d) {
+    return d.scale > 0.f ? d.scale : 1.0f / std::sqrt(static_cast<float>(d.head_dim));
+}
+
+// The host-side checks every attention entry point shares: the descriptor, then the kernel choice
+// (ALPACA_ATTN_AUTO resolved) and its limits.
+alpaca_cuda_status prepare(const alpaca_attn_desc* dp, alpaca_attn_kernel& kind) {
     alpaca_cuda_status st = validate(dp);
     if (st != ALPACA_CUDA_OK) return st;
-    const alpaca_attn_desc& d = *dp;
-    if (kind == ALPACA_ATTN_AUTO) kind = select_kernel(d);
-    st = check_kind(d, kind);
-    if (st != ALPACA_CUDA_OK) return st;
+    if (kind == ALPACA_ATTN_AUTO) kind = select_kernel(*dp);
+    return check_kind(*dp, kind);
+}
+
+// The device set-up every launch shares (SM count, this stream's error word); `who` prefixes the message.
+alpaca_cuda_status device_for(cudaStream_t stream, const char* who, DeviceInfo* di) {
+    const cudaError_t e = device_info(stream, di);
+    if (e != cudaSuccess) return fail(ALPACA_CUDA_ERR_CUDA, std::string(who) + ": device query: " + cudaGetErrorString(e));
+    return ok();
+}
+
+// Caller workspace against what `kind` needs for `d`.
+alpaca_cuda_status check_workspace(const alpaca_attn_desc& d, alpaca_attn_kernel kind, const void* ws, size_t ws_bytes,
+                                   const char* who) {
     const size_t need = workspace_for(d, kind);
     if (need > 0 && (ws_bytes < need || !ws))
-        return fail(ALPACA_CUDA_ERR_WORKSPACE_TOO_SMALL,
-                    "attention: workspace of " + std::to_string(ws_bytes) + " bytes, " + std::to_string(need) + " needed");
-    if (need > 0 && !aligned16(ws)) return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "attention: workspace must be 16-byte aligned");
+        return fail(ALPACA_CUDA_ERR_WORKSPACE_TOO_SMALL, std::string(who) + ": workspace of " + std::to_string(ws_bytes) +
+                                                             " bytes, " + std::to_string(need) + " needed");
+    if (need > 0 && !aligned16(ws))
+        return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, std::string(who) + ": workspace must be 16-byte aligned");
+    return ok();
+}
+
+alpaca_cuda_status launched(cudaError_t e, const char* who) {
+    if (e != cudaSuccess)
+        return fail(ALPACA_CUDA_ERR_LAUNCH_FAILED, std::string(who) + " launch failed: " + cudaGetErrorString(e));
+    return ok();
+}
+
+alpaca_cuda_status run(const alpaca_attn_desc* dp, alpaca_attn_kernel kind, void* ws, size_t ws_bytes,
+                       cudaStream_t stream) {
+    alpaca_cuda_status st = prepare(dp, kind);
+    if (st != ALPACA_CUDA_OK) return st;
+    const alpaca_attn_desc& d = *dp;
+    st = check_workspace(d, kind, ws, ws_bytes, "attention");
+    if (st != ALPACA_CUDA_OK) return st;
     DeviceInfo di;
-    cudaError_t e = device_info(&di);
-    if (e != cudaSuccess) return fail(ALPACA_CUDA_ERR_CUDA, std::string("attention: device query: ") + cudaGetErrorString(e));
-    Call c{&d, d.scale > 0.f ? d.scale : 1.0f / std::sqrt(static_cast<float>(d.head_dim)), di.err, ws, ws_bytes, di.num_sms};
+    st = device_for(stream, "attention", &di);
+    if (st != ALPACA_CUDA_OK) return st;
+    Call c{&d, call_scale(d), di.err, ws, ws_bytes, di.num_sms};
+    cudaError_t e;
     switch (kind) {
         case ALPACA_ATTN_DECODE_SPLIT: e = launch_decode(c, stream); break;
         case ALPACA_ATTN_PREFILL_TC: e = launch_prefill(c, stream); break;
         default: e = launch_general(c, stream); break;
     }
-    if (e != cudaSuccess)
-        return fail(ALPACA_CUDA_ERR_LAUNCH_FAILED, std::string("attention launch failed: ") + cudaGetErrorString(e));
-    return ok();
+    return launched(e, "attention");
 }
 
 }  // namespace
@@ -296,9 +370,9 @@ alpaca_cuda_status alpaca_attn_decode(const alpaca_attn_desc* desc, void* worksp
 }
 
 alpaca_cuda_status alpaca_attn_decode_noalloc(const alpaca_attn_desc* desc, alpaca_stream_t stream) {
-    alpaca_cuda_status st = validate(desc);
-    if (st != ALPACA_CUDA_OK) return st;
-    st = check_kind(*desc, ALPACA_ATTN_DECODE_SPLIT);
+    const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    alpaca_attn_kernel kind = ALPACA_ATTN_DECODE_SPLIT;
+    alpaca_cuda_status st = prepare(desc, kind);
     if (st != ALPACA_CUDA_OK) return st;
     const size_t need = decode_workspace_bytes(*desc);
     if (need > kDecodeBuiltinScratchBytes)
@@ -307,25 +381,21 @@ alpaca_cuda_status alpaca_attn_decode_noalloc(const alpaca_attn_desc* desc, alpa
                         "scratch holds " + std::to_string(kDecodeBuiltinScratchBytes) +
                         " bytes (use alpaca_attn_decode with a workspace)");
     DeviceInfo di;
-    cudaError_t e = device_info(&di);
-    if (e != cudaSuccess) return fail(ALPACA_CUDA_ERR_CUDA, std::string("decode_noalloc: device query: ") + cudaGetErrorString(e));
+    st = device_for(s, "decode_noalloc", &di);
+    if (st != ALPACA_CUDA_OK) return st;
     void* scratch = nullptr;
-    e = decode_builtin_scratch(&scratch);
+    const cudaError_t e = decode_builtin_scratch(&scratch);
     if (e != cudaSuccess)
         return fail(ALPACA_CUDA_ERR_CUDA, std::string("decode_noalloc: scratch address: ") + cudaGetErrorString(e));
-    Call c{desc, desc->scale > 0.f ? desc->scale : 1.0f / std::sqrt(static_cast<float>(desc->head_dim)), di.err, scratch,
-           kDecodeBuiltinScratchBytes, di.num_sms};
-    e = launch_decode(c, reinterpret_cast<cudaStream_t>(stream));
-    if (e != cudaSuccess)
-        return fail(ALPACA_CUDA_ERR_LAUNCH_FAILED, std::string("decode_noalloc launch failed: ") + cudaGetErrorString(e));
-    return ok();
+    Call c{desc, call_scale(*desc), di.err, scratch, kDecodeBuiltinScratchBytes, di.num_sms};
+    return launched(launch_decode(c, s), "decode_noalloc");
 }
 
 alpaca_cuda_status alpaca_attn_decode_rope(const alpaca_attn_desc* attn, const alpaca_rope_desc* rope,
                                            void* workspace, size_t workspace_bytes, alpaca_stream_t stream) {
-    alpaca_cuda_status st = validate(attn);
-    if (st != ALPACA_CUDA_OK) return st;
-    st = check_kind(*attn, ALPACA_ATTN_DECODE_SPLIT);
+    const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    alpaca_attn_kernel kind = ALPACA_ATTN_DECODE_SPLIT;
+    alpaca_cuda_status st = prepare(attn, kind);
     if (st != ALPACA_CUDA_OK) return st;
     st = validate_rope(rope);
     if (st != ALPACA_CUDA_OK) return st;
@@ -347,33 +417,24 @@ alpaca_cuda_status alpaca_attn_decode_rope(const alpaca_attn_desc* attn, const a
     if (r.positions || (!d.ctx_lens && r.start_position != d.start_position))
         return bad("the new token's position is the attention call's (ctx_lens - 1, or start_position): positions "
                    "must be NULL and start_position equal to the attention descriptor's");
-    const size_t need = decode_workspace_bytes(d);
-    if (need > 0 && (workspace_bytes < need || !workspace))
-        return fail(ALPACA_CUDA_ERR_WORKSPACE_TOO_SMALL, "decode_rope: workspace of " + std::to_string(workspace_bytes) +
-                                                             " bytes, " + std::to_string(need) + " needed");
-    if (need > 0 && !aligned16(workspace))
-        return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "decode_rope: workspace must be 16-byte aligned");
+    st = check_workspace(d, kind, workspace, workspace_bytes, "decode_rope");
+    if (st != ALPACA_CUDA_OK) return st;
     DeviceInfo di;
-    cudaError_t e = device_info(&di);
-    if (e != cudaSuccess) return fail(ALPACA_CUDA_ERR_CUDA, std::string("decode_rope: device query: ") + cudaGetErrorString(e));
-    Call c{attn, d.scale > 0.f ? d.scale : 1.0f / std::sqrt(static_cast<float>(d.head_dim)), di.err, workspace,
-           workspace_bytes, di.num_sms};
+    st = device_for(s, "decode_rope", &di);
+    if (st != ALPACA_CUDA_OK) return st;
+    Call c{attn, call_scale(d), di.err, workspace, workspace_bytes, di.num_sms};
     c.rope = rope;
-    e = launch_decode(c, reinterpret_cast<cudaStream_t>(stream));
-    if (e != cudaSuccess) return fail(ALPACA_CUDA_ERR_LAUNCH_FAILED, std::string("decode_rope launch failed: ") + cudaGetErrorString(e));
-    return ok();
+    return launched(launch_decode(c, s), "decode_rope");
 }
 
 alpaca_cuda_status alpaca_rope_kv_append(const alpaca_rope_desc* desc, alpaca_stream_t stream) {
     alpaca_cuda_status st = validate_rope(desc);
     if (st != ALPACA_CUDA_OK) return st;
+    const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     DeviceInfo di;
-    cudaError_t e = device_info(&di);
-    if (e != cudaSuccess) return fail(ALPACA_CUDA_ERR_CUDA, std::string("rope: ") + cudaGetErrorString(e));
-    e = launch_rope_kv(*desc, di.err, reinterpret_cast<cudaStream_t>(stream));
-    if (e != cudaSuccess)
-        return fail(ALPACA_CUDA_ERR_LAUNCH_FAILED, std::string("rope: launch failed: ") + cudaGetErrorString(e));
-    return ok();
+    st = device_for(s, "rope", &di);
+    if (st != ALPACA_CUDA_OK) return st;
+    return launched(launch_rope_kv(*desc, di.err, s), "rope");
 }
 
 alpaca_cuda_status alpaca_attention_workspace_bytes(const alpaca_attn_desc* desc, alpaca_attn_kernel kind,
@@ -397,19 +458,28 @@ alpaca_cuda_status alpaca_attention_select(const alpaca_attn_desc* desc, alpaca_
 }
 
 alpaca_cuda_status alpaca_cuda_device_status(alpaca_stream_t stream, int clear) {
-    cudaError_t e = cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream));
+    const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) return fail(ALPACA_CUDA_ERR_CUDA, std::string("device status: ") + cudaGetErrorString(e));
+    DeviceInfo di;
+    int slot = -1;
+    e = device_info(s, &di, /*assign=*/false, &slot);
+    if (e != cudaSuccess) return fail(ALPACA_CUDA_ERR_CUDA, std::string("device status: ") + cudaGetErrorString(e));
+    if (slot < 0) return ok();  // this stream has made no call on the current device
     unsigned word = 0;
-    e = cudaMemcpyFromSymbol(&word, g_device_error, sizeof(word));
+    const size_t off = sizeof(unsigned) * static_cast<size_t>(slot);
+    e = cudaMemcpyFromSymbol(&word, g_error_slots, sizeof(word), off);
     if (e != cudaSuccess) return fail(ALPACA_CUDA_ERR_CUDA, std::string("device status: ") + cudaGetErrorString(e));
     if (clear && word) {
         const unsigned zero = 0;
-        e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero));
+        e = cudaMemcpyToSymbol(g_error_slots, &zero, sizeof(zero), off);
         if (e != cudaSuccess) return fail(ALPACA_CUDA_ERR_CUDA, std::string("device status: ") + cudaGetErrorString(e));
     }
     if (word & kDevErrTimeout) return fail(ALPACA_CUDA_ERR_DEVICE_TIMEOUT, "a bounded device-side wait gave up");
     if (word & kDevErrBadIndex)
-        return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "a block table entry lay outside the KV pool (rows read as zero)");
+        return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT,
+                    "a device-side contract check failed: a block table entry outside the KV pool (rows read as zero), "
+                    "a context length outside [1, max_ctx_len], or a position outside the cache");
     if (word) return fail(ALPACA_CUDA_ERR_CUDA, "device error word " + std::to_string(word));
     return ok();
 }

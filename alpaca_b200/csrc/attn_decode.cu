@@ -705,12 +705,14 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(const D
     const int G = a.n_heads / a.n_kv_heads;
     // The context lengths are read before the wait for the split kernel: that kernel does not write them, and this
     // grid launches only once every split CTA has passed its own griddepcontrol.wait, so whatever wrote them
-    // before the split kernel is complete and visible. The length read then overlaps the split grid's drain, and
-    // single-split units leave without waiting.
+    // before the split kernel is complete and visible. The length read then overlaps the split grid's drain.
     const int L = ctx_len_of(a, seq);
     const int nsp = (L + Geo<D>::SL - 1) / Geo<D>::SL;
-    if (nsp <= 1) return;
+    // Every CTA waits for the split grid, single-split units included (they only return afterwards): this grid then
+    // completes after the split kernel, so a later launch on the stream that reads `out` sees the split kernel's
+    // writes even when no CTA has records to combine.
     asm volatile("griddepcontrol.wait;" ::: "memory");  // split kernel's writes are visible after this
+    if (nsp <= 1) return;
     // The next stream-ordered kernel may launch now (it waits for this grid to finish before touching memory).
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int rec = G * (D + 2);                 // floats per split

@@ -106,6 +106,10 @@ struct PrefillArgs {
     unsigned flags;
     const int* block_table;  // paged cache: [seq][max_blocks] (null: contiguous caches)
     int block_rows, max_blocks, pool_blocks, last_block;  // last_block: block (of a sequence) holding row kv_len - 1
+    // Ragged form: the work list the plan kernel wrote into the workspace. plan[0].x = units; unit u is
+    // plan[1 + 2u] = {sequence, packed row of its first query, absolute position of that query, query rows} and
+    // plan[2 + 2u].x = the sequence's context end (start + tokens). Units are ordered heaviest first.
+    const int4* plan;
 };
 
 template <int D, int NT = 2>
@@ -119,6 +123,7 @@ struct SmemLayout {
     __half v[kStages][PG<D, NT>::BN * D];
     uint64_t q_full[NT], q_empty[NT];
     uint64_t k_full[kStages], k_empty[kStages], v_full[kStages], v_empty[kStages];
+    uint64_t v_ready[kStages];  // ragged form: V rows past the sequence's context zeroed (warp 3), P·V may read
     uint64_t s_full[NT], s_empty[NT], p_full[NT], o_done[NT];
     uint64_t xbar[2][4];       // per (tile, lane quarter): the two half-row warps exchange partial row state
     uint64_t dbg, fin[NT], retire;
@@ -136,8 +141,15 @@ constexpr size_t smem_bytes() { return sizeof(SmemLayout<D, NT>) + 1024; }  // +
 static_assert(smem_bytes<64>() <= 232448 && smem_bytes<128>() <= 232448 && smem_bytes<64, 3>() <= 232448,
               "shared memory exceeds 227 KB per CTA");
 
+// One work item: NT query tiles of 128 rows of one (sequence, head). First NT entries of the arrays used.
 struct Item {
-    int seq, head, row0[3], nblk[3];  // first NT entries used
+    int seq, head;  // sequence (cache / block-table index) and query head
+    int cseq;       // sequence coordinate of the Q and output tensor maps (0 in the packed ragged layout)
+    int row0[3];    // Q / output map row of each tile's first query
+    int pos0[3];    // absolute position of each tile's first query
+    int nrows[3];   // query rows of each tile that exist (ragged form; the uniform form clips through the maps)
+    int nblk[3];    // KV blocks each tile attends to
+    int ctx_end;    // ragged form: the sequence's context end; rows at or past it are never used
 };
 
 template <int BN>
@@ -148,17 +160,38 @@ __device__ __forceinline__ int tile_blocks(const PrefillArgs& a, int row0) {
     return (visible + BN - 1) / BN;
 }
 
-template <int BN, int NT>
+template <int BN, int NT, bool VL>
 __device__ __forceinline__ Item decode_item(const PrefillArgs& a, int it) {
+    Item x;
+    if constexpr (VL) {
+        // unit-major, head-minor: consecutive items share the unit's queries and (within a KV head) its K/V
+        const int unit = it / a.n_heads;
+        x.head = it - unit * a.n_heads;
+        const int4 r = __ldg(a.plan + 1 + 2 * unit);
+        x.seq = r.x;
+        x.cseq = 0;
+        x.ctx_end = __ldg(a.plan + 2 + 2 * unit).x;
+#pragma unroll
+        for (int t = 0; t < NT; t++) {
+            x.row0[t] = r.y + t * kBM;
+            x.pos0[t] = r.z + t * kBM;
+            x.nrows[t] = max(0, min(kBM, r.w - t * kBM));
+            x.nblk[t] = x.nrows[t] > 0 ? (x.pos0[t] + x.nrows[t] + BN - 1) / BN : 0;
+        }
+        return x;
+    }
     const int per_rank = a.n_seqs * a.n_heads;
     const int rank = it / per_rank, rem = it - rank * per_rank;
-    Item x;
     const int group = a.n_groups - 1 - rank;  // heaviest groups first
     x.seq = rem / a.n_heads;
     x.head = rem - x.seq * a.n_heads;
+    x.cseq = x.seq;
+    x.ctx_end = a.kv_len;
 #pragma unroll
     for (int t = 0; t < NT; t++) {
         x.row0[t] = (group * NT + t) * kBM;
+        x.pos0[t] = a.start + x.row0[t];
+        x.nrows[t] = kBM;
         x.nblk[t] = tile_blocks<BN>(a, x.row0[t]);
     }
     return x;
@@ -207,7 +240,7 @@ __device__ __forceinline__ void mma_pv(const SmemLayout<D, NT>* sm, int tile, in
 
 // ---------------------------------------------------------------------------------------------- kernel
 
-template <int D, int kEmuPairs, int R, int NT>
+template <int D, int kEmuPairs, int R, int NT, bool VL = false>
 __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_kt,
@@ -254,6 +287,7 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
             mbar_init(&sm->k_empty[i], NT);  // released by every tile's MMA issuer
             mbar_init(&sm->v_full[i], 1);
             mbar_init(&sm->v_empty[i], NT);
+            mbar_init(&sm->v_ready[i], 1);
         }
         mbar_init(&sm->dbg, 1);
         mbar_init(&sm->retire, 4 * R * NT + 2);  // the softmax warps, the producer and tile 0's issuer
@@ -278,14 +312,16 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
     // kernel on the stream drains; no global memory is touched before its writes are complete and visible.
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const uint32_t tmem_base = sm->tmem_base;
+    // Work items: fixed by the call's shape, or (ragged form) units of the plan the previous launch wrote x heads.
+    const int total_items = VL ? __ldg(&a.plan[0].x) * a.n_heads : a.total_items;
     if (warp == 0) {
         if constexpr (R == 2 || NT == 3) setmaxnreg_dec<kRegsControl>();
         if (lane != 0) return;
         // ------------------------------------------------------------------ TMA producer
         uint32_t kv_it = 0, k_issued = 0, v_issued = 0, q_uses[NT] = {};
         bool ok = true;
-        for (int r = 0, it = item_of(0); ok && it < a.total_items; it = item_of(++r)) {
-            const Item x = decode_item<kBN, NT>(a, it);
+        for (int r = 0, it = item_of(0); ok && it < total_items; it = item_of(++r)) {
+            const Item x = decode_item<kBN, NT, VL>(a, it);
             const int kvh = x.head / (a.n_heads / a.n_kv_heads);
             for (int t = 0; t < NT && ok; t++) {
                 if (x.nblk[t] == 0) continue;
@@ -294,7 +330,7 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
                 mbar_arrive_expect_tx(&sm->q_full[t], G::kQBytes);
 #pragma unroll
                 for (int cb = 0; cb < G::CB; cb++)
-                    tma_load_4d(sm->q[t] + cb * kBM * 64, &tm_q, 64 * cb, x.head, x.row0[t], x.seq, &sm->q_full[t]);
+                    tma_load_4d(sm->q[t] + cb * kBM * 64, &tm_q, 64 * cb, x.head, x.row0[t], x.cseq, &sm->q_full[t]);
                 q_uses[t]++;
             }
             const int nmax = item_blocks<NT>(x);
@@ -359,8 +395,8 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
             uint32_t kv_it = 0, q_uses = 0, s_uses = 0, p_uses = 0;
             bool ok = true;
             if (debug_timeout && t == 0) ok = mbar_wait(&sm->dbg, 0, ab);  // nothing arrives: exercises the give-up path
-            for (int r = 0, it = item_of(0); ok && it < a.total_items; it = item_of(++r)) {
-                const Item x = decode_item<kBN, NT>(a, it);
+            for (int r = 0, it = item_of(0); ok && it < total_items; it = item_of(++r)) {
+                const Item x = decode_item<kBN, NT, VL>(a, it);
                 const int n = x.nblk[t];
                 const int nmax = item_blocks<NT>(x);
                 if (n > 0) {
@@ -392,7 +428,8 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
                         const int b = j - 1;
                         const uint32_t prv = kv_it + b;
                         const int sp = prv % kStages;
-                        ok = mbar_wait(&sm->v_full[sp], (prv / kStages) & 1, ab);
+                        // ragged form: warp 3 has zeroed the V rows past the context (and is done with the stage)
+                        ok = mbar_wait(VL ? &sm->v_ready[sp] : &sm->v_full[sp], (prv / kStages) & 1, ab);
                         if (!ok) break;
                         if (b < n) {
                             ok = mbar_wait(&sm->p_full[t], p_uses & 1, ab);
@@ -429,6 +466,35 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
         }
     } else if (warp == 3) {
         if constexpr (R == 2 || NT == 3) setmaxnreg_dec<kRegsControl>();
+        if constexpr (VL) {
+            // ------------------------------------------------------------------ ragged form: V tail fix-up
+            // A sequence's cache rows at or past its context end (start + tokens) may hold anything, and the
+            // tensor maps only bound the rows at max_ctx_len. P is 0 in those columns for every query that exists,
+            // but 0 x NaN is NaN in the P·V MMA, so the warp zeroes those rows of each landed V block before
+            // releasing it to the MMA issuers (v_ready); K needs nothing (the causal mask replaces those scores).
+            uint32_t kv_it = 0;
+            bool ok = true;
+            for (int r = 0, it = item_of(0); ok && it < total_items; it = item_of(++r)) {
+                const Item x = decode_item<kBN, NT, VL>(a, it);
+                const int nmax = item_blocks<NT>(x);
+                for (int j = 0; j < nmax; j++, kv_it++) {
+                    const int st = kv_it % kStages;
+                    ok = __all_sync(0xffffffffu, mbar_wait(&sm->v_full[st], (kv_it / kStages) & 1, ab));
+                    if (!ok) break;
+                    const int keep = max(0, x.ctx_end - j * kBN);  // rows of this block inside the context
+                    if (keep < kBN) {
+#pragma unroll
+                        for (int cb = 0; cb < G::CB; cb++) {
+                            uint4* blk = reinterpret_cast<uint4*>(sm->v[st] + cb * kBN * 64);  // 8 x 16 B per row
+                            for (int i = keep * 8 + lane; i < kBN * 8; i += 32) blk[i] = make_uint4(0u, 0u, 0u, 0u);
+                        }
+                        fence_proxy_async_smem();  // the zeros are visible to the tensor core's reads
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&sm->v_ready[st]);
+                }
+            }
+        }
     } else if constexpr (R == 1) {
         if constexpr (NT == 3) setmaxnreg_inc<kRegsSoftmax3>();
         // ------------------------------------------------------------------ softmax warps, one thread per row
@@ -444,12 +510,12 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
         uint32_t s_uses = 0, o_uses = 0, ep_uses = 0;
         const bool issuer = kTmaOut && ((warp - 4) & 3) == 0 && lane == 0;  // the tile's output TMA thread
         bool ok = true;
-        for (int r = 0, it = item_of(0); ok && it < a.total_items; it = item_of(++r)) {
-            const Item x = decode_item<kBN, NT>(a, it);
+        for (int r = 0, it = item_of(0); ok && it < total_items; it = item_of(++r)) {
+            const Item x = decode_item<kBN, NT, VL>(a, it);
             const int nb = x.nblk[tile];
             if (nb == 0) continue;
             const int row0 = x.row0[tile];
-            const int qpos = a.start + row0 + row;  // absolute position of this thread's query
+            const int qpos = x.pos0[tile] + row;  // absolute position of this thread's query
             float m_used = -INFINITY;
             float2 lsum = make_float2(0.f, 0.f);
             for (int j = 0; j < nb; j++) {
@@ -466,7 +532,7 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
                 if (lane == 0) mbar_arrive(&sm->s_empty[tile]);
 
                 const int kv0 = j * kBN;
-                if (kv0 + kBN - 1 > a.start + row0) {  // the block reaches past the tile's first query: mask
+                if (kv0 + kBN - 1 > x.pos0[tile]) {  // the block reaches past the tile's first query: mask
 #pragma unroll
                     for (int c = 0; c < kBN; c++)
                         if (kv0 + c > qpos) s[c] = -INFINITY;
@@ -540,8 +606,10 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
             o_uses++;
             tc_fence_after();
             const float inv = 1.f / (lsum.x + lsum.y);
-            const int t = row0 + row;
-            if constexpr (kTmaOut) {
+            // whole tiles leave through the staging box and TMA stores; in the ragged form a sequence's last,
+            // partial tile is stored row by row (its map rows past the tile belong to the next sequence)
+            const bool tma_tile = kTmaOut && (!VL || x.nrows[tile] == kBM);
+            if (tma_tile) {
                 // Two rounds of 64 columns through the tile's staging boxes and one thread's TMA stores, with the
                 // same o_free / o_staged hand-offs as the two-thread form.
                 float* stage = sm->o_stage + tile * (kBM * 64);
@@ -590,10 +658,10 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
                         sent = mbar_wait(&sm->o_staged[tile], ep_uses & 1, ab);
                         if (sent) {
                             if (a.out_f16) {
-                                tma_store_4d(&tm_o, stage, r64 * 64, x.head, row0, x.seq);
+                                tma_store_4d(&tm_o, stage, r64 * 64, x.head, row0, x.cseq);
                             } else {
-                                tma_store_4d(&tm_o, stage, r64 * 64, x.head, row0, x.seq);
-                                tma_store_4d(&tm_o, stage + kBM * 32, r64 * 64 + 32, x.head, row0, x.seq);
+                                tma_store_4d(&tm_o, stage, r64 * 64, x.head, row0, x.cseq);
+                                tma_store_4d(&tm_o, stage + kBM * 32, r64 * 64 + 32, x.head, row0, x.cseq);
                             }
                             bulk_commit();
                         }
@@ -606,14 +674,16 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
                 tc_fence_before();
                 continue;
             }
-            const int64_t off = x.seq * a.out_seq_stride + static_cast<int64_t>(t) * a.out_token_stride +
+            const int t = row0 + row;  // row of the output map
+            const bool have = VL ? row < x.nrows[tile] : t < a.tokens;
+            const int64_t off = x.cseq * a.out_seq_stride + static_cast<int64_t>(t) * a.out_token_stride +
                                 static_cast<int64_t>(x.head) * D;
 #pragma unroll
             for (int c0 = 0; c0 < D; c0 += 32) {
                 float o[32];
                 tmem_ld32(o_addr + c0, o);
                 tmem_wait_ld();
-                if (t < a.tokens) {
+                if (have) {
                     if (a.out_f16) {
                         uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(a.out) + off + c0);
 #pragma unroll
@@ -652,12 +722,12 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
         uint32_t s_uses = 0, o_uses = 0, x_uses = 0, ep_uses = 0;
         const bool issuer = kTmaOut && ((warp - 4) & 7) == 0 && lane == 0;  // the tile's output TMA thread
         bool ok = true;
-        for (int r = 0, it = item_of(0); ok && it < a.total_items; it = item_of(++r)) {
-            const Item x = decode_item<kBN, NT>(a, it);
+        for (int r = 0, it = item_of(0); ok && it < total_items; it = item_of(++r)) {
+            const Item x = decode_item<kBN, NT, VL>(a, it);
             const int nb = x.nblk[tile];
             if (nb == 0) continue;
             const int row0 = x.row0[tile];
-            const int qpos = a.start + row0 + row;  // absolute position of this thread's query
+            const int qpos = x.pos0[tile] + row;  // absolute position of this thread's query
             float m_used = -INFINITY;
             float2 lsum = make_float2(0.f, 0.f);    // this thread's half of the row sum (two lanes of a pair)
             for (int j = 0; j < nb; j++) {
@@ -674,7 +744,7 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
                 if (lane == 0) mbar_arrive(&sm->s_empty[tile]);
 
                 const int kv0 = j * kBN + half * SC;
-                if (kv0 + SC - 1 > a.start + row0) {  // these columns reach past the tile's first query: mask
+                if (kv0 + SC - 1 > x.pos0[tile]) {  // these columns reach past the tile's first query: mask
 #pragma unroll
                     for (int c = 0; c < SC; c++)
                         if (kv0 + c > qpos) s[c] = -INFINITY;
@@ -794,8 +864,11 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
             if (!ok) break;
             x_uses++;
             const float l = lpart + sm->xl[tile][half ^ 1][row];
-            const int t = row0 + row;
-            if constexpr (kTmaOut) {
+            const int t = row0 + row;  // row of the output map
+            // whole tiles leave through the staging box and TMA stores; in the ragged form a sequence's last,
+            // partial tile is stored row by row (its map rows past the tile belong to the next sequence)
+            const bool tma_tile = kTmaOut && (!VL || x.nrows[tile] == kBM);
+            if (tma_tile) {
                 // The rows go through the tile's staging box and one thread's TMA stores (rows past the tokens are
                 // clipped by the tensor map). Hand-offs on mbarriers with bounded waits: o_free (the previous
                 // store has read the box) and o_staged (all 8 warps have written their rows).
@@ -836,10 +909,10 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
                     sent = mbar_wait(&sm->o_staged[tile], ep_uses & 1, ab);
                     if (sent) {
                         if (a.out_f16) {
-                            tma_store_4d(&tm_o, stage, 0, x.head, row0, x.seq);
+                            tma_store_4d(&tm_o, stage, 0, x.head, row0, x.cseq);
                         } else {
-                            tma_store_4d(&tm_o, stage, 0, x.head, row0, x.seq);
-                            tma_store_4d(&tm_o, stage + kBM * 32, 32, x.head, row0, x.seq);
+                            tma_store_4d(&tm_o, stage, 0, x.head, row0, x.cseq);
+                            tma_store_4d(&tm_o, stage + kBM * 32, 32, x.head, row0, x.cseq);
                         }
                         bulk_commit();
                     }
@@ -847,9 +920,9 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
                 ok = __all_sync(0xffffffffu, sent);
                 if (!ok) break;
                 ep_uses++;
-            } else if (t < a.tokens) {
+            } else if (VL ? row < x.nrows[tile] : t < a.tokens) {
                 const float inv = 1.f / l;
-                const int64_t off = x.seq * a.out_seq_stride + static_cast<int64_t>(t) * a.out_token_stride +
+                const int64_t off = x.cseq * a.out_seq_stride + static_cast<int64_t>(t) * a.out_token_stride +
                                     static_cast<int64_t>(x.head) * D + half * OC;
                 if (a.out_f16) {
                     uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(a.out) + off);
@@ -884,6 +957,98 @@ __global__ void q_to_half_kernel(const float* __restrict__ q, int64_t token_stri
         const int64_t c = i % hd_total, r = i / hd_total;
         const int64_t t = r % tokens, sq = r / tokens;
         dst[i] = __float2half_rn(q[sq * seq_stride + t * token_stride + c]);
+    }
+}
+
+// ---------------------------------------------------------------------------------------------- ragged plan
+
+// Work list of a ragged call. A unit is one group of kUnitTiles query tiles of one sequence (all heads: the prefill
+// kernel takes unit-major, head-minor items). One CTA counts the units per cost (KV blocks the unit's last query
+// attends to), turns the counts into write positions in descending cost order, and writes every unit's record at
+// its position, so the persistent kernel deals the heaviest units first across every sequence of the call.
+constexpr int kPlanThreads = 1024;
+constexpr int kPlanBuckets = 2 * kPlanThreads;  // costs above kPlanBuckets - 1 blocks share the first bucket
+constexpr int kUnitTiles = 2;                   // query tiles per unit (the two-tile forms)
+
+struct PlanArgs {
+    const int* q_offsets;
+    const int* start_positions;
+    int4* plan;
+    int n_seqs, max_tokens, max_ctx, total_tokens, bn;
+    unsigned* err;
+};
+
+// Sequence s's packed offset, query count and start position. False for an empty sequence and for one that breaks
+// the call's bounds (reported through the error word; its queries are not computed).
+__device__ __forceinline__ bool plan_span(const PlanArgs& p, int s, int& off, int& len, int& start) {
+    off = p.q_offsets[s];
+    const int end = p.q_offsets[s + 1];
+    start = p.start_positions[s];
+    len = end - off;
+    const bool in_range = off >= 0 && end >= off && end <= p.total_tokens;
+    if (in_range && len == 0) return false;
+    if (!in_range || len > p.max_tokens || start < 0 || static_cast<int64_t>(start) + len > p.max_ctx) {
+        atomicOr(p.err, kDevErrBadIndex);
+        return false;
+    }
+    return true;
+}
+
+__device__ __forceinline__ int plan_bucket(const PlanArgs& p, int start, int len, int g) {
+    const int last = min(len, (g + 1) * kUnitTiles * kBM);  // exclusive: the unit's last query row + 1
+    const int cost = (start + last + p.bn - 1) / p.bn;
+    return kPlanBuckets - 1 - min(cost, kPlanBuckets - 1);  // heaviest first
+}
+
+__global__ void __launch_bounds__(kPlanThreads) prefill_plan_kernel(const PlanArgs p) {
+    __shared__ int cnt[kPlanBuckets];  // units per bucket, then the buckets' write cursors
+    __shared__ int warp_tot[kPlanThreads / 32];
+    // The prefill kernel may launch now; it waits for this grid's memory before reading the plan.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    for (int i = tid; i < kPlanBuckets; i += kPlanThreads) cnt[i] = 0;
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // the offsets may come from the previous kernel
+    __syncthreads();
+    for (int s = tid; s < p.n_seqs; s += kPlanThreads) {
+        int off, len, start;
+        if (!plan_span(p, s, off, len, start)) continue;
+        for (int g = 0; g * kUnitTiles * kBM < len; g++) atomicAdd(&cnt[plan_bucket(p, start, len, g)], 1);
+    }
+    __syncthreads();
+    // exclusive prefix sum of the counts: thread i owns buckets 2i and 2i + 1
+    const int c0 = cnt[2 * tid], c1 = cnt[2 * tid + 1];
+    int incl = c0 + c1;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += n;
+    }
+    if (lane == 31) warp_tot[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        int w = warp_tot[lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int n = __shfl_up_sync(0xffffffffu, w, o);
+            if (lane >= o) w += n;
+        }
+        warp_tot[lane] = w;  // inclusive over warps
+    }
+    __syncthreads();
+    const int before = (warp > 0 ? warp_tot[warp - 1] : 0) + incl - c0 - c1;
+    cnt[2 * tid] = before;
+    cnt[2 * tid + 1] = before + c0;
+    if (tid == kPlanThreads - 1) p.plan[0] = make_int4(before + c0 + c1, 0, 0, 0);
+    __syncthreads();
+    for (int s = tid; s < p.n_seqs; s += kPlanThreads) {
+        int off, len, start;
+        if (!plan_span(p, s, off, len, start)) continue;
+        for (int g = 0; g * kUnitTiles * kBM < len; g++) {
+            const int u = atomicAdd(&cnt[plan_bucket(p, start, len, g)], 1);
+            const int r0 = g * kUnitTiles * kBM;
+            p.plan[1 + 2 * u] = make_int4(s, off + r0, start + r0, min(kUnitTiles * kBM, len - r0));
+            p.plan[2 + 2 * u] = make_int4(start + len, 0, 0, 0);
+        }
     }
 }
 
@@ -1020,18 +1185,37 @@ bool prefill_supported(const alpaca_attn_desc& d) {
            d.ctx_lens == nullptr;
 }
 
-size_t prefill_workspace_bytes(const alpaca_attn_desc& d) {
+namespace {
+bool is_varlen(const alpaca_attn_desc& d) { return (d.flags & ALPACA_ATTN_FLAG_VARLEN) != 0; }
+
+// Bytes of f16 queries staged for an f32-Q call, rounded up to 16 so the ragged work list after them is aligned.
+size_t q_stage_bytes(const alpaca_attn_desc& d) {
     if (d.q_dtype != ALPACA_F32) return 0;
-    return sizeof(__half) * static_cast<size_t>(d.n_seqs) * d.tokens * d.n_heads * d.head_dim;
+    const size_t rows = is_varlen(d) ? static_cast<size_t>(d.total_tokens) : static_cast<size_t>(d.n_seqs) * d.tokens;
+    return (sizeof(__half) * rows * d.n_heads * d.head_dim + 15) / 16 * 16;
+}
+
+// Units of a ragged call at most: every sequence's token bound split into groups of kUnitTiles tiles.
+size_t plan_units(const alpaca_attn_desc& d) {
+    const int group = kUnitTiles * kBM;
+    return static_cast<size_t>(d.n_seqs) * ((d.tokens + group - 1) / group);
+}
+}  // namespace
+
+size_t prefill_workspace_bytes(const alpaca_attn_desc& d) {
+    return q_stage_bytes(d) + (is_varlen(d) ? sizeof(int4) * (1 + 2 * plan_units(d)) : 0);
 }
 
 cudaError_t launch_prefill(const Call& c, cudaStream_t s) {
     const alpaca_attn_desc& d = *c.d;
     const bool d128 = d.head_dim == 128;
-    const int tiles = prefill_tiles(d.head_dim);
-    const int rows = (d128 || tiles == 3) ? 1 : prefill_row_threads(d.head_dim);
-    const int emu = prefill_emu_pairs(tiles);
-    const PrefillFn fn = d128 ? prefill_variant<128>(emu, rows, tiles) : prefill_variant<64>(emu, rows, tiles);
+    const bool vl = is_varlen(d);
+    // The ragged form is built in the default two-tile forms only (the switches select among the uniform forms).
+    const int tiles = vl ? kUnitTiles : prefill_tiles(d.head_dim);
+    const int rows = (d128 || tiles == 3) ? 1 : (vl ? 2 : prefill_row_threads(d.head_dim));
+    const int emu = vl ? 0 : prefill_emu_pairs(tiles);
+    const PrefillFn fn = vl ? (d128 ? prefill_kernel<128, 0, 1, 2, true> : prefill_kernel<64, 0, 2, 2, true>)
+                            : (d128 ? prefill_variant<128>(emu, rows, tiles) : prefill_variant<64>(emu, rows, tiles));
     const size_t smem = d128 ? smem_bytes<128>() : (tiles == 3 ? smem_bytes<64, 3>() : smem_bytes<64>());
     const int bn = d128 ? PG<128>::BN : (tiles == 3 ? PG<64, 3>::BN : PG<64>::BN);
     // per-device function attribute (host-side, cheap next to the launch itself)
@@ -1039,26 +1223,52 @@ cudaError_t launch_prefill(const Call& c, cudaStream_t s) {
                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (attr_err != cudaSuccess) return attr_err;
 
+    // Queries (and outputs) as maps over [seqs][tokens]; the packed ragged layout is one sequence of total_tokens.
+    const int q_seqs = vl ? 1 : d.n_seqs, q_rows = vl ? d.total_tokens : d.tokens;
     const void* qh = d.q;
-    int64_t q_ts = d.q_token_stride, q_ss = d.q_seq_stride;
+    int64_t q_ts = d.q_token_stride, q_ss = vl ? 0 : d.q_seq_stride;
     if (d.q_dtype == ALPACA_F32) {
         __half* dst = static_cast<__half*>(c.ws);
         const int hd_total = d.n_heads * d.head_dim;
-        const int64_t n = static_cast<int64_t>(d.n_seqs) * d.tokens * hd_total;
+        const int64_t n = static_cast<int64_t>(q_seqs) * q_rows * hd_total;
         const int blocks = static_cast<int>(std::min<int64_t>((n + 255) / 256, 4096));
-        q_to_half_kernel<<<blocks, 256, 0, s>>>(static_cast<const float*>(d.q), d.q_token_stride, d.q_seq_stride,
-                                                dst, d.n_seqs, d.tokens, hd_total);
+        q_to_half_kernel<<<blocks, 256, 0, s>>>(static_cast<const float*>(d.q), d.q_token_stride, q_ss, dst, q_seqs,
+                                                q_rows, hd_total);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
         qh = dst;
         q_ts = hd_total;
-        q_ss = static_cast<int64_t>(d.tokens) * hd_total;
+        q_ss = static_cast<int64_t>(q_rows) * hd_total;
     }
-    const int kv_len = d.start_position + d.tokens;
+    int4* plan = nullptr;
+    if (vl) {
+        plan = reinterpret_cast<int4*>(static_cast<uint8_t*>(c.ws) + q_stage_bytes(d));
+        PlanArgs pa{d.q_offsets, d.start_positions, plan, d.n_seqs, d.tokens, d.max_ctx_len, d.total_tokens, bn, c.err};
+        cudaLaunchConfig_t pcfg = {};
+        pcfg.gridDim = dim3(1, 1, 1);
+        pcfg.blockDim = dim3(kPlanThreads, 1, 1);
+        pcfg.stream = s;
+        cudaLaunchAttribute pattr[1];
+        pattr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        pattr[0].val.programmaticStreamSerializationAllowed = 1;
+        pcfg.attrs = pattr;
+        pcfg.numAttrs = pdl_enabled() ? 1 : 0;
+        const cudaError_t e = cudaLaunchKernelEx(&pcfg, prefill_plan_kernel, pa);
+        if (e != cudaSuccess) return e;
+    }
+    // KV rows each sequence's map covers: the uniform call's visible rows, or the ragged call's bound.
+    const int kv_len = vl ? d.max_ctx_len : d.start_position + d.tokens;
     CUtensorMap tq, tk, tv, tkt, tvt;
-    if (!make_map(&tq, qh, d.head_dim, d.n_heads, d.tokens, d.n_seqs, q_ts, q_ss, kBM)) return cudaErrorInvalidValue;
+    if (!make_map(&tq, qh, d.head_dim, d.n_heads, q_rows, q_seqs, q_ts, q_ss, kBM)) return cudaErrorInvalidValue;
     int last_block = -1;
-    if (d.block_table) {
+    if (d.block_table && vl) {
+        // pool maps only: warp 3 zeroes the V rows past each sequence's context in its last block
+        if (!make_map(&tk, d.k, d.head_dim, d.n_kv_heads, d.block_rows, d.pool_blocks, d.kv_row_stride, d.block_stride, bn) ||
+            !make_map(&tv, d.v, d.head_dim, d.n_kv_heads, d.block_rows, d.pool_blocks, d.kv_row_stride, d.block_stride, bn))
+            return cudaErrorInvalidValue;
+        tkt = tk;
+        tvt = tv;
+    } else if (d.block_table) {
         // pool maps: [pool_blocks][block_rows] rows; tail maps end at the last visible row of its block
         last_block = (kv_len - 1) / d.block_rows;
         const int tail_rows = kv_len - last_block * d.block_rows;
@@ -1077,8 +1287,8 @@ cudaError_t launch_prefill(const Call& c, cudaStream_t s) {
 
     CUtensorMap to = tq;  // unused by the forms that store the output directly
     if ((d128 || rows != 1 || tiles == 3) &&
-        !make_out_map(&to, d.out, d.out_dtype == ALPACA_F16, d.head_dim, d.n_heads, d.tokens, d.n_seqs,
-                      d.out_token_stride, d.out_seq_stride))
+        !make_out_map(&to, d.out, d.out_dtype == ALPACA_F16, d.head_dim, d.n_heads, q_rows, q_seqs,
+                      d.out_token_stride, vl ? 0 : d.out_seq_stride))
         return cudaErrorInvalidValue;
 
     PrefillArgs a;
@@ -1093,7 +1303,8 @@ cudaError_t launch_prefill(const Call& c, cudaStream_t s) {
     a.start = d.start_position;
     a.kv_len = kv_len;
     a.n_groups = (d.tokens + tiles * kBM - 1) / (tiles * kBM);
-    a.total_items = a.n_groups * d.n_seqs * d.n_heads;
+    // ragged form: the plan's unit count, read by the kernel; the grid is sized for the bound
+    a.total_items = vl ? static_cast<int>(plan_units(d)) * d.n_heads : a.n_groups * d.n_seqs * d.n_heads;
     a.scale_log2 = c.scale * kLog2e;
     a.err = c.err;
     a.flags = d.flags;
@@ -1102,6 +1313,7 @@ cudaError_t launch_prefill(const Call& c, cudaStream_t s) {
     a.max_blocks = d.max_blocks;
     a.pool_blocks = d.pool_blocks;
     a.last_block = last_block;
+    a.plan = plan;
     const int grid = std::max(1, std::min(a.total_items, c.num_sms));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid, 1, 1);

@@ -43,7 +43,7 @@
 extern "C" {
 #endif
 
-#define ALPACA_CUDA_VERSION 10000 /* 1.0.0 */
+#define ALPACA_CUDA_VERSION 10100 /* 1.1.0 */
 
 /* Same object as cudaStream_t; NULL is the legacy default stream. */
 typedef struct CUstream_st* alpaca_stream_t;
@@ -77,6 +77,10 @@ typedef enum alpaca_attn_kernel {
 
 /* Descriptor flags. */
 #define ALPACA_ATTN_FLAG_NONE 0u
+/* Ragged (varlen) prefill: the call's sequences have their own query counts and start positions, given by the
+ * q_offsets / start_positions / total_tokens fields below (read only with this flag). Served by the tensor-core
+ * prefill (ALPACA_ATTN_PREFILL_TC, or AUTO). */
+#define ALPACA_ATTN_FLAG_VARLEN (1u << 0)
 /* Fault-injection hook for tests: the tensor-core prefill kernel waits on a barrier nothing arrives at, with a
  * ~2 ms limit, so its bounded-wait give-up path runs. The call still returns OK (it only enqueues);
  * alpaca_cuda_device_status then reports ALPACA_CUDA_ERR_DEVICE_TIMEOUT. The output is unspecified. */
@@ -120,6 +124,22 @@ typedef struct alpaca_attn_desc {
     int64_t block_stride;       /* elements between blocks of the pool */
     int32_t pool_blocks;        /* blocks in each pool (bounds of the TMA maps) */
     int32_t reserved1;
+    /* Ragged prefill (flags & ALPACA_ATTN_FLAG_VARLEN; ignored otherwise): several sequences' query chunks in one
+     * call, as a serving loop prefills the 512-token chunks of several sessions at their own positions
+     * (MetalLlamaModel.swift:293-298 runs one session's chunk per call at a moving startPosition). q and out are
+     * packed: sequence s owns token rows q_offsets[s] .. q_offsets[s+1]-1 of them (q_token_stride /
+     * out_token_stride apart; q_seq_stride, out_seq_stride and start_position are ignored), and its query token t
+     * sits at absolute position start_positions[s] + t of its own cache (kv_seq_stride apart, or through
+     * block_table), whose first start_positions[s] + t + 1 rows it attends to. A sequence with no tokens is
+     * skipped. Host-side bounds: `tokens` >= every sequence's token count (it sizes the workspace), max_ctx_len >=
+     * every start_positions[s] + token count (each contiguous cache must hold max_ctx_len rows; a block table must
+     * cover them), total_tokens = the rows of q and out. Rows of a cache past its sequence's context are never
+     * used. Device arrays that break these bounds are reported by alpaca_cuda_device_status (INVALID_ARGUMENT) and
+     * that sequence's output is not written. */
+    const int32_t* q_offsets;       /* DEVICE [n_seqs + 1], non-decreasing, from >= 0 to <= total_tokens */
+    const int32_t* start_positions; /* DEVICE [n_seqs], >= 0 */
+    int32_t total_tokens;           /* rows of the packed q and out */
+    int32_t reserved2;
 } alpaca_attn_desc;
 
 /* Enqueue attention described by `desc` with the kernel `kind` on `stream`.
@@ -129,7 +149,9 @@ alpaca_cuda_status alpaca_attention(const alpaca_attn_desc* desc, alpaca_attn_ke
 
 /* Tensor-core causal prefill (tcgen05 + TMEM + TMA). f16 KV; f16 or f32 Q (f32 Q is converted into the
  * workspace first, as MetalLlamaModel.swift:327 converts Q to half). Replaces KernelEncoder.attentionTensor
- * (KernelEncoder.swift:284-292) and the tiled attn_prefill branch (KernelEncoder.swift:328-335). */
+ * (KernelEncoder.swift:284-292) and the tiled attn_prefill branch (KernelEncoder.swift:328-335). With
+ * ALPACA_ATTN_FLAG_VARLEN it prefills sequences of different lengths and start positions in one launch, their work
+ * dealt to the SMs heaviest first across all sequences (the workspace then also holds that work list). */
 alpaca_cuda_status alpaca_attn_prefill(const alpaca_attn_desc* desc, void* workspace, size_t workspace_bytes,
                                        alpaca_stream_t stream);
 
@@ -148,7 +170,9 @@ alpaca_cuda_status alpaca_attn_decode(const alpaca_attn_desc* desc, void* worksp
  *     (head_dim + 2) * 4 bytes, see alpaca_attention_workspace_bytes) is rejected with
  *     ALPACA_CUDA_ERR_WORKSPACE_TOO_SMALL before anything is enqueued.
  *   - The first call on a device looks up the array's device address (cudaGetSymbolAddress, with that device
- *     current) and caches it; make that first call before any stream capture.
+ *     current) and caches it; make that first call before any stream capture. The cached address is that of the
+ *     runtime's primary context: the entry point is not meant for a caller's own driver-API context or for use
+ *     across cudaDeviceReset (which unloads the array).
  *   - All calls on a device share the array, which keeps the last call's contents. Nothing in it needs to start at
  *     zero: every split state the combine step reads is written earlier in the same call. Calls that overlap on
  *     the GPU (different streams without ordering) race on the array; order them on one stream or with events.
@@ -229,8 +253,15 @@ alpaca_cuda_status alpaca_rope_kv_append(const alpaca_rope_desc* desc, alpaca_st
 alpaca_cuda_status alpaca_attn_decode_rope(const alpaca_attn_desc* attn, const alpaca_rope_desc* rope,
                                            void* workspace, size_t workspace_bytes, alpaca_stream_t stream);
 
-/* Synchronises `stream`, then reports and (when `clear` != 0) resets the device-side error word of the current
- * device: ALPACA_CUDA_ERR_DEVICE_TIMEOUT when a bounded wait gave up, ALPACA_CUDA_OK otherwise. */
+/* Synchronises `stream`, then reports and (when `clear` != 0) resets the device-side error word of that stream on the
+ * current device: ALPACA_CUDA_ERR_DEVICE_TIMEOUT when a bounded wait gave up, ALPACA_CUDA_ERR_INVALID_ARGUMENT when
+ * a device-side contract check failed (a block-table entry outside the pool, a ctx_lens entry outside
+ * [1, max_ctx_len], a RoPE position outside the cache), ALPACA_CUDA_OK otherwise.
+ * Each stream gets its own word on its first call on a device, so calls on other streams do not show here (the
+ * streams beyond the first 1023 on a device share one word). Kernels captured into a CUDA graph report into the word
+ * of the stream they were captured on, wherever the graph is replayed. The word addresses are looked up once per
+ * device in the runtime's primary context: the library is not meant for other contexts or for use across
+ * cudaDeviceReset. */
 alpaca_cuda_status alpaca_cuda_device_status(alpaca_stream_t stream, int clear);
 
 /* Static description of a status code. */

@@ -37,7 +37,7 @@ def test_header_declarations_match_bindings():
 def test_library_exports_every_declared_symbol(lib):
     for name in declared_functions():
         assert hasattr(lib, name), name
-    assert lib.alpaca_cuda_version() == 10000
+    assert lib.alpaca_cuda_version() == 10100
 
 
 def test_status_strings(lib):

@@ -14,35 +14,12 @@ import pytest
 import torch
 
 import oracle
-from tests._util import max_abs_check
+from tests._util import max_abs_check, pool as _pool
 
 pytestmark = pytest.mark.gpu
 
 DECODE_TOL = 1e-5
 F16_BOUND = 2e-3
-
-
-def _pool(caches, block_rows, rng, max_rows, extra_blocks=3):
-    """Scatter per-sequence caches [S][rows][Hkv][d] (rows may differ) into a NaN pool of shuffled blocks; the table
-    has room for max_rows rows per sequence. Returns (pool, block_table [S, max_blocks] int32 numpy)."""
-    S = len(caches)
-    Hkv, d = caches[0].shape[1:]
-    nblk = [-(-c.shape[0] // block_rows) for c in caches]
-    max_blocks = -(-max_rows // block_rows)
-    total = sum(nblk) + extra_blocks
-    order = rng.permutation(total)
-    pool = np.full((total, block_rows, Hkv, d), np.nan, np.float32)
-    table = np.full((S, max_blocks), -1, np.int32)
-    nxt = 0
-    for s, c in enumerate(caches):
-        for b in range(nblk[s]):
-            blk = int(order[nxt])
-            nxt += 1
-            table[s, b] = blk
-            rows = c[b * block_rows:(b + 1) * block_rows]
-            pool[blk, :rows.shape[0]] = rows
-    table[table < 0] = int(order[-1])  # unused entries point at a valid (NaN) block
-    return pool, table
 
 
 @pytest.mark.parametrize("d,G,block_rows", [(64, 3, 256), (64, 3, 128), (128, 4, 384)])

@@ -301,3 +301,35 @@ def test_prefill_output_views(cuda_lib, d, odt):
     pad = torch.ones_like(big, dtype=torch.bool)
     pad[:, 3:3 + T, 1:1 + H] = False
     assert torch.all(big[pad] == 7.0)
+
+
+@pytest.mark.parametrize("d", [64, 128])
+def test_decode_output_ordered_for_next_launch(cuda_lib, d):
+    """Every context fits one split unit (128 rows at head_dim 64, 64 at 128) while max_ctx_len allows several, so
+    the split kernel finishes every sequence itself and the combine kernel has nothing to merge. A plain torch
+    kernel launched right after on the same stream, with no synchronisation in between, must still read the split
+    kernel's output: stream order holds across the dependent launches."""
+    from alpaca_b200 import Kernel, attention_device, device_status
+    S, H, kvh, cap = 64, 9, 3, 4096
+    unit = 128 if d == 64 else 64
+    rng = np.random.default_rng(41 + d)
+    lens = rng.integers(1, unit + 1, size=S).astype(np.int32)
+    q = _normal(141, (S, 1, H, d), False)
+    k = _normal(142, (S, unit, kvh, d))
+    v = _normal(143, (S, unit, kvh, d))
+    dev = torch.device("cuda")
+    qd = torch.from_numpy(q).to(dev)
+    kd, vd = torch.from_numpy(k).to(dev).half(), torch.from_numpy(v).to(dev).half()
+    ld = torch.from_numpy(lens).to(dev)
+    out = torch.full((S, 1, H, d), float("nan"), dtype=torch.float32, device=dev)
+    ws = torch.empty(1 << 24, dtype=torch.uint8, device=dev)
+    for _ in range(3):
+        out.fill_(float("nan"))
+        attention_device(qd, kd, vd, out, ctx_lens=ld, max_ctx_len=cap, kind=Kernel.DECODE_SPLIT, workspace=ws)
+        twice = out * 2.0  # next launch on the same stream, no sync
+        device_status()
+        got = (twice / 2.0).cpu().numpy()
+        for s in range(S):
+            L = int(lens[s])
+            ref = oracle.attention(q[s], k[s], v[s], L - 1, length=L)
+            max_abs_check(got[s], ref, 1e-5, f"ordered decode output d={d} seq {s} ctx={L}")
