@@ -197,6 +197,39 @@ __device__ __forceinline__ Item decode_item(const PrefillArgs& a, int it) {
     return x;
 }
 
+// One tile of work item `it`, as the softmax warps of tile `t` (a run-time, warp-uniform index) need it: scalar
+// fields, so they live in registers (an Item indexed by a run-time tile would sit in local memory).
+struct TileWork {
+    int seq, head, cseq, row0, pos0, nrows, nblk;
+};
+
+template <int BN, int NT, bool VL>
+__device__ __forceinline__ TileWork tile_work(const PrefillArgs& a, int it, int t) {
+    TileWork w;
+    if constexpr (VL) {
+        const int unit = it / a.n_heads;
+        w.head = it - unit * a.n_heads;
+        const int4 r = __ldg(a.plan + 1 + 2 * unit);
+        w.seq = r.x;
+        w.cseq = 0;
+        w.row0 = r.y + t * kBM;
+        w.pos0 = r.z + t * kBM;
+        w.nrows = max(0, min(kBM, r.w - t * kBM));
+        w.nblk = w.nrows > 0 ? (w.pos0 + w.nrows + BN - 1) / BN : 0;
+        return w;
+    }
+    const int per_rank = a.n_seqs * a.n_heads;
+    const int rank = it / per_rank, rem = it - rank * per_rank;
+    w.seq = rem / a.n_heads;
+    w.head = rem - w.seq * a.n_heads;
+    w.cseq = w.seq;
+    w.row0 = ((a.n_groups - 1 - rank) * NT + t) * kBM;  // heaviest groups first, as decode_item
+    w.pos0 = a.start + w.row0;
+    w.nrows = kBM;
+    w.nblk = tile_blocks<BN>(a, w.row0);
+    return w;
+}
+
 template <int NT>
 __device__ __forceinline__ int item_blocks(const Item& x) {
     int n = x.nblk[0];
@@ -323,10 +356,11 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
         for (int r = 0, it = item_of(0); ok && it < total_items; it = item_of(++r)) {
             const Item x = decode_item<kBN, NT, VL>(a, it);
             const int kvh = x.head / (a.n_heads / a.n_kv_heads);
-            for (int t = 0; t < NT && ok; t++) {
-                if (x.nblk[t] == 0) continue;
+#pragma unroll
+            for (int t = 0; t < NT; t++) {  // unrolled: the Item and q_uses stay in registers
+                if (!ok || x.nblk[t] == 0) continue;
                 ok = mbar_wait(&sm->q_empty[t], (q_uses[t] & 1) ^ 1, ab);
-                if (!ok) break;
+                if (!ok) continue;
                 mbar_arrive_expect_tx(&sm->q_full[t], G::kQBytes);
 #pragma unroll
                 for (int cb = 0; cb < G::CB; cb++)
@@ -396,9 +430,8 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
             bool ok = true;
             if (debug_timeout && t == 0) ok = mbar_wait(&sm->dbg, 0, ab);  // nothing arrives: exercises the give-up path
             for (int r = 0, it = item_of(0); ok && it < total_items; it = item_of(++r)) {
-                const Item x = decode_item<kBN, NT, VL>(a, it);
-                const int n = x.nblk[t];
-                const int nmax = item_blocks<NT>(x);
+                const int n = tile_work<kBN, NT, VL>(a, it, t).nblk;  // this issuer's tile
+                const int nmax = item_blocks<NT>(decode_item<kBN, NT, VL>(a, it));
                 if (n > 0) {
                     ok = mbar_wait(&sm->q_full[t], q_uses & 1, ab);
                     if (!ok) break;
@@ -511,11 +544,12 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
         const bool issuer = kTmaOut && ((warp - 4) & 3) == 0 && lane == 0;  // the tile's output TMA thread
         bool ok = true;
         for (int r = 0, it = item_of(0); ok && it < total_items; it = item_of(++r)) {
-            const Item x = decode_item<kBN, NT, VL>(a, it);
-            const int nb = x.nblk[tile];
+            const TileWork x = tile_work<kBN, NT, VL>(a, it, tile);
+            const int nb = x.nblk;
             if (nb == 0) continue;
-            const int row0 = x.row0[tile];
-            const int qpos = x.pos0[tile] + row;  // absolute position of this thread's query
+            const int row0 = x.row0;
+            const int pos0 = x.pos0;     // absolute position of the tile's first query
+            const int qpos = pos0 + row;  // and of this thread's
             float m_used = -INFINITY;
             float2 lsum = make_float2(0.f, 0.f);
             for (int j = 0; j < nb; j++) {
@@ -532,7 +566,7 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
                 if (lane == 0) mbar_arrive(&sm->s_empty[tile]);
 
                 const int kv0 = j * kBN;
-                if (kv0 + kBN - 1 > x.pos0[tile]) {  // the block reaches past the tile's first query: mask
+                if (kv0 + kBN - 1 > pos0) {  // the block reaches past the tile's first query: mask
 #pragma unroll
                     for (int c = 0; c < kBN; c++)
                         if (kv0 + c > qpos) s[c] = -INFINITY;
@@ -608,7 +642,7 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
             const float inv = 1.f / (lsum.x + lsum.y);
             // whole tiles leave through the staging box and TMA stores; in the ragged form a sequence's last,
             // partial tile is stored row by row (its map rows past the tile belong to the next sequence)
-            const bool tma_tile = kTmaOut && (!VL || x.nrows[tile] == kBM);
+            const bool tma_tile = kTmaOut && (!VL || x.nrows == kBM);
             if (tma_tile) {
                 // Two rounds of 64 columns through the tile's staging boxes and one thread's TMA stores, with the
                 // same o_free / o_staged hand-offs as the two-thread form.
@@ -675,7 +709,7 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
                 continue;
             }
             const int t = row0 + row;  // row of the output map
-            const bool have = VL ? row < x.nrows[tile] : t < a.tokens;
+            const bool have = VL ? row < x.nrows : t < a.tokens;
             const int64_t off = x.cseq * a.out_seq_stride + static_cast<int64_t>(t) * a.out_token_stride +
                                 static_cast<int64_t>(x.head) * D;
 #pragma unroll
@@ -723,11 +757,12 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
         const bool issuer = kTmaOut && ((warp - 4) & 7) == 0 && lane == 0;  // the tile's output TMA thread
         bool ok = true;
         for (int r = 0, it = item_of(0); ok && it < total_items; it = item_of(++r)) {
-            const Item x = decode_item<kBN, NT, VL>(a, it);
-            const int nb = x.nblk[tile];
+            const TileWork x = tile_work<kBN, NT, VL>(a, it, tile);
+            const int nb = x.nblk;
             if (nb == 0) continue;
-            const int row0 = x.row0[tile];
-            const int qpos = x.pos0[tile] + row;  // absolute position of this thread's query
+            const int row0 = x.row0;
+            const int pos0 = x.pos0;     // absolute position of the tile's first query
+            const int qpos = pos0 + row;  // and of this thread's
             float m_used = -INFINITY;
             float2 lsum = make_float2(0.f, 0.f);    // this thread's half of the row sum (two lanes of a pair)
             for (int j = 0; j < nb; j++) {
@@ -744,7 +779,7 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
                 if (lane == 0) mbar_arrive(&sm->s_empty[tile]);
 
                 const int kv0 = j * kBN + half * SC;
-                if (kv0 + SC - 1 > x.pos0[tile]) {  // these columns reach past the tile's first query: mask
+                if (kv0 + SC - 1 > pos0) {  // these columns reach past the tile's first query: mask
 #pragma unroll
                     for (int c = 0; c < SC; c++)
                         if (kv0 + c > qpos) s[c] = -INFINITY;
@@ -867,7 +902,7 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
             const int t = row0 + row;  // row of the output map
             // whole tiles leave through the staging box and TMA stores; in the ragged form a sequence's last,
             // partial tile is stored row by row (its map rows past the tile belong to the next sequence)
-            const bool tma_tile = kTmaOut && (!VL || x.nrows[tile] == kBM);
+            const bool tma_tile = kTmaOut && (!VL || x.nrows == kBM);
             if (tma_tile) {
                 // The rows go through the tile's staging box and one thread's TMA stores (rows past the tokens are
                 // clipped by the tensor map). Hand-offs on mbarriers with bounded waits: o_free (the previous
@@ -920,7 +955,7 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
                 ok = __all_sync(0xffffffffu, sent);
                 if (!ok) break;
                 ep_uses++;
-            } else if (VL ? row < x.nrows[tile] : t < a.tokens) {
+            } else if (VL ? row < x.nrows : t < a.tokens) {
                 const float inv = 1.f / l;
                 const int64_t off = x.cseq * a.out_seq_stride + static_cast<int64_t>(t) * a.out_token_stride +
                                     static_cast<int64_t>(x.head) * D + half * OC;

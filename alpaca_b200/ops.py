@@ -20,7 +20,7 @@ import ctypes
 import numpy as np
 import torch
 
-from ._lib import AlpacaCUDAError, AttnDesc, DType, Kernel, RopeDesc, Status, check, load
+from ._lib import FLAG_VARLEN, AlpacaCUDAError, AttnDesc, DType, Kernel, RopeDesc, Status, check, load
 
 KV_PADDING_ROWS = 32  # KernelEncoder.kvPaddingRows (KernelEncoder.swift:73)
 
@@ -77,6 +77,54 @@ def make_desc(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tens
     d_.out, d_.out_token_stride, d_.out_seq_stride = o4.data_ptr(), o4.stride(1), o4.stride(0) if S > 1 else 0
     d_.scale, d_.flags = float(scale), int(flags) & 0xFFFFFFFF
     return d_
+
+
+def make_varlen_desc(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor, q_offsets: torch.Tensor,
+                     start_positions: torch.Tensor, *, max_tokens: int, max_ctx_len: int, scale: float = 0.0,
+                     flags: int = 0, block_table: torch.Tensor | None = None) -> AttnDesc:
+    """Descriptor of a ragged prefill (ALPACA_ATTN_FLAG_VARLEN): several sequences' query chunks in one call.
+
+    q [total_tokens, H, d] and out [total_tokens, H, d] are packed: sequence s owns rows q_offsets[s] ..
+    q_offsets[s+1]-1 (q_offsets: CUDA int32 [S + 1]) and its query t sits at absolute position start_positions[s] + t
+    (CUDA int32 [S]) of its own cache, k/v [S, rows >= max_ctx_len, Hkv, d], or pools with `block_table` as for
+    make_desc. `max_tokens` bounds every sequence's query count and `max_ctx_len` every start + count."""
+    for name, t, n in (("q_offsets", q_offsets, None), ("start_positions", start_positions, None)):
+        if t.dtype != torch.int32 or not t.is_cuda or t.dim() != 1 or not t.is_contiguous():
+            raise AlpacaCUDAError(Status.INVALID_ARGUMENT, f"{name} must be a contiguous CUDA int32 vector")
+    S = start_positions.numel()
+    if q_offsets.numel() != S + 1:
+        raise AlpacaCUDAError(Status.INVALID_ARGUMENT, "q_offsets must hold n_seqs + 1 entries")
+    if q.dim() != 3 or out.dim() != 3 or out.shape[:1] != q.shape[:1]:
+        raise AlpacaCUDAError(Status.INVALID_ARGUMENT, "ragged q and out must be packed [total_tokens, heads, head_dim]")
+    k4 = _as4(k, "k")
+    if block_table is None and k4.shape[0] != S:
+        raise AlpacaCUDAError(Status.INVALID_ARGUMENT, "k / v must hold one cache per sequence")
+    # the per-sequence cache layout, with a stand-in q / out of S sequences (their strides are ignored)
+    d_ = make_desc(q.unsqueeze(0).expand(S, *q.shape), k, v, out.unsqueeze(0).expand(S, *out.shape),
+                   scale=scale, flags=flags, block_table=block_table)
+    d_.flags = (int(flags) | FLAG_VARLEN) & 0xFFFFFFFF
+    d_.q_seq_stride = d_.out_seq_stride = 0
+    d_.tokens = int(max_tokens)
+    d_.start_position = 0
+    d_.max_ctx_len = int(max_ctx_len)
+    d_.q_offsets, d_.start_positions = q_offsets.data_ptr(), start_positions.data_ptr()
+    d_.total_tokens = q.shape[0]
+    return d_
+
+
+def prefill_varlen(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor, q_offsets: torch.Tensor,
+                   start_positions: torch.Tensor, *, max_tokens: int, max_ctx_len: int, scale: float = 0.0,
+                   flags: int = 0, workspace: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None,
+                   block_table: torch.Tensor | None = None) -> AttnDesc:
+    """Enqueue a ragged prefill (make_varlen_desc) on the tensor-core kernel; allocates the workspace (work list,
+    f16 staging of f32 queries) with torch when none is given."""
+    desc = make_varlen_desc(q, k, v, out, q_offsets, start_positions, max_tokens=max_tokens, max_ctx_len=max_ctx_len,
+                            scale=scale, flags=flags, block_table=block_table)
+    need = workspace_bytes(desc, Kernel.PREFILL_TC)
+    if need and (workspace is None or workspace.numel() * workspace.element_size() < need):
+        workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+    launch(desc, Kernel.PREFILL_TC, workspace, stream)
+    return desc
 
 
 def workspace_bytes(desc: AttnDesc, kind: Kernel = Kernel.AUTO) -> int:

@@ -15,22 +15,23 @@ from dataclasses import dataclass, field
 @dataclass(frozen=True)
 class Unit:
     seq: int            # sequence index in the batch
-    kv_head: int        # KV head index (the unit covers its G query heads)
+    kv_head: int        # first KV head of the unit (the unit covers their G query heads each)
     tokens: int         # query tokens (1 for decode)
     start: int          # absolute position of the first query token (decode: context length - 1)
     group: int          # query heads per KV head (G)
     head_dim: int = 64
+    kv_heads: int = 1   # consecutive KV heads in the unit
 
     @property
     def flops(self) -> float:
-        """QKᵀ + P·V FLOPs of the visible (query, key) pairs: Σ_t 4·d·(start + t + 1), times G."""
+        """QKᵀ + P·V FLOPs of the visible (query, key) pairs: Σ_t 4·d·(start + t + 1), times G and the KV heads."""
         T, s = self.tokens, self.start
-        return self.group * 4.0 * self.head_dim * (T * s + T * (T + 1) / 2.0)
+        return self.kv_heads * self.group * 4.0 * self.head_dim * (T * s + T * (T + 1) / 2.0)
 
     @property
     def kv_bytes(self) -> float:
         """f16 K and V rows this unit reads once."""
-        return (self.start + self.tokens) * self.head_dim * 2.0 * 2.0
+        return self.kv_heads * (self.start + self.tokens) * self.head_dim * 2.0 * 2.0
 
     def cost(self, tflops: float = 1000.0, hbm_gbs: float = 6000.0) -> float:
         """Seconds under the slower of the tensor-core and HBM rooflines."""
@@ -61,6 +62,16 @@ def units_for_batch(seq_tokens: list[int], seq_starts: list[int], n_heads: int, 
             for h in range(n_kv_heads)]
 
 
+def head_group_units(seq_tokens: list[int], seq_starts: list[int], n_kv_heads: int, kv_heads_per_unit: int,
+                     group: int = 1, head_dim: int = 64, first_seq: int = 0) -> list[Unit]:
+    """Units of `kv_heads_per_unit` consecutive KV heads (a divisor of n_kv_heads) per sequence: the same split as
+    units_for_batch, coarser, so that a rank's units all have one head count and run as one call."""
+    if n_kv_heads % kv_heads_per_unit:
+        raise ValueError("kv_heads_per_unit must divide n_kv_heads")
+    return [Unit(first_seq + s, h, int(t), int(st), group, head_dim, kv_heads_per_unit)
+            for s, (t, st) in enumerate(zip(seq_tokens, seq_starts)) for h in range(0, n_kv_heads, kv_heads_per_unit)]
+
+
 def partition(units: list[Unit], n_ranks: int, tflops: float = 1000.0, hbm_gbs: float = 6000.0) -> Plan:
     """Longest-processing-time-first packing of units onto n_ranks (deterministic: ties go to the lower rank,
     equal-cost units keep their input order)."""
@@ -88,7 +99,7 @@ def head_ranges(units: list[Unit]) -> list[tuple[int, int, int]]:
     for u in sorted(units, key=lambda u: (u.seq, u.kv_head)):
         if runs and runs[-1][0] == u.seq and runs[-1][1] + runs[-1][2] == u.kv_head:
             s, h0, n = runs[-1]
-            runs[-1] = (s, h0, n + 1)
+            runs[-1] = (s, h0, n + u.kv_heads)
         else:
-            runs.append((u.seq, u.kv_head, 1))
+            runs.append((u.seq, u.kv_head, u.kv_heads))
     return runs

@@ -351,3 +351,30 @@ def test_rope_cache_rows_checked(lib, bad):
     d = rope_desc(**bad)
     assert lib.alpaca_rope_kv_append(ctypes.byref(d), None) == Status.INVALID_ARGUMENT
     assert lib.alpaca_cuda_last_error().startswith(b"rope")
+
+
+def test_varlen_prefill_host_checks(lib):
+    """The ragged prefill flag: AUTO picks the tensor-core prefill, the other kernels refuse it, the workspace holds
+    the heaviest-first work list (16 bytes + 32 per unit of two 128-row tiles) plus the f16 staging of f32
+    queries, and the descriptor's own contradictions are refused before anything is enqueued."""
+    from alpaca_b200 import FLAG_VARLEN, DType, Kernel, Status
+    base = dict(flags=FLAG_VARLEN, n_seqs=3, tokens=600, max_ctx_len=2000, total_tokens=900, q_offsets=FAKE,
+                start_positions=FAKE + 256, kv_seq_stride=2000 * 3 * 64)
+    st, k = select(lib, desc(**base))
+    assert (st, k) == (Status.OK, Kernel.PREFILL_TC)
+    units = 3 * 3  # ceil(600 / 256) units per sequence
+    assert ws(lib, desc(**base)) == (Status.OK, 16 + 32 * units)
+    assert ws(lib, desc(**base, q_dtype=int(DType.F32), q_token_stride=9 * 64)) == \
+        (Status.OK, 900 * 9 * 64 * 2 + 16 + 32 * units)
+    assert ws(lib, desc(**base), int(Kernel.GENERAL))[0] == Status.UNSUPPORTED
+    assert ws(lib, desc(**base), int(Kernel.DECODE_SPLIT))[0] == Status.UNSUPPORTED
+    # q / out sequence strides are ignored (packed rows); the per-sequence caches still need theirs
+    assert select(lib, desc(**{**base, "kv_seq_stride": 0}))[0] == Status.INVALID_ARGUMENT
+    for bad in (dict(q_offsets=0), dict(start_positions=0), dict(total_tokens=0), dict(max_ctx_len=0),
+                dict(ctx_lens=FAKE)):
+        assert select(lib, desc(**{**base, **bad}))[0] == Status.INVALID_ARGUMENT, bad
+    # a paged ragged call: the block table must cover max_ctx_len rows
+    paged = {**base, "kv_seq_stride": 0, "block_table": FAKE, "block_rows": 256, "pool_blocks": 64,
+             "block_stride": 256 * 3 * 64}
+    assert select(lib, desc(**paged, max_blocks=8))[0] == Status.OK
+    assert select(lib, desc(**paged, max_blocks=7))[0] == Status.INVALID_ARGUMENT

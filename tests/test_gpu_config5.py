@@ -124,3 +124,45 @@ def test_config5_dispatch_policy(cuda_lib):
     lens = torch.full((4,), 300, dtype=torch.int32, device=dev)
     assert ab.select_kernel(ab.make_desc(q1, kv, kv, q1, ctx_lens=lens, max_ctx_len=512)) == ab.Kernel.DECODE_SPLIT
     assert ab.select_kernel(ab.make_desc(qT, kv[:1], kv[:1], qT.float())) == ab.Kernel.PREFILL_TC
+
+
+@pytest.mark.parametrize("paged", [False, True], ids=["contiguous", "paged"])
+def test_config5_prefill_one_ragged_call(cuda_lib, paged):
+    """The three prefill sequences (128, 3000 and 8192 tokens) in one ragged launch: packed queries, one cache (or
+    block table) per sequence. Every output row equals the per-sequence uniform call bit for bit, and sampled rows,
+    the last token of every head included, match the oracle."""
+    from alpaca_b200 import Kernel, attention_device, device_status, prefill_varlen
+    dev = torch.device("cuda")
+    ins = [_prefill_inputs(T, 500 + 10 * i) for i, T in enumerate(PREFILL_T)]
+    lens = np.array(PREFILL_T, np.int32)
+    offs = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    cap = int(lens.max())
+    qd = torch.from_numpy(np.concatenate([x[0] for x in ins])).to(dev).half()
+    out = torch.empty((int(offs[-1]), H, D), dtype=torch.float32, device=dev)
+    starts = torch.zeros(len(PREFILL_T), dtype=torch.int32, device=dev)
+    if paged:
+        kp, table = pool([x[1] for x in ins], BLOCK_ROWS, np.random.default_rng(77), cap)
+        vp, _ = pool([x[2] for x in ins], BLOCK_ROWS, np.random.default_rng(77), cap)
+        prefill_varlen(qd, torch.from_numpy(kp).to(dev).half(), torch.from_numpy(vp).to(dev).half(), out,
+                       torch.from_numpy(offs).to(dev), starts, max_tokens=cap, max_ctx_len=cap,
+                       block_table=torch.from_numpy(table).to(dev))
+    else:
+        kd = torch.full((len(ins), cap, HKV, D), float("nan"), dtype=torch.float16, device=dev)
+        vd = torch.full_like(kd, float("nan"))
+        for s, x in enumerate(ins):
+            kd[s, :x[1].shape[0]] = torch.from_numpy(x[1]).to(dev).half()
+            vd[s, :x[2].shape[0]] = torch.from_numpy(x[2]).to(dev).half()
+        prefill_varlen(qd, kd, vd, out, torch.from_numpy(offs).to(dev), starts, max_tokens=cap, max_ctx_len=cap)
+    device_status()
+    for s, (T, (q, k, v)) in enumerate(zip(PREFILL_T, ins)):
+        o0 = int(offs[s])
+        uni = torch.empty((T, H, D), dtype=torch.float32, device=dev)
+        attention_device(qd[o0:o0 + T], torch.from_numpy(k).to(dev).half(), torch.from_numpy(v).to(dev).half(), uni,
+                         kind=Kernel.PREFILL_TC)
+        device_status()
+        assert torch.equal(uni, out[o0:o0 + T]), f"T={T}: ragged call differs from the uniform call"
+        rows = _sample_rows(T, 997 if T > 4096 else 101)
+        cpu = oracle.attention_rows(q, k, v, 0, rows)
+        sel = oracle.rows_mask(rows, T, H)
+        max_abs_check(out[o0:o0 + T].cpu().numpy()[sel], cpu[sel], F16_BOUND,
+                      f"config 5 ragged prefill T={T} {'paged' if paged else 'contiguous'}")

@@ -126,3 +126,28 @@ def test_two_gloo_ranks_match_single_process(tmp_path):
     assert np.all(res["cover"] == 1)  # every (seq, token, head) produced by exactly one rank
     ref = np.stack([oracle.attention(q[s], k[s], v[s], starts[s], length=starts[s] + T) for s in range(S)])
     assert np.array_equal(res["out"], ref)
+
+
+def test_head_group_units_cost_and_balance():
+    """Config-5-shaped batch split into units of 8 KV heads: every (sequence, head group) once, costs 8 heads' worth,
+    and the LPT split over 8 ranks stays within 1% of the mean."""
+    from alpaca_b200.partition import head_group_units
+    rng = np.random.default_rng(20260105)
+    toks = [int(x) for x in np.round(np.exp(rng.uniform(np.log(128), np.log(8192), 256)))]
+    units = head_group_units(toks, [0] * 256, 32, 8) + \
+        head_group_units([1] * 512, [int(x) for x in rng.integers(0, 8192, 512)], 32, 8, first_seq=256)
+    assert len(units) == (256 + 512) * 4
+    one = Unit(0, 0, toks[0], 0, 1)
+    assert units[0].flops == pytest.approx(8 * one.flops) and units[0].kv_bytes == pytest.approx(8 * one.kv_bytes)
+    for n in (1, 2, 4, 8):
+        p = partition(units, n)
+        assert sorted((u.seq, u.kv_head) for r in p.ranks for u in r) == sorted((u.seq, u.kv_head) for u in units)
+        assert p.imbalance < 1.01, (n, p.imbalance)
+    with pytest.raises(ValueError):
+        head_group_units([8], [0], 32, 5)
+
+
+def test_head_ranges_of_head_group_units():
+    from alpaca_b200.partition import head_group_units
+    units = [u for u in head_group_units([8, 8], [0, 0], 32, 8) if (u.seq, u.kv_head) != (0, 16)]
+    assert head_ranges(units) == [(0, 0, 16), (0, 24, 8), (1, 0, 32)]
