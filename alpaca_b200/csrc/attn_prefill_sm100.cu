@@ -108,7 +108,8 @@ struct PrefillArgs {
     int block_rows, max_blocks, pool_blocks, last_block;  // last_block: block (of a sequence) holding row kv_len - 1
     // Ragged form: the work list the plan kernel wrote into the workspace. plan[0].x = units; unit u is
     // plan[1 + 2u] = {sequence, packed row of its first query, absolute position of that query, query rows} and
-    // plan[2 + 2u].x = the sequence's context end (start + tokens). Units are ordered heaviest first.
+    // plan[2 + 2u].x = the sequence's context end (start + tokens). Sequences heaviest first, each one's units
+    // together and heaviest first.
     const int4* plan;
 };
 
@@ -998,9 +999,13 @@ __global__ void q_to_half_kernel(const float* __restrict__ q, int64_t token_stri
 // ---------------------------------------------------------------------------------------------- ragged plan
 
 // Work list of a ragged call. A unit is one group of kUnitTiles query tiles of one sequence (all heads: the prefill
-// kernel takes unit-major, head-minor items). One CTA counts the units per cost (KV blocks the unit's last query
-// attends to), turns the counts into write positions in descending cost order, and writes every unit's record at
-// its position, so the persistent kernel deals the heaviest units first across every sequence of the call.
+// kernel takes unit-major, head-minor items). Sequences come heaviest first (by the KV blocks their last query
+// attends to) and each sequence's units stay together, heaviest first: the items a persistent kernel runs at the
+// same time then share the K/V rows of a few sequences, so the re-reads of those rows by the sequence's other query
+// tiles hit L2 (ordering units by cost across sequences spread each sequence's re-reads over the whole launch and
+// sent them to DRAM), while the lightest sequences still fill the tail. One CTA counts the units per cost bucket of
+// their sequence, turns the counts into write positions in descending order, and each sequence claims a contiguous
+// range of its bucket.
 constexpr int kPlanThreads = 1024;
 constexpr int kPlanBuckets = 2 * kPlanThreads;  // costs above kPlanBuckets - 1 blocks share the first bucket
 constexpr int kUnitTiles = 2;                   // query tiles per unit (the two-tile forms)
@@ -1029,11 +1034,13 @@ __device__ __forceinline__ bool plan_span(const PlanArgs& p, int s, int& off, in
     return true;
 }
 
-__device__ __forceinline__ int plan_bucket(const PlanArgs& p, int start, int len, int g) {
-    const int last = min(len, (g + 1) * kUnitTiles * kBM);  // exclusive: the unit's last query row + 1
-    const int cost = (start + last + p.bn - 1) / p.bn;
-    return kPlanBuckets - 1 - min(cost, kPlanBuckets - 1);  // heaviest first
+// Bucket of a sequence: the KV blocks its last query attends to, heaviest first.
+__device__ __forceinline__ int plan_bucket(const PlanArgs& p, int start, int len) {
+    const int cost = (start + len + p.bn - 1) / p.bn;
+    return kPlanBuckets - 1 - min(cost, kPlanBuckets - 1);
 }
+
+__device__ __forceinline__ int plan_units_of(int len) { return (len + kUnitTiles * kBM - 1) / (kUnitTiles * kBM); }
 
 __global__ void __launch_bounds__(kPlanThreads) prefill_plan_kernel(const PlanArgs p) {
     __shared__ int cnt[kPlanBuckets];  // units per bucket, then the buckets' write cursors
@@ -1047,7 +1054,7 @@ __global__ void __launch_bounds__(kPlanThreads) prefill_plan_kernel(const PlanAr
     for (int s = tid; s < p.n_seqs; s += kPlanThreads) {
         int off, len, start;
         if (!plan_span(p, s, off, len, start)) continue;
-        for (int g = 0; g * kUnitTiles * kBM < len; g++) atomicAdd(&cnt[plan_bucket(p, start, len, g)], 1);
+        atomicAdd(&cnt[plan_bucket(p, start, len)], plan_units_of(len));
     }
     __syncthreads();
     // exclusive prefix sum of the counts: thread i owns buckets 2i and 2i + 1
@@ -1078,11 +1085,12 @@ __global__ void __launch_bounds__(kPlanThreads) prefill_plan_kernel(const PlanAr
     for (int s = tid; s < p.n_seqs; s += kPlanThreads) {
         int off, len, start;
         if (!plan_span(p, s, off, len, start)) continue;
-        for (int g = 0; g * kUnitTiles * kBM < len; g++) {
-            const int u = atomicAdd(&cnt[plan_bucket(p, start, len, g)], 1);
-            const int r0 = g * kUnitTiles * kBM;
-            p.plan[1 + 2 * u] = make_int4(s, off + r0, start + r0, min(kUnitTiles * kBM, len - r0));
-            p.plan[2 + 2 * u] = make_int4(start + len, 0, 0, 0);
+        const int n = plan_units_of(len);
+        const int base = atomicAdd(&cnt[plan_bucket(p, start, len)], n);
+        for (int i = 0; i < n; i++) {  // the sequence's units, last (heaviest) group first
+            const int g = n - 1 - i, r0 = g * kUnitTiles * kBM;
+            p.plan[1 + 2 * (base + i)] = make_int4(s, off + r0, start + r0, min(kUnitTiles * kBM, len - r0));
+            p.plan[2 + 2 * (base + i)] = make_int4(start + len, 0, 0, 0);
         }
     }
 }
