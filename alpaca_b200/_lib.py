@@ -113,6 +113,32 @@ class RopeDesc(ctypes.Structure):
     ]
 
 
+class ProjDesc(ctypes.Structure):
+    """alpaca_proj_desc (include/alpaca_cuda.h)."""
+    _fields_ = [
+        ("n_tokens", ctypes.c_int32),
+        ("k", ctypes.c_int32),
+        ("rows", ctypes.c_int32 * 3),
+        ("format", ctypes.c_int32),
+        ("flags", ctypes.c_uint32),
+        ("eps", ctypes.c_float),
+        ("w", ctypes.c_void_p * 3),
+        ("x", ctypes.c_void_p),
+        ("x_stride", ctypes.c_int64),
+        ("norm_weight", ctypes.c_void_p),
+        ("y", ctypes.c_void_p * 3),
+        ("y_stride", ctypes.c_int64 * 3),
+    ]
+
+
+class WeightFormat(IntEnum):
+    F16 = 0
+    Q8_0 = 1
+    Q4_0 = 2
+
+
+PROJ_NORM, PROJ_SILU, PROJ_ADD = 1, 2, 4
+
 EXPORTED_SYMBOLS = (
     "alpaca_attention",
     "alpaca_attn_prefill",
@@ -126,6 +152,7 @@ EXPORTED_SYMBOLS = (
     "alpaca_cuda_last_error",
     "alpaca_cuda_version",
     "alpaca_rope_kv_append",
+    "alpaca_decode_project",
 )
 
 _lib: ctypes.CDLL | None = None
@@ -162,6 +189,8 @@ def load() -> ctypes.CDLL:
     L.alpaca_cuda_version.argtypes = []
     L.alpaca_rope_kv_append.restype = ctypes.c_int
     L.alpaca_rope_kv_append.argtypes = [ctypes.POINTER(RopeDesc), ctypes.c_void_p]
+    L.alpaca_decode_project.restype = ctypes.c_int
+    L.alpaca_decode_project.argtypes = [ctypes.POINTER(ProjDesc), ctypes.c_void_p]
     L.alpaca_attn_decode_rope.restype = ctypes.c_int
     L.alpaca_attn_decode_rope.argtypes = [P, ctypes.POINTER(RopeDesc), ctypes.c_void_p, ctypes.c_size_t,
                                           ctypes.c_void_p]

@@ -17,7 +17,7 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libalpaca_cuda.so"
-SOURCES = ["api.cu", "attn_decode.cu", "attn_general.cu", "attn_prefill_sm100.cu", "rope_kv.cu"]
+SOURCES = ["api.cu", "attn_decode.cu", "attn_general.cu", "attn_prefill_sm100.cu", "rope_kv.cu", "decode_proj.cu"]
 HEADERS = ["common.cuh", "internal.h"]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -437,6 +437,48 @@ alpaca_cuda_status alpaca_rope_kv_append(const alpaca_rope_desc* desc, alpaca_st
     return launched(launch_rope_kv(*desc, di.err, s), "rope");
 }
 
+alpaca_cuda_status alpaca_decode_project(const alpaca_proj_desc* dp, alpaca_stream_t stream) {
+    if (!dp) return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "project: null descriptor");
+    const alpaca_proj_desc& d = *dp;
+    char sh[160];
+    std::snprintf(sh, sizeof(sh), "tokens=%d k=%d rows=%d/%d/%d format=%d flags=%u", d.n_tokens, d.k, d.rows[0],
+                  d.rows[1], d.rows[2], d.format, d.flags);
+    auto bad = [&](const char* what) {
+        return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, std::string("project: ") + what + ": " + sh);
+    };
+    if (d.format != ALPACA_W_F16 && d.format != ALPACA_W_Q8_0 && d.format != ALPACA_W_Q4_0)
+        return fail(ALPACA_CUDA_ERR_UNSUPPORTED, std::string("project: unknown weight format: ") + sh);
+    if (d.flags & ~(ALPACA_PROJ_NORM | ALPACA_PROJ_SILU | ALPACA_PROJ_ADD)) return bad("unknown flags");
+    if (d.n_tokens < 1 || d.k < 32 || d.k % 32 || d.k > 16384) return bad("n_tokens >= 1 and k a multiple of 32 up to 16384");
+    const bool silu = (d.flags & ALPACA_PROJ_SILU) != 0;
+    if (silu && (d.flags & ALPACA_PROJ_ADD)) return bad("SILU and ADD together");
+    if (silu ? (d.rows[0] < 1 || d.rows[1] != 0 || d.rows[2] != 0)
+             : (d.rows[0] < 0 || d.rows[1] < 0 || d.rows[2] < 0 || d.rows[0] + d.rows[1] + d.rows[2] < 1))
+        return bad("row counts");
+    const int used = silu ? 2 : 3;
+    for (int i = 0; i < used; i++) {
+        const bool present = silu || d.rows[i] > 0;
+        if (!present) continue;
+        if (!d.w[i] || !aligned16(d.w[i])) return bad("weights null or not 16-byte aligned");
+        if (i == 0 || !silu) {
+            if (!d.y[i] || (reinterpret_cast<uintptr_t>(d.y[i]) & 3u)) return bad("outputs null or not 4-byte aligned");
+            const int r = d.rows[i];
+            if (d.n_tokens > 1 && d.y_stride[i] < r) return bad("output stride smaller than its rows");
+        }
+    }
+    if (!d.x || (reinterpret_cast<uintptr_t>(d.x) & 3u)) return bad("input null or not 4-byte aligned");
+    if (d.n_tokens > 1 && d.x_stride < d.k) return bad("input stride smaller than k");
+    if (d.flags & ALPACA_PROJ_NORM) {
+        if (!d.norm_weight || (reinterpret_cast<uintptr_t>(d.norm_weight) & 3u)) return bad("norm weight null or unaligned");
+        if (!(d.eps > 0.f) || !std::isfinite(d.eps)) return bad("eps must be finite and > 0");
+    }
+    const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    DeviceInfo di;
+    const alpaca_cuda_status st = device_for(s, "project", &di);
+    if (st != ALPACA_CUDA_OK) return st;
+    return launched(launch_proj(d, di.num_sms, s), "project");
+}
+
 alpaca_cuda_status alpaca_attention_workspace_bytes(const alpaca_attn_desc* desc, alpaca_attn_kernel kind,
                                                     size_t* bytes) {
     if (!bytes) return fail(ALPACA_CUDA_ERR_INVALID_ARGUMENT, "workspace_bytes: null output");

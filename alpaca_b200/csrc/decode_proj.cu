@@ -1,0 +1,727 @@
+// decode_proj.cu — fused single-token projections of a decode step: optional RMSNorm of the input row, then up to
+// three weight matrices applied to it (Q / K / V in one launch), or the SwiGLU gate + up pair, or one matrix with the
+// result added to the output (the out- and down-projections with their residual). Same job as alpaca.swift's
+// dec_f16 / dec_q8_0 / dec_q4_0 (Sources/AlpacaMetal/Kernels/decode_fused.metal:32-122), dispatched by
+// KernelEncoder.decodeQKV / decodeProjection / decodeGateUp (Sources/AlpacaMetal/Backend/KernelEncoder.swift:
+// 386-400); weights f16 or GGUF q8_0 / q4_0.
+//
+// HBM-bound (every weight byte is read once per launch; the input rows are a few KB), so the design is about bytes in
+// flight and cheap decoding:
+//   * each CTA (8 warps) stages the call's input rows, RMS-normalised when asked, in shared memory once; one warp
+//     computes one output row at a time, lanes striding over the row's 16-byte f16 chunks or GGUF blocks;
+//   * quantised blocks (34 / 18 bytes, 2-byte aligned) are read with aligned 4-byte loads and realigned with funnel
+//     shifts; int8 and 4-bit values become floats through a byte permute into 2^23 + v (no conversion instructions);
+//   * for quantised formats the staged row is stored transposed per block (element j of block b at
+//     j * (blocks + 1) + b), so the 32 lanes of a warp, which work on 32 consecutive blocks, read 32 consecutive words
+//     of shared memory, and the staging writes (consecutive elements, one block apart) fall in 32 different banks
+//     (without the pad word the stride is a multiple of 32 words: a 32-way conflict on every staging store, which
+//     held q8_0 projections near 0.4 TB/s);
+//   * up to 4 input rows (tokens of a batched decode step) share every weight load; more rows take more passes.
+#include <algorithm>
+#include <cmath>
+#include <cstdlib>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace alpaca {
+namespace {
+
+constexpr int kProjThreads = 256;
+constexpr int kProjWarps = kProjThreads / 32;
+constexpr int kProjMaxTokens = 4;
+constexpr size_t kProjSmemBudget = 160 * 1024;  // staged input rows per CTA
+
+struct ProjArgs {
+    const uint8_t* w[3];
+    const uint8_t* w_end[3];  // one past each matrix (bounds of the 4-byte loads at its end)
+    int rows[3];
+    int total_rows;          // rows the warps iterate over (SiLU: rows[0])
+    int k, units;            // input width; 16-byte chunks (f16) or blocks (quantised) per row
+    int64_t row_bytes;
+    unsigned flags;
+    float eps;
+    const float* x;
+    int64_t x_stride;
+    const float* g;
+    float* y[3];
+    int64_t y_stride[3];
+    int n_tokens;
+    int wpr;       // warps per row (1, 2, 4 or 8): each takes every wpr-th group of 32 units of the row
+    int prefetch;  // bulk L2 prefetch of the CTA's weight rows at the start
+};
+
+__device__ __forceinline__ uint32_t ldg32(const uint8_t* p) { return __ldg(reinterpret_cast<const unsigned int*>(p)); }
+__device__ __forceinline__ uint32_t ldg16(const uint8_t* p) {
+    return __ldg(reinterpret_cast<const unsigned short*>(p));
+}
+
+// Four signed bytes -> floats: byte v + 128 placed in the low mantissa bits of 2^23, minus 2^23 + 128.
+__device__ __forceinline__ void i8x4_to_f32(uint32_t w, float (&f)[4]) {
+    const uint32_t u = w ^ 0x80808080u;
+#pragma unroll
+    for (int e = 0; e < 4; e++) f[e] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540u + e)) - 8388736.0f;
+}
+// Four bytes holding 4-bit values n -> floats n - 8.
+__device__ __forceinline__ void n4x4_to_f32(uint32_t w, float (&f)[4]) {
+#pragma unroll
+    for (int e = 0; e < 4; e++) f[e] = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540u + e)) - 8388616.0f;
+}
+
+// The 32 bytes after the 2-byte scale of a q8_0 block at p (2-byte aligned), as 8 words, and the scale.
+__device__ __forceinline__ float q8_block(const uint8_t* p, const uint8_t* end, uint32_t (&q)[8]) {
+    if (reinterpret_cast<uintptr_t>(p) & 2u) {  // scale in the high half of the word before p + 2
+        const uint8_t* b = p - 2;
+        const uint32_t w0 = ldg32(b);
+#pragma unroll
+        for (int i = 0; i < 8; i++) q[i] = ldg32(b + 4 + 4 * i);
+        return __half2float(__ushort_as_half(static_cast<unsigned short>(w0 >> 16)));
+    }
+    uint32_t w[9];
+#pragma unroll
+    for (int i = 0; i < 8; i++) w[i] = ldg32(p + 4 * i);
+    w[8] = (p + 36 <= end) ? ldg32(p + 32) : ldg16(p + 32);  // the block may end the matrix
+#pragma unroll
+    for (int i = 0; i < 8; i++) q[i] = __funnelshift_r(w[i], w[i + 1], 16);
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(w[0] & 0xFFFFu)));
+}
+
+// The 16 bytes of nibbles after the scale of a q4_0 block at p (2-byte aligned), as 4 words, and the scale.
+__device__ __forceinline__ float q4_block(const uint8_t* p, const uint8_t* end, uint32_t (&q)[4]) {
+    if (reinterpret_cast<uintptr_t>(p) & 2u) {
+        const uint8_t* b = p - 2;
+        const uint32_t w0 = ldg32(b);
+#pragma unroll
+        for (int i = 0; i < 4; i++) q[i] = ldg32(b + 4 + 4 * i);
+        return __half2float(__ushort_as_half(static_cast<unsigned short>(w0 >> 16)));
+    }
+    uint32_t w[5];
+#pragma unroll
+    for (int i = 0; i < 4; i++) w[i] = ldg32(p + 4 * i);
+    w[4] = (p + 20 <= end) ? ldg32(p + 16) : ldg16(p + 16);
+#pragma unroll
+    for (int i = 0; i < 4; i++) q[i] = __funnelshift_r(w[i], w[i + 1], 16);
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(w[0] & 0xFFFFu)));
+}
+
+// Shared-memory index of element i of a staged row: plain for f16, transposed per 32-element block otherwise, each
+// of the 32 element planes padded by one word.
+template <int F>
+__device__ __forceinline__ int xs_index(int i, int units) {
+    if constexpr (F == 0) return i;
+    return (i & 31) * (units + 1) + (i >> 5);
+}
+// Floats of one staged row.
+template <int F>
+__host__ __device__ __forceinline__ int xs_row(int k, int units) {
+    return F == 0 ? k : 32 * (units + 1);
+}
+
+// One unit of a weight row in registers: a 16-byte f16 chunk, or a q8_0 / q4_0 block's scale and quant words.
+template <int F>
+struct UnitRegs {
+    uint32_t q[F == 0 ? 4 : (F == 1 ? 8 : 4)];
+    float d;
+};
+
+template <int F>
+__device__ __forceinline__ void load_unit(const uint8_t* rowp, const uint8_t* end, int u, UnitRegs<F>& r) {
+    if constexpr (F == 0) {
+        const uint4 w = __ldg(reinterpret_cast<const uint4*>(rowp) + u);
+        r.q[0] = w.x;
+        r.q[1] = w.y;
+        r.q[2] = w.z;
+        r.q[3] = w.w;
+        r.d = 1.f;
+    } else if constexpr (F == 1) {
+        r.d = q8_block(rowp + static_cast<int64_t>(u) * 34, end, r.q);
+    } else {
+        r.d = q4_block(rowp + static_cast<int64_t>(u) * 18, end, r.q);
+    }
+}
+
+// acc[t] += unit u of the row . xn_t
+template <int F, int TP>
+__device__ __forceinline__ void dot_unit(const UnitRegs<F>& r, int u, const float* xs, int XR, int P, float (&acc)[TP]) {
+    if constexpr (F == 0) {
+        float wf[8];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&r.q[i]));
+            wf[2 * i] = f.x;
+            wf[2 * i + 1] = f.y;
+        }
+#pragma unroll
+        for (int t = 0; t < TP; t++) {
+            const float4 x0 = *reinterpret_cast<const float4*>(xs + t * XR + 8 * u);
+            const float4 x1 = *reinterpret_cast<const float4*>(xs + t * XR + 8 * u + 4);
+            float s = acc[t];
+            s = fmaf(wf[0], x0.x, s);
+            s = fmaf(wf[1], x0.y, s);
+            s = fmaf(wf[2], x0.z, s);
+            s = fmaf(wf[3], x0.w, s);
+            s = fmaf(wf[4], x1.x, s);
+            s = fmaf(wf[5], x1.y, s);
+            s = fmaf(wf[6], x1.z, s);
+            s = fmaf(wf[7], x1.w, s);
+            acc[t] = s;
+        }
+    } else {
+        float s[TP];
+#pragma unroll
+        for (int t = 0; t < TP; t++) s[t] = 0.f;
+        const float* xb = xs + u;  // element j of this block at xb[j * P] (+ t * XR)
+        if constexpr (F == 1) {
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                float f[4];
+                i8x4_to_f32(r.q[i], f);
+#pragma unroll
+                for (int e = 0; e < 4; e++)
+#pragma unroll
+                    for (int t = 0; t < TP; t++) s[t] = fmaf(f[e], xb[t * XR + (4 * i + e) * P], s[t]);
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                float lo[4], hi[4];
+                n4x4_to_f32(r.q[i] & 0x0F0F0F0Fu, lo);
+                n4x4_to_f32((r.q[i] >> 4) & 0x0F0F0F0Fu, hi);
+#pragma unroll
+                for (int e = 0; e < 4; e++)
+#pragma unroll
+                    for (int t = 0; t < TP; t++) {
+                        s[t] = fmaf(lo[e], xb[t * XR + (4 * i + e) * P], s[t]);
+                        s[t] = fmaf(hi[e], xb[t * XR + (4 * i + e + 16) * P], s[t]);
+                    }
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < TP; t++) acc[t] = fmaf(r.d, s[t], acc[t]);
+    }
+}
+
+// This warp's share of NR rows at once (row n's bytes at rowp[n]; a null rowp skips it) against the TP staged rows:
+// acc[n][t] = the sum over units u = base, base + S, ... of W[row n] . xn_t. Every lane ends with the warp's sums.
+// Two units of each row per lane are loaded before any is used, so a warp keeps 2 NR loads (or blocks) in flight.
+template <int F, int TP, int NR>
+__device__ __forceinline__ void rows_dot(const ProjArgs& a, const uint8_t* const (&rowp)[NR],
+                                         const uint8_t* const (&end)[NR], const float* xs, int base, int S,
+                                         float (&acc)[NR][TP]) {
+#pragma unroll
+    for (int n = 0; n < NR; n++)
+#pragma unroll
+        for (int t = 0; t < TP; t++) acc[n][t] = 0.f;
+    const int U = a.units, XR = xs_row<F>(a.k, U), P = U + 1;
+    for (int u0 = base; u0 < U; u0 += 2 * S) {
+        UnitRegs<F> r[NR][2];
+#pragma unroll
+        for (int n = 0; n < NR; n++)
+#pragma unroll
+            for (int h = 0; h < 2; h++)
+                if (rowp[n] && u0 + h * S < U) load_unit<F>(rowp[n], end[n], u0 + h * S, r[n][h]);
+#pragma unroll
+        for (int n = 0; n < NR; n++)
+#pragma unroll
+            for (int h = 0; h < 2; h++)
+                if (rowp[n] && u0 + h * S < U) dot_unit<F, TP>(r[n][h], u0 + h * S, xs, XR, P, acc[n]);
+    }
+#pragma unroll
+    for (int n = 0; n < NR; n++)
+#pragma unroll
+        for (int t = 0; t < TP; t++)
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) acc[n][t] += __shfl_xor_sync(0xffffffffu, acc[n][t], o);
+}
+
+// L2 prefetch of bytes [p, p + n) of a matrix (16-byte aligned start, whole 16-byte units inside [p, end)).
+__device__ __forceinline__ void prefetch_l2(const uint8_t* p, int64_t n, const uint8_t* end) {
+    const uintptr_t a0 = reinterpret_cast<uintptr_t>(p) & ~uintptr_t(15);
+    const uintptr_t a1 = std::min(reinterpret_cast<uintptr_t>(p + n) + 15, reinterpret_cast<uintptr_t>(end)) &
+                         ~uintptr_t(15);
+    for (uintptr_t a = a0; a < a1; a += (1u << 20)) {
+        const uint32_t len = static_cast<uint32_t>(std::min<uintptr_t>(a1 - a, 1u << 20));
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a), "r"(len) : "memory");
+    }
+}
+
+// grid (row CTAs, token passes), 256 threads; dynamic shared memory TP staged rows. One staged row: 64 registers per
+// thread, 4 CTAs (32 warps) per SM, so each SM keeps enough weight bytes in flight (at 110 registers only 2 CTAs fit
+// and a q8_0 gate + up launch ran at 1.2 TB/s); more staged rows need the registers of their accumulators.
+template <int F, int TP>
+__global__ void __launch_bounds__(kProjThreads, TP == 1 ? 4 : 2) proj_kernel(const ProjArgs a) {
+    extern __shared__ __align__(16) float xs[];
+    __shared__ float red[kProjWarps][TP];
+    __shared__ float scale[TP];
+    // The next stream-ordered kernel may launch now; it waits for this grid before touching memory.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const bool silu = (a.flags & ALPACA_PROJ_SILU) != 0;
+    const int RPC = (kProjWarps / a.wpr) * (silu ? 1 : 2);  // output rows per CTA pass
+    if (a.prefetch && threadIdx.x == 0 && blockIdx.y == 0) {
+        // Start the DRAM reads of this CTA's weight rows into L2 at once, while the previous kernel drains and the
+        // input rows are staged (a prefetch changes no memory, so it may precede the dependency wait).
+        for (int r0 = blockIdx.x * RPC; r0 < a.total_rows; r0 += gridDim.x * RPC) {
+            const int r1 = min(r0 + RPC, a.total_rows);
+            if (silu) {
+                for (int m = 0; m < 2; m++) prefetch_l2(a.w[m] + r0 * a.row_bytes, (r1 - r0) * a.row_bytes, a.w_end[m]);
+                continue;
+            }
+            for (int m = 0, base = 0; m < 3; base += a.rows[m], m++) {
+                const int lo = max(r0, base), hi = min(r1, base + a.rows[m]);
+                if (lo < hi) prefetch_l2(a.w[m] + (lo - base) * a.row_bytes, (hi - lo) * a.row_bytes, a.w_end[m]);
+            }
+        }
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // x (and y when adding) come from the previous kernel
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int t0 = blockIdx.y * TP;
+    const int nt = min(TP, a.n_tokens - t0);
+    const int k = a.k, XR = xs_row<F>(k, a.units);
+
+    // Stage the input rows (and their sums of squares).
+    float ss[TP];
+#pragma unroll
+    for (int t = 0; t < TP; t++) ss[t] = 0.f;
+    for (int i = tid; i < k; i += kProjThreads) {
+#pragma unroll
+        for (int t = 0; t < TP; t++) {
+            const float v = t < nt ? a.x[(t0 + t) * a.x_stride + i] : 0.f;
+            xs[t * XR + xs_index<F>(i, a.units)] = v;
+            ss[t] = fmaf(v, v, ss[t]);
+        }
+    }
+    if (a.flags & ALPACA_PROJ_NORM) {
+#pragma unroll
+        for (int t = 0; t < TP; t++) {
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) ss[t] += __shfl_xor_sync(0xffffffffu, ss[t], o);
+            if (lane == 0) red[warp][t] = ss[t];
+        }
+        __syncthreads();
+        if (tid < TP) {
+            float tot = 0.f;
+#pragma unroll
+            for (int w = 0; w < kProjWarps; w++) tot += red[w][tid];
+            scale[tid] = 1.0f / sqrtf(tot / static_cast<float>(k) + a.eps);  // CPUOps.rmsNorm's scale
+        }
+        __syncthreads();
+        for (int i = tid; i < k; i += kProjThreads) {
+            const float gi = a.g[i];
+#pragma unroll
+            for (int t = 0; t < TP; t++) {
+                float* p = xs + t * XR + xs_index<F>(i, a.units);
+                *p = (*p * scale[t]) * gi;  // x * scale * w, in that order
+            }
+        }
+    }
+    __syncthreads();
+
+    // Warps [slot * wpr, slot * wpr + wpr) share their rows: each takes every wpr-th group of 32 units, and the first
+    // of them adds the others' sums from shared memory (double-buffered by pass, one barrier per pass). A warp works
+    // on two rows at once: the gate and up rows of one output (SiLU), or two consecutive output rows.
+    __shared__ float part[2][kProjWarps][2][TP];
+    const int WPR = a.wpr, slot = warp / WPR, piece = warp - slot * WPR;
+    const int RPW = silu ? 1 : 2;  // output rows per warp slot
+    int buf = 0;
+    for (int r0 = blockIdx.x * RPC; r0 < a.total_rows; r0 += gridDim.x * RPC, buf ^= 1) {  // uniform per CTA
+        int m[2] = {0, 0}, lr[2];
+        const uint8_t* rp[2] = {nullptr, nullptr};
+        const uint8_t* re[2] = {nullptr, nullptr};
+#pragma unroll
+        for (int n = 0; n < 2; n++) {
+            const int r = r0 + slot * RPW + (silu ? 0 : n);
+            lr[n] = r;
+            if (r >= a.total_rows) continue;
+            if (silu) {
+                m[n] = n;  // gate (W0) and up (W1) rows of output r
+            } else if (lr[n] >= a.rows[0]) {
+                lr[n] -= a.rows[0];
+                m[n] = 1;
+                if (lr[n] >= a.rows[1]) {
+                    lr[n] -= a.rows[1];
+                    m[n] = 2;
+                }
+            }
+            rp[n] = a.w[m[n]] + lr[n] * a.row_bytes;
+            re[n] = a.w_end[m[n]];
+        }
+        float acc[2][TP];
+        rows_dot<F, TP, 2>(a, rp, re, xs, 32 * piece + lane, 32 * WPR, acc);
+        if (WPR > 1) {
+            if (lane == 0)
+#pragma unroll
+                for (int n = 0; n < 2; n++)
+#pragma unroll
+                    for (int t = 0; t < TP; t++) part[buf][warp][n][t] = acc[n][t];
+            __syncthreads();
+            if (piece == 0)
+#pragma unroll
+                for (int n = 0; n < 2; n++)
+#pragma unroll
+                    for (int t = 0; t < TP; t++) {
+                        float sum = 0.f;
+                        for (int p = 0; p < WPR; p++) sum += part[buf][warp + p][n][t];
+                        acc[n][t] = sum;
+                    }
+        }
+        if (piece != 0 || lane != 0) continue;
+        if (silu) {
+            if (!rp[0]) continue;
+#pragma unroll
+            for (int t = 0; t < TP; t++)
+                if (t < nt) {
+                    const float gt = acc[0][t];
+                    a.y[0][(t0 + t) * a.y_stride[0] + lr[0]] = (gt / (1.0f + expf(-gt))) * acc[1][t];
+                }
+            continue;
+        }
+#pragma unroll
+        for (int n = 0; n < 2; n++) {
+            if (!rp[n]) continue;
+#pragma unroll
+            for (int t = 0; t < TP; t++)
+                if (t < nt) {
+                    float* yp = a.y[m[n]] + (t0 + t) * a.y_stride[m[n]] + lr[n];
+                    *yp = ((a.flags & ALPACA_PROJ_ADD) ? *yp : 0.f) + acc[n][t];
+                }
+        }
+    }
+}
+
+// ---- single-token path: the input slice each lane needs lives in registers.
+// A lane always multiplies the same units of every row (units piece*32 + lane + j*32*wpr), so after the CTA has
+// staged (and normalised) the input row once, each lane copies its UPL units' elements into registers and the row loop
+// is weight loads and FMAs only: no shared-memory reads in the inner loop. Each warp slot works on RR rows per pass, all
+// their loads issued before any is used; partial sums of a row's wpr pieces meet in shared memory once per pass.
+constexpr int kRegRows = 2;  // rows per warp slot per pass (SiLU: 1 output, its gate and up rows)
+
+template <int F>
+struct RegGeo {
+    static constexpr int E = F == 0 ? 8 : 32;   // elements per unit (16-byte chunk or block)
+    static constexpr int UPL = F == 0 ? 4 : 1;  // units per lane
+};
+
+template <int F>
+__global__ void __launch_bounds__(kProjThreads, 3) proj_reg_kernel(const ProjArgs a) {
+    using G = RegGeo<F>;
+    constexpr int E = G::E, UPL = G::UPL;
+    extern __shared__ __align__(16) float xs[];  // the staged input row [k]
+    __shared__ float red[kProjWarps];
+    __shared__ float scale;
+    __shared__ float part[2][kProjWarps][kRegRows];
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const bool silu = (a.flags & ALPACA_PROJ_SILU) != 0;
+    const int WPR = a.wpr, SLOTS = kProjWarps / WPR;
+    const int RPC = SLOTS * (silu ? kRegRows / 2 : kRegRows);  // output rows per CTA pass
+    if (a.prefetch && threadIdx.x == 0) {
+        for (int r0 = blockIdx.x * RPC; r0 < a.total_rows; r0 += gridDim.x * RPC) {
+            const int r1 = min(r0 + RPC, a.total_rows);
+            if (silu) {
+                for (int m = 0; m < 2; m++) prefetch_l2(a.w[m] + r0 * a.row_bytes, (r1 - r0) * a.row_bytes, a.w_end[m]);
+                continue;
+            }
+            for (int m = 0, base = 0; m < 3; base += a.rows[m], m++) {
+                const int lo = max(r0, base), hi = min(r1, base + a.rows[m]);
+                if (lo < hi) prefetch_l2(a.w[m] + (lo - base) * a.row_bytes, (hi - lo) * a.row_bytes, a.w_end[m]);
+            }
+        }
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, k = a.k, U = a.units;
+
+    // stage the row (sum of squares alongside), normalise in place when asked
+    float ss = 0.f;
+    for (int i = tid; i < k; i += kProjThreads) {
+        const float v = a.x[i];
+        xs[i] = v;
+        ss = fmaf(v, v, ss);
+    }
+    if (a.flags & ALPACA_PROJ_NORM) {
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        if (tid == 0) {
+            float tot = 0.f;
+#pragma unroll
+            for (int w = 0; w < kProjWarps; w++) tot += red[w];
+            scale = 1.0f / sqrtf(tot / static_cast<float>(k) + a.eps);  // CPUOps.rmsNorm's scale
+        }
+        __syncthreads();
+        for (int i = tid; i < k; i += kProjThreads) xs[i] = (xs[i] * scale) * a.g[i];  // x * scale * w
+    }
+    __syncthreads();
+
+    // this lane's units and their input elements
+    const int slot = warp / WPR, piece = warp - slot * WPR;
+    int uidx[UPL];
+    float xr[UPL][E];
+#pragma unroll
+    for (int j = 0; j < UPL; j++) {
+        uidx[j] = piece * 32 + lane + j * 32 * WPR;
+        const bool in = uidx[j] < U;
+#pragma unroll
+        for (int e = 0; e < E; e += 4) {
+            const float4 v = in ? *reinterpret_cast<const float4*>(xs + uidx[j] * E + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+            xr[j][e] = v.x;
+            xr[j][e + 1] = v.y;
+            xr[j][e + 2] = v.z;
+            xr[j][e + 3] = v.w;
+        }
+    }
+
+    int buf = 0;
+    for (int r0 = blockIdx.x * RPC; r0 < a.total_rows; r0 += gridDim.x * RPC, buf ^= 1) {  // uniform per CTA
+        // the slot's rows: SiLU: gate / up of outputs o0, o0 + 1; otherwise kRegRows consecutive outputs
+        const uint8_t* rp[kRegRows];
+        const uint8_t* re[kRegRows];
+#pragma unroll
+        for (int n = 0; n < kRegRows; n++) {
+            int r, m = 0;
+            if (silu) {
+                r = r0 + slot * (kRegRows / 2) + n / 2;
+                m = n & 1;
+            } else {
+                r = r0 + slot * kRegRows + n;
+            }
+            rp[n] = nullptr;
+            re[n] = nullptr;
+            if (r >= a.total_rows) continue;
+            int lr = r;
+            if (!silu && lr >= a.rows[0]) {
+                lr -= a.rows[0];
+                m = 1;
+                if (lr >= a.rows[1]) {
+                    lr -= a.rows[1];
+                    m = 2;
+                }
+            }
+            rp[n] = a.w[m] + lr * a.row_bytes;
+            re[n] = a.w_end[m];
+        }
+        UnitRegs<F> w[kRegRows][UPL];
+#pragma unroll
+        for (int n = 0; n < kRegRows; n++)
+#pragma unroll
+            for (int j = 0; j < UPL; j++)
+                if (rp[n] && uidx[j] < U) load_unit<F>(rp[n], re[n], uidx[j], w[n][j]);
+        float acc[kRegRows];
+#pragma unroll
+        for (int n = 0; n < kRegRows; n++) {
+            float sacc = 0.f;
+#pragma unroll
+            for (int j = 0; j < UPL; j++) {
+                if (!rp[n] || uidx[j] >= U) continue;
+                if constexpr (F == 0) {
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[n][j].q[i]));
+                        sacc = fmaf(f.x, xr[j][2 * i], sacc);
+                        sacc = fmaf(f.y, xr[j][2 * i + 1], sacc);
+                    }
+                } else if constexpr (F == 1) {
+                    float sb = 0.f;
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        float f[4];
+                        i8x4_to_f32(w[n][j].q[i], f);
+#pragma unroll
+                        for (int e = 0; e < 4; e++) sb = fmaf(f[e], xr[j][4 * i + e], sb);
+                    }
+                    sacc = fmaf(w[n][j].d, sb, sacc);
+                } else {
+                    float sb = 0.f;
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        float lo[4], hi[4];
+                        n4x4_to_f32(w[n][j].q[i] & 0x0F0F0F0Fu, lo);
+                        n4x4_to_f32((w[n][j].q[i] >> 4) & 0x0F0F0F0Fu, hi);
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            sb = fmaf(lo[e], xr[j][4 * i + e], sb);
+                            sb = fmaf(hi[e], xr[j][4 * i + e + 16], sb);
+                        }
+                    }
+                    sacc = fmaf(w[n][j].d, sb, sacc);
+                }
+            }
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) sacc += __shfl_xor_sync(0xffffffffu, sacc, o);
+            acc[n] = sacc;
+        }
+        if (WPR > 1) {
+            if (lane == 0)
+#pragma unroll
+                for (int n = 0; n < kRegRows; n++) part[buf][warp][n] = acc[n];
+            __syncthreads();
+            if (piece == 0)
+#pragma unroll
+                for (int n = 0; n < kRegRows; n++) {
+                    float sum = 0.f;
+                    for (int p = 0; p < WPR; p++) sum += part[buf][warp + p][n];
+                    acc[n] = sum;
+                }
+        }
+        if (piece != 0 || lane != 0) continue;
+        if (silu) {
+#pragma unroll
+            for (int o = 0; o < kRegRows / 2; o++) {
+                if (!rp[2 * o]) continue;
+                const int out = r0 + slot * (kRegRows / 2) + o;
+                const float gt = acc[2 * o];
+                a.y[0][out] = (gt / (1.0f + expf(-gt))) * acc[2 * o + 1];
+            }
+            continue;
+        }
+#pragma unroll
+        for (int n = 0; n < kRegRows; n++) {
+            if (!rp[n]) continue;
+            int lr = r0 + slot * kRegRows + n, m = 0;
+            if (lr >= a.rows[0]) {
+                lr -= a.rows[0];
+                m = 1;
+                if (lr >= a.rows[1]) {
+                    lr -= a.rows[1];
+                    m = 2;
+                }
+            }
+            float* yp = a.y[m] + lr;
+            *yp = ((a.flags & ALPACA_PROJ_ADD) ? *yp : 0.f) + acc[n];
+        }
+    }
+}
+
+int proj_env(const char* name, int fallback) {
+    const char* e = std::getenv(name);
+    return (e && *e) ? std::atoi(e) : fallback;
+}
+int proj_ctas_per_sm(int fallback) {
+    static const int v = proj_env("ALPACA_PROJ_CTAS", 0);
+    return v > 0 ? v : fallback;
+}
+
+// Single-token launch of the register form: wpr from the lane's unit count, the row staged in shared memory.
+template <int F>
+cudaError_t launch_reg(ProjArgs a, int num_sms, cudaStream_t s) {
+    constexpr int per_warp = 32 * RegGeo<F>::UPL;  // units one warp covers
+    const int want = (a.units + per_warp - 1) / per_warp;
+    a.wpr = want >= 8 ? 8 : (want >= 4 ? 4 : (want >= 2 ? 2 : 1));
+    const size_t smem = sizeof(float) * static_cast<size_t>(a.k);
+    const auto fn = proj_reg_kernel<F>;
+    if (smem > 48 * 1024) {
+        const cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+    }
+    const bool silu = (a.flags & ALPACA_PROJ_SILU) != 0;
+    const int rpc = (kProjWarps / a.wpr) * (silu ? kRegRows / 2 : kRegRows);
+    const int row_ctas = (a.total_rows + rpc - 1) / rpc;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(std::max(1, std::min(row_ctas, num_sms * proj_ctas_per_sm(3))), 1, 1);
+    cfg.blockDim = dim3(kProjThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, fn, a);
+}
+
+// Whether the register form covers k: at most 8 warps of 32 lanes x UPL units per row.
+bool reg_form_fits(int format, int k) {
+    return format == ALPACA_W_F16 ? k <= 8 * 32 * 4 * 8 : k <= 8 * 32 * 32;
+}
+
+template <int F>
+cudaError_t launch_f(const ProjArgs& a, int tp, int num_sms, cudaStream_t s) {
+    using Fn = void (*)(ProjArgs);
+    Fn fn = tp == 1 ? proj_kernel<F, 1> : (tp == 2 ? proj_kernel<F, 2> : proj_kernel<F, 4>);
+    const int tpk = tp;  // 1, 2 or 4 rows staged per pass
+    const size_t smem = sizeof(float) * static_cast<size_t>(tpk) * xs_row<F>(a.k, a.units);
+    if (smem > 48 * 1024) {
+        const cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+    }
+    const int rpc = (kProjWarps / a.wpr) * ((a.flags & ALPACA_PROJ_SILU) ? 1 : 2);
+    const int row_ctas = (a.total_rows + rpc - 1) / rpc;
+    const int resident = proj_ctas_per_sm(tpk == 1 ? 4 : 2);  // CTAs per SM under the launch bounds
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(std::max(1, std::min(row_ctas, num_sms * resident)), (a.n_tokens + tpk - 1) / tpk, 1);
+    cfg.blockDim = dim3(kProjThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, fn, a);
+}
+
+}  // namespace
+
+int64_t proj_row_bytes(int format, int k) {
+    switch (format) {
+        case ALPACA_W_F16: return 2 * static_cast<int64_t>(k);
+        case ALPACA_W_Q8_0: return static_cast<int64_t>(k / 32) * 34;
+        case ALPACA_W_Q4_0: return static_cast<int64_t>(k / 32) * 18;
+        default: return 0;
+    }
+}
+
+// Input rows staged per pass: 4, 2 or 1, as the shared-memory budget allows for rows of k (+ 32 pad) floats.
+int proj_max_tokens_per_pass(int k) {
+    const size_t by_smem = kProjSmemBudget / (sizeof(float) * static_cast<size_t>(k + 32));
+    return by_smem >= kProjMaxTokens ? kProjMaxTokens : (by_smem >= 2 ? 2 : 1);
+}
+
+cudaError_t launch_proj(const alpaca_proj_desc& d, int num_sms, cudaStream_t s) {
+    ProjArgs a;
+    const bool silu = (d.flags & ALPACA_PROJ_SILU) != 0;
+    a.row_bytes = proj_row_bytes(d.format, d.k);
+    for (int i = 0; i < 3; i++) {
+        const int mi = silu ? (i < 2 ? i : 1) : i;
+        const int rows = silu ? d.rows[0] : d.rows[i];
+        a.w[i] = static_cast<const uint8_t*>(d.w[mi] ? d.w[mi] : d.w[0]);
+        a.w_end[i] = a.w[i] + static_cast<int64_t>(rows) * a.row_bytes;
+        a.rows[i] = silu ? (i == 0 ? d.rows[0] : 0) : d.rows[i];
+        a.y[i] = d.y[i] ? d.y[i] : d.y[0];
+        a.y_stride[i] = d.y[i] ? d.y_stride[i] : d.y_stride[0];
+    }
+    a.total_rows = silu ? d.rows[0] : d.rows[0] + d.rows[1] + d.rows[2];
+    a.k = d.k;
+    a.units = d.format == ALPACA_W_F16 ? d.k / 8 : d.k / 32;
+    a.flags = d.flags;
+    a.eps = d.eps;
+    a.x = d.x;
+    a.x_stride = d.x_stride;
+    a.g = d.norm_weight;
+    a.n_tokens = d.n_tokens;
+    // warps per row: about two units (16-byte chunks or blocks) per lane per row, up to the CTA's 8 warps
+    const int want = (a.units + 63) / 64;
+    a.wpr = want >= 8 ? 8 : (want >= 4 ? 4 : (want >= 2 ? 2 : 1));
+    static const int wpr_cap = proj_env("ALPACA_PROJ_WPR", 8);
+    a.wpr = std::min(a.wpr, std::max(1, wpr_cap));
+    static const int prefetch = proj_env("ALPACA_PROJ_PREFETCH", 1);
+    a.prefetch = prefetch;
+    const int cap = proj_max_tokens_per_pass(d.k);
+    const int tp = d.n_tokens >= cap ? cap : (d.n_tokens == 1 ? 1 : (d.n_tokens == 2 ? 2 : std::min(cap, 4)));
+    static const int reg_form = proj_env("ALPACA_PROJ_REG", 1);
+    if (d.n_tokens == 1 && reg_form && reg_form_fits(d.format, d.k)) {
+        switch (d.format) {
+            case ALPACA_W_F16: return launch_reg<0>(a, num_sms, s);
+            case ALPACA_W_Q8_0: return launch_reg<1>(a, num_sms, s);
+            default: return launch_reg<2>(a, num_sms, s);
+        }
+    }
+    switch (d.format) {
+        case ALPACA_W_F16: return launch_f<0>(a, tp, num_sms, s);
+        case ALPACA_W_Q8_0: return launch_f<1>(a, tp, num_sms, s);
+        default: return launch_f<2>(a, tp, num_sms, s);
+    }
+}
+
+}  // namespace alpaca

@@ -39,6 +39,10 @@ cudaError_t launch_general(const Call& c, cudaStream_t s);
 int rope_max_head_dim();
 cudaError_t launch_rope_kv(const alpaca_rope_desc& d, unsigned* err, cudaStream_t s);
 
+// ---- fused decode projections (decode_proj.cu)
+int64_t proj_row_bytes(int format, int k);  // bytes of one weight row (0 for an unknown format)
+cudaError_t launch_proj(const alpaca_proj_desc& d, int num_sms, cudaStream_t s);
+
 // ---- tcgen05 prefill (attn_prefill_sm100.cu)
 bool prefill_supported(const alpaca_attn_desc& d);
 size_t prefill_workspace_bytes(const alpaca_attn_desc& d);  // f32 -> f16 Q staging when q_dtype is f32

@@ -20,7 +20,8 @@ import ctypes
 import numpy as np
 import torch
 
-from ._lib import FLAG_VARLEN, AlpacaCUDAError, AttnDesc, DType, Kernel, RopeDesc, Status, check, load
+from ._lib import (FLAG_VARLEN, PROJ_ADD, PROJ_NORM, PROJ_SILU, AlpacaCUDAError, AttnDesc, DType, Kernel,
+                   ProjDesc, RopeDesc, Status, WeightFormat, check, load)
 
 KV_PADDING_ROWS = 32  # KernelEncoder.kvPaddingRows (KernelEncoder.swift:73)
 
@@ -305,3 +306,59 @@ def rope(x: np.ndarray, start_position: int, theta: float, interleaved: bool = T
     rope_kv_append(t, None, None, None, None, theta=theta, start_position=start_position, interleaved=interleaved)
     torch.cuda.synchronize()
     return t.cpu().numpy()
+
+
+# ---------------------------------------------------------------------------------------------- decode projections
+
+_WF = {"f16": WeightFormat.F16, "q8_0": WeightFormat.Q8_0, "q4_0": WeightFormat.Q4_0}
+
+
+def make_proj_desc(weights: list[torch.Tensor], fmt: str, k: int, x: torch.Tensor, outs: list[torch.Tensor], *,
+                   norm_weight: torch.Tensor | None = None, eps: float = 1e-5, silu_gate: bool = False,
+                   add: bool = False) -> ProjDesc:
+    """Descriptor of alpaca_decode_project: weights are CUDA uint8 [rows, row bytes] tensors in `fmt` ("f16", "q8_0",
+    "q4_0"; f16 may also be given as float16 [rows, k]), x f32 [tokens, >= k], outs f32 [tokens, >= rows_i] (one
+    per matrix; one for silu_gate, which takes the gate and up matrices)."""
+    if fmt not in _WF:
+        raise AlpacaCUDAError(Status.UNSUPPORTED, f"weight format {fmt!r}")
+    if not 1 <= len(weights) <= (2 if silu_gate else 3) or len(outs) != (1 if silu_gate else len(weights)):
+        raise AlpacaCUDAError(Status.INVALID_ARGUMENT, "project: 1-3 matrices with one output each (silu: 2 and 1)")
+    x2 = x if x.dim() == 2 else x.reshape(1, -1)
+    d = ProjDesc()
+    d.n_tokens, d.k, d.format = x2.shape[0], int(k), int(_WF[fmt])
+    d.flags = (PROJ_NORM if norm_weight is not None else 0) | (PROJ_SILU if silu_gate else 0) | (PROJ_ADD if add else 0)
+    d.eps = float(eps)
+    for i, w in enumerate(weights):
+        if not w.is_cuda or not w.is_contiguous():
+            raise AlpacaCUDAError(Status.INVALID_ARGUMENT, "project: weights must be contiguous CUDA tensors")
+        d.w[i] = w.data_ptr()
+        if i == 0 or not silu_gate:
+            d.rows[i] = w.shape[0]
+    if silu_gate:
+        d.rows[1] = 0
+    for i, o in enumerate(outs):
+        o2 = o if o.dim() == 2 else o.reshape(1, -1)
+        if o2.dtype != torch.float32 or o2.stride(-1) != 1:
+            raise AlpacaCUDAError(Status.INVALID_ARGUMENT, "project: outputs must be f32 rows")
+        d.y[i], d.y_stride[i] = o2.data_ptr(), o2.stride(0)
+    if x2.dtype != torch.float32 or x2.stride(-1) != 1:
+        raise AlpacaCUDAError(Status.INVALID_ARGUMENT, "project: x must be f32 rows")
+    d.x, d.x_stride = x2.data_ptr(), x2.stride(0)
+    if norm_weight is not None:
+        d.norm_weight = norm_weight.data_ptr()
+    return d
+
+
+def project_launch(desc: ProjDesc, stream: torch.cuda.Stream | None = None) -> None:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    check(load().alpaca_decode_project(ctypes.byref(desc), ctypes.c_void_p(s.cuda_stream)))
+
+
+def decode_project(weights: list[torch.Tensor], fmt: str, k: int, x: torch.Tensor, outs: list[torch.Tensor], *,
+                   norm_weight: torch.Tensor | None = None, eps: float = 1e-5, silu_gate: bool = False,
+                   add: bool = False, stream: torch.cuda.Stream | None = None) -> ProjDesc:
+    """Enqueue the fused decode projection (KernelEncoder.decodeQKV / decodeProjection / decodeGateUp,
+    KernelEncoder.swift:386-400) on device tensors; see make_proj_desc."""
+    d = make_proj_desc(weights, fmt, k, x, outs, norm_weight=norm_weight, eps=eps, silu_gate=silu_gate, add=add)
+    project_launch(d, stream)
+    return d

@@ -12,6 +12,8 @@ The same JSON line carries the other measured legs, each with its own timing, cl
   e2e / e2e_f16_out  the headline step through the C ABI with pinned host buffers, copies inside the timed region
   decode             config 3: split-KV decode (batch 64, one token each, contexts U[1,4096], 30 layers of f16 caches)
   rope_kv_append     the RoPE + KV-cache append upstream of the attention, config-2 shape
+  decode_proj        the fused decode projections around the attention (norm + QKV, out + residual, gate/up + SiLU,
+                     down + residual), one token through the 24 q8_0 layers of SmolLM2-1.7B
   cfg4               config 4: 8 x 4096 tokens at 15/5 heads (SmolLM2-360M), strong scaling: the 40 (sequence, KV-head)
                      units split over the ranks
   cfg5               config 5: the SmolLM2-1.7B ragged mixed batch (256 prefill sequences, lengths log-uniform in
@@ -530,6 +532,62 @@ def leg_rope(c: Ctx):
             "clocks": clk, "gpu_launches": steps * LAY}
 
 
+PROJ_LAYERS, PROJ_HIDDEN, PROJ_FFN = 24, 2048, 8192  # SmolLM2-1.7B
+
+
+def leg_proj(c: Ctx):
+    """The fused decode projections around the attention of one token through the 24 layers of SmolLM2-1.7B (hidden
+    2048, 32/32 heads of 64, FFN 8192) with q8_0 weights, as alpaca.swift's fused decode path issues them
+    (MetalLlamaModel.swift:344-354): per layer Q/K/V with the attention norm, the out-projection added to the
+    residual, gate + up with the FFN norm and SiLU, down added to the residual. 71.3 MB of weights per layer, 1.71 GB
+    per step (>> L2), 96 launches per step replayed from a CUDA graph. HBM-bound: GB/s of weight bytes."""
+    torch, ab, args = c.torch, c.ab, c.args
+    Hd, F = PROJ_HIDDEN, PROJ_FFN
+    g = torch.Generator(device=c.dev)
+    g.manual_seed(20260107 + 1000 * c.rank)
+
+    def q8(rows, k):  # random int8 weights with a fixed f16 scale per 32-weight block
+        w = torch.randint(-127, 128, (rows, k // 32, 34), generator=g, device=c.dev, dtype=torch.int8).view(torch.uint8)
+        w[:, :, 0:2] = torch.tensor([0.002], dtype=torch.float16).view(torch.uint8).to(c.dev)
+        return w.reshape(rows, k // 32 * 34).contiguous()
+
+    layers = []
+    for _ in range(PROJ_LAYERS):
+        layers.append(dict(q=q8(Hd, Hd), k=q8(Hd, Hd), v=q8(Hd, Hd), o=q8(Hd, Hd), gate=q8(F, Hd), up=q8(F, Hd),
+                           down=q8(Hd, F), ga=torch.ones(Hd, device=c.dev), gf=torch.ones(Hd, device=c.dev)))
+    x = torch.randn((1, Hd), generator=g, device=c.dev)
+    qo, ko, vo = (torch.empty((1, Hd), device=c.dev) for _ in range(3))
+    gate = torch.empty((1, F), device=c.dev)
+    descs = []
+    for L in layers:
+        descs.append(ab.make_proj_desc([L["q"], L["k"], L["v"]], "q8_0", Hd, x, [qo, ko, vo], norm_weight=L["ga"]))
+        descs.append(ab.make_proj_desc([L["o"]], "q8_0", Hd, qo, [x], add=True))  # the attention output stands in
+        descs.append(ab.make_proj_desc([L["gate"], L["up"]], "q8_0", Hd, x, [gate], norm_weight=L["gf"],
+                                       silu_gate=True))
+        descs.append(ab.make_proj_desc([L["down"]], "q8_0", F, gate, [x], add=True))
+
+    def step():
+        for d in descs:
+            ab.project_launch(d)
+
+    gr = c.graph(step)
+    steps = max(5, args.steps)
+    ms, ms_max, clk = c.timed(gr.replay, steps, max(3, args.warmup))
+    del gr
+    wbytes = float(sum(t.numel() for L in layers for key, t in L.items() if key not in ("ga", "gf")))
+    gbs = wbytes / (ms * 1e-3) / 1e9
+    return {"workload": f"fused decode projections, SmolLM2-1.7B shape (hidden {Hd}, FFN {F}), q8_0 weights, one token "
+                        f"through {PROJ_LAYERS} layers: QKV + norm, out-proj + residual, gate/up + norm + SiLU, down + "
+                        "residual per layer, replayed from a CUDA graph",
+            "value": c.world * wbytes / (ms_max * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms_max,
+            "tokens_per_s": c.world / (ms_max * 1e-3), "bytes_per_step": wbytes,
+            "l2": f"{wbytes / 1e9:.2f} GB of weights per step vs 126 MB L2 (no flush)",
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": c.pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": gbs / c.pk["hbm_gbs"], "traffic": None,
+                         "kernel": "alpaca::proj_kernel<q8_0> per projection"},
+            "clocks": clk, "gpu_launches": steps * PROJ_LAYERS * 4}
+
+
 def _spot_rows(T: int, heads: int):
     return sorted({0, 1, min(129, T - 1), T - 1, min(T + 5, heads * T - 1), heads * T - 1})
 
@@ -745,6 +803,8 @@ def run_ours(args):
     torch.cuda.empty_cache()
     rope_kv = leg_rope(c) if not args.no_rope else None
     torch.cuda.empty_cache()
+    proj = leg_proj(c) if not args.no_proj else None
+    torch.cuda.empty_cache()
     cfg4 = leg_cfg4(c) if not args.no_cfg4 else None
     torch.cuda.empty_cache()
     cfg5 = leg_cfg5(c) if not args.no_cfg5 else None
@@ -783,6 +843,7 @@ def run_ours(args):
             "spot_check_max_abs": p2["spot"],
             "decode": decode,
             "rope_kv_append": rope_kv,
+            "decode_proj": proj,
             "cfg4": cfg4,
             "cfg5": cfg5,
             "gather_ms": gather_ms,
@@ -842,7 +903,7 @@ def main():
     ap.add_argument("--tokens", type=int, default=T_PREFILL)
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--dec-layers", type=int, default=LAYERS)
-    for leg in ("decode", "rope", "cpu", "e2e", "cfg4", "cfg5"):
+    for leg in ("decode", "rope", "proj", "cpu", "e2e", "cfg4", "cfg5"):
         ap.add_argument(f"--no-{leg}", action="store_true")
     ap.add_argument("--e2e-chunk", type=int, default=0, help="sequences per ABI call in the e2e pipeline (0: 1/6 of them)")
     ap.add_argument("--cpu-seconds", type=float, default=3.0, help="minimum seconds of the all-thread CPU baseline")

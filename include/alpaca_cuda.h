@@ -253,6 +253,46 @@ alpaca_cuda_status alpaca_rope_kv_append(const alpaca_rope_desc* desc, alpaca_st
 alpaca_cuda_status alpaca_attn_decode_rope(const alpaca_attn_desc* attn, const alpaca_rope_desc* rope,
                                            void* workspace, size_t workspace_bytes, alpaca_stream_t stream);
 
+/* ---- Fused decode projections: the mat-vec steps around the attention in a single-token decode step. */
+
+/* Weight formats of alpaca_proj_desc: f16 rows, or GGUF blocks of 32 weights (q8_0: f16 scale + 32 int8, 34 bytes;
+ * q4_0: f16 scale + 16 bytes whose low / high nibbles hold weights j / j + 16 as value + 8, 18 bytes). */
+typedef enum alpaca_weight_format {
+    ALPACA_W_F16 = 0,
+    ALPACA_W_Q8_0 = 1,
+    ALPACA_W_Q4_0 = 2
+} alpaca_weight_format;
+
+#define ALPACA_PROJ_NORM 1u /* RMS-normalise each input row first: x * (1 / sqrt(mean(x^2) + eps)) * norm_weight */
+#define ALPACA_PROJ_SILU 2u /* y[0] = silu(W0 . xn) * (W1 . xn): the SwiGLU gate + up pair (rows[0] rows each) */
+#define ALPACA_PROJ_ADD 4u  /* y_i += W_i . xn instead of y_i = W_i . xn: the projection with its residual */
+
+/* y_i[t] = W_i . xn_t for the n_tokens input rows x_t (xn_t = x_t, or RMS-normalised with ALPACA_PROJ_NORM), up to
+ * three matrices in one launch (Q, K and V: rows[0..2]), all in one format, f32 accumulation, f32 outputs. */
+typedef struct alpaca_proj_desc {
+    int32_t n_tokens;         /* input rows (one token, or one per sequence of a batched decode step), >= 1 */
+    int32_t k;                /* input width: a multiple of 32, <= 16384 */
+    int32_t rows[3];          /* output rows of W0, W1, W2 (0 for an absent matrix); ALPACA_PROJ_SILU: rows[0] rows
+                                 in both W0 and W1, rows[1] = rows[2] = 0 */
+    int32_t format;           /* alpaca_weight_format of every matrix */
+    uint32_t flags;           /* ALPACA_PROJ_* */
+    float eps;                /* RMSNorm epsilon (> 0) with ALPACA_PROJ_NORM */
+    const void* w[3];         /* DEVICE weight matrices [rows_i][k] in `format`, 16-byte aligned */
+    const float* x;           /* DEVICE input rows [n_tokens][x_stride] */
+    int64_t x_stride;         /* elements between input rows, >= k */
+    const float* norm_weight; /* DEVICE RMSNorm weight [k] (ALPACA_PROJ_NORM) */
+    float* y[3];              /* DEVICE outputs [n_tokens][y_stride[i]] of matrix i (SILU: y[0] only) */
+    int64_t y_stride[3];      /* elements between output rows, >= rows[i] */
+} alpaca_proj_desc;
+
+/* Enqueue the fused projection on `stream`. Replaces KernelEncoder.decodeQKV (norm + Q / K / V),
+ * decodeProjection (optional norm, optional residual add: the out- and down-projections and the final logits) and
+ * decodeGateUp (norm + SwiGLU gate and up) (Sources/AlpacaMetal/Backend/KernelEncoder.swift:386-400) and their
+ * kernels dec_f16 / dec_q8_0 / dec_q4_0 (Sources/AlpacaMetal/Kernels/decode_fused.metal:32-122). alpaca.swift
+ * runs these for one token (KernelEncoder.canFuseDecode, :362-366); n_tokens > 1 serves a batched decode step, every
+ * weight read once per pass of up to 4 rows (larger batches belong to a GEMM). */
+alpaca_cuda_status alpaca_decode_project(const alpaca_proj_desc* desc, alpaca_stream_t stream);
+
 /* Synchronises `stream`, then reports and (when `clear` != 0) resets the device-side error word of that stream on the
  * current device: ALPACA_CUDA_ERR_DEVICE_TIMEOUT when a bounded wait gave up, ALPACA_CUDA_ERR_INVALID_ARGUMENT when
  * a device-side contract check failed (a block-table entry outside the pool, a ctx_lens entry outside

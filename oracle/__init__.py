@@ -29,7 +29,8 @@ _f64p = ctypes.POINTER(ctypes.c_double)
 
 def build(force: bool = False) -> Path:
     """Compile liboracle.so with the committed Makefile (gcc, no fast-math, no FMA contraction)."""
-    srcs = [_HERE / n for n in ("cpu_attention.c", "cpu_attention.h", "cpu_rope.c", "cpu_rope.h")]
+    srcs = [_HERE / n for n in ("cpu_attention.c", "cpu_attention.h", "cpu_rope.c", "cpu_rope.h", "cpu_proj.c",
+                                "cpu_proj.h")]
     if force or not _LIB_PATH.exists() or any(_LIB_PATH.stat().st_mtime < p.stat().st_mtime for p in srcs):
         subprocess.run(["make", "-s", "-C", str(_HERE), "liboracle.so"], check=True)
     return _LIB_PATH
@@ -64,6 +65,19 @@ def lib() -> ctypes.CDLL:
         L.oracle_rope.argtypes = [_f32p] + [ctypes.c_int] * 4 + [ctypes.c_double, ctypes.c_int]
         L.oracle_rope_kv_append.argtypes = ([_f32p, _f32p, _f32p, _f32p, _f32p] + [ctypes.c_int] * 5 +
                                             [ctypes.c_double, ctypes.c_int, ctypes.c_int])
+        L.oracle_row_bytes.restype = ctypes.c_int64
+        L.oracle_row_bytes.argtypes = [ctypes.c_int, ctypes.c_int]
+        L.oracle_row_dot.restype = ctypes.c_float
+        L.oracle_row_dot.argtypes = [ctypes.c_int, ctypes.c_void_p, _f32p, ctypes.c_int]
+        L.oracle_rmsnorm.argtypes = [_f32p, _f32p, ctypes.c_int64, ctypes.c_int, ctypes.c_float, _f32p]
+        L.oracle_silu.restype = ctypes.c_float
+        L.oracle_silu.argtypes = [ctypes.c_float]
+        L.oracle_dequantize.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_int64, _f32p]
+        L.oracle_quantize.argtypes = [ctypes.c_int, _f32p, ctypes.c_int64, ctypes.c_void_p]
+        L.oracle_decode_project.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_int), ctypes.c_uint,
+                                            ctypes.c_float, ctypes.POINTER(ctypes.c_void_p), _f32p, ctypes.c_int,
+                                            ctypes.c_int64, _f32p, ctypes.POINTER(ctypes.c_void_p),
+                                            ctypes.POINTER(ctypes.c_int64)]
         _lib = L
     return _lib
 
@@ -188,6 +202,89 @@ def rope_kv_append(q, k, v, k_cache, v_cache, start: int, theta: float, interlea
     lib().oracle_rope_kv_append(_p32(q), _p32(k), _p32(v), _p32(kc), _p32(vc), T, H, Hkv, D, int(start),
                                 float(np.float32(theta)), int(bool(interleaved)), int(bool(cache_f16)))
     return q, kc, vc
+
+
+# ---------------------------------------------------------------------------------------------- projections
+
+WEIGHT_FORMATS = {"f16": 0, "q8_0": 1, "q4_0": 2, "f32": 3}
+
+
+def row_bytes(fmt: str, k: int) -> int:
+    return int(lib().oracle_row_bytes(WEIGHT_FORMATS[fmt], k))
+
+
+def quantize(values, fmt: str) -> np.ndarray:
+    """quantize() (Quantization.swift:39-73): f32 values (a multiple of 32, row-major [n, k]) -> GGUF blocks (uint8)."""
+    v = np.ascontiguousarray(values, np.float32)
+    k = v.shape[-1]
+    n = v.size // k
+    if fmt == "f16":
+        return np.frombuffer(f16_round(v).astype(np.float16).tobytes(), np.uint8).reshape(n, 2 * k).copy()
+    out = np.zeros(n * row_bytes(fmt, k), np.uint8)
+    lib().oracle_quantize(WEIGHT_FORMATS[fmt], _p32(v), v.size, out.ctypes.data)
+    return out.reshape(n, row_bytes(fmt, k))
+
+
+def dequantize(blocks, fmt: str, n: int, k: int) -> np.ndarray:
+    """dequantize() (Quantization.swift:9-35) of [n, k] weights stored as `fmt` rows."""
+    b = np.ascontiguousarray(blocks, np.uint8)
+    out = np.empty(n * k, np.float32)
+    lib().oracle_dequantize(WEIGHT_FORMATS[fmt], b.ctypes.data, n * k, _p32(out))
+    return out.reshape(n, k)
+
+
+def linear(x, blocks, fmt: str, n: int) -> np.ndarray:
+    """CPUOps.linear (CPUOps.swift:77-105): y[m, n] = x[m, k] . W[n, k]^T with CPUOps.dot per row."""
+    x = np.ascontiguousarray(x, np.float32)
+    m, k = x.shape
+    b = np.ascontiguousarray(blocks, np.uint8).reshape(n, -1)
+    y = np.empty((m, n), np.float32)
+    L = lib()
+    for i in range(m):
+        xi = np.ascontiguousarray(x[i])
+        for r in range(n):
+            y[i, r] = L.oracle_row_dot(WEIGHT_FORMATS[fmt], b[r].ctypes.data, _p32(xi), k)
+    return y
+
+
+def rmsnorm(x, w, eps: float) -> np.ndarray:
+    """CPUOps.rmsNorm (CPUOps.swift:144-158) over the last dimension."""
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    d = x.shape[-1]
+    out = np.empty_like(x)
+    lib().oracle_rmsnorm(_p32(x), _p32(w), x.size // d, d, float(eps), _p32(out))
+    return out
+
+
+def silu(x) -> np.ndarray:
+    """CPUOps.silu (CPUOps.swift:49-53)."""
+    f = lib().oracle_silu
+    return np.array([f(float(v)) for v in np.asarray(x, np.float32).reshape(-1)], np.float32).reshape(np.shape(x))
+
+
+def decode_project(fmt: str, weights, x, *, norm_weight=None, eps: float = 1e-5, silu_gate: bool = False,
+                   add_to=None) -> list[np.ndarray]:
+    """The fused projection of the dec_* kernels (decode_fused.metal:32-122) on the CPU path: x [tokens, k] f32,
+    optionally RMS-normalised (norm_weight [k]), then each weight matrix (GGUF rows, list of up to 3 [n_i, row
+    bytes] uint8 arrays) applied; silu_gate: [silu(W0 xn) * (W1 xn)]; add_to: list of [tokens, n_i] arrays the
+    results are added to (residual). Returns the outputs."""
+    x = np.ascontiguousarray(x, np.float32)
+    T, k = x.shape
+    mats = [np.ascontiguousarray(w, np.uint8) for w in weights]
+    rows = [m.shape[0] for m in mats] + [0] * (3 - len(mats))
+    if silu_gate:
+        rows = [rows[0], 0, 0]
+    outs = [np.array(add_to[i], np.float32, copy=True) if add_to is not None else np.zeros((T, rows[i]), np.float32)
+            for i in range(1 if silu_gate else len(mats))]
+    flags = (1 if norm_weight is not None else 0) | (2 if silu_gate else 0) | (4 if add_to is not None else 0)
+    wp = (ctypes.c_void_p * 3)(*[mats[min(i, len(mats) - 1)].ctypes.data for i in range(3)])
+    yp = (ctypes.c_void_p * 3)(*[outs[min(i, len(outs) - 1)].ctypes.data for i in range(3)])
+    ys = (ctypes.c_int64 * 3)(*[outs[min(i, len(outs) - 1)].shape[1] for i in range(3)])
+    g = np.ascontiguousarray(norm_weight if norm_weight is not None else np.zeros(k), np.float32)
+    lib().oracle_decode_project(WEIGHT_FORMATS[fmt], k, (ctypes.c_int * 3)(*rows), flags, float(eps), wp, _p32(x), T,
+                                k, _p32(g), yp, ys)
+    return outs
 
 
 def rows_mask(rows, T: int, H: int) -> np.ndarray:

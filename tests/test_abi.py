@@ -182,11 +182,12 @@ def test_descriptor_layouts_match_the_c_compiler(tmp_path):
     import shutil
     import subprocess
 
-    from alpaca_b200 import AttnDesc, RopeDesc
+    from alpaca_b200 import AttnDesc, ProjDesc, RopeDesc
     if not shutil.which("gcc"):
         pytest.skip("gcc not available")
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "alpaca_cuda.h"', 'int main(void) {']
-    for cname, cls in (("alpaca_attn_desc", AttnDesc), ("alpaca_rope_desc", RopeDesc)):
+    structs = (("alpaca_attn_desc", AttnDesc), ("alpaca_rope_desc", RopeDesc), ("alpaca_proj_desc", ProjDesc))
+    for cname, cls in structs:
         lines.append(f'printf("{cname} size %zu\\n", sizeof({cname}));')
         for f, _ in cls._fields_:
             lines.append(f'printf("{cname} {f} %zu\\n", offsetof({cname}, {f}));')
@@ -197,7 +198,7 @@ def test_descriptor_layouts_match_the_c_compiler(tmp_path):
     subprocess.run(["gcc", "-I", str(HEADER.parent), str(src), "-o", str(exe)], check=True)
     out = dict((" ".join(l.split()[:2]), int(l.split()[2])) for l in subprocess.run([str(exe)], capture_output=True,
                                                                                       text=True, check=True).stdout.splitlines())
-    for cname, cls in (("alpaca_attn_desc", AttnDesc), ("alpaca_rope_desc", RopeDesc)):
+    for cname, cls in structs:
         assert out[f"{cname} size"] == ctypes.sizeof(cls), cname
         for f, _ in cls._fields_:
             assert out[f"{cname} {f}"] == getattr(cls, f).offset, (cname, f)
@@ -378,3 +379,46 @@ def test_varlen_prefill_host_checks(lib):
              "block_stride": 256 * 3 * 64}
     assert select(lib, desc(**paged, max_blocks=8))[0] == Status.OK
     assert select(lib, desc(**paged, max_blocks=7))[0] == Status.INVALID_ARGUMENT
+
+
+# ---------------------------------------------------------------------------------------------- decode projections
+
+def proj_desc(**kw):
+    from alpaca_b200 import ProjDesc, WeightFormat
+    d = ProjDesc()
+    d.n_tokens, d.k, d.format, d.eps = 1, 576, int(WeightFormat.Q8_0), 1e-5
+    d.rows[0], d.rows[1], d.rows[2] = 576, 192, 192
+    for i in range(3):
+        d.w[i] = FAKE + 4096 * i
+        d.y[i] = FAKE + 65536 + 4096 * i
+        d.y_stride[i] = 576
+    d.x, d.x_stride, d.norm_weight = FAKE + 8192, 576, FAKE + 12288
+    for key, v in kw.items():
+        setattr(d, key, v)
+    return d
+
+
+def test_decode_project_host_checks(lib):
+    """alpaca_decode_project refuses what the kernels cannot serve before enqueueing anything (no GPU needed): formats,
+    flags, k (a multiple of 32 up to 16384), row counts, SILU's pairing rules, pointer alignment, strides, eps."""
+    from alpaca_b200 import PROJ_ADD, PROJ_NORM, PROJ_SILU, Status
+
+    def st(d):
+        return lib.alpaca_decode_project(ctypes.byref(d), None)
+
+    assert st(proj_desc(format=7)) == Status.UNSUPPORTED
+    for bad in (dict(flags=8), dict(k=100), dict(k=0), dict(k=32768), dict(n_tokens=0),
+                dict(flags=PROJ_NORM, eps=0.0), dict(flags=PROJ_NORM, norm_weight=0), dict(flags=PROJ_SILU | PROJ_ADD),
+                dict(x=FAKE + 2), dict(n_tokens=2, x_stride=100)):
+        assert st(proj_desc(**bad)) == Status.INVALID_ARGUMENT, bad
+    d = proj_desc()
+    d.w[1] = FAKE + 8  # not 16-byte aligned
+    assert st(d) == Status.INVALID_ARGUMENT
+    d = proj_desc(flags=PROJ_SILU)  # SILU: rows[1] and rows[2] must be 0 (W1 has rows[0] rows)
+    assert st(d) == Status.INVALID_ARGUMENT
+    d = proj_desc()
+    d.rows[0] = d.rows[1] = d.rows[2] = 0
+    assert st(d) == Status.INVALID_ARGUMENT
+    d = proj_desc(n_tokens=2)
+    d.y_stride[2] = 100  # smaller than rows[2] = 192
+    assert st(d) == Status.INVALID_ARGUMENT

@@ -221,3 +221,77 @@ def test_rope_kv_append_composition():
     assert np.all(kc[rest] == 7.0) and np.all(vc[rest] == -7.0)
     _, kc32, _ = oracle.rope_kv_append(q, k, v, kc0, vc0, start, 1e5, False, False)
     assert np.array_equal(kc32[start:start + T], oracle.rope(k, start, 1e5, False))
+
+
+# ---------------------------------------------------------------------------------------------- decode projections
+
+def _proj_kat():
+    return json.loads((GOLDEN / "proj_kat.json").read_text())
+
+
+def _close(got, expected, atol, rtol, label):
+    e = np.asarray(expected, np.float64).reshape(-1)
+    g = np.asarray(got, np.float64).reshape(-1)
+    bad = np.abs(g - e) > atol + rtol * np.abs(e)
+    print(f"[metrics] oracle {label}: max-abs {float(np.abs(g - e).max()):.2e} (atol {atol}, rtol {rtol})")
+    assert not bad.any(), f"{label}: element {int(np.argmax(bad))}"
+
+
+def test_linear_rmsnorm_silu_known_answers():
+    """CPUOps.linear (f32 and f16 weights, and the single-row mat-vec of decode), rmsNorm and silu restated, against
+    the reference's fixtures ops.json["linear"], ["rmsnorm"], ["silu"] at OperationTests.swift:24-53's tolerances."""
+    c = _proj_kat()
+    tol = c["tolerance"]
+    lin = c["linear"]
+    m, k, n = lin["m"], lin["k"], lin["n"]
+    x = np.array(lin["x"], np.float32).reshape(m, k)
+    w = np.array(lin["w"], np.float32).reshape(n, k)
+    y = oracle.linear(x, np.frombuffer(w.tobytes(), np.uint8), "f32", n)
+    _close(y, lin["expected"], *tol["linear"], "linear f32")
+    y16 = oracle.linear(x, oracle.quantize(w, "f16"), "f16", n)
+    _close(y16, lin["expected_f16"], *tol["linear"], "linear f16")
+    _close(oracle.linear(x[:1], oracle.quantize(w, "f16"), "f16", n), lin["expected_f16"][:n], *tol["linear"],
+           "mat-vec f16")
+    rn = c["rmsnorm"]
+    xr = np.array(rn["x"], np.float32).reshape(rn["shape"])
+    _close(oracle.rmsnorm(xr, np.array(rn["w"], np.float32), rn["eps"]), rn["expected"], *tol["rmsnorm"], "rmsnorm")
+    si = c["silu"]
+    _close(oracle.silu(np.array(si["x"], np.float32)), si["expected"], *tol["silu"], "silu")
+
+
+@pytest.mark.parametrize("fmt", ["q8_0", "q4_0"])
+def test_quantized_formats_known_answers(fmt):
+    """GGUF q8_0 / q4_0 (testQuantizedFormatsAgainstGGUFReference, OperationTests.swift:88-107): the fixture's blocks
+    (written by the gguf package) dequantise to its values, the quantised mat-vec matches its float mat-vec on the
+    dequantised weights, and the reference quantiser restated here reproduces the blocks byte for byte."""
+    import base64
+    c = _proj_kat()
+    q = c[fmt]
+    k, n, m = q["k"], q["n"], q["m"]
+    raw = np.frombuffer(base64.b64decode(q["blocks"]), np.uint8)
+    assert raw.size == n * oracle.row_bytes(fmt, k)
+    _close(oracle.dequantize(raw, fmt, n, k), q["dequantized"], *c["tolerance"]["dequantize"], f"{fmt} dequantize")
+    x = np.array(q["x"], np.float32).reshape(m, k)
+    _close(oracle.linear(x, raw, fmt, n), q["expected"], *c["tolerance"]["quantized_linear"], f"{fmt} linear")
+    mine = oracle.quantize(np.array(q["original"], np.float32).reshape(n, k), fmt)
+    assert np.array_equal(mine.reshape(-1), raw), f"{fmt} quantiser differs from the gguf blocks"
+
+
+@pytest.mark.parametrize("fmt", ["f16", "q8_0", "q4_0"])
+def test_decode_project_composition(fmt):
+    """The fused projection (decode_fused.metal:32-122) on the CPU path is the composition of the restated ops:
+    norm + three matrices (QKV), silu(W0 xn) * (W1 xn) (gate + up), and the residual add of the out-projection."""
+    T, k = 2, 96
+    x = oracle.splitmix_normal(41, (T, k))
+    g = oracle.splitmix_normal(42, (k,))
+    ws = [oracle.quantize(oracle.splitmix_normal(43 + i, (n, k)) * 0.05, fmt) for i, n in enumerate((8, 4, 4))]
+    xn = oracle.rmsnorm(x, g, 1e-5)
+    outs = oracle.decode_project(fmt, ws, x, norm_weight=g, eps=1e-5)
+    for w, o in zip(ws, outs):
+        assert np.array_equal(o, oracle.linear(xn, w, fmt, w.shape[0]))
+    (gu,) = oracle.decode_project(fmt, ws[1:], x, norm_weight=g, eps=1e-5, silu_gate=True)
+    a, b = oracle.linear(xn, ws[1], fmt, 4), oracle.linear(xn, ws[2], fmt, 4)
+    assert np.array_equal(gu, (oracle.silu(a) * b).astype(np.float32))
+    res = oracle.splitmix_normal(44, (T, 8))
+    (yo,) = oracle.decode_project(fmt, ws[:1], x, add_to=[res])
+    assert np.array_equal(yo, (res + oracle.linear(x, ws[0], fmt, 8)).astype(np.float32))
