@@ -591,6 +591,285 @@ __global__ void __launch_bounds__(kProjThreads, 3) proj_reg_kernel(const ProjArg
     }
 }
 
+// ---- single-token path for GGUF blocks: coalesced staging of each warp's span of 32 blocks.
+// A warp piece covers 32 consecutive blocks of a row (1088 bytes of q8_0, 576 of q4_0), contiguous in memory: the warp
+// copies the span into its own shared-memory buffer with 16-byte cp.async (one copy per lane and 16 bytes instead of
+// nine 4-byte loads per lane and block), double-buffered across passes so the next rows' copies are in flight while
+// the current ones are used. Two lanes share a block (16 quants, or 8 bytes of nibble pairs, each), so a lane always
+// meets the same elements of every row and keeps those 32 input values in registers; each lane scales its partial dot
+// by its block's scale, so blocks need no cross-lane reduction. Quants are read as aligned words and funnel-shifted by
+// the block's 2-byte phase (no branch: neighbouring blocks alternate phase) and multiplied as f32 pairs.
+constexpr int kQRows = 2;  // rows per warp slot per pass (SiLU: one output, its gate and up rows)
+
+template <int F>
+struct QGeo {
+    static constexpr int BB = F == 1 ? 34 : 18;             // bytes per block
+    static constexpr int QB = F == 1 ? 16 : 8;              // quant bytes per lane (half of the block's)
+    static constexpr int SPAN = 32 * BB;                    // bytes of a warp's 32 blocks
+    static constexpr int BUF = (SPAN + 32 + 15) / 16 * 16;  // the span's 16-byte-aligned cover (+ the funnel word)
+};
+
+__device__ __forceinline__ void cp_async16_zfill(void* smem_dst, const void* gsrc, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)), "l"(gsrc), "r"(src_bytes)
+                 : "memory");
+}
+
+// Copy the 16-byte cover of [p, p + n) (n <= SPAN) into buf; bytes at or past `end` are zero-filled, never read.
+// Returns the offset of p inside buf.
+template <int F>
+__device__ __forceinline__ int stage_span(uint8_t* buf, const uint8_t* p, int n, const uint8_t* end, int lane) {
+    const uintptr_t a0 = reinterpret_cast<uintptr_t>(p) & ~uintptr_t(15);
+    const uintptr_t a1 = reinterpret_cast<uintptr_t>(p + n);
+    const uintptr_t lim = reinterpret_cast<uintptr_t>(end);
+    for (uintptr_t a = a0 + 16 * lane; a < a1; a += 16 * 32) {
+        const uint32_t src = a >= lim ? 0u : static_cast<uint32_t>(std::min<uintptr_t>(16, lim - a));
+        cp_async16_zfill(buf + (a - a0), reinterpret_cast<const void*>(src ? a : a0), src);
+    }
+    return static_cast<int>(reinterpret_cast<uintptr_t>(p) - a0);
+}
+
+__device__ __forceinline__ uint32_t lds32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
+// 4 bytes at a 2-byte aligned shared-memory address.
+__device__ __forceinline__ uint32_t lds32_at2(const uint8_t* p) {
+    const uintptr_t u = reinterpret_cast<uintptr_t>(p);
+    if (u & 2u) return __funnelshift_r(lds32(p - 2), lds32(p + 2), 16);
+    return lds32(p);
+}
+
+template <int F>
+__global__ void __launch_bounds__(kProjThreads, 3) proj_q_kernel(const ProjArgs a) {
+    using G = QGeo<F>;
+    constexpr int BB = G::BB, BUF = G::BUF;
+    extern __shared__ __align__(16) uint8_t smem[];
+    float* xs = reinterpret_cast<float*>(smem);                                    // the staged row [k]
+    uint8_t* spans = smem + ((sizeof(float) * a.k + 15) / 16) * 16;               // [warp][2 passes][kQRows][BUF]
+    __shared__ float red[kProjWarps];
+    __shared__ float scale;
+    __shared__ float part[2][kProjWarps][kQRows];
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const bool silu = (a.flags & ALPACA_PROJ_SILU) != 0;
+    const int WPR = a.wpr, SLOTS = kProjWarps / WPR;
+    const int RPC = SLOTS * (silu ? kQRows / 2 : kQRows);
+    if (a.prefetch && threadIdx.x == 0) {
+        for (int r0 = blockIdx.x * RPC; r0 < a.total_rows; r0 += gridDim.x * RPC) {
+            const int r1 = min(r0 + RPC, a.total_rows);
+            if (silu) {
+                for (int m = 0; m < 2; m++) prefetch_l2(a.w[m] + r0 * a.row_bytes, (r1 - r0) * a.row_bytes, a.w_end[m]);
+                continue;
+            }
+            for (int m = 0, base = 0; m < 3; base += a.rows[m], m++) {
+                const int lo = max(r0, base), hi = min(r1, base + a.rows[m]);
+                if (lo < hi) prefetch_l2(a.w[m] + (lo - base) * a.row_bytes, (hi - lo) * a.row_bytes, a.w_end[m]);
+            }
+        }
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, k = a.k, U = a.units;
+    const int slot = warp / WPR, piece = warp - slot * WPR;
+    uint8_t* wbuf = spans + warp * (2 * kQRows * BUF);
+
+    // The rows of pass (r0): row n of the slot, its matrix row pointer (null past the end).
+    auto rows_of = [&](int r0, const uint8_t* (&rp)[kQRows], const uint8_t* (&re)[kQRows]) {
+#pragma unroll
+        for (int n = 0; n < kQRows; n++) {
+            int r, m = 0;
+            if (silu) {
+                r = r0 + slot * (kQRows / 2) + n / 2;
+                m = n & 1;
+            } else {
+                r = r0 + slot * kQRows + n;
+            }
+            rp[n] = nullptr;
+            re[n] = nullptr;
+            if (r >= a.total_rows) continue;
+            int lr = r;
+            if (!silu && lr >= a.rows[0]) {
+                lr -= a.rows[0];
+                m = 1;
+                if (lr >= a.rows[1]) {
+                    lr -= a.rows[1];
+                    m = 2;
+                }
+            }
+            rp[n] = a.w[m] + lr * a.row_bytes;
+            re[n] = a.w_end[m];
+        }
+    };
+    const int nblk = min(32, U - piece * 32);  // blocks of this piece (may be < 32 at the row's end, or <= 0)
+    auto stage_pass = [&](int r0, int buf, int (&off)[kQRows]) {
+        const uint8_t* rp[kQRows];
+        const uint8_t* re[kQRows];
+        rows_of(r0, rp, re);
+#pragma unroll
+        for (int n = 0; n < kQRows; n++)
+            off[n] = (rp[n] && nblk > 0)
+                         ? stage_span<F>(wbuf + (buf * kQRows + n) * BUF, rp[n] + piece * 32 * BB, nblk * BB, re[n], lane)
+                         : 0;
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+
+    // first pass's copies go out before the input row is staged
+    int off[2][kQRows];
+    const int first = blockIdx.x * RPC;
+    if (first < a.total_rows) stage_pass(first, 0, off[0]);
+
+    float ss = 0.f;
+    for (int i = tid; i < k; i += kProjThreads) {
+        const float v = a.x[i];
+        xs[i] = v;
+        ss = fmaf(v, v, ss);
+    }
+    if (a.flags & ALPACA_PROJ_NORM) {
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        if (tid == 0) {
+            float tot = 0.f;
+#pragma unroll
+            for (int w = 0; w < kProjWarps; w++) tot += red[w];
+            scale = 1.0f / sqrtf(tot / static_cast<float>(k) + a.eps);  // CPUOps.rmsNorm's scale
+        }
+        __syncthreads();
+        for (int i = tid; i < k; i += kProjThreads) xs[i] = (xs[i] * scale) * a.g[i];  // x * scale * w
+    }
+    __syncthreads();
+
+    // the lane's elements: half h of blocks bq and bq + 16 of the piece (q8_0: quants 16h..16h+15; q4_0: bytes
+    // 8h..8h+7, whose low nibbles are elements 8h + j and high nibbles 16 + 8h + j), as f32 pairs
+    const int h = lane & 1, bq = lane >> 1;
+    constexpr int QB = G::QB, NW = QB / 4;  // quant words per lane and block
+    float2 xr[2][8];
+#pragma unroll
+    for (int st = 0; st < 2; st++) {
+        const int bl = bq + 16 * st;
+        const bool in = bl < nblk;
+        const float* xb = xs + (piece * 32 + bl) * 32;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            int c0;
+            if constexpr (F == 1) c0 = 16 * h + 2 * j;
+            else c0 = (j < 4 ? 8 * h : 16 + 8 * h) + 2 * (j & 3);
+            xr[st][j] = in ? make_float2(xb[c0], xb[c0 + 1]) : make_float2(0.f, 0.f);
+        }
+    }
+    const float2 bias = F == 1 ? make_float2(-8388736.0f, -8388736.0f) : make_float2(-8388616.0f, -8388616.0f);
+
+    int pb = 0;
+    for (int r0 = first; r0 < a.total_rows; r0 += gridDim.x * RPC, pb ^= 1) {  // uniform per CTA
+        const int r0n = r0 + gridDim.x * RPC;
+        if (r0n < a.total_rows) {
+            stage_pass(r0n, pb ^ 1, off[pb ^ 1]);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncwarp();
+        const uint8_t* rp[kQRows];
+        const uint8_t* re[kQRows];
+        rows_of(r0, rp, re);
+        float acc[kQRows];
+#pragma unroll
+        for (int n = 0; n < kQRows; n++) {
+            float2 acc2 = make_float2(0.f, 0.f);
+            if (rp[n]) {
+                const uint8_t* sb = wbuf + (pb * kQRows + n) * BUF + off[pb][n];
+#pragma unroll
+                for (int st = 0; st < 2; st++) {
+                    const int bl = bq + 16 * st;
+                    if (bl >= nblk) continue;
+                    const uint8_t* blk = sb + bl * BB;
+                    const float d = __half2float(*reinterpret_cast<const __half*>(blk));
+                    // the lane's quant bytes at blk + 2 + QB h: aligned words from floor4, shifted by the phase
+                    const uintptr_t qa = reinterpret_cast<uintptr_t>(blk + 2 + QB * h);
+                    const uint32_t* wp = reinterpret_cast<const uint32_t*>(qa & ~uintptr_t(3));
+                    const uint32_t sh = static_cast<uint32_t>(qa & 3u) * 8u;
+                    uint32_t wv[NW + 1];
+#pragma unroll
+                    for (int i = 0; i <= NW; i++) wv[i] = wp[i];
+                    float2 sp = make_float2(0.f, 0.f);
+#pragma unroll
+                    for (int i = 0; i < NW; i++) {
+                        const uint32_t w = __funnelshift_r(wv[i], wv[i + 1], sh);
+                        if constexpr (F == 1) {
+                            const uint32_t u = w ^ 0x80808080u;
+                            const float2 f0 = __fadd2_rn(
+                                make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540u)),
+                                            __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541u))), bias);
+                            const float2 f1 = __fadd2_rn(
+                                make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542u)),
+                                            __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543u))), bias);
+                            sp = __ffma2_rn(f0, xr[st][2 * i], sp);
+                            sp = __ffma2_rn(f1, xr[st][2 * i + 1], sp);
+                        } else {
+                            const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
+                            const float2 l0 = __fadd2_rn(
+                                make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7540u)),
+                                            __uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7541u))), bias);
+                            const float2 l1 = __fadd2_rn(
+                                make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7542u)),
+                                            __uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7543u))), bias);
+                            const float2 h0 = __fadd2_rn(
+                                make_float2(__uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7540u)),
+                                            __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7541u))), bias);
+                            const float2 h1 = __fadd2_rn(
+                                make_float2(__uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7542u)),
+                                            __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7543u))), bias);
+                            sp = __ffma2_rn(l0, xr[st][2 * i], sp);
+                            sp = __ffma2_rn(l1, xr[st][2 * i + 1], sp);
+                            sp = __ffma2_rn(h0, xr[st][4 + 2 * i], sp);
+                            sp = __ffma2_rn(h1, xr[st][4 + 2 * i + 1], sp);
+                        }
+                    }
+                    acc2 = __ffma2_rn(make_float2(d, d), sp, acc2);
+                }
+            }
+            float sacc = acc2.x + acc2.y;
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) sacc += __shfl_xor_sync(0xffffffffu, sacc, o);
+            acc[n] = sacc;
+        }
+        __syncwarp();  // the buffer of this pass is free for the pass after next
+        if (WPR > 1) {
+            if (lane == 0)
+#pragma unroll
+                for (int n = 0; n < kQRows; n++) part[pb][warp][n] = acc[n];
+            __syncthreads();
+            if (piece == 0)
+#pragma unroll
+                for (int n = 0; n < kQRows; n++) {
+                    float sum = 0.f;
+                    for (int p = 0; p < WPR; p++) sum += part[pb][warp + p][n];
+                    acc[n] = sum;
+                }
+        }
+        if (piece != 0 || lane != 0) continue;
+        if (silu) {
+            if (!rp[0]) continue;
+            const int out = r0 + slot * (kQRows / 2);
+            const float gt = acc[0];
+            a.y[0][out] = (gt / (1.0f + expf(-gt))) * acc[1];
+            continue;
+        }
+#pragma unroll
+        for (int n = 0; n < kQRows; n++) {
+            if (!rp[n]) continue;
+            int lr = r0 + slot * kQRows + n, m = 0;
+            if (lr >= a.rows[0]) {
+                lr -= a.rows[0];
+                m = 1;
+                if (lr >= a.rows[1]) {
+                    lr -= a.rows[1];
+                    m = 2;
+                }
+            }
+            float* yp = a.y[m] + lr;
+            *yp = ((a.flags & ALPACA_PROJ_ADD) ? *yp : 0.f) + acc[n];
+        }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+}
+
 int proj_env(const char* name, int fallback) {
     const char* e = std::getenv(name);
     return (e && *e) ? std::atoi(e) : fallback;
@@ -615,6 +894,34 @@ cudaError_t launch_reg(ProjArgs a, int num_sms, cudaStream_t s) {
     }
     const bool silu = (a.flags & ALPACA_PROJ_SILU) != 0;
     const int rpc = (kProjWarps / a.wpr) * (silu ? kRegRows / 2 : kRegRows);
+    const int row_ctas = (a.total_rows + rpc - 1) / rpc;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(std::max(1, std::min(row_ctas, num_sms * proj_ctas_per_sm(3))), 1, 1);
+    cfg.blockDim = dim3(kProjThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, fn, a);
+}
+
+// Single-token launch of the staged-block form (quantised weights): one warp per 32 blocks of a row.
+template <int F>
+cudaError_t launch_q(ProjArgs a, int num_sms, cudaStream_t s) {
+    const int want = (a.units + 31) / 32;
+    a.wpr = want >= 8 ? 8 : (want >= 4 ? 4 : (want >= 2 ? 2 : 1));
+    const size_t smem = (sizeof(float) * a.k + 15) / 16 * 16 + static_cast<size_t>(kProjWarps) * 2 * kQRows * QGeo<F>::BUF;
+    const auto fn = proj_q_kernel<F>;
+    if (smem > 48 * 1024) {
+        const cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+    }
+    const bool silu = (a.flags & ALPACA_PROJ_SILU) != 0;
+    const int rpc = (kProjWarps / a.wpr) * (silu ? kQRows / 2 : kQRows);
     const int row_ctas = (a.total_rows + rpc - 1) / rpc;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(std::max(1, std::min(row_ctas, num_sms * proj_ctas_per_sm(3))), 1, 1);
@@ -713,8 +1020,8 @@ cudaError_t launch_proj(const alpaca_proj_desc& d, int num_sms, cudaStream_t s) 
     if (d.n_tokens == 1 && reg_form && reg_form_fits(d.format, d.k)) {
         switch (d.format) {
             case ALPACA_W_F16: return launch_reg<0>(a, num_sms, s);
-            case ALPACA_W_Q8_0: return launch_reg<1>(a, num_sms, s);
-            default: return launch_reg<2>(a, num_sms, s);
+            case ALPACA_W_Q8_0: return reg_form == 2 ? launch_reg<1>(a, num_sms, s) : launch_q<1>(a, num_sms, s);
+            default: return reg_form == 2 ? launch_reg<2>(a, num_sms, s) : launch_q<2>(a, num_sms, s);
         }
     }
     switch (d.format) {
