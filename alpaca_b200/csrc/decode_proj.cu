@@ -20,6 +20,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdlib>
+#include <mutex>
 
 #include "common.cuh"
 #include "internal.h"
@@ -870,6 +871,337 @@ __global__ void __launch_bounds__(kProjThreads, 3) proj_q_kernel(const ProjArgs 
     asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
+// ---- single-token quantised form on the tensor cores: int8 mma.sync against exact digit planes of the input.
+//
+// The input row (normalised when asked) is rewritten once per CTA as signed base-128 digits: with E the exponent of
+// the row's largest |x|, F = rint(x * 2^(26 - E)) (|F| < 2^27; exact to 2^-27 of that largest value) = d0 * 2^21 +
+// d1 * 2^14 + d2 * 2^7 + d3 with d1..d3 in [-64, 63] and d0 in [-65, 65]: four int8 planes per 32-element block.
+// One mma.sync m16n8k32 (s8 x s8 -> s32) per block takes the planes (rows 0-3 of A) against the block's 32 quants
+// of 8 weight rows (B; q4_0 nibbles as unsigned 0..15, 8 x the digit sums subtracted after). The int32 sums are
+// exact; each is multiplied by its row's f16 block scale and accumulated in f32 per plane, and the planes meet,
+// weighted by 2^(7 (3 - plane) + E - 26), at the end of the row. Per block and row that is ~2.5 warp instructions,
+// against ~13 for the float dot product.
+// Each warp owns a tile of 8 weight rows (SiLU: 8 gate + 8 up rows for 8 outputs) and a strided share of the row's
+// blocks (wpr warps per tile); a job = its KB blocks of the 8 (16) rows, staged with 16-byte cp.async into a
+// two-stage ring (row slots 16 mod 128 bytes apart, so the 8 rows' words fall in different banks).
+template <int F, int S, int H>
+struct MmaGeo {
+    static constexpr int BB = F == 1 ? 34 : 18;                 // bytes per block
+    static constexpr int NR = S ? 16 : 8;                       // weight rows per warp tile
+    static constexpr int KB = 16 / (S ? 2 : 1) / (H ? 2 : 1);   // blocks per job (H: half jobs)
+    static constexpr int SPAN = KB * BB;
+    static constexpr int CH = (SPAN + 30 + 15) / 16;            // 16-byte chunks of a span's cover at any 2-byte phase
+    static constexpr int RS = 16 + 128 * ((CH * 16 + 4 - 16 + 127) / 128);  // row slot: >= cover + 4, 16 mod 128
+    static constexpr int STAGE = NR * RS;
+};
+
+__device__ __forceinline__ void mma_s8_16832(int (&c)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+    asm(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%10, %10, %10, %10};"
+        : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1), "r"(0));
+}
+
+template <int F, int S, int H>
+__global__ void __launch_bounds__(kProjThreads, 2) proj_mma_kernel(const ProjArgs a) {
+    using Gm = MmaGeo<F, S, H>;
+    constexpr int BB = Gm::BB, KB = Gm::KB, CH = Gm::CH, RS = Gm::RS, STAGE = Gm::STAGE;
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int U = a.units;
+    uint8_t* xq = smem;                                              // [U][4 planes][32] int8 digits
+    int* xsum = reinterpret_cast<int*>(smem + U * 128);              // [U][4] digit sums (q4_0)
+    uint8_t* stg = smem + U * 128 + (F == 2 ? U * 16 : 0);           // [8 warps][2][STAGE], 16-byte aligned
+    __shared__ float red[kProjWarps];
+    __shared__ float scale;
+    __shared__ float part[2][kProjWarps][16];
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int WPR = a.wpr, SLOTS = kProjWarps / WPR, RPC = SLOTS * 8;  // output rows per CTA pass
+    const int total = a.total_rows;
+    if (a.prefetch && threadIdx.x == 0) {
+        for (int r0 = blockIdx.x * RPC; r0 < total; r0 += gridDim.x * RPC) {
+            const int r1 = min(r0 + RPC, total);
+            if (S) {
+                for (int m = 0; m < 2; m++) prefetch_l2(a.w[m] + r0 * a.row_bytes, (r1 - r0) * a.row_bytes, a.w_end[m]);
+                continue;
+            }
+            for (int m = 0, base = 0; m < 3; base += a.rows[m], m++) {
+                const int lo = max(r0, base), hi = min(r1, base + a.rows[m]);
+                if (lo < hi) prefetch_l2(a.w[m] + (lo - base) * a.row_bytes, (hi - lo) * a.row_bytes, a.w_end[m]);
+            }
+        }
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int slot = warp / WPR, piece = warp - slot * WPR;
+    const int NCH = (U + KB - 1) / KB;                              // jobs per row tile
+    const int nj = piece < NCH ? (NCH - piece + WPR - 1) / WPR : 0;  // this warp's jobs per pass
+    uint8_t* wst = stg + warp * 2 * STAGE;
+
+    // Weight row i of the tile whose first output row is o0 (SiLU: rows 0-7 gate, 8-15 up): its start, or null.
+    auto row_ptr = [&](int o0, int i, const uint8_t*& end) -> const uint8_t* {
+        int r, m = 0;
+        if (S) {
+            r = o0 + (i & 7);
+            m = i >> 3;
+        } else {
+            r = o0 + i;
+        }
+        end = nullptr;
+        if (r >= total) return nullptr;
+        if (!S && r >= a.rows[0]) {
+            r -= a.rows[0];
+            m = 1;
+            if (r >= a.rows[1]) {
+                r -= a.rows[1];
+                m = 2;
+            }
+        }
+        end = a.w_end[m];
+        return a.w[m] + static_cast<int64_t>(r) * a.row_bytes;
+    };
+    // Staging: lane l copies for weight row (S ? l / 2 : l / 4) of the tile, every (S ? 2 : 4)-th 16-byte chunk of
+    // the cover of the row's KB blocks of the job; bytes past a matrix are zero-filled. The row's start is looked up
+    // once per pass.
+    constexpr int CSUB = S ? 2 : 4;
+    const int crow = lane / CSUB, csub = lane % CSUB;
+    int c_o0 = -1;                 // pass whose copy row is cached
+    const uint8_t* c_rp = nullptr;
+    const uint8_t* c_end = nullptr;
+    auto issue = [&](int o0, int c, int st) {
+        if (o0 != c_o0) {
+            c_rp = row_ptr(o0, crow, c_end);
+            c_o0 = o0;
+        }
+        if (c_rp) {
+            uint8_t* dst = wst + st * STAGE + crow * RS;
+            const uint8_t* p = c_rp + static_cast<int64_t>(c) * KB * BB;
+            const uintptr_t a0 = reinterpret_cast<uintptr_t>(p) & ~uintptr_t(15);
+            const uintptr_t stop = reinterpret_cast<uintptr_t>(p + min(KB, U - c * KB) * BB);
+            const uintptr_t lim = reinterpret_cast<uintptr_t>(c_end);
+#pragma unroll
+            for (int ch = csub; ch < CH; ch += CSUB) {
+                const uintptr_t ad = a0 + 16 * ch;
+                if (ad >= stop) break;
+                const uint32_t src = ad >= lim ? 0u : static_cast<uint32_t>(lim - ad >= 16 ? 16 : lim - ad);
+                cp_async16_zfill(dst + 16 * ch, reinterpret_cast<const void*>(src ? ad : a0), src);
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    const int first = blockIdx.x * RPC;
+    if (nj > 0 && first < total) issue(first + slot * 8, piece, 0);  // in flight while the input is prepared
+
+    // ---- the input row as digit planes: staged as floats in the planes' own bytes (one batch of loads), normalised
+    // in place when asked, then each warp rewrites its blocks in place (a block's 32 floats and its four 32-byte
+    // planes take the same 128 bytes). One exponent for the whole row (that of its largest |value|), so the digit
+    // sums of every block carry the same scale and it is applied once, after the row's sum.
+    float* xs = reinterpret_cast<float*>(xq);
+    __shared__ int s_exp;
+    {
+        float ss = 0.f;
+        for (int i = tid; i < a.k; i += kProjThreads) {
+            const float v = a.x[i];
+            xs[i] = v;
+            ss = fmaf(v, v, ss);
+        }
+        if (a.flags & ALPACA_PROJ_NORM) {
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            if (lane == 0) red[warp] = ss;
+            __syncthreads();
+            if (tid == 0) {
+                float tot = 0.f;
+#pragma unroll
+                for (int w = 0; w < kProjWarps; w++) tot += red[w];
+                scale = 1.0f / sqrtf(tot / static_cast<float>(a.k) + a.eps);  // CPUOps.rmsNorm's scale
+            }
+        }
+        __syncthreads();
+        uint32_t mx = 0u;
+        for (int i = tid; i < a.k; i += kProjThreads) {
+            float v = xs[i];
+            if (a.flags & ALPACA_PROJ_NORM) {
+                v = (v * scale) * a.g[i];  // x * scale * w
+                xs[i] = v;
+            }
+            mx = max(mx, __float_as_uint(v) & 0x7fffffffu);
+        }
+        mx = __reduce_max_sync(0xffffffffu, mx);
+        if (lane == 0) red[warp] = __uint_as_float(mx);
+        __syncthreads();
+        if (tid == 0) {
+            uint32_t m = 0u;
+#pragma unroll
+            for (int w = 0; w < kProjWarps; w++) m = max(m, __float_as_uint(red[w]));
+            s_exp = static_cast<int>(m >> 23) - 127;  // exponent of the row's largest |value|
+        }
+        __syncthreads();
+    }
+    const int E = s_exp;
+    // F = rint(x * 2^(26 - E)), |F| < 2^27; a row whose largest |value| is below 2^-100 counts as zero
+    const float fscale = E >= -100 ? __int_as_float((127 + 26 - E) << 23) : 0.f;
+    for (int b = warp; b < U; b += kProjWarps) {
+        const float v = xs[b * 32 + lane];
+        __syncwarp();  // every lane holds its float before the block's bytes are rewritten
+        const int Fx = __float2int_rn(v * fscale);
+        const int d3 = (Fx << 25) >> 25;
+        const int f1 = (Fx - d3) >> 7;
+        const int d2 = (f1 << 25) >> 25;
+        const int f2 = (f1 - d2) >> 7;
+        const int d1 = (f2 << 25) >> 25;
+        const int d0 = (f2 - d1) >> 7;
+        int8_t* xb = reinterpret_cast<int8_t*>(xq + b * 128);
+        xb[lane] = static_cast<int8_t>(d0);
+        xb[32 + lane] = static_cast<int8_t>(d1);
+        xb[64 + lane] = static_cast<int8_t>(d2);
+        xb[96 + lane] = static_cast<int8_t>(d3);
+        if constexpr (F == 2) {
+            const int s0 = __reduce_add_sync(0xffffffffu, d0), s1 = __reduce_add_sync(0xffffffffu, d1);
+            const int s2 = __reduce_add_sync(0xffffffffu, d2), s3 = __reduce_add_sync(0xffffffffu, d3);
+            if (lane == 0) *reinterpret_cast<int4*>(xsum + 4 * b) = make_int4(s0, s1, s2, s3);
+        }
+    }
+    __syncthreads();
+
+    // ---- lane roles: B column n = weight row n (and 8 + n), k group t; A row g = digit plane g (lanes g < 4);
+    // C: plane g, columns 2t / 2t + 1 = weight rows 2t / 2t + 1
+    const int n = lane >> 2, t = lane & 3, g = lane >> 2;
+    // plane g's weight in the row: 2^(7 (3 - g)) x 2^(E - 26) (exact; 0 for the zero rows of A, or a zero row)
+    const float psc = (g < 4 && E >= -100) ? __int_as_float((127 + 7 * (3 - g) + E - 26) << 23) : 0.f;
+    const uint32_t amask = g < 4 ? 0xFFFFFFFFu : 0u;  // A rows 4-7 (and 8-15) are zero
+    auto row_phase = [&](int o0, int i) -> int {  // the row start's offset in its 16-byte line
+        const uint8_t* end;
+        const uint8_t* rp = row_ptr(o0, i, end);
+        return rp ? static_cast<int>(reinterpret_cast<uintptr_t>(rp) & 15u) : 0;
+    };
+
+    int pb = 0, st = 0;
+    for (int r0 = first; r0 < total; r0 += gridDim.x * RPC, pb ^= 1) {  // uniform per CTA
+        const int o0 = r0 + slot * 8;
+        const int r0n = r0 + gridDim.x * RPC;
+        // per pass: the phases of the lane's B row and scale rows (the span of chunk c starts at phase + c KB BB)
+        int ph_b[2], ph_d[2][2];
+#pragma unroll
+        for (int h = 0; h < (S ? 2 : 1); h++) {
+            ph_b[h] = row_phase(o0, 8 * h + n);
+            ph_d[h][0] = row_phase(o0, 8 * h + 2 * t);
+            ph_d[h][1] = row_phase(o0, 8 * h + 2 * t + 1);
+        }
+        float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};  // [gate / only, up][row 2t, 2t + 1]
+        for (int j = 0; j < nj; j++) {
+            const int c = piece + j * WPR;
+            // the next job: this tile's next chunk, else the first chunk of the next pass
+            __syncwarp();  // every lane is done with the stage the next job goes into
+            if (j + 1 < nj) issue(o0, c + WPR, st ^ 1);
+            else if (r0n < total) issue(r0n + slot * 8, piece, st ^ 1);
+            else asm volatile("cp.async.commit_group;" ::: "memory");
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+            __syncwarp();
+            const uint8_t* sbp = wst + st * STAGE;
+            const int cb = c * KB * BB;
+            // per-job lane pointers; BB = 2 mod 4, so the blocks' quants alternate between two phases: even blocks
+            // at the first word phase, odd ones at the other, each from its own aligned base (immediate offsets)
+            const uint8_t* qe[2];
+            const uint8_t* qo[2];
+            const uint8_t* dp[2][2];
+            uint32_t she = 0, sho = 0;
+#pragma unroll
+            for (int h = 0; h < (S ? 2 : 1); h++) {
+                const uintptr_t q0 = reinterpret_cast<uintptr_t>(sbp + (8 * h + n) * RS + ((ph_b[h] + cb) & 15) + 2 + 4 * t);
+                const uint32_t ph = static_cast<uint32_t>(q0 & 3u);  // 0 or 2
+                qe[h] = reinterpret_cast<const uint8_t*>(q0 - ph);
+                qo[h] = reinterpret_cast<const uint8_t*>(q0 - ph + (ph ? 2 : -2));
+                she = ph * 8u;
+                sho = 16u - she;
+                dp[h][0] = sbp + (8 * h + 2 * t) * RS + ((ph_d[h][0] + cb) & 15);
+                dp[h][1] = sbp + (8 * h + 2 * t + 1) * RS + ((ph_d[h][1] + cb) & 15);
+            }
+            const uint8_t* xa = xq + (c * KB) * 128 + (g & 3) * 32 + 4 * t;  // plane g & 3 of the job's first block
+            const int* xsm = xsum + 4 * (c * KB) + (g & 3);
+            auto block = [&](int bl) {
+                const uint32_t a0 = *reinterpret_cast<const uint32_t*>(xa + bl * 128) & amask;
+                const uint32_t a2 = *reinterpret_cast<const uint32_t*>(xa + bl * 128 + 16) & amask;
+                int corr = 0;
+                if constexpr (F == 2) corr = 8 * static_cast<int>(static_cast<uint32_t>(xsm[4 * bl]) & amask);
+#pragma unroll
+                for (int h = 0; h < (S ? 2 : 1); h++) {
+                    const uint8_t* w = ((bl & 1) ? qo[h] : qe[h]) + bl * BB;
+                    const uint32_t sh = (bl & 1) ? sho : she;
+                    uint32_t b0, b1;
+                    if constexpr (F == 1) {
+                        b0 = __funnelshift_r(*reinterpret_cast<const uint32_t*>(w), *reinterpret_cast<const uint32_t*>(w + 4), sh);
+                        b1 = __funnelshift_r(*reinterpret_cast<const uint32_t*>(w + 16), *reinterpret_cast<const uint32_t*>(w + 20), sh);
+                    } else {  // byte j holds element j (low nibble) and element 16 + j (high nibble)
+                        const uint32_t x = __funnelshift_r(*reinterpret_cast<const uint32_t*>(w), *reinterpret_cast<const uint32_t*>(w + 4), sh);
+                        b0 = x & 0x0F0F0F0Fu;
+                        b1 = (x >> 4) & 0x0F0F0F0Fu;
+                    }
+                    int cc[4];
+                    mma_s8_16832(cc, a0, a2, b0, b1);
+                    const float w0 = __half2float(*reinterpret_cast<const __half*>(dp[h][0] + bl * BB));
+                    const float w1 = __half2float(*reinterpret_cast<const __half*>(dp[h][1] + bl * BB));
+                    acc[h][0] = fmaf(w0, static_cast<float>(cc[0] - corr), acc[h][0]);
+                    acc[h][1] = fmaf(w1, static_cast<float>(cc[1] - corr), acc[h][1]);
+                }
+            };
+            const int nb = min(KB, U - c * KB);
+            if (nb == KB) {
+#pragma unroll
+                for (int bl = 0; bl < KB; bl++) block(bl);
+            } else {
+                for (int bl = 0; bl < nb; bl++) block(bl);
+            }
+            st ^= 1;
+        }
+        // planes 0-3 (lanes t, 4 + t, 8 + t, 12 + t), each scaled by its weight, meet in lanes 0-3; then the wpr
+        // warps of the tile
+#pragma unroll
+        for (int h = 0; h < 2; h++)
+#pragma unroll
+            for (int x = 0; x < 2; x++) {
+                acc[h][x] *= psc;
+                acc[h][x] += __shfl_down_sync(0xffffffffu, acc[h][x], 8);
+                acc[h][x] += __shfl_down_sync(0xffffffffu, acc[h][x], 4);
+            }
+        if (lane < 4) {
+            part[pb][warp][2 * lane] = acc[0][0];
+            part[pb][warp][2 * lane + 1] = acc[0][1];
+            if (S) {
+                part[pb][warp][8 + 2 * lane] = acc[1][0];
+                part[pb][warp][8 + 2 * lane + 1] = acc[1][1];
+            }
+        }
+        __syncthreads();
+        if (tid < RPC) {
+            const int s = tid >> 3, i = tid & 7, out = r0 + tid;
+            if (out < total) {
+                float v0 = 0.f, v1 = 0.f;
+                for (int p = 0; p < WPR; p++) {
+                    v0 += part[pb][s * WPR + p][i];
+                    if (S) v1 += part[pb][s * WPR + p][8 + i];
+                }
+                if (S) {
+                    a.y[0][out] = (v0 / (1.0f + expf(-v0))) * v1;
+                } else {
+                    int lr = out, m = 0;
+                    if (lr >= a.rows[0]) {
+                        lr -= a.rows[0];
+                        m = 1;
+                        if (lr >= a.rows[1]) {
+                            lr -= a.rows[1];
+                            m = 2;
+                        }
+                    }
+                    float* yp = a.y[m] + lr;
+                    *yp = ((a.flags & ALPACA_PROJ_ADD) ? *yp : 0.f) + v0;
+                }
+            }
+        }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+}
+
 int proj_env(const char* name, int fallback) {
     const char* e = std::getenv(name);
     return (e && *e) ? std::atoi(e) : fallback;
@@ -934,6 +1266,69 @@ cudaError_t launch_q(ProjArgs a, int num_sms, cudaStream_t s) {
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() ? 1 : 0;
     return cudaLaunchKernelEx(&cfg, fn, a);
+}
+
+// Single-token launch of the int8 tensor-core form: wpr = the smallest power of two >= the row's jobs (at most 8).
+template <int F, int S, int H>
+size_t mma_smem(int units) {
+    return static_cast<size_t>(units) * (128 + (F == 2 ? 16 : 0)) + 2 * kProjWarps * MmaGeo<F, S, H>::STAGE;
+}
+template <int F, int S, int H>
+int mma_wpr(int units) {
+    const int nch = (units + MmaGeo<F, S, H>::KB - 1) / MmaGeo<F, S, H>::KB;
+    return nch > 4 ? 8 : (nch > 2 ? 4 : nch);
+}
+template <int F, int S, int H>
+cudaError_t launch_mma_fsh(ProjArgs a, int num_sms, cudaStream_t s) {
+    a.wpr = mma_wpr<F, S, H>(a.units);
+    const size_t smem = mma_smem<F, S, H>(a.units);
+    const auto fn = proj_mma_kernel<F, S, H>;
+    if (smem > 48 * 1024) {
+        const cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+    }
+    static std::mutex mu;
+    static size_t last_smem = 0;
+    static int last_occ = 1;
+    int occ;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (last_smem != smem) {
+            int o = 0;
+            const cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, fn, kProjThreads, smem);
+            if (e != cudaSuccess) return e;
+            last_occ = std::max(1, o);
+            last_smem = smem;
+        }
+        occ = last_occ;
+    }
+    const int rpc = (kProjWarps / a.wpr) * 8;
+    const int row_ctas = (a.total_rows + rpc - 1) / rpc;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(std::max(1, std::min(row_ctas, num_sms * proj_ctas_per_sm(occ))), 1, 1);
+    cfg.blockDim = dim3(kProjThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, fn, a);
+}
+// Full jobs unless they leave fewer than two CTAs per SM of row tiles (small matrices: more warps per row) or two
+// CTAs of them do not fit an SM (long rows: the staged input takes the room).
+template <int F, int S>
+cudaError_t launch_mma_fs(ProjArgs a, int num_sms, cudaStream_t s) {
+    const int rpc = (kProjWarps / mma_wpr<F, S, 0>(a.units)) * 8;
+    const int row_ctas = (a.total_rows + rpc - 1) / rpc;
+    const bool half = row_ctas < 2 * num_sms || mma_smem<F, S, 0>(a.units) > 113 * 1024;
+    return half ? launch_mma_fsh<F, S, 1>(a, num_sms, s) : launch_mma_fsh<F, S, 0>(a, num_sms, s);
+}
+template <int F>
+cudaError_t launch_mma(ProjArgs a, int num_sms, cudaStream_t s) {
+    return (a.flags & ALPACA_PROJ_SILU) ? launch_mma_fs<F, 1>(a, num_sms, s) : launch_mma_fs<F, 0>(a, num_sms, s);
 }
 
 // Whether the register form covers k: at most 8 warps of 32 lanes x UPL units per row.
@@ -1017,6 +1412,9 @@ cudaError_t launch_proj(const alpaca_proj_desc& d, int num_sms, cudaStream_t s) 
     const int cap = proj_max_tokens_per_pass(d.k);
     const int tp = d.n_tokens >= cap ? cap : (d.n_tokens == 1 ? 1 : (d.n_tokens == 2 ? 2 : std::min(cap, 4)));
     static const int reg_form = proj_env("ALPACA_PROJ_REG", 1);
+    static const int mma_form = proj_env("ALPACA_PROJ_MMA", 1);
+    if (d.n_tokens == 1 && mma_form && d.format != ALPACA_W_F16)
+        return d.format == ALPACA_W_Q8_0 ? launch_mma<1>(a, num_sms, s) : launch_mma<2>(a, num_sms, s);
     if (d.n_tokens == 1 && reg_form && reg_form_fits(d.format, d.k)) {
         switch (d.format) {
             case ALPACA_W_F16: return launch_reg<0>(a, num_sms, s);
