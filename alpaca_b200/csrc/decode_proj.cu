@@ -16,7 +16,10 @@
 //     of shared memory, and the staging writes (consecutive elements, one block apart) fall in 32 different banks
 //     (without the pad word the stride is a multiple of 32 words: a 32-way conflict on every staging store, which
 //     held q8_0 projections near 0.4 TB/s);
-//   * up to 4 input rows (tokens of a batched decode step) share every weight load; more rows take more passes.
+//   * up to 4 input rows (tokens of a batched decode step) share every weight load; more rows take more passes;
+//   * single-token q8_0 / q4_0 calls run on the tensor cores instead (proj_mma_kernel): the input row as exact int8
+//     digit planes against the weight quants in mma.sync m16n8k32 (s8), the block scales applied to the exact int32
+//     sums.
 #include <algorithm>
 #include <cmath>
 #include <cstdlib>
