@@ -135,3 +135,56 @@ def test_strided_rows_and_untouched_padding(cuda_lib):
     (ref,) = oracle.decode_project("q8_0", [w], x)
     _check(ybuf[:, :n], ref, "q8_0", "strided rows")
     assert torch.all(ybuf[:, n:] == 7.0)
+
+
+@pytest.mark.parametrize("fmt", ["q8_0", "q4_0"])
+def test_single_token_quantised_shapes(cuda_lib, fmt):
+    """Single-token quantised calls (the int8 tensor-core form) beyond the model layers above: Q/K/V with the norm
+    whose row counts end in partial 8-row tiles, one of them a middle matrix (8-row tiles straddling two matrices);
+    80001 rows at k = 256 (one 8-block job per tile, hundreds of tiles per CTA); SwiGLU at k = 8192; the
+    out-projection's residual add on a row count that ends in a partial tile."""
+    from alpaca_b200 import decode_project, device_status
+    dev = torch.device("cuda")
+    # Q / K / V, k = 512, norm: rows 1000 + 264 + 261 and 1000 + 259 + 261
+    k = 512
+    x = oracle.splitmix_normal(301, (1, k))
+    g = 1.0 + 0.1 * oracle.splitmix_normal(302, (k,))
+    for rows in ((1000, 264, 261), (1000, 259, 261)):
+        ws = [_weights(303 + i, n, k, fmt) for i, n in enumerate(rows)]
+        outs = [torch.full((1, n), float("nan"), device=dev) for n in rows]
+        decode_project([w[1] for w in ws], fmt, k, torch.from_numpy(x).to(dev), outs,
+                       norm_weight=torch.from_numpy(g).to(dev), eps=1e-5)
+        device_status()
+        refs = oracle.decode_project(fmt, [w[0] for w in ws], x, norm_weight=g, eps=1e-5)
+        for name, o, r in zip("QKV", outs, refs):
+            _check(o, r, fmt, f"{fmt} k={k} {name} rows={rows}")
+    # 80001 rows of k = 256
+    k, n = 256, 80001
+    x = oracle.splitmix_normal(311, (1, k))
+    w, wd = _weights(312, n, k, fmt)
+    out = torch.full((1, n), float("nan"), device=dev)
+    decode_project([wd], fmt, k, torch.from_numpy(x).to(dev), [out])
+    device_status()
+    (ref,) = oracle.decode_project(fmt, [w], x)
+    _check(out, ref, fmt, f"{fmt} k={k} rows={n}")
+    # SwiGLU, k = 8192, 1003 rows
+    k, n = 8192, 1003
+    x = oracle.splitmix_normal(321, (1, k))
+    g = 1.0 + 0.1 * oracle.splitmix_normal(322, (k,))
+    (wg, wg_d), (wu, wu_d) = _weights(323, n, k, fmt), _weights(324, n, k, fmt)
+    gate = torch.full((1, n), float("nan"), device=dev)
+    decode_project([wg_d, wu_d], fmt, k, torch.from_numpy(x).to(dev), [gate],
+                   norm_weight=torch.from_numpy(g).to(dev), eps=1e-5, silu_gate=True)
+    device_status()
+    (ref_g,) = oracle.decode_project(fmt, [wg, wu], x, norm_weight=g, eps=1e-5, silu_gate=True)
+    _check(gate, ref_g, fmt, f"{fmt} k={k} gate*up rows={n}")
+    # out-projection + residual, 2050 rows
+    k, n = 2048, 2050
+    x = oracle.splitmix_normal(331, (1, k))
+    resid0 = oracle.splitmix_normal(332, (1, n))
+    w, wd = _weights(333, n, k, fmt)
+    resid = torch.from_numpy(resid0.copy()).to(dev)
+    decode_project([wd], fmt, k, torch.from_numpy(x).to(dev), [resid], add=True)
+    device_status()
+    (ref,) = oracle.decode_project(fmt, [w], x, add_to=[resid0])
+    _check(resid, ref, fmt, f"{fmt} k={k} rows={n} + residual")

@@ -2,11 +2,12 @@
 
 Some callers cannot call cudaMalloc or hand the library a scratch buffer — a host runtime that owns every device
 allocation through a fixed memory plan, or code running where allocation is not allowed. For them the library
-keeps the split-decode scratch in a built-in device array. This test enqueues two such calls back to back on one
-stream with no synchronisation in between (different sequences, context lengths and split counts, so the second call
-runs over split records the first one left in the shared array), then checks each output against the existing
-workspace entry point, alpaca_attn_decode, and every sequence against the CPU oracle, within the decode tolerance
-the other tests use. It also checks that a call needing more split scratch than the built-in 8 MiB is rejected
+keeps the split-decode scratch in a built-in device array. This test first fills that array's split records with NaN
+(a call whose queries are NaN), then enqueues two such calls back to back on one stream with no synchronisation in
+between (different sequences, context lengths and split counts, so the second call runs over split records the first
+one left in the shared array): a record read before the call wrote it would show as NaN. It checks each output
+against the existing workspace entry point, alpaca_attn_decode, and every sequence against the CPU oracle, within
+the decode tolerance the other tests use. It also checks that a call needing more split scratch than the built-in 8 MiB is rejected
 before anything is enqueued.
 
 The file name makes pytest collect it last; it passes alone in a fresh process and after the other tests.
@@ -59,6 +60,17 @@ def test_decode_noalloc_matches_workspace_entry_point(cuda_lib):
         ab.device_status()
         dnew = ab.make_desc(dev["q"], dev["k"], dev["v"], got, ctx_lens=dev["lens"], max_ctx_len=cap)
         cases.append((q, k, v, lens, dev, ref, got, dnew))
+
+    # A first call with NaN queries fills the split records of the built-in array (64 sequences x 4096 rows covers
+    # every record the two calls below use) with NaN, so a record that either call read without writing it first
+    # would turn its output into NaN.
+    S0, cap0 = 64, 4096
+    pq = torch.full((S0, 1, H, D), float("nan"), dtype=torch.float32, device="cuda")
+    pkv = torch.zeros((S0, cap0, KVH, D), dtype=torch.float16, device="cuda")
+    pout = torch.empty((S0, 1, H, D), dtype=torch.float32, device="cuda")
+    plens = torch.full((S0,), cap0, dtype=torch.int32, device="cuda")
+    dpoison = ab.make_desc(pq, pkv, pkv, pout, ctx_lens=plens, max_ctx_len=cap0)
+    assert lib.alpaca_attn_decode_noalloc(ctypes.byref(dpoison), sp) == ab.Status.OK, lib.alpaca_cuda_last_error()
 
     # the no-allocation entry point: both calls enqueued back to back, one synchronisation
     for c in cases:
