@@ -584,7 +584,7 @@ def leg_proj(c: Ctx):
             "l2": f"{wbytes / 1e9:.2f} GB of weights per step vs 126 MB L2 (no flush)",
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": c.pk["hbm_gbs"], "unit": "GB/s",
                          "frac": gbs / c.pk["hbm_gbs"], "traffic": profile_traffic("decode_proj_q8_1p7b"),
-                         "kernel": "alpaca::proj_q_kernel<1> (q8_0, one token) per projection; traffic: the "
+                         "kernel": "alpaca::proj_mma_kernel<q8_0> (int8 tensor-core form, one token) per projection; traffic: the "
                                    "gate + up launch"},
             "clocks": clk, "gpu_launches": steps * PROJ_LAYERS * 4}
 
