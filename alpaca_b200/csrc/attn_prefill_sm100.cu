@@ -432,7 +432,8 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
             if (debug_timeout && t == 0) ok = mbar_wait(&sm->dbg, 0, ab);  // nothing arrives: exercises the give-up path
             for (int r = 0, it = item_of(0); ok && it < total_items; it = item_of(++r)) {
                 const int n = tile_work<kBN, NT, VL>(a, it, t).nblk;  // this issuer's tile
-                const int nmax = item_blocks<NT>(decode_item<kBN, NT, VL>(a, it));
+                const Item xi = decode_item<kBN, NT, VL>(a, it);
+                const int nmax = item_blocks<NT>(xi);
                 if (n > 0) {
                     ok = mbar_wait(&sm->q_full[t], q_uses & 1, ab);
                     if (!ok) break;
@@ -462,8 +463,12 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
                         const int b = j - 1;
                         const uint32_t prv = kv_it + b;
                         const int sp = prv % kStages;
-                        // ragged form: warp 3 has zeroed the V rows past the context (and is done with the stage)
-                        ok = mbar_wait(VL ? &sm->v_ready[sp] : &sm->v_full[sp], (prv / kStages) & 1, ab);
+                        // ragged form: in a block that reaches the sequence's context end, warp 3 zeroes the V rows
+                        // past it first (v_ready); every other block goes to the MMA as soon as it lands. (warp 3
+                        // arrives on v_ready for every block, so its phases stay one per use of the stage; it cannot
+                        // run two uses ahead, since the stage's next load waits for this P.V.)
+                        const bool vfix = VL && xi.ctx_end - b * kBN < kBN;
+                        ok = mbar_wait(vfix ? &sm->v_ready[sp] : &sm->v_full[sp], (prv / kStages) & 1, ab);
                         if (!ok) break;
                         if (b < n) {
                             ok = mbar_wait(&sm->p_full[t], p_uses & 1, ab);

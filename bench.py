@@ -614,11 +614,22 @@ def leg_cfg4(c: Ctx):
         k[i] = torch.randn((T, 1, D), generator=g, device=c.dev).half()
         v[i] = torch.randn((T, 1, D), generator=g, device=c.dev).half()
     out = torch.empty((U, T, G, D), dtype=torch.float32, device=c.dev)
-    desc = ab.make_desc(q, k, v, out)
     in_bytes = (q.numel() + k.numel() + v.numel()) * 2
-    flush = in_bytes < L2_BYTES
-    ms, ms_max, clk = c.timed(lambda: ab.launch(desc, ab.Kernel.PREFILL_TC, None, c.stream), args.steps, args.warmup,
-                              flush=flush)
+    # Identical copies of the rank's inputs and outputs, used in turn, so that the calls between two uses of a copy
+    # touch more than the L2 holds: every call reads its inputs from HBM, and the calls run back to back as a
+    # model's layers do (a flush before each call would also time a dirty L2's write-backs and the launch ramp).
+    copy_bytes = in_bytes + out.numel() * 4
+    n_copies = 1 + -(-(3 * L2_BYTES // 2) // copy_bytes)
+    bufs = [(q, k, v, out)] + [(q.clone(), k.clone(), v.clone(), torch.empty_like(out)) for _ in range(n_copies - 1)]
+    descs = [ab.make_desc(*b) for b in bufs]
+    turn = [0]
+
+    def call():
+        ab.launch(descs[turn[0] % n_copies], ab.Kernel.PREFILL_TC, None, c.stream)
+        turn[0] += 1
+
+    ms, ms_max, clk = c.timed(call, args.steps, args.warmup)
+    ab.launch(descs[0], ab.Kernel.PREFILL_TC, None, c.stream)  # copy 0's output for the spot check
     import oracle
     rows = _spot_rows(T, G)
     ref = oracle.attention_rows(q[0].float().cpu().numpy(), k[0].float().cpu().numpy(), v[0].float().cpu().numpy(),
@@ -633,8 +644,9 @@ def leg_cfg4(c: Ctx):
             "value": job / (ms_max * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms_max,
             "tokens_per_s": CFG4_SEQS * T / (ms_max * 1e-3), "scaling": "strong", "units_rank0": U,
             "plan_imbalance": plan.imbalance,
-            "l2": (f"inputs {in_bytes / 1e6:.0f} MB per rank: L2 flushed (256 MB written) before every timed call"
-                   if flush else f"inputs {in_bytes / 1e6:.0f} MB per rank vs 126 MB L2 (no flush)"),
+            "l2": (f"inputs {in_bytes / 1e6:.0f} MB + outputs {out.numel() * 4 / 1e6:.0f} MB per rank, used in turn "
+                   f"from {n_copies} identical copies ({n_copies * copy_bytes / 1e6:.0f} MB vs 126 MB L2): every call "
+                   "reads its inputs from HBM; calls back to back, no flush"),
             "roofline": {"bound": "tensor", "achieved": kt, "peak": c.pk["tflops"], "unit": "TFLOP/s",
                          "frac": kt / c.pk["tflops"], "traffic": None,
                          "kernel": "alpaca::prefill_kernel (tcgen05, persistent), rank 0's launch"},
