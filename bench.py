@@ -601,8 +601,10 @@ def leg_cfg4(c: Ctx):
     from alpaca_b200.partition import partition, units_for_batch
     T, G = args.tokens, CFG4_H // CFG4_KVH
     units = units_for_batch([T] * CFG4_SEQS, [0] * CFG4_SEQS, CFG4_H, CFG4_KVH)
-    plan = partition(units, c.world, tflops=c.pk["tflops"] * 0.45, hbm_gbs=c.pk["hbm_gbs"] * 0.7)
-    mine = plan.ranks[c.rank]
+    # --cfg4-ranks R (one process): time rank 0's share of an R-rank plan, the per-rank work of R GPUs on this one
+    emulated = args.cfg4_ranks if (args.cfg4_ranks > 0 and c.world == 1) else 0
+    plan = partition(units, emulated or c.world, tflops=c.pk["tflops"] * 0.45, hbm_gbs=c.pk["hbm_gbs"] * 0.7)
+    mine = plan.ranks[0 if emulated else c.rank]
     U = len(mine)
     q = torch.empty((U, T, G, D), dtype=torch.float16, device=c.dev)
     k = torch.empty((U, T, 1, D), dtype=torch.float16, device=c.dev)
@@ -639,6 +641,13 @@ def leg_cfg4(c: Ctx):
     flops_rank = U * G * flops_prefill(T, 1)
     kt = flops_rank / (ms * 1e-3) / 1e12
     job = CFG4_SEQS * flops_prefill(T, CFG4_H)
+    if emulated:
+        return {"workload": f"config 4: rank 0's share of a {emulated}-rank plan ({U} (sequence, KV-head) units of 3 "
+                            f"query heads x T={T}), one call, timed on one GPU",
+                "emulated_ranks": emulated, "units": U, "value": kt, "unit": "TFLOP/s", "ms_per_step": ms_max,
+                "l2": f"calls take turns over {n_copies} identical copies of the inputs and outputs "
+                      f"({n_copies * copy_bytes / 1e6:.0f} MB vs 126 MB L2), back to back, no flush",
+                "clocks": clk, "spot_check_max_abs": spot, "gpu_launches": args.steps}
     return {"workload": f"config 4: SmolLM2-360M causal GQA prefill, {CFG4_SEQS} sequences x T={T}, 15/5 heads, d=64; "
                         f"(sequence, KV-head) units split over {c.world} GPU(s), one call per rank",
             "value": job / (ms_max * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms_max,
@@ -920,6 +929,8 @@ def main():
         ap.add_argument(f"--no-{leg}", action="store_true")
     ap.add_argument("--e2e-chunk", type=int, default=0, help="sequences per ABI call in the e2e pipeline (0: 1/6 of them)")
     ap.add_argument("--cpu-seconds", type=float, default=3.0, help="minimum seconds of the all-thread CPU baseline")
+    ap.add_argument("--cfg4-ranks", type=int, default=0,
+                    help="with one process: the cfg4 leg times rank 0's share of this many ranks' plan")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
