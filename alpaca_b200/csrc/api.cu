@@ -312,7 +312,8 @@ alpaca_cuda_status device_for(cudaStream_t stream, const char* who, DeviceInfo* 
 // Caller workspace against what `kind` needs for `d`.
 alpaca_cuda_status check_workspace(const alpaca_attn_desc& d, alpaca_attn_kernel kind, const void* ws, size_t ws_bytes,
                                    const char* who) {
-    const size_t need = workspace_for(d, kind);
+    // the tensor-core prefill runs unsplit when given less than its query size, so only its minimum is required
+    const size_t need = kind == ALPACA_ATTN_PREFILL_TC ? prefill_workspace_min_bytes(d) : workspace_for(d, kind);
     if (need > 0 && (ws_bytes < need || !ws))
         return fail(ALPACA_CUDA_ERR_WORKSPACE_TOO_SMALL, std::string(who) + ": workspace of " + std::to_string(ws_bytes) +
                                                              " bytes, " + std::to_string(need) + " needed");

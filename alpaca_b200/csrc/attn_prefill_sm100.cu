@@ -63,6 +63,7 @@ __host__ __device__ constexpr int threads_for() { return 32 * (4 + 4 * R * NT); 
 constexpr int kThreads = threads_for<2, 2>();
 constexpr int kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;      // log2 units
+constexpr int kMaxKvSplits = 8;                // split-KV parts of a work item at most
 
 // Geometry per head dim and number of query tiles per work item (NT). Rows of Q, K and V live in shared memory as
 // D/64 column blocks [rows][64] (128 bytes per row, 128-byte swizzle), the layout a 64 x 1 x rows x 1 TMA box
@@ -104,6 +105,11 @@ struct PrefillArgs {
     float scale_log2;
     unsigned* err;
     unsigned flags;
+    // Split KV (uniform form, calls with fewer work items than SMs): each item's KV blocks are cut into kv_splits
+    // parts, each part an item of its own that leaves its unnormalised rows and their (max, sum) in `part`
+    // ([item][tile][row][D + 2] f32), and prefill_merge_kernel writes the output; kv_splits = 1 otherwise.
+    int kv_splits;
+    float* part;
     const int* block_table;  // paged cache: [seq][max_blocks] (null: contiguous caches)
     int block_rows, max_blocks, pool_blocks, last_block;  // last_block: block (of a sequence) holding row kv_len - 1
     // Ragged form: the work list the plan kernel wrote into the workspace. plan[0].x = units; unit u is
@@ -151,6 +157,7 @@ struct Item {
     int nrows[3];   // query rows of each tile that exist (ragged form; the uniform form clips through the maps)
     int nblk[3];    // KV blocks each tile attends to
     int ctx_end;    // ragged form: the sequence's context end; rows at or past it are never used
+    int jb0, jb1;   // KV blocks [jb0, jb1) of this item (of its part, with split KV; else 0 .. the most of any tile)
 };
 
 template <int BN>
@@ -161,7 +168,7 @@ __device__ __forceinline__ int tile_blocks(const PrefillArgs& a, int row0) {
     return (visible + BN - 1) / BN;
 }
 
-template <int BN, int NT, bool VL>
+template <int BN, int NT, bool VL, bool KS = false>
 __device__ __forceinline__ Item decode_item(const PrefillArgs& a, int it) {
     Item x;
     if constexpr (VL) {
@@ -179,22 +186,33 @@ __device__ __forceinline__ Item decode_item(const PrefillArgs& a, int it) {
             x.nrows[t] = max(0, min(kBM, r.w - t * kBM));
             x.nblk[t] = x.nrows[t] > 0 ? (x.pos0[t] + x.nrows[t] + BN - 1) / BN : 0;
         }
+        x.jb0 = 0;
+        x.jb1 = x.nblk[0];
+#pragma unroll
+        for (int t = 1; t < NT; t++) x.jb1 = max(x.jb1, x.nblk[t]);
         return x;
     }
     const int per_rank = a.n_seqs * a.n_heads;
-    const int rank = it / per_rank, rem = it - rank * per_rank;
-    const int group = a.n_groups - 1 - rank;  // heaviest groups first
+    const int slot = it / per_rank, rem = it - slot * per_rank;
+    // heaviest groups first, then (split KV) their parts; without the split the part range is the whole, as constants
+    const int splits = KS ? a.kv_splits : 1;
+    const int group = a.n_groups - 1 - (KS ? slot / splits : slot);
+    const int part = KS ? slot - (slot / splits) * splits : 0;
     x.seq = rem / a.n_heads;
     x.head = rem - x.seq * a.n_heads;
     x.cseq = x.seq;
     x.ctx_end = a.kv_len;
+    int nmax = 0;
 #pragma unroll
     for (int t = 0; t < NT; t++) {
         x.row0[t] = (group * NT + t) * kBM;
         x.pos0[t] = a.start + x.row0[t];
         x.nrows[t] = kBM;
         x.nblk[t] = tile_blocks<BN>(a, x.row0[t]);
+        nmax = max(nmax, x.nblk[t]);
     }
+    x.jb0 = KS ? part * nmax / splits : 0;
+    x.jb1 = KS ? (part + 1) * nmax / splits : nmax;
     return x;
 }
 
@@ -202,9 +220,10 @@ __device__ __forceinline__ Item decode_item(const PrefillArgs& a, int it) {
 // fields, so they live in registers (an Item indexed by a run-time tile would sit in local memory).
 struct TileWork {
     int seq, head, cseq, row0, pos0, nrows, nblk;
+    int jb0, jb1;  // this tile's KV blocks [jb0, jb1) in the item (its part; empty when jb1 <= jb0)
 };
 
-template <int BN, int NT, bool VL>
+template <int BN, int NT, bool VL, bool KS = false>
 __device__ __forceinline__ TileWork tile_work(const PrefillArgs& a, int it, int t) {
     TileWork w;
     if constexpr (VL) {
@@ -217,26 +236,34 @@ __device__ __forceinline__ TileWork tile_work(const PrefillArgs& a, int it, int 
         w.pos0 = r.z + t * kBM;
         w.nrows = max(0, min(kBM, r.w - t * kBM));
         w.nblk = w.nrows > 0 ? (w.pos0 + w.nrows + BN - 1) / BN : 0;
+        w.jb0 = 0;
+        w.jb1 = w.nblk;
         return w;
     }
     const int per_rank = a.n_seqs * a.n_heads;
-    const int rank = it / per_rank, rem = it - rank * per_rank;
+    const int slot = it / per_rank, rem = it - slot * per_rank;
+    const int splits = KS ? a.kv_splits : 1;  // as decode_item
+    const int group = a.n_groups - 1 - (KS ? slot / splits : slot);
+    const int part = KS ? slot - (slot / splits) * splits : 0;
     w.seq = rem / a.n_heads;
     w.head = rem - w.seq * a.n_heads;
     w.cseq = w.seq;
-    w.row0 = ((a.n_groups - 1 - rank) * NT + t) * kBM;  // heaviest groups first, as decode_item
+    w.row0 = (group * NT + t) * kBM;
     w.pos0 = a.start + w.row0;
     w.nrows = kBM;
     w.nblk = tile_blocks<BN>(a, w.row0);
-    return w;
-}
-
-template <int NT>
-__device__ __forceinline__ int item_blocks(const Item& x) {
-    int n = x.nblk[0];
+    if constexpr (KS) {
+        // the item's block count is its last existing tile's (later tiles see more positions)
+        int nmax = 0;
 #pragma unroll
-    for (int t = 1; t < NT; t++) n = max(n, x.nblk[t]);
-    return n;
+        for (int u = 0; u < NT; u++) nmax = max(nmax, tile_blocks<BN>(a, (group * NT + u) * kBM));
+        w.jb0 = part * nmax / splits;
+        w.jb1 = min(w.nblk, (part + 1) * nmax / splits);
+    } else {
+        w.jb0 = 0;
+        w.jb1 = w.nblk;
+    }
+    return w;
 }
 
 // ---------------------------------------------------------------------------------------------- MMA helpers
@@ -274,7 +301,7 @@ __device__ __forceinline__ void mma_pv(const SmemLayout<D, NT>* sm, int tile, in
 
 // ---------------------------------------------------------------------------------------------- kernel
 
-template <int D, int kEmuPairs, int R, int NT, bool VL = false>
+template <int D, int kEmuPairs, int R, int NT, bool VL = false, bool KS = false>
 __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_kt,
@@ -284,6 +311,7 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
     constexpr int kStages = stages_for<D, NT>();
     constexpr bool kTmaOut = tma_out<D, R, NT>();
     static_assert(D == 64 || R == 1, "head_dim 128 is built in the one-thread-per-row form only");
+    static_assert(!KS || (NT == 2 && !VL), "split KV in the uniform two-tile forms only");
     static_assert(NT == 2 || R == 1, "three query tiles in the one-thread-per-row form only");
     constexpr int kBN = G::BN, SC = G::SC, OC = G::OC;
     extern __shared__ uint8_t smem_raw[];
@@ -355,11 +383,11 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
         uint32_t kv_it = 0, k_issued = 0, v_issued = 0, q_uses[NT] = {};
         bool ok = true;
         for (int r = 0, it = item_of(0); ok && it < total_items; it = item_of(++r)) {
-            const Item x = decode_item<kBN, NT, VL>(a, it);
+            const Item x = decode_item<kBN, NT, VL, KS>(a, it);
             const int kvh = x.head / (a.n_heads / a.n_kv_heads);
 #pragma unroll
             for (int t = 0; t < NT; t++) {  // unrolled: the Item and q_uses stay in registers
-                if (!ok || x.nblk[t] == 0) continue;
+                if (!ok || min(x.nblk[t], x.jb1) <= x.jb0) continue;  // no KV block of this tile in the item
                 ok = mbar_wait(&sm->q_empty[t], (q_uses[t] & 1) ^ 1, ab);
                 if (!ok) continue;
                 mbar_arrive_expect_tx(&sm->q_full[t], G::kQBytes);
@@ -368,8 +396,7 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
                     tma_load_4d(sm->q[t] + cb * kBM * 64, &tm_q, 64 * cb, x.head, x.row0[t], x.cseq, &sm->q_full[t]);
                 q_uses[t]++;
             }
-            const int nmax = item_blocks<NT>(x);
-            for (int j = 0; ok && j < nmax; j++, kv_it++) {
+            for (int j = x.jb0; ok && j < x.jb1; j++, kv_it++) {
                 const int st = kv_it % kStages;
                 const uint32_t ph = (kv_it / kStages) & 1;
                 // Contiguous caches: coordinates (row, sequence) of the per-sequence map. Paged: (row within the
@@ -431,18 +458,20 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
             bool ok = true;
             if (debug_timeout && t == 0) ok = mbar_wait(&sm->dbg, 0, ab);  // nothing arrives: exercises the give-up path
             for (int r = 0, it = item_of(0); ok && it < total_items; it = item_of(++r)) {
-                const int n = tile_work<kBN, NT, VL>(a, it, t).nblk;  // this issuer's tile
-                const Item xi = decode_item<kBN, NT, VL>(a, it);
-                const int nmax = item_blocks<NT>(xi);
-                if (n > 0) {
+                const TileWork tw = tile_work<kBN, NT, VL, KS>(a, it, t);  // this issuer's tile
+                const int n = tw.jb1;                                    // its blocks are [j0, n)
+                const Item xi = decode_item<kBN, NT, VL, KS>(a, it);
+                const int j0 = xi.jb0, j1 = xi.jb1;                      // the item's blocks
+                const bool has = n > j0;
+                if (has) {
                     ok = mbar_wait(&sm->q_full[t], q_uses & 1, ab);
                     if (!ok) break;
                 }
                 // Iteration j consumes K(j) (S of block j) and then V(j-1) (P·V of block j-1): the producer's load
                 // order, so every wait here depends only on releases made kStages iterations earlier.
-                for (int j = 0; ok && j <= nmax; j++) {
-                    if (j < nmax) {
-                        const uint32_t cur = kv_it + j;
+                for (int j = j0; ok && j <= j1; j++) {
+                    if (j < j1) {
+                        const uint32_t cur = kv_it + (j - j0);
                         const int st = cur % kStages;
                         ok = mbar_wait(&sm->k_full[st], (cur / kStages) & 1, ab);
                         if (!ok) break;
@@ -459,9 +488,9 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
                             mbar_arrive(&sm->k_empty[st]);  // block this tile does not use
                         }
                     }
-                    if (j > 0) {
+                    if (j > j0) {
                         const int b = j - 1;
-                        const uint32_t prv = kv_it + b;
+                        const uint32_t prv = kv_it + (b - j0);
                         const int sp = prv % kStages;
                         // ragged form: in a block that reaches the sequence's context end, warp 3 zeroes the V rows
                         // past it first (v_ready); every other block goes to the MMA as soon as it lands. (warp 3
@@ -474,7 +503,7 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
                             ok = mbar_wait(&sm->p_full[t], p_uses & 1, ab);
                             if (!ok) break;
                             tc_fence_after();
-                            mma_pv<D, NT>(sm, t, sp, tmem_base, b > 0);
+                            mma_pv<D, NT>(sm, t, sp, tmem_base, b > j0);  // the part's first block starts O
                             tc_commit(&sm->o_done[t]);
                             tc_commit(&sm->v_empty[sp]);
                             p_uses++;
@@ -484,8 +513,8 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
                     }
                 }
                 if (!ok) break;
-                kv_it += nmax;
-                if (n > 0) q_uses++;
+                kv_it += j1 - j0;
+                if (has) q_uses++;
             }
             // Retire every MMA this thread issued before TMEM is freed.
             int dummy = 0;
@@ -514,9 +543,8 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
             uint32_t kv_it = 0;
             bool ok = true;
             for (int r = 0, it = item_of(0); ok && it < total_items; it = item_of(++r)) {
-                const Item x = decode_item<kBN, NT, VL>(a, it);
-                const int nmax = item_blocks<NT>(x);
-                for (int j = 0; j < nmax; j++, kv_it++) {
+                const Item x = decode_item<kBN, NT, VL, KS>(a, it);
+                for (int j = x.jb0; j < x.jb1; j++, kv_it++) {
                     const int st = kv_it % kStages;
                     ok = __all_sync(0xffffffffu, mbar_wait(&sm->v_full[st], (kv_it / kStages) & 1, ab));
                     if (!ok) break;
@@ -550,15 +578,15 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
         const bool issuer = kTmaOut && ((warp - 4) & 3) == 0 && lane == 0;  // the tile's output TMA thread
         bool ok = true;
         for (int r = 0, it = item_of(0); ok && it < total_items; it = item_of(++r)) {
-            const TileWork x = tile_work<kBN, NT, VL>(a, it, tile);
-            const int nb = x.nblk;
-            if (nb == 0) continue;
+            const TileWork x = tile_work<kBN, NT, VL, KS>(a, it, tile);
+            const int jb0 = x.jb0;  // this tile's KV blocks [jb0, jb1) in the item
+            if (x.jb1 <= jb0) continue;
             const int row0 = x.row0;
             const int pos0 = x.pos0;     // absolute position of the tile's first query
             const int qpos = pos0 + row;  // and of this thread's
             float m_used = -INFINITY;
             float2 lsum = make_float2(0.f, 0.f);
-            for (int j = 0; j < nb; j++) {
+            for (int j = jb0; j < x.jb1; j++) {
                 ok = __all_sync(0xffffffffu, mbar_wait(&sm->s_full[tile], s_uses & 1, ab));
                 if (!ok) break;
                 s_uses++;
@@ -589,7 +617,7 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
                 const float pmax = fmaxf(fmax3(mv[0], mv[1], mv[2]), fmax3(fmax3(mv[3], mv[4], mv[5]), mv[6], mv[7]));
                 // running max in log2 units; it moves only when the block exceeds it by more than the threshold
                 const float pms = pmax * a.scale_log2;
-                const float m_new = (j == 0 || pms > m_used + kRescaleThreshold) ? pms : m_used;
+                const float m_new = (j == jb0 || pms > m_used + kRescaleThreshold) ? pms : m_used;
                 const float m_sub = (m_new == -INFINITY) ? 0.f : m_new;
                 const float2 c2 = make_float2(a.scale_log2, a.scale_log2), nm2 = make_float2(-m_sub, -m_sub);
                 uint32_t pk[kBN / 2];
@@ -607,7 +635,7 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
                 const float2 lb = __fadd2_rn(__fadd2_rn(ls[0], ls[1]), __fadd2_rn(ls[2], ls[3]));
                 bool rescale = false;
                 float alpha = 1.f;
-                if (j > 0 && m_new > m_used) {
+                if (j > jb0 && m_new > m_used) {
                     alpha = ex2_approx(m_used - m_new);
                     rescale = true;
                     lsum.x *= alpha;
@@ -615,7 +643,7 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
                 }
                 m_used = m_new;
                 lsum = __fadd2_rn(lsum, lb);
-                if (j > 0) {  // PV(j-1) must be done before P is overwritten or O is rescaled
+                if (j > jb0) {  // PV(j-1) must be done before P is overwritten or O is rescaled
                     ok = __all_sync(0xffffffffu, mbar_wait(&sm->o_done[tile], o_uses & 1, ab));
                     if (!ok) break;
                     o_uses++;
@@ -645,6 +673,21 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
             if (!ok) break;
             o_uses++;
             tc_fence_after();
+            if (KS) {  // split KV: this part's rows unnormalised, with their max (log2 units) and sum
+                float* rec = a.part + ((static_cast<int64_t>(it) * NT + tile) * kBM + row) * (D + 2);
+#pragma unroll
+                for (int c0 = 0; c0 < D; c0 += 32) {
+                    float o[32];
+                    tmem_ld32(o_addr + c0, o);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int c = 0; c < 32; c += 2)  // records are 8-byte aligned ((D + 2) x 4 bytes each)
+                        *reinterpret_cast<float2*>(rec + c0 + c) = make_float2(o[c], o[c + 1]);
+                }
+                *reinterpret_cast<float2*>(rec + D) = make_float2(m_used, lsum.x + lsum.y);
+                tc_fence_before();
+                continue;
+            }
             const float inv = 1.f / (lsum.x + lsum.y);
             // whole tiles leave through the staging box and TMA stores; in the ragged form a sequence's last,
             // partial tile is stored row by row (its map rows past the tile belong to the next sequence)
@@ -763,15 +806,15 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
         const bool issuer = kTmaOut && ((warp - 4) & 7) == 0 && lane == 0;  // the tile's output TMA thread
         bool ok = true;
         for (int r = 0, it = item_of(0); ok && it < total_items; it = item_of(++r)) {
-            const TileWork x = tile_work<kBN, NT, VL>(a, it, tile);
-            const int nb = x.nblk;
-            if (nb == 0) continue;
+            const TileWork x = tile_work<kBN, NT, VL, KS>(a, it, tile);
+            const int jb0 = x.jb0;  // this tile's KV blocks [jb0, jb1) in the item
+            if (x.jb1 <= jb0) continue;
             const int row0 = x.row0;
             const int pos0 = x.pos0;     // absolute position of the tile's first query
             const int qpos = pos0 + row;  // and of this thread's
             float m_used = -INFINITY;
             float2 lsum = make_float2(0.f, 0.f);    // this thread's half of the row sum (two lanes of a pair)
-            for (int j = 0; j < nb; j++) {
+            for (int j = jb0; j < x.jb1; j++) {
                 ok = __all_sync(0xffffffffu, mbar_wait(&sm->s_full[tile], s_uses & 1, ab));
                 if (!ok) break;
                 s_uses++;
@@ -807,7 +850,7 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
                 // without waiting; the row max is the larger candidate, and a half whose candidate was lower
                 // scales its P pairs down afterwards (rare: first block of a tile, or a max that jumped).
                 const float pms = pmax * a.scale_log2;
-                const float m_mine = (j == 0 || pms > m_used + kRescaleThreshold) ? pms : m_used;
+                const float m_mine = (j == jb0 || pms > m_used + kRescaleThreshold) ? pms : m_used;
                 const int par = x_uses & 1;
                 sm->xmax[tile][par][half][row] = m_mine;
                 __threadfence_block();
@@ -837,8 +880,10 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
                 x_uses++;
                 const float m_row = fmaxf(m_mine, sm->xmax[tile][par][half ^ 1][row]);
                 if (__any_sync(0xffffffffu, m_mine < m_row)) {
-                    // f16 factor, applied identically to the P pairs and to this half's row sum
-                    const __half2 f2 = __float2half2_rn(ex2_approx(m_mine - m_row));  // 1 where m_mine == m_row
+                    // f16 factor, applied identically to the P pairs and to this half's row sum: 1 where m_mine ==
+                    // m_row, including a row that sees no key of this block range (both -inf, whose difference is
+                    // NaN: a split-KV part that starts past the row's position)
+                    const __half2 f2 = __float2half2_rn(m_mine == m_row ? 1.f : ex2_approx(m_mine - m_row));
                     const float f = __low2float(f2);
 #pragma unroll
                     for (int pr = 0; pr < SC / 2; pr++) {
@@ -851,7 +896,7 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
                 }
                 bool rescale = false;
                 float alpha = 1.f;
-                if (j > 0 && m_row > m_used) {
+                if (j > jb0 && m_row > m_used) {
                     alpha = ex2_approx(m_used - m_row);
                     rescale = true;
                     lsum.x *= alpha;
@@ -859,7 +904,7 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
                 }
                 m_used = m_row;
                 lsum = __fadd2_rn(lsum, lb);
-                if (j > 0) {  // PV(j-1) must be done before P is overwritten or O is rescaled
+                if (j > jb0) {  // PV(j-1) must be done before P is overwritten or O is rescaled
                     ok = __all_sync(0xffffffffu, mbar_wait(&sm->o_done[tile], o_uses & 1, ab));
                     if (!ok) break;
                     o_uses++;
@@ -905,6 +950,14 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
             if (!ok) break;
             x_uses++;
             const float l = lpart + sm->xl[tile][half ^ 1][row];
+            if (KS) {  // split KV: this part's rows unnormalised, with their max (log2 units) and sum
+                float* rec = a.part + ((static_cast<int64_t>(it) * NT + tile) * kBM + row) * (D + 2);
+#pragma unroll
+                for (int c = 0; c < OC; c += 2)  // records are 8-byte aligned ((D + 2) x 4 bytes each)
+                    *reinterpret_cast<float2*>(rec + half * OC + c) = make_float2(o[c], o[c + 1]);
+                if (half == 0) *reinterpret_cast<float2*>(rec + D) = make_float2(m_used, l);
+                continue;
+            }
             const int t = row0 + row;  // row of the output map
             // whole tiles leave through the staging box and TMA stores; in the ragged form a sequence's last,
             // partial tile is stored row by row (its map rows past the tile belong to the next sequence)
@@ -987,6 +1040,71 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
         if (lane == 0) mbar_arrive(&sm->retire);
     }
 
+}
+
+// Split KV: one warp per output row (item of the unsplit call, tile, row) merges the row's parts. With m_p the part's
+// running max (log2 units, -inf where the part saw no visible key), l_p its sum and O_p its unnormalised context,
+// out = sum_p 2^(m_p - M) O_p / sum_p 2^(m_p - M) l_p, M = max_p m_p. A part that holds no KV block of the tile wrote
+// nothing and is skipped (the block ranges are recomputed as the prefill kernel cut them).
+template <int D, int BN>
+__global__ void __launch_bounds__(256) prefill_merge_kernel(const PrefillArgs a) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // every part of the prefill launch has been written
+    constexpr int NT = 2, CPL = D / 32;                  // columns per lane
+    const int w = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    const int per_rank = a.n_seqs * a.n_heads;
+    const int row = w % kBM, tile = (w / kBM) % NT, base = w / (kBM * NT);
+    const int gr = base / per_rank, rem = base - gr * per_rank;  // group rank (heaviest first) and (seq, head)
+    if (gr >= a.n_groups) return;
+    const int group = a.n_groups - 1 - gr;
+    const int seq = rem / a.n_heads, head = rem - seq * a.n_heads;
+    const int row0 = (group * NT + tile) * kBM;
+    const int t = row0 + row;
+    if (t >= a.tokens) return;
+    const int nblk = tile_blocks<BN>(a, row0);
+    int nmax = 0;
+#pragma unroll
+    for (int u = 0; u < NT; u++) nmax = max(nmax, tile_blocks<BN>(a, (group * NT + u) * kBM));
+    const int S = a.kv_splits;
+    // every part's loads first (up to kMaxKvSplits parts, unrolled), then the sums
+    float mp[kMaxKvSplits], lp[kMaxKvSplits], op[kMaxKvSplits][CPL];
+#pragma unroll
+    for (int p = 0; p < kMaxKvSplits; p++) {
+        const bool use = p < S && min(nblk, (p + 1) * nmax / S) > p * nmax / S;
+        mp[p] = -INFINITY;
+        lp[p] = 0.f;
+#pragma unroll
+        for (int c = 0; c < CPL; c++) op[p][c] = 0.f;
+        if (use) {
+            const float* rec =
+                a.part + ((static_cast<int64_t>((gr * S + p) * per_rank + rem) * NT + tile) * kBM + row) * (D + 2);
+            const float2 ml = __ldg(reinterpret_cast<const float2*>(rec + D));
+            mp[p] = ml.x;
+            lp[p] = ml.y;
+#pragma unroll
+            for (int c = 0; c < CPL; c++) op[p][c] = __ldg(rec + lane + 32 * c);
+        }
+    }
+    float M = -INFINITY;
+#pragma unroll
+    for (int p = 0; p < kMaxKvSplits; p++) M = fmaxf(M, mp[p]);
+    float acc[CPL] = {};
+    float L = 0.f;
+#pragma unroll
+    for (int p = 0; p < kMaxKvSplits; p++) {
+        const float wgt = mp[p] == -INFINITY ? 0.f : exp2f(mp[p] - M);  // a part that saw no visible key: 0
+        L = fmaf(wgt, lp[p], L);
+#pragma unroll
+        for (int c = 0; c < CPL; c++) acc[c] = fmaf(wgt, op[p][c], acc[c]);
+    }
+    const float inv = 1.f / L;
+    const int64_t off = static_cast<int64_t>(seq) * a.out_seq_stride + static_cast<int64_t>(t) * a.out_token_stride +
+                        static_cast<int64_t>(head) * D;
+#pragma unroll
+    for (int c = 0; c < CPL; c++) {
+        if (a.out_f16) static_cast<__half*>(a.out)[off + lane + 32 * c] = __float2half_rn(acc[c] * inv);
+        else static_cast<float*>(a.out)[off + lane + 32 * c] = acc[c] * inv;
+    }
 }
 
 // f32 -> f16 copy of Q into the workspace ([seq][token][head][d], dense), for f32 callers.
@@ -1248,10 +1366,42 @@ size_t plan_units(const alpaca_attn_desc& d) {
     const int group = kUnitTiles * kBM;
     return static_cast<size_t>(d.n_seqs) * ((d.tokens + group - 1) / group);
 }
+// Split KV for uniform calls with fewer work items than one per SM of a B200 (148): each item's KV blocks are cut
+// into up to 8 parts of at least 4 blocks of its heaviest group, so the call fills the SMs (a smaller call does not
+// repay the merge: a 512-token chunk at position 0 measured 12.2 us per layer unsplit against 18.7 in two parts). This is the case of
+// alpaca.swift's prefill loop, one session's 512-token chunk per call at a moving start position
+// (MetalLlamaModel.swift:293-298): 18 items at SmolLM2-135M's 9 heads. ALPACA_PREFILL_SPLITS caps the parts (1 turns
+// the split off).
+constexpr int kSplitTargetItems = 148;
+int prefill_kv_splits(const alpaca_attn_desc& d) {
+    static const int cap = [] {
+        const char* e = std::getenv("ALPACA_PREFILL_SPLITS");
+        const int v = (e && *e) ? std::atoi(e) : kMaxKvSplits;
+        return std::max(1, std::min(kMaxKvSplits, v));
+    }();
+    if (is_varlen(d) || prefill_tiles(d.head_dim) != 2 || d.tokens <= 0) return 1;
+    const int bn = d.head_dim == 128 ? PG<128>::BN : PG<64>::BN;
+    const int64_t items = static_cast<int64_t>((d.tokens + 2 * kBM - 1) / (2 * kBM)) * d.n_seqs * d.n_heads;
+    if (items >= kSplitTargetItems) return 1;
+    const int nmax = (d.start_position + d.tokens + bn - 1) / bn;  // KV blocks of the call's heaviest tile
+    const int want = static_cast<int>((kSplitTargetItems + items - 1) / items);
+    return std::max(1, std::min(std::min(cap, want), nmax / 4));  // at least 4 blocks per part
+}
+// Partial records of a split call: [item][part][tile][row][head_dim + 2] f32.
+size_t split_bytes(const alpaca_attn_desc& d) {
+    const int splits = prefill_kv_splits(d);
+    if (splits <= 1) return 0;
+    const size_t items = static_cast<size_t>((d.tokens + 2 * kBM - 1) / (2 * kBM)) * d.n_seqs * d.n_heads;
+    return items * splits * 2 * kBM * (d.head_dim + 2) * sizeof(float);
+}
 }  // namespace
 
-size_t prefill_workspace_bytes(const alpaca_attn_desc& d) {
+size_t prefill_workspace_min_bytes(const alpaca_attn_desc& d) {
     return q_stage_bytes(d) + (is_varlen(d) ? sizeof(int4) * (1 + 2 * plan_units(d)) : 0);
+}
+
+size_t prefill_workspace_bytes(const alpaca_attn_desc& d) {
+    return prefill_workspace_min_bytes(d) + split_bytes(d);
 }
 
 cudaError_t launch_prefill(const Call& c, cudaStream_t s) {
@@ -1262,8 +1412,15 @@ cudaError_t launch_prefill(const Call& c, cudaStream_t s) {
     const int tiles = vl ? kUnitTiles : prefill_tiles(d.head_dim);
     const int rows = (d128 || tiles == 3) ? 1 : (vl ? 2 : prefill_row_threads(d.head_dim));
     const int emu = vl ? 0 : prefill_emu_pairs(tiles);
-    const PrefillFn fn = vl ? (d128 ? prefill_kernel<128, 0, 1, 2, true> : prefill_kernel<64, 0, 2, 2, true>)
-                            : (d128 ? prefill_variant<128>(emu, rows, tiles) : prefill_variant<64>(emu, rows, tiles));
+    // split KV when the call is short of work items and the caller's workspace holds the partial records (a
+    // workspace of the minimum size runs the call unsplit); split calls take the default two-tile forms
+    int splits = prefill_kv_splits(d);
+    if (splits > 1 && (c.ws_bytes < prefill_workspace_bytes(d) || !c.ws || (reinterpret_cast<uintptr_t>(c.ws) & 15u)))
+        splits = 1;
+    const PrefillFn fn =
+        vl ? (d128 ? prefill_kernel<128, 0, 1, 2, true> : prefill_kernel<64, 0, 2, 2, true>)
+           : splits > 1 ? (d128 ? prefill_kernel<128, 0, 1, 2, false, true> : prefill_kernel<64, 0, 2, 2, false, true>)
+                        : (d128 ? prefill_variant<128>(emu, rows, tiles) : prefill_variant<64>(emu, rows, tiles));
     const size_t smem = d128 ? smem_bytes<128>() : (tiles == 3 ? smem_bytes<64, 3>() : smem_bytes<64>());
     const int bn = d128 ? PG<128>::BN : (tiles == 3 ? PG<64, 3>::BN : PG<64>::BN);
     // per-device function attribute (host-side, cheap next to the launch itself)
@@ -1351,8 +1508,10 @@ cudaError_t launch_prefill(const Call& c, cudaStream_t s) {
     a.start = d.start_position;
     a.kv_len = kv_len;
     a.n_groups = (d.tokens + tiles * kBM - 1) / (tiles * kBM);
+    a.kv_splits = splits;
+    a.part = splits > 1 ? reinterpret_cast<float*>(static_cast<uint8_t*>(c.ws) + q_stage_bytes(d)) : nullptr;
     // ragged form: the plan's unit count, read by the kernel; the grid is sized for the bound
-    a.total_items = vl ? static_cast<int>(plan_units(d)) * d.n_heads : a.n_groups * d.n_seqs * d.n_heads;
+    a.total_items = vl ? static_cast<int>(plan_units(d)) * d.n_heads : a.n_groups * d.n_seqs * d.n_heads * splits;
     a.scale_log2 = c.scale * kLog2e;
     a.err = c.err;
     a.flags = d.flags;
@@ -1373,7 +1532,16 @@ cudaError_t launch_prefill(const Call& c, cudaStream_t s) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, fn, tq, tk, tv, tkt, tvt, to, a);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, fn, tq, tk, tv, tkt, tvt, to, a);
+    if (e != cudaSuccess || splits <= 1) return e;
+    // the merge: one warp per output row of the unsplit items (8 rows per CTA)
+    const int64_t out_rows = static_cast<int64_t>(a.n_groups) * d.n_seqs * d.n_heads * 2 * kBM;
+    cudaLaunchConfig_t mcfg = cfg;
+    mcfg.gridDim = dim3(static_cast<unsigned>((out_rows + 7) / 8), 1, 1);
+    mcfg.blockDim = dim3(256, 1, 1);
+    mcfg.dynamicSmemBytes = 0;
+    return d128 ? cudaLaunchKernelEx(&mcfg, prefill_merge_kernel<128, PG<128>::BN>, a)
+                : cudaLaunchKernelEx(&mcfg, prefill_merge_kernel<64, PG<64>::BN>, a);
 }
 
 }  // namespace alpaca

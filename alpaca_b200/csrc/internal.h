@@ -45,7 +45,10 @@ cudaError_t launch_proj(const alpaca_proj_desc& d, int num_sms, cudaStream_t s);
 
 // ---- tcgen05 prefill (attn_prefill_sm100.cu)
 bool prefill_supported(const alpaca_attn_desc& d);
-size_t prefill_workspace_bytes(const alpaca_attn_desc& d);  // f32 -> f16 Q staging when q_dtype is f32
+// f32 -> f16 Q staging when q_dtype is f32, the ragged work list, and the split-KV records of a call with fewer
+// work items than SMs (the query size; a call given only the minimum runs unsplit)
+size_t prefill_workspace_bytes(const alpaca_attn_desc& d);
+size_t prefill_workspace_min_bytes(const alpaca_attn_desc& d);
 cudaError_t launch_prefill(const Call& c, cudaStream_t s);
 
 }  // namespace alpaca

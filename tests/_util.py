@@ -51,3 +51,19 @@ def pool(caches, block_rows, rng, max_rows, extra_blocks=3):
             pool[blk, :rows.shape[0]] = rows
     table[table < 0] = int(order[-1])  # unused entries point at a valid (NaN) block
     return pool, table
+
+
+def prefill_unsplit(q, k, v, out, start_position: int = 0):
+    """A uniform tensor-core prefill given only its minimum workspace (the f32 queries' staging), so the library runs
+    it unsplit: one work item per (sequence, head, pair of query tiles) over the whole KV range, the arithmetic the
+    ragged form shares bit for bit (a split-KV call sums its parts in another order)."""
+    import torch
+
+    import alpaca_b200 as ab
+    desc = ab.make_desc(q, k, v, out, start_position=start_position)
+    n = 1
+    for x in q.shape[:-1]:
+        n *= x
+    minimum = (n * q.shape[-1] * 2 + 15) // 16 * 16 if q.dtype == torch.float32 else 0
+    ws = torch.empty(minimum, dtype=torch.uint8, device=q.device) if minimum else None
+    ab.launch(desc, ab.Kernel.PREFILL_TC, ws)

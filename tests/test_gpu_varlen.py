@@ -15,7 +15,7 @@ import numpy as np
 import pytest
 
 import oracle
-from tests._util import max_abs_check, pool
+from tests._util import max_abs_check, pool, prefill_unsplit
 
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
@@ -57,7 +57,7 @@ def _caches(ks, vs, cap, dev):
 @pytest.mark.parametrize("d,H,Hkv", [(64, 9, 3), (128, 8, 2)])
 @pytest.mark.parametrize("q_dtype,out_dtype", [(torch.float16, torch.float32), (torch.float32, torch.float16)])
 def test_varlen_prefill_matches_oracle_and_uniform_calls(cuda_lib, d, H, Hkv, q_dtype, out_dtype):
-    from alpaca_b200 import Kernel, attention_device, device_status, prefill_varlen
+    from alpaca_b200 import device_status, prefill_varlen
     q, ks, vs, lens, starts, offs, max_ctx = _inputs(SEQS, H, Hkv, d, 900 + d)
     dev = torch.device("cuda")
     total, pad = q.shape[0], 5
@@ -77,10 +77,9 @@ def test_varlen_prefill_matches_oracle_and_uniform_calls(cuda_lib, d, H, Hkv, q_
         o0 = int(offs[s])
         ref = oracle.attention(q[o0:o0 + T], ks[s], vs[s], start)
         max_abs_check(got[o0:o0 + T], ref, bound, f"varlen d={d} seq {s} T={T} start={start} q={q_dtype} out={out_dtype}")
-        # the same sequence as its own uniform call: identical bits
+        # the same sequence as its own (unsplit) uniform call: identical bits
         uni = torch.empty((T, H, d), dtype=out_dtype, device=dev)
-        attention_device(qd[o0:o0 + T], kd[s, :start + T], vd[s, :start + T], uni, start_position=start,
-                         kind=Kernel.PREFILL_TC)
+        prefill_unsplit(qd[o0:o0 + T], kd[s, :start + T], vd[s, :start + T], uni, start_position=start)
         device_status()
         assert torch.equal(uni, out[o0:o0 + T]), f"seq {s}: ragged and uniform calls differ"
 
@@ -136,7 +135,7 @@ def test_chunked_prefill_of_several_sessions(cuda_lib):
     """Three sessions' prompts prefilled in 512-token chunks, every active session's next chunk in one ragged call
     per step (each at its own moving start, as MetalLlamaModel.swift:293-298 moves startPosition), equal each
     session's one-shot prefill bit for bit."""
-    from alpaca_b200 import Kernel, attention_device, device_status, prefill_varlen
+    from alpaca_b200 import device_status, prefill_varlen
     H, Hkv, d, chunk = 9, 3, 64, 512
     prompts = [1300, 512, 2000]
     dev = torch.device("cuda")
@@ -160,6 +159,6 @@ def test_chunked_prefill_of_several_sessions(cuda_lib):
     device_status()
     for i, n in enumerate(prompts):
         one = torch.empty((n, H, d), dtype=torch.float32, device=dev)
-        attention_device(qs[i], kc[i, :n], vc[i, :n], one, kind=Kernel.PREFILL_TC)
+        prefill_unsplit(qs[i], kc[i, :n], vc[i, :n], one)
         device_status()
         assert torch.equal(one, outs[i]), f"session {i}: chunked and one-shot prefill differ"
