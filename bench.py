@@ -10,6 +10,8 @@ a SplitMix64 + Box-Muller generator (`synth_normal`), the same draws the referen
 
 The same JSON line carries the other measured legs, each with its own timing, clocks and roofline:
   e2e / e2e_f16_out  the headline step through the C ABI with pinned host buffers, copies inside the timed region
+  chunked_prefill    alpaca.swift's own prefill loop: the config-2 prompt in 512-token chunks at moving start positions,
+                     30 layers per chunk (calls short of work items split their KV range over the SMs)
   decode             config 3: split-KV decode (batch 64, one token each, contexts U[1,4096], 30 layers of f16 caches)
   rope_kv_append     the RoPE + KV-cache append upstream of the attention, config-2 shape
   decode_proj        the fused decode projections around the attention (norm + QKV, out + residual, gate/up + SiLU,
@@ -212,14 +214,15 @@ def dist_setup(gpus: int):
         import datetime
         import torch.distributed as dist
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
-                                device_id=torch.device("cuda", local))
-        pg = dist
-        # Communicator set-up may print a banner on stdout; keep stdout for the one JSON result line.
+        # Communicator set-up (eager with device_id: inside init_process_group) may print a banner on stdout; keep
+        # stdout for the one JSON result line.
         sys.stdout.flush()
         saved = os.dup(1)
         os.dup2(2, 1)
         try:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                    device_id=torch.device("cuda", local))
+            pg = dist
             dist.barrier()
             torch.cuda.synchronize()
         finally:
@@ -421,6 +424,51 @@ def leg_e2e(c: Ctx, q, k, v, out_dtype, job_flops):
             "clocks": clk,
             "api": "alpaca_attention (C ABI via ctypes), one call per chunk of sequences; pinned host Q/K/V in, "
                    "context out, every step; copy-in / compute / copy-out on three streams"}
+
+
+def leg_chunked(c: Ctx):
+    """alpaca.swift's own prefill loop (MetalLlamaModel.swift:293-298): one session's 4096-token prompt in 512-token
+    chunks at a moving start position, every chunk through the 30 layers before the next (240 calls per step, each
+    one layer's chunk, replayed from a CUDA graph), config 2's heads and FLOPs. A chunk has 18 work items (9 heads x 2
+    pairs of query tiles), so the library splits the KV range of the later chunks' items over the SMs and merges the
+    parts; the workspace is the size the library asks for."""
+    torch, ab, args = c.torch, c.ab, c.args
+    T, L, CH = args.tokens, args.layers, 512
+    g = torch.Generator(device=c.dev)
+    g.manual_seed(20260108 + 1000 * c.rank)
+    k = [torch.randn((T, KVH, D), generator=g, device=c.dev).half() for _ in range(L)]
+    v = [torch.randn((T, KVH, D), generator=g, device=c.dev).half() for _ in range(L)]
+    q = [torch.randn((T, H, D), generator=g, device=c.dev).half() for _ in range(L)]
+    out = [torch.empty((T, H, D), dtype=torch.float32, device=c.dev) for _ in range(L)]
+    descs = [ab.make_desc(q[l][c0:c0 + CH], k[l][:c0 + CH], v[l][:c0 + CH], out[l][c0:c0 + CH], start_position=c0)
+             for c0 in range(0, T, CH) for l in range(L)]
+    needs = [ab.workspace_bytes(d, ab.Kernel.PREFILL_TC) for d in descs]  # > 0: a split call (f16 queries)
+    need = max(needs)
+    ws = torch.empty(max(need, 16), dtype=torch.uint8, device=c.dev)  # stream-ordered calls share it
+    launches = sum(2 if n > 0 else 1 for n in needs)  # a split call adds the merge kernel
+
+    def step():
+        for d in descs:
+            ab.launch(d, ab.Kernel.PREFILL_TC, ws)
+
+    gr = c.graph(step)
+    ms, ms_max, clk = c.timed(gr.replay, args.steps, args.warmup)
+    del gr
+    import oracle
+    rows = _spot_rows(T, H)
+    ref = oracle.attention_rows(q[0].float().cpu().numpy(), k[0].float().cpu().numpy(), v[0].float().cpu().numpy(),
+                                0, rows)
+    sel = oracle.rows_mask(rows, T, H)
+    spot = max_over_ranks(float(abs(out[0].cpu().numpy()[sel] - ref[sel]).max()), c.pg)
+    flops = L * flops_prefill(T)
+    return {"workload": f"alpaca's chunked prefill: a {T}-token prompt in {CH}-token chunks at moving start "
+                        f"positions, {L} layers per chunk ({len(descs)} calls per step), 9/3 heads, d=64, f16 in / "
+                        "f32 out; calls short of work items split their KV range over the SMs",
+            "value": c.world * flops / (ms_max * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms_max,
+            "tokens_per_s": c.world * T / (ms_max * 1e-3), "scaling": "weak", "workspace_bytes": need,
+            "l2": f"{L} layers' K/V and Q ({L * T * (H + 2 * KVH) * D * 2 / 1e6:.0f} MB) vs 126 MB L2 (no flush)",
+            "split_calls_per_step": sum(1 for n in needs if n > 0),
+            "clocks": clk, "spot_check_max_abs": spot, "gpu_launches": args.steps * launches}
 
 
 def leg_decode(c: Ctx):
@@ -821,6 +869,8 @@ def run_ours(args):
         e2e16 = leg_e2e(c, p2["q"], p2["k"], p2["v"], torch.float16, job_flops)
     del p2["q"], p2["k"], p2["v"], p2["out"]
     torch.cuda.empty_cache()
+    chunked = leg_chunked(c) if not args.no_chunked else None
+    torch.cuda.empty_cache()
     decode = leg_decode(c) if not args.no_decode else None
     torch.cuda.empty_cache()
     rope_kv = leg_rope(c) if not args.no_rope else None
@@ -863,6 +913,7 @@ def run_ours(args):
             "gpu_launches": args.steps,
             "clocks": p2["clk"],
             "spot_check_max_abs": p2["spot"],
+            "chunked_prefill": chunked,
             "decode": decode,
             "rope_kv_append": rope_kv,
             "decode_proj": proj,
@@ -925,7 +976,7 @@ def main():
     ap.add_argument("--tokens", type=int, default=T_PREFILL)
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--dec-layers", type=int, default=LAYERS)
-    for leg in ("decode", "rope", "proj", "cpu", "e2e", "cfg4", "cfg5"):
+    for leg in ("decode", "rope", "proj", "cpu", "e2e", "cfg4", "cfg5", "chunked"):
         ap.add_argument(f"--no-{leg}", action="store_true")
     ap.add_argument("--e2e-chunk", type=int, default=0, help="sequences per ABI call in the e2e pipeline (0: 1/6 of them)")
     ap.add_argument("--cpu-seconds", type=float, default=3.0, help="minimum seconds of the all-thread CPU baseline")
