@@ -492,12 +492,12 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
                         const int b = j - 1;
                         const uint32_t prv = kv_it + (b - j0);
                         const int sp = prv % kStages;
-                        // ragged form: in a block that reaches the sequence's context end, warp 3 zeroes the V rows
-                        // past it first (v_ready); every other block goes to the MMA as soon as it lands. (warp 3
-                        // arrives on v_ready for every block, so its phases stay one per use of the stage; it cannot
-                        // run two uses ahead, since the stage's next load waits for this P.V.)
-                        const bool vfix = VL && xi.ctx_end - b * kBN < kBN;
-                        ok = mbar_wait(vfix ? &sm->v_ready[sp] : &sm->v_full[sp], (prv / kStages) & 1, ab);
+                        // ragged form: warp 3 has zeroed the V rows past the context (and is done with the stage).
+                        // Every block waits for it, not only the blocks that reach the context end: the stage's
+                        // next load follows this P.V, and warp 3 must have seen this load's barrier phase before the
+                        // next one completes (a version that sent inner blocks straight to the MMA let warp 3 fall
+                        // a phase behind and zero the wrong block).
+                        ok = mbar_wait(VL ? &sm->v_ready[sp] : &sm->v_full[sp], (prv / kStages) & 1, ab);
                         if (!ok) break;
                         if (b < n) {
                             ok = mbar_wait(&sm->p_full[t], p_uses & 1, ab);
@@ -1410,13 +1410,14 @@ cudaError_t launch_prefill(const Call& c, cudaStream_t s) {
     const bool vl = is_varlen(d);
     // The ragged form is built in the default two-tile forms only (the switches select among the uniform forms).
     const int tiles = vl ? kUnitTiles : prefill_tiles(d.head_dim);
-    const int rows = (d128 || tiles == 3) ? 1 : (vl ? 2 : prefill_row_threads(d.head_dim));
     const int emu = vl ? 0 : prefill_emu_pairs(tiles);
     // split KV when the call is short of work items and the caller's workspace holds the partial records (a
     // workspace of the minimum size runs the call unsplit); split calls take the default two-tile forms
     int splits = prefill_kv_splits(d);
     if (splits > 1 && (c.ws_bytes < prefill_workspace_bytes(d) || !c.ws || (reinterpret_cast<uintptr_t>(c.ws) & 15u)))
         splits = 1;
+    // softmax threads per query row of the form launched (its thread count and output path follow from it)
+    const int rows = (d128 || tiles == 3) ? 1 : ((vl || splits > 1) ? 2 : prefill_row_threads(d.head_dim));
     const PrefillFn fn =
         vl ? (d128 ? prefill_kernel<128, 0, 1, 2, true> : prefill_kernel<64, 0, 2, 2, true>)
            : splits > 1 ? (d128 ? prefill_kernel<128, 0, 1, 2, false, true> : prefill_kernel<64, 0, 2, 2, false, true>)
