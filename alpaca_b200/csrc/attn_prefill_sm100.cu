@@ -160,6 +160,10 @@ struct Item {
     int jb0, jb1;   // KV blocks [jb0, jb1) of this item (of its part, with split KV; else 0 .. the most of any tile)
 };
 
+// Split-KV parts a ragged unit of `nmax` KV blocks uses out of the call's `splits`: at least 4 blocks per part (the
+// host sizes `splits` from the call's bounds, and a unit near the start of its sequence has few blocks).
+__host__ __device__ __forceinline__ int unit_parts(int splits, int nmax) { return max(1, min(splits, nmax / 4)); }
+
 template <int BN>
 __device__ __forceinline__ int tile_blocks(const PrefillArgs& a, int row0) {
     if (row0 >= a.tokens) return 0;
@@ -172,9 +176,12 @@ template <int BN, int NT, bool VL, bool KS = false>
 __device__ __forceinline__ Item decode_item(const PrefillArgs& a, int it) {
     Item x;
     if constexpr (VL) {
-        // unit-major, head-minor: consecutive items share the unit's queries and (within a KV head) its K/V
-        const int unit = it / a.n_heads;
-        x.head = it - unit * a.n_heads;
+        // unit-major (then, split KV, its parts), head-minor: consecutive items share the unit's queries and (within
+        // a KV head) its K/V
+        const int slot = it / a.n_heads;
+        const int unit = KS ? slot / a.kv_splits : slot;
+        const int part = KS ? slot - unit * a.kv_splits : 0;
+        x.head = it - slot * a.n_heads;
         const int4 r = __ldg(a.plan + 1 + 2 * unit);
         x.seq = r.x;
         x.cseq = 0;
@@ -186,10 +193,17 @@ __device__ __forceinline__ Item decode_item(const PrefillArgs& a, int it) {
             x.nrows[t] = max(0, min(kBM, r.w - t * kBM));
             x.nblk[t] = x.nrows[t] > 0 ? (x.pos0[t] + x.nrows[t] + BN - 1) / BN : 0;
         }
-        x.jb0 = 0;
-        x.jb1 = x.nblk[0];
+        int nmax = x.nblk[0];
 #pragma unroll
-        for (int t = 1; t < NT; t++) x.jb1 = max(x.jb1, x.nblk[t]);
+        for (int t = 1; t < NT; t++) nmax = max(nmax, x.nblk[t]);
+        if constexpr (KS) {
+            const int up = unit_parts(a.kv_splits, nmax);  // parts at or past `up` hold no block
+            x.jb0 = part < up ? part * nmax / up : nmax;
+            x.jb1 = part < up ? (part + 1) * nmax / up : nmax;
+        } else {
+            x.jb0 = 0;
+            x.jb1 = nmax;
+        }
         return x;
     }
     const int per_rank = a.n_seqs * a.n_heads;
@@ -227,8 +241,10 @@ template <int BN, int NT, bool VL, bool KS = false>
 __device__ __forceinline__ TileWork tile_work(const PrefillArgs& a, int it, int t) {
     TileWork w;
     if constexpr (VL) {
-        const int unit = it / a.n_heads;
-        w.head = it - unit * a.n_heads;
+        const int slot = it / a.n_heads;  // as decode_item
+        const int unit = KS ? slot / a.kv_splits : slot;
+        const int part = KS ? slot - unit * a.kv_splits : 0;
+        w.head = it - slot * a.n_heads;
         const int4 r = __ldg(a.plan + 1 + 2 * unit);
         w.seq = r.x;
         w.cseq = 0;
@@ -236,8 +252,20 @@ __device__ __forceinline__ TileWork tile_work(const PrefillArgs& a, int it, int 
         w.pos0 = r.z + t * kBM;
         w.nrows = max(0, min(kBM, r.w - t * kBM));
         w.nblk = w.nrows > 0 ? (w.pos0 + w.nrows + BN - 1) / BN : 0;
-        w.jb0 = 0;
-        w.jb1 = w.nblk;
+        if constexpr (KS) {
+            int nmax = 0;
+#pragma unroll
+            for (int u = 0; u < NT; u++) {
+                const int rows = max(0, min(kBM, r.w - u * kBM));
+                nmax = max(nmax, rows > 0 ? (r.z + u * kBM + rows + BN - 1) / BN : 0);
+            }
+            const int up = unit_parts(a.kv_splits, nmax);
+            w.jb0 = part < up ? part * nmax / up : nmax;
+            w.jb1 = part < up ? min(w.nblk, (part + 1) * nmax / up) : nmax;
+        } else {
+            w.jb0 = 0;
+            w.jb1 = w.nblk;
+        }
         return w;
     }
     const int per_rank = a.n_seqs * a.n_heads;
@@ -311,7 +339,7 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
     constexpr int kStages = stages_for<D, NT>();
     constexpr bool kTmaOut = tma_out<D, R, NT>();
     static_assert(D == 64 || R == 1, "head_dim 128 is built in the one-thread-per-row form only");
-    static_assert(!KS || (NT == 2 && !VL), "split KV in the uniform two-tile forms only");
+    static_assert(!KS || NT == 2, "split KV in the two-tile forms only");
     static_assert(NT == 2 || R == 1, "three query tiles in the one-thread-per-row form only");
     constexpr int kBN = G::BN, SC = G::SC, OC = G::OC;
     extern __shared__ uint8_t smem_raw[];
@@ -375,7 +403,7 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const uint32_t tmem_base = sm->tmem_base;
     // Work items: fixed by the call's shape, or (ragged form) units of the plan the previous launch wrote x heads.
-    const int total_items = VL ? __ldg(&a.plan[0].x) * a.n_heads : a.total_items;
+    const int total_items = VL ? __ldg(&a.plan[0].x) * a.n_heads * (KS ? a.kv_splits : 1) : a.total_items;
     if (warp == 0) {
         if constexpr (R == 2 || NT == 3) setmaxnreg_dec<kRegsControl>();
         if (lane != 0) return;
@@ -1046,38 +1074,65 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
 // running max (log2 units, -inf where the part saw no visible key), l_p its sum and O_p its unnormalised context,
 // out = sum_p 2^(m_p - M) O_p / sum_p 2^(m_p - M) l_p, M = max_p m_p. A part that holds no KV block of the tile wrote
 // nothing and is skipped (the block ranges are recomputed as the prefill kernel cut them).
-template <int D, int BN>
+template <int D, int BN, bool VL>
 __global__ void __launch_bounds__(256) prefill_merge_kernel(const PrefillArgs a) {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");  // every part of the prefill launch has been written
     constexpr int NT = 2, CPL = D / 32;                  // columns per lane
     const int w = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    const int per_rank = a.n_seqs * a.n_heads;
     const int row = w % kBM, tile = (w / kBM) % NT, base = w / (kBM * NT);
-    const int gr = base / per_rank, rem = base - gr * per_rank;  // group rank (heaviest first) and (seq, head)
-    if (gr >= a.n_groups) return;
-    const int group = a.n_groups - 1 - gr;
-    const int seq = rem / a.n_heads, head = rem - seq * a.n_heads;
-    const int row0 = (group * NT + tile) * kBM;
-    const int t = row0 + row;
-    if (t >= a.tokens) return;
-    const int nblk = tile_blocks<BN>(a, row0);
-    int nmax = 0;
-#pragma unroll
-    for (int u = 0; u < NT; u++) nmax = max(nmax, tile_blocks<BN>(a, (group * NT + u) * kBM));
     const int S = a.kv_splits;
+    int nblk, nmax, up;      // the tile's KV blocks, the item's, and the parts the item was cut into
+    int64_t item0, pstep;    // record item of part p: item0 + p * pstep
+    int64_t off;             // output element of the row's first column
+    if constexpr (VL) {
+        // base = (unit, head) of the ragged work list (unit-major, head-minor, as the prefill kernel deals it)
+        const int unit = base / a.n_heads, head = base - unit * a.n_heads;
+        if (unit >= __ldg(&a.plan[0].x)) return;
+        const int4 r = __ldg(a.plan + 1 + 2 * unit);
+        const int rows_t = max(0, min(kBM, r.w - tile * kBM));
+        if (row >= rows_t) return;
+        nblk = (r.z + tile * kBM + rows_t + BN - 1) / BN;
+        nmax = 0;
+#pragma unroll
+        for (int u = 0; u < NT; u++) {
+            const int rows = max(0, min(kBM, r.w - u * kBM));
+            nmax = max(nmax, rows > 0 ? (r.z + u * kBM + rows + BN - 1) / BN : 0);
+        }
+        up = unit_parts(S, nmax);
+        item0 = static_cast<int64_t>(unit) * S * a.n_heads + head;
+        pstep = a.n_heads;
+        off = static_cast<int64_t>(r.y + tile * kBM + row) * a.out_token_stride + static_cast<int64_t>(head) * D;
+    } else {
+        const int per_rank = a.n_seqs * a.n_heads;
+        const int gr = base / per_rank, rem = base - gr * per_rank;  // group rank (heaviest first) and (seq, head)
+        if (gr >= a.n_groups) return;
+        const int group = a.n_groups - 1 - gr;
+        const int seq = rem / a.n_heads, head = rem - seq * a.n_heads;
+        const int row0 = (group * NT + tile) * kBM;
+        const int t = row0 + row;
+        if (t >= a.tokens) return;
+        nblk = tile_blocks<BN>(a, row0);
+        nmax = 0;
+#pragma unroll
+        for (int u = 0; u < NT; u++) nmax = max(nmax, tile_blocks<BN>(a, (group * NT + u) * kBM));
+        up = S;
+        item0 = static_cast<int64_t>(gr) * S * per_rank + rem;
+        pstep = per_rank;
+        off = static_cast<int64_t>(seq) * a.out_seq_stride + static_cast<int64_t>(t) * a.out_token_stride +
+              static_cast<int64_t>(head) * D;
+    }
     // every part's loads first (up to kMaxKvSplits parts, unrolled), then the sums
     float mp[kMaxKvSplits], lp[kMaxKvSplits], op[kMaxKvSplits][CPL];
 #pragma unroll
     for (int p = 0; p < kMaxKvSplits; p++) {
-        const bool use = p < S && min(nblk, (p + 1) * nmax / S) > p * nmax / S;
+        const bool use = p < up && min(nblk, (p + 1) * nmax / up) > p * nmax / up;
         mp[p] = -INFINITY;
         lp[p] = 0.f;
 #pragma unroll
         for (int c = 0; c < CPL; c++) op[p][c] = 0.f;
         if (use) {
-            const float* rec =
-                a.part + ((static_cast<int64_t>((gr * S + p) * per_rank + rem) * NT + tile) * kBM + row) * (D + 2);
+            const float* rec = a.part + ((item0 + p * pstep) * NT + tile) * kBM * (D + 2) + row * (D + 2);
             const float2 ml = __ldg(reinterpret_cast<const float2*>(rec + D));
             mp[p] = ml.x;
             lp[p] = ml.y;
@@ -1098,8 +1153,6 @@ __global__ void __launch_bounds__(256) prefill_merge_kernel(const PrefillArgs a)
         for (int c = 0; c < CPL; c++) acc[c] = fmaf(wgt, op[p][c], acc[c]);
     }
     const float inv = 1.f / L;
-    const int64_t off = static_cast<int64_t>(seq) * a.out_seq_stride + static_cast<int64_t>(t) * a.out_token_stride +
-                        static_cast<int64_t>(head) * D;
 #pragma unroll
     for (int c = 0; c < CPL; c++) {
         if (a.out_f16) static_cast<__half*>(a.out)[off + lane + 32 * c] = __float2half_rn(acc[c] * inv);
@@ -1379,11 +1432,15 @@ int prefill_kv_splits(const alpaca_attn_desc& d) {
         const int v = (e && *e) ? std::atoi(e) : kMaxKvSplits;
         return std::max(1, std::min(kMaxKvSplits, v));
     }();
-    if (is_varlen(d) || prefill_tiles(d.head_dim) != 2 || d.tokens <= 0) return 1;
+    const bool vl = is_varlen(d);  // the ragged form runs the two-tile forms whatever the switches say
+    if ((!vl && prefill_tiles(d.head_dim) != 2) || d.tokens <= 0) return 1;
     const int bn = d.head_dim == 128 ? PG<128>::BN : PG<64>::BN;
-    const int64_t items = static_cast<int64_t>((d.tokens + 2 * kBM - 1) / (2 * kBM)) * d.n_seqs * d.n_heads;
+    // items and KV blocks of the heaviest tile: exact for a uniform call, the host bounds for a ragged one (whose
+    // units then each use as many of the parts as their own blocks allow, unit_parts)
+    const int64_t items = vl ? static_cast<int64_t>(plan_units(d)) * d.n_heads
+                             : static_cast<int64_t>((d.tokens + 2 * kBM - 1) / (2 * kBM)) * d.n_seqs * d.n_heads;
     if (items >= kSplitTargetItems) return 1;
-    const int nmax = (d.start_position + d.tokens + bn - 1) / bn;  // KV blocks of the call's heaviest tile
+    const int nmax = ((vl ? d.max_ctx_len : d.start_position + d.tokens) + bn - 1) / bn;
     const int want = static_cast<int>((kSplitTargetItems + items - 1) / items);
     return std::max(1, std::min(std::min(cap, want), nmax / 4));  // at least 4 blocks per part
 }
@@ -1391,7 +1448,8 @@ int prefill_kv_splits(const alpaca_attn_desc& d) {
 size_t split_bytes(const alpaca_attn_desc& d) {
     const int splits = prefill_kv_splits(d);
     if (splits <= 1) return 0;
-    const size_t items = static_cast<size_t>((d.tokens + 2 * kBM - 1) / (2 * kBM)) * d.n_seqs * d.n_heads;
+    const size_t items = is_varlen(d) ? plan_units(d) * d.n_heads
+                                      : static_cast<size_t>((d.tokens + 2 * kBM - 1) / (2 * kBM)) * d.n_seqs * d.n_heads;
     return items * splits * 2 * kBM * (d.head_dim + 2) * sizeof(float);
 }
 }  // namespace
@@ -1419,7 +1477,8 @@ cudaError_t launch_prefill(const Call& c, cudaStream_t s) {
     // softmax threads per query row of the form launched (its thread count and output path follow from it)
     const int rows = (d128 || tiles == 3) ? 1 : ((vl || splits > 1) ? 2 : prefill_row_threads(d.head_dim));
     const PrefillFn fn =
-        vl ? (d128 ? prefill_kernel<128, 0, 1, 2, true> : prefill_kernel<64, 0, 2, 2, true>)
+        vl ? (splits > 1 ? (d128 ? prefill_kernel<128, 0, 1, 2, true, true> : prefill_kernel<64, 0, 2, 2, true, true>)
+                         : (d128 ? prefill_kernel<128, 0, 1, 2, true> : prefill_kernel<64, 0, 2, 2, true>))
            : splits > 1 ? (d128 ? prefill_kernel<128, 0, 1, 2, false, true> : prefill_kernel<64, 0, 2, 2, false, true>)
                         : (d128 ? prefill_variant<128>(emu, rows, tiles) : prefill_variant<64>(emu, rows, tiles));
     const size_t smem = d128 ? smem_bytes<128>() : (tiles == 3 ? smem_bytes<64, 3>() : smem_bytes<64>());
@@ -1510,9 +1569,11 @@ cudaError_t launch_prefill(const Call& c, cudaStream_t s) {
     a.kv_len = kv_len;
     a.n_groups = (d.tokens + tiles * kBM - 1) / (tiles * kBM);
     a.kv_splits = splits;
-    a.part = splits > 1 ? reinterpret_cast<float*>(static_cast<uint8_t*>(c.ws) + q_stage_bytes(d)) : nullptr;
+    // the parts' records follow the f32 queries' staging and the ragged work list
+    a.part = splits > 1 ? reinterpret_cast<float*>(static_cast<uint8_t*>(c.ws) + prefill_workspace_min_bytes(d))
+                        : nullptr;
     // ragged form: the plan's unit count, read by the kernel; the grid is sized for the bound
-    a.total_items = vl ? static_cast<int>(plan_units(d)) * d.n_heads : a.n_groups * d.n_seqs * d.n_heads * splits;
+    a.total_items = vl ? static_cast<int>(plan_units(d)) * d.n_heads * splits : a.n_groups * d.n_seqs * d.n_heads * splits;
     a.scale_log2 = c.scale * kLog2e;
     a.err = c.err;
     a.flags = d.flags;
@@ -1536,13 +1597,18 @@ cudaError_t launch_prefill(const Call& c, cudaStream_t s) {
     cudaError_t e = cudaLaunchKernelEx(&cfg, fn, tq, tk, tv, tkt, tvt, to, a);
     if (e != cudaSuccess || splits <= 1) return e;
     // the merge: one warp per output row of the unsplit items (8 rows per CTA)
-    const int64_t out_rows = static_cast<int64_t>(a.n_groups) * d.n_seqs * d.n_heads * 2 * kBM;
+    // (ragged: for the bound of units; the units past the plan's count return at once)
+    const int64_t out_rows = (vl ? static_cast<int64_t>(plan_units(d)) : static_cast<int64_t>(a.n_groups) * d.n_seqs) *
+                             d.n_heads * 2 * kBM;
     cudaLaunchConfig_t mcfg = cfg;
     mcfg.gridDim = dim3(static_cast<unsigned>((out_rows + 7) / 8), 1, 1);
     mcfg.blockDim = dim3(256, 1, 1);
     mcfg.dynamicSmemBytes = 0;
-    return d128 ? cudaLaunchKernelEx(&mcfg, prefill_merge_kernel<128, PG<128>::BN>, a)
-                : cudaLaunchKernelEx(&mcfg, prefill_merge_kernel<64, PG<64>::BN>, a);
+    if (vl)
+        return d128 ? cudaLaunchKernelEx(&mcfg, prefill_merge_kernel<128, PG<128>::BN, true>, a)
+                    : cudaLaunchKernelEx(&mcfg, prefill_merge_kernel<64, PG<64>::BN, true>, a);
+    return d128 ? cudaLaunchKernelEx(&mcfg, prefill_merge_kernel<128, PG<128>::BN, false>, a)
+                : cudaLaunchKernelEx(&mcfg, prefill_merge_kernel<64, PG<64>::BN, false>, a);
 }
 
 }  // namespace alpaca

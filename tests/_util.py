@@ -67,3 +67,17 @@ def prefill_unsplit(q, k, v, out, start_position: int = 0):
     minimum = (n * q.shape[-1] * 2 + 15) // 16 * 16 if q.dtype == torch.float32 else 0
     ws = torch.empty(minimum, dtype=torch.uint8, device=q.device) if minimum else None
     ab.launch(desc, ab.Kernel.PREFILL_TC, ws)
+
+
+def varlen_unsplit(q, k, v, out, q_offsets, start_positions, *, max_tokens: int, max_ctx_len: int):
+    """A ragged prefill given only its minimum workspace (the f32 queries' staging and the work list), so the library
+    runs it unsplit (see prefill_unsplit)."""
+    import torch
+
+    import alpaca_b200 as ab
+    desc = ab.make_varlen_desc(q, k, v, out, q_offsets, start_positions, max_tokens=max_tokens,
+                               max_ctx_len=max_ctx_len)
+    units = (q_offsets.numel() - 1) * -(-max_tokens // 256)
+    stage = (q.shape[0] * q.shape[1] * q.shape[2] * 2 + 15) // 16 * 16 if q.dtype == torch.float32 else 0
+    ws = torch.empty(stage + 16 * (1 + 2 * units), dtype=torch.uint8, device=q.device)
+    ab.launch(desc, ab.Kernel.PREFILL_TC, ws)

@@ -356,17 +356,24 @@ def test_rope_cache_rows_checked(lib, bad):
 
 def test_varlen_prefill_host_checks(lib):
     """The ragged prefill flag: AUTO picks the tensor-core prefill, the other kernels refuse it, the workspace holds
-    the heaviest-first work list (16 bytes + 32 per unit of two 128-row tiles) plus the f16 staging of f32
-    queries, and the descriptor's own contradictions are refused before anything is enqueued."""
+    the heaviest-first work list (16 bytes + 32 per unit of two 128-row tiles), the f16 staging of f32 queries and,
+    for a call with fewer work items than SMs at its bounds, the split-KV records, and the descriptor's own
+    contradictions are refused before anything is enqueued."""
     from alpaca_b200 import FLAG_VARLEN, DType, Kernel, Status
     base = dict(flags=FLAG_VARLEN, n_seqs=3, tokens=600, max_ctx_len=2000, total_tokens=900, q_offsets=FAKE,
                 start_positions=FAKE + 256, kv_seq_stride=2000 * 3 * 64)
     st, k = select(lib, desc(**base))
     assert (st, k) == (Status.OK, Kernel.PREFILL_TC)
     units = 3 * 3  # ceil(600 / 256) units per sequence
-    assert ws(lib, desc(**base)) == (Status.OK, 16 + 32 * units)
+    items = units * 9  # x heads: 81, fewer than 148, so the call splits its KV range
+    splits = min(8, -(-148 // items), -(-2000 // 128) // 4)  # 2 parts
+    records = items * splits * 2 * 128 * (64 + 2) * 4
+    assert ws(lib, desc(**base)) == (Status.OK, 16 + 32 * units + records)
     assert ws(lib, desc(**base, q_dtype=int(DType.F32), q_token_stride=9 * 64)) == \
-        (Status.OK, 900 * 9 * 64 * 2 + 16 + 32 * units)
+        (Status.OK, 900 * 9 * 64 * 2 + 16 + 32 * units + records)
+    # 3 x 16 units x 9 heads = 432 items: no split, the work list alone
+    big = {**base, "tokens": 4096, "max_ctx_len": 8192, "total_tokens": 9000, "kv_seq_stride": 8192 * 3 * 64}
+    assert ws(lib, desc(**big)) == (Status.OK, 16 + 32 * 3 * 16)
     assert ws(lib, desc(**base), int(Kernel.GENERAL))[0] == Status.UNSUPPORTED
     assert ws(lib, desc(**base), int(Kernel.DECODE_SPLIT))[0] == Status.UNSUPPORTED
     # q / out sequence strides are ignored (packed rows); the per-sequence caches still need theirs

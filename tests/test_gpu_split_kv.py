@@ -132,3 +132,56 @@ def test_split_kv_batch_and_paged_pool(cuda_lib):
         for name, g in results.items():
             max_abs_check(g[s][sel], cpu[sel], F16_BOUND, f"split-KV batch seq {s} {name}")
     assert np.array_equal(results["contiguous"], results["paged"])
+
+
+@pytest.mark.parametrize("d,H,kvh,odt", [(64, 9, 3, torch.float32), (128, 8, 2, torch.float16)])
+def test_split_kv_ragged_call(cuda_lib, d, H, kvh, odt):
+    """A ragged call of four sessions' chunks (24 units at most x heads: fewer items than SMs) splits too. Each unit
+    uses as many parts as its own KV blocks allow, so the chunk at position 0 stays whole. Each cache holds NaN past
+    its context; rows of a sequence's last KV block past its context are zeroed inside whichever part holds that
+    block. Checked against the oracle on sampled rows and against the same call given only the minimum workspace
+    (unsplit)."""
+    import alpaca_b200 as ab
+    from tests._util import varlen_unsplit
+    dev = torch.device("cuda")
+    seqs = [(512, 3584), (300, 2000), (100, 4000), (512, 0)]
+    cap = 4200
+    lens = [t for t, _ in seqs]
+    offs_np = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    q = _normal(700, (int(offs_np[-1]), H, d))
+    ks, vs = [], []
+    kc = np.full((len(seqs), cap, kvh, d), np.nan, np.float32)
+    vc = np.full((len(seqs), cap, kvh, d), np.nan, np.float32)
+    for s, (T, start) in enumerate(seqs):
+        ks.append(_normal(710 + s, (start + T, kvh, d)))
+        vs.append(_normal(720 + s, (start + T, kvh, d)))
+        kc[s, :start + T], vc[s, :start + T] = ks[-1], vs[-1]
+    qd = torch.from_numpy(q).to(dev).half()
+    kd, vd = torch.from_numpy(kc).to(dev).half(), torch.from_numpy(vc).to(dev).half()
+    offs = torch.from_numpy(offs_np).to(dev)
+    starts = torch.tensor([st for _, st in seqs], dtype=torch.int32, device=dev)
+    outs = []
+    for split in (True, False):
+        out = torch.full((int(offs_np[-1]), H, d), float("nan"), dtype=odt, device=dev)
+        if split:
+            desc = ab.make_varlen_desc(qd, kd, vd, out, offs, starts, max_tokens=512, max_ctx_len=cap)
+            need = ab.workspace_bytes(desc, ab.Kernel.PREFILL_TC)
+            minimum = 16 * (1 + 2 * len(seqs) * 2)
+            assert need > minimum, "the ragged call should ask for split-KV records"
+            ab.launch(desc, ab.Kernel.PREFILL_TC, torch.empty(need, dtype=torch.uint8, device=dev))
+        else:
+            varlen_unsplit(qd, kd, vd, out, offs, starts, max_tokens=512, max_ctx_len=cap)
+        ab.device_status()
+        outs.append(out.float().cpu().numpy())
+    bound = F16_BOUND + (F16_OUT if odt == torch.float16 else 0.0)
+    for s, (T, start) in enumerate(seqs):
+        o0 = int(offs_np[s])
+        rows = _rows(T, H, 730 + s)
+        cpu = oracle.attention_rows(q[o0:o0 + T], ks[s], vs[s], start, rows)
+        sel = oracle.rows_mask(rows, T, H)
+        for name, g in zip(("split", "unsplit"), outs):
+            assert np.isfinite(g[o0:o0 + T]).all(), f"{name} seq {s}"
+            max_abs_check(g[o0:o0 + T][sel], cpu[sel], bound, f"ragged split-KV d={d} seq {s} {name}")
+    diff = float(np.abs(outs[0] - outs[1]).max())
+    print(f"[metrics] ragged split-KV d={d}: split vs unsplit max-abs {diff:.3e}")
+    assert diff <= bound

@@ -15,7 +15,7 @@ import numpy as np
 import pytest
 
 import oracle
-from tests._util import max_abs_check, pool, prefill_unsplit
+from tests._util import max_abs_check, pool, prefill_unsplit, varlen_unsplit
 
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
@@ -134,7 +134,10 @@ def test_varlen_prefill_bad_sequence_is_reported_and_skipped(cuda_lib):
 def test_chunked_prefill_of_several_sessions(cuda_lib):
     """Three sessions' prompts prefilled in 512-token chunks, every active session's next chunk in one ragged call
     per step (each at its own moving start, as MetalLlamaModel.swift:293-298 moves startPosition), equal each
-    session's one-shot prefill bit for bit."""
+    session's one-shot prefill bit for bit. A step has 54 work items at most, so with the workspace the library asks
+    for, its later steps split their KV range over the SMs; that loop is checked against the one-shot prefill at the
+    f16 bound (the parts sum in another order), and the loop given only the minimum workspace (unsplit) bit for
+    bit."""
     from alpaca_b200 import device_status, prefill_varlen
     H, Hkv, d, chunk = 9, 3, 64, 512
     prompts = [1300, 512, 2000]
@@ -143,22 +146,31 @@ def test_chunked_prefill_of_several_sessions(cuda_lib):
           for i, n in enumerate(prompts)]
     kc = torch.from_numpy(oracle.f16_round(oracle.splitmix_normal(995, (3, 2048, Hkv, d)))).to(dev).half()
     vc = torch.from_numpy(oracle.f16_round(oracle.splitmix_normal(996, (3, 2048, Hkv, d)))).to(dev).half()
-    outs = [torch.empty((n, H, d), dtype=torch.float32, device=dev) for n in prompts]
-    done = [0, 0, 0]
-    while any(done[i] < prompts[i] for i in range(3)):
-        # sessions with no tokens left take part with an empty chunk
-        take = [min(chunk, prompts[i] - done[i]) for i in range(3)]
-        offs = np.concatenate([[0], np.cumsum(take)]).astype(np.int32)
-        qpack = torch.cat([qs[i][done[i]:done[i] + take[i]] for i in range(3)])
-        opack = torch.empty((int(offs[-1]), H, d), dtype=torch.float32, device=dev)
-        prefill_varlen(qpack, kc, vc, opack, torch.from_numpy(offs).to(dev),
-                       torch.tensor(done, dtype=torch.int32, device=dev), max_tokens=chunk, max_ctx_len=2048)
-        for i in range(3):
-            outs[i][done[i]:done[i] + take[i]] = opack[offs[i]:offs[i + 1]]
-            done[i] += take[i]
-    device_status()
+    results = {}
+    for split in (False, True):
+        outs = [torch.empty((n, H, d), dtype=torch.float32, device=dev) for n in prompts]
+        done = [0, 0, 0]
+        while any(done[i] < prompts[i] for i in range(3)):
+            # sessions with no tokens left take part with an empty chunk
+            take = [min(chunk, prompts[i] - done[i]) for i in range(3)]
+            offs = torch.from_numpy(np.concatenate([[0], np.cumsum(take)]).astype(np.int32)).to(dev)
+            starts = torch.tensor(done, dtype=torch.int32, device=dev)
+            qpack = torch.cat([qs[i][done[i]:done[i] + take[i]] for i in range(3)])
+            opack = torch.empty((int(offs[-1]), H, d), dtype=torch.float32, device=dev)
+            if split:
+                prefill_varlen(qpack, kc, vc, opack, offs, starts, max_tokens=chunk, max_ctx_len=2048)
+            else:
+                varlen_unsplit(qpack, kc, vc, opack, offs, starts, max_tokens=chunk, max_ctx_len=2048)
+            for i in range(3):
+                outs[i][done[i]:done[i] + take[i]] = opack[int(offs[i]):int(offs[i + 1])]
+                done[i] += take[i]
+        device_status()
+        results[split] = outs
     for i, n in enumerate(prompts):
         one = torch.empty((n, H, d), dtype=torch.float32, device=dev)
         prefill_unsplit(qs[i], kc[i, :n], vc[i, :n], one)
         device_status()
-        assert torch.equal(one, outs[i]), f"session {i}: chunked and one-shot prefill differ"
+        assert torch.equal(one, results[False][i]), f"session {i}: chunked and one-shot prefill differ"
+        diff = float((one - results[True][i]).abs().max())
+        print(f"[metrics] session {i}: split-KV chunk loop vs one-shot max-abs {diff:.3e}")
+        assert np.isfinite(diff) and diff <= 2e-3, f"session {i}: split-KV chunk loop differs by {diff:.3e}"
