@@ -235,6 +235,7 @@ __device__ __forceinline__ Item decode_item(const PrefillArgs& a, int it) {
 struct TileWork {
     int seq, head, cseq, row0, pos0, nrows, nblk;
     int jb0, jb1;  // this tile's KV blocks [jb0, jb1) in the item (its part; empty when jb1 <= jb0)
+    bool rec;      // split KV: the item is one of several parts and writes a record, not the output
 };
 
 template <int BN, int NT, bool VL, bool KS = false>
@@ -262,9 +263,11 @@ __device__ __forceinline__ TileWork tile_work(const PrefillArgs& a, int it, int 
             const int up = unit_parts(a.kv_splits, nmax);
             w.jb0 = part < up ? part * nmax / up : nmax;
             w.jb1 = part < up ? min(w.nblk, (part + 1) * nmax / up) : nmax;
+            w.rec = up > 1;  // a unit left whole writes its output as the unsplit form does
         } else {
             w.jb0 = 0;
             w.jb1 = w.nblk;
+            w.rec = false;
         }
         return w;
     }
@@ -291,6 +294,7 @@ __device__ __forceinline__ TileWork tile_work(const PrefillArgs& a, int it, int 
         w.jb0 = 0;
         w.jb1 = w.nblk;
     }
+    w.rec = KS;  // a uniform split call cuts every item into its `splits` parts
     return w;
 }
 
@@ -701,7 +705,7 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
             if (!ok) break;
             o_uses++;
             tc_fence_after();
-            if (KS) {  // split KV: this part's rows unnormalised, with their max (log2 units) and sum
+            if (KS && x.rec) {  // split KV: this part's rows unnormalised, with their max (log2 units) and sum
                 float* rec = a.part + ((static_cast<int64_t>(it) * NT + tile) * kBM + row) * (D + 2);
 #pragma unroll
                 for (int c0 = 0; c0 < D; c0 += 32) {
@@ -978,7 +982,7 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
             if (!ok) break;
             x_uses++;
             const float l = lpart + sm->xl[tile][half ^ 1][row];
-            if (KS) {  // split KV: this part's rows unnormalised, with their max (log2 units) and sum
+            if (KS && x.rec) {  // split KV: this part's rows unnormalised, with their max (log2 units) and sum
                 float* rec = a.part + ((static_cast<int64_t>(it) * NT + tile) * kBM + row) * (D + 2);
 #pragma unroll
                 for (int c = 0; c < OC; c += 2)  // records are 8-byte aligned ((D + 2) x 4 bytes each)
@@ -1073,7 +1077,8 @@ __global__ void __launch_bounds__(threads_for<R, NT>(), 1)
 // Split KV: one warp per output row (item of the unsplit call, tile, row) merges the row's parts. With m_p the part's
 // running max (log2 units, -inf where the part saw no visible key), l_p its sum and O_p its unnormalised context,
 // out = sum_p 2^(m_p - M) O_p / sum_p 2^(m_p - M) l_p, M = max_p m_p. A part that holds no KV block of the tile wrote
-// nothing and is skipped (the block ranges are recomputed as the prefill kernel cut them).
+// nothing and is skipped (the block ranges are recomputed as the prefill kernel cut them). A ragged unit that ran
+// whole (one part) wrote its output itself and is skipped too.
 template <int D, int BN, bool VL>
 __global__ void __launch_bounds__(256) prefill_merge_kernel(const PrefillArgs a) {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -1100,6 +1105,7 @@ __global__ void __launch_bounds__(256) prefill_merge_kernel(const PrefillArgs a)
             nmax = max(nmax, rows > 0 ? (r.z + u * kBM + rows + BN - 1) / BN : 0);
         }
         up = unit_parts(S, nmax);
+        if (up <= 1) return;  // the unit ran whole and wrote its output itself
         item0 = static_cast<int64_t>(unit) * S * a.n_heads + head;
         pstep = a.n_heads;
         off = static_cast<int64_t>(r.y + tile * kBM + row) * a.out_token_stride + static_cast<int64_t>(head) * D;
@@ -1419,12 +1425,13 @@ size_t plan_units(const alpaca_attn_desc& d) {
     const int group = kUnitTiles * kBM;
     return static_cast<size_t>(d.n_seqs) * ((d.tokens + group - 1) / group);
 }
-// Split KV for uniform calls with fewer work items than one per SM of a B200 (148): each item's KV blocks are cut
-// into up to 8 parts of at least 4 blocks of its heaviest group, so the call fills the SMs (a smaller call does not
-// repay the merge: a 512-token chunk at position 0 measured 12.2 us per layer unsplit against 18.7 in two parts). This is the case of
-// alpaca.swift's prefill loop, one session's 512-token chunk per call at a moving start position
-// (MetalLlamaModel.swift:293-298): 18 items at SmolLM2-135M's 9 heads. ALPACA_PREFILL_SPLITS caps the parts (1 turns
-// the split off).
+// Split KV for calls with fewer work items than one per SM of a B200 (148): each item's KV blocks are cut into up to
+// 8 parts of at least 4 blocks of its heaviest group, as many as keep the call in one wave of items, so the call fills
+// the SMs (a smaller call does not repay the merge: a 512-token chunk at position 0 measured 12.2 us per layer
+// unsplit against 18.7 in two parts). This is the case of alpaca.swift's prefill loop, one session's 512-token chunk
+// per call at a moving start position (MetalLlamaModel.swift:293-298): 18 items at SmolLM2-135M's 9 heads. A ragged
+// call is sized from its bounds (units x heads, max_ctx_len); each unit then uses the parts its own blocks allow.
+// ALPACA_PREFILL_SPLITS caps the parts (1 turns the split off).
 constexpr int kSplitTargetItems = 148;
 int prefill_kv_splits(const alpaca_attn_desc& d) {
     static const int cap = [] {
@@ -1441,7 +1448,8 @@ int prefill_kv_splits(const alpaca_attn_desc& d) {
                              : static_cast<int64_t>((d.tokens + 2 * kBM - 1) / (2 * kBM)) * d.n_seqs * d.n_heads;
     if (items >= kSplitTargetItems) return 1;
     const int nmax = ((vl ? d.max_ctx_len : d.start_position + d.tokens) + bn - 1) / bn;
-    const int want = static_cast<int>((kSplitTargetItems + items - 1) / items);
+    // the most parts that keep every item in one wave: a second wave puts two parts on some SMs
+    const int want = static_cast<int>(kSplitTargetItems / items);
     return std::max(1, std::min(std::min(cap, want), nmax / 4));  // at least 4 blocks per part
 }
 // Partial records of a split call: [item][part][tile][row][head_dim + 2] f32.

@@ -632,14 +632,6 @@ __device__ __forceinline__ int stage_span(uint8_t* buf, const uint8_t* p, int n,
     return static_cast<int>(reinterpret_cast<uintptr_t>(p) - a0);
 }
 
-__device__ __forceinline__ uint32_t lds32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
-// 4 bytes at a 2-byte aligned shared-memory address.
-__device__ __forceinline__ uint32_t lds32_at2(const uint8_t* p) {
-    const uintptr_t u = reinterpret_cast<uintptr_t>(p);
-    if (u & 2u) return __funnelshift_r(lds32(p - 2), lds32(p + 2), 16);
-    return lds32(p);
-}
-
 template <int F>
 __global__ void __launch_bounds__(kProjThreads, 3) proj_q_kernel(const ProjArgs a) {
     using G = QGeo<F>;
@@ -924,13 +916,13 @@ __global__ void __launch_bounds__(kProjThreads, 2) proj_mma_kernel(const ProjArg
     if (a.prefetch && threadIdx.x == 0) {
         for (int r0 = blockIdx.x * RPC; r0 < total; r0 += gridDim.x * RPC) {
             const int r1 = min(r0 + RPC, total);
-            if (S) {
+            if constexpr (S) {
                 for (int m = 0; m < 2; m++) prefetch_l2(a.w[m] + r0 * a.row_bytes, (r1 - r0) * a.row_bytes, a.w_end[m]);
-                continue;
-            }
-            for (int m = 0, base = 0; m < 3; base += a.rows[m], m++) {
-                const int lo = max(r0, base), hi = min(r1, base + a.rows[m]);
-                if (lo < hi) prefetch_l2(a.w[m] + (lo - base) * a.row_bytes, (hi - lo) * a.row_bytes, a.w_end[m]);
+            } else {
+                for (int m = 0, base = 0; m < 3; base += a.rows[m], m++) {
+                    const int lo = max(r0, base), hi = min(r1, base + a.rows[m]);
+                    if (lo < hi) prefetch_l2(a.w[m] + (lo - base) * a.row_bytes, (hi - lo) * a.row_bytes, a.w_end[m]);
+                }
             }
         }
     }

@@ -365,12 +365,14 @@ def test_varlen_prefill_host_checks(lib):
     st, k = select(lib, desc(**base))
     assert (st, k) == (Status.OK, Kernel.PREFILL_TC)
     units = 3 * 3  # ceil(600 / 256) units per sequence
-    items = units * 9  # x heads: 81, fewer than 148, so the call splits its KV range
-    splits = min(8, -(-148 // items), -(-2000 // 128) // 4)  # 2 parts
-    records = items * splits * 2 * 128 * (64 + 2) * 4
-    assert ws(lib, desc(**base)) == (Status.OK, 16 + 32 * units + records)
+    # 81 items (units x heads): two parts each would need 162 > 148 SMs, so the call runs unsplit
+    assert ws(lib, desc(**base)) == (Status.OK, 16 + 32 * units)
     assert ws(lib, desc(**base, q_dtype=int(DType.F32), q_token_stride=9 * 64)) == \
-        (Status.OK, 900 * 9 * 64 * 2 + 16 + 32 * units + records)
+        (Status.OK, 900 * 9 * 64 * 2 + 16 + 32 * units)
+    # one sequence: 3 units x 9 heads = 27 items, floor(148 / 27) = 5 parts, capped at ceil(2000 / 128) / 4 = 4
+    one = {**base, "n_seqs": 1, "total_tokens": 600}
+    records = 27 * 4 * 2 * 128 * (64 + 2) * 4
+    assert ws(lib, desc(**one)) == (Status.OK, 16 + 32 * 3 + records)
     # 3 x 16 units x 9 heads = 432 items: no split, the work list alone
     big = {**base, "tokens": 4096, "max_ctx_len": 8192, "total_tokens": 9000, "kv_seq_stride": 8192 * 3 * 64}
     assert ws(lib, desc(**big)) == (Status.OK, 16 + 32 * 3 * 16)
