@@ -12,6 +12,7 @@ The same JSON line carries the other measured legs, each with its own timing, cl
   e2e / e2e_f16_out  the headline step through the C ABI with pinned host buffers, copies inside the timed region
   chunked_prefill    alpaca.swift's own prefill loop: the config-2 prompt in 512-token chunks at moving start positions,
                      30 layers per chunk (calls short of work items split their KV range over the SMs)
+  chunked_sessions   the same loop for 3 sessions at once: every session's next chunk in one ragged call per layer
   decode             config 3: split-KV decode (batch 64, one token each, contexts U[1,4096], 30 layers of f16 caches)
   rope_kv_append     the RoPE + KV-cache append upstream of the attention, config-2 shape
   decode_proj        the fused decode projections around the attention (norm + QKV, out + residual, gate/up + SiLU,
@@ -49,6 +50,7 @@ LAYERS = 30
 T_PREFILL = 4096
 SEED_CFG2 = 20260102
 DEC_BATCH, DEC_CAP = 64, 4096
+SESSIONS = 3             # sessions of the ragged chunk-loop leg
 CFG4_SEQS, CFG4_H, CFG4_KVH = 8, 15, 5
 CFG5_H = CFG5_KVH = 32
 CFG5_UNIT_HEADS = 8      # KV heads per config-5 unit
@@ -471,6 +473,55 @@ def leg_chunked(c: Ctx):
             "clocks": clk, "spot_check_max_abs": spot, "gpu_launches": args.steps * launches}
 
 
+def leg_chunked_sessions(c: Ctx):
+    """The same chunk loop serving several sessions at once: SESSIONS prompts of the config-2 length, every session's
+    next 512-token chunk in one ragged call per layer (packed queries, each session's own KV cache and start
+    position), 30 layers per chunk. A call has 18 work items per session, fewer than the SMs, so the library splits
+    the units' KV ranges too (each unit into as many parts as its own blocks allow)."""
+    torch, ab, args = c.torch, c.ab, c.args
+    T, L, CH, S = args.tokens, args.layers, 512, SESSIONS
+    NC = T // CH
+    g = torch.Generator(device=c.dev)
+    g.manual_seed(20260109 + 1000 * c.rank)
+    k = [torch.randn((S, T, KVH, D), generator=g, device=c.dev).half() for _ in range(L)]
+    v = [torch.randn((S, T, KVH, D), generator=g, device=c.dev).half() for _ in range(L)]
+    q = [torch.randn((NC, S * CH, H, D), generator=g, device=c.dev).half() for _ in range(L)]  # packed per chunk
+    out = [torch.empty((NC, S * CH, H, D), dtype=torch.float32, device=c.dev) for _ in range(L)]
+    offs = torch.arange(0, S + 1, dtype=torch.int32, device=c.dev) * CH
+    starts = [torch.full((S,), j * CH, dtype=torch.int32, device=c.dev) for j in range(NC)]
+    descs = [ab.make_varlen_desc(q[l][j], k[l], v[l], out[l][j], offs, starts[j], max_tokens=CH, max_ctx_len=T)
+             for j in range(NC) for l in range(L)]
+    need = max(ab.workspace_bytes(d, ab.Kernel.PREFILL_TC) for d in descs)
+    ws = torch.empty(need, dtype=torch.uint8, device=c.dev)  # stream-ordered calls share it
+
+    def step():
+        for d in descs:
+            ab.launch(d, ab.Kernel.PREFILL_TC, ws)
+
+    gr = c.graph(step)
+    ms, ms_max, clk = c.timed(gr.replay, args.steps, args.warmup)
+    del gr
+    import oracle
+    rows = _spot_rows(T, H)
+    sel = oracle.rows_mask(rows, T, H)
+    spot = 0.0
+    for s in (0, S - 1):  # first and last session of layer 0, their chunks put back in prompt order
+        qs = torch.cat([q[0][j][s * CH:(s + 1) * CH] for j in range(NC)]).float().cpu().numpy()
+        os_ = torch.cat([out[0][j][s * CH:(s + 1) * CH] for j in range(NC)]).cpu().numpy()
+        ref = oracle.attention_rows(qs, k[0][s].float().cpu().numpy(), v[0][s].float().cpu().numpy(), 0, rows)
+        spot = max(spot, float(abs(os_[sel] - ref[sel]).max()))
+    spot = max_over_ranks(spot, c.pg)
+    flops = S * L * flops_prefill(T)
+    return {"workload": f"{S} sessions' {T}-token prompts in {CH}-token chunks, every session's next chunk in one "
+                        f"ragged call per layer, {L} layers per chunk ({len(descs)} calls per step), 9/3 heads, d=64, "
+                        "f16 in / f32 out; calls short of work items split their units' KV ranges over the SMs",
+            "value": c.world * flops / (ms_max * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms_max,
+            "tokens_per_s": c.world * S * T / (ms_max * 1e-3), "scaling": "weak", "workspace_bytes": need,
+            "l2": f"{L} layers' K/V and Q ({L * S * T * (H + 2 * KVH) * D * 2 / 1e6:.0f} MB) vs 126 MB L2 (no flush)",
+            "clocks": clk, "spot_check_max_abs": spot,
+            "gpu_launches": args.steps * len(descs) * 3}  # plan, prefill and merge kernels per call
+
+
 def leg_decode(c: Ctx):
     torch, ab, args = c.torch, c.ab, c.args
     Kernel = ab.Kernel
@@ -871,6 +922,8 @@ def run_ours(args):
     torch.cuda.empty_cache()
     chunked = leg_chunked(c) if not args.no_chunked else None
     torch.cuda.empty_cache()
+    sessions = leg_chunked_sessions(c) if not args.no_sessions else None
+    torch.cuda.empty_cache()
     decode = leg_decode(c) if not args.no_decode else None
     torch.cuda.empty_cache()
     rope_kv = leg_rope(c) if not args.no_rope else None
@@ -914,6 +967,7 @@ def run_ours(args):
             "clocks": p2["clk"],
             "spot_check_max_abs": p2["spot"],
             "chunked_prefill": chunked,
+            "chunked_sessions": sessions,
             "decode": decode,
             "rope_kv_append": rope_kv,
             "decode_proj": proj,
@@ -976,7 +1030,7 @@ def main():
     ap.add_argument("--tokens", type=int, default=T_PREFILL)
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--dec-layers", type=int, default=LAYERS)
-    for leg in ("decode", "rope", "proj", "cpu", "e2e", "cfg4", "cfg5", "chunked"):
+    for leg in ("decode", "rope", "proj", "cpu", "e2e", "cfg4", "cfg5", "chunked", "sessions"):
         ap.add_argument(f"--no-{leg}", action="store_true")
     ap.add_argument("--e2e-chunk", type=int, default=0, help="sequences per ABI call in the e2e pipeline (0: 1/6 of them)")
     ap.add_argument("--cpu-seconds", type=float, default=3.0, help="minimum seconds of the all-thread CPU baseline")
