@@ -136,13 +136,14 @@ def test_split_kv_batch_and_paged_pool(cuda_lib):
 
 @pytest.mark.parametrize("d,H,kvh,odt", [(64, 9, 3, torch.float32), (128, 8, 2, torch.float16)])
 def test_split_kv_ragged_call(cuda_lib, d, H, kvh, odt):
-    """A ragged call of four sessions' chunks (24 units at most x heads: fewer items than SMs) splits too. Each unit
-    uses as many parts as its own KV blocks allow, so the chunk at position 0 stays whole. Each cache holds NaN past
-    its context; rows of a sequence's last KV block past its context are zeroed inside whichever part holds that
-    block. Checked against the oracle on sampled rows and against the same call given only the minimum workspace
-    (unsplit)."""
+    """A ragged call of four sessions' chunks (8 units x heads: fewer items than SMs) splits too. Each unit uses as
+    many parts as its own KV blocks allow, so the chunk at position 0 stays whole and writes its output directly.
+    Each cache holds NaN past its context; rows of a sequence's last KV block past its context are zeroed inside
+    whichever part holds that block. Checked against the oracle on sampled rows and against the same call given only
+    the minimum workspace (unsplit); the split call over shuffled 256-row blocks of a NaN pool equals the contiguous
+    split call bit for bit."""
     import alpaca_b200 as ab
-    from tests._util import varlen_unsplit
+    from tests._util import pool, varlen_unsplit
     dev = torch.device("cuda")
     seqs = [(512, 3584), (300, 2000), (100, 4000), (512, 0)]
     cap = 4200
@@ -185,3 +186,18 @@ def test_split_kv_ragged_call(cuda_lib, d, H, kvh, odt):
     diff = float(np.abs(outs[0] - outs[1]).max())
     print(f"[metrics] ragged split-KV d={d}: split vs unsplit max-abs {diff:.3e}")
     assert diff <= bound
+    kp, table = pool(ks, 256, np.random.default_rng(740), cap)
+    vp, _ = pool(vs, 256, np.random.default_rng(740), cap)
+    out_p = torch.full((int(offs_np[-1]), H, d), float("nan"), dtype=odt, device=dev)
+    ab.prefill_varlen(qd, torch.from_numpy(kp).to(dev).half(), torch.from_numpy(vp).to(dev).half(), out_p, offs,
+                      starts, max_tokens=512, max_ctx_len=cap, block_table=torch.from_numpy(table).to(dev))
+    ab.device_status()
+    got = out_p.float().cpu().numpy()
+    differ = []
+    for s in range(len(seqs)):
+        a, b = got[offs_np[s]:offs_np[s + 1]], outs[0][offs_np[s]:offs_np[s + 1]]
+        bad = np.nonzero(~((a == b) | (np.isnan(a) & np.isnan(b))).all(axis=(1, 2)))[0]
+        if bad.size:
+            differ.append(f"seq {s}: {bad.size} rows ({bad.min()}-{bad.max()}), "
+                          f"{int((~np.isfinite(a[bad])).any(axis=(1, 2)).sum())} of them non-finite")
+    assert not differ, "paged split call differs from the contiguous one: " + "; ".join(differ)
