@@ -354,6 +354,37 @@ def test_rope_cache_rows_checked(lib, bad):
     assert lib.alpaca_cuda_last_error().startswith(b"rope")
 
 
+def test_prefill_split_kv_workspace_policy(lib):
+    """A uniform prefill with fewer work items (sequences x heads x pairs of 128-query tiles) than a B200's 148 SMs
+    asks for split-KV records: parts = min(8, floor(148 / items), KV blocks / 4), so all parts run in one wave and
+    each has at least 4 blocks; records of items x parts x 2 tiles x 128 rows x (d + 2) f32 follow the f32 queries'
+    staging. A call that cannot use two parts asks for none."""
+    from alpaca_b200 import DType, Kernel, Status
+    pf = int(Kernel.PREFILL_TC)
+
+    def rec(items, parts, d=64):
+        return items * parts * 2 * 128 * (d + 2) * 4
+
+    # alpaca's last 512-token chunk of a 4096-token prompt: 18 items, 32 KV blocks of 128 rows, 8 parts
+    assert ws(lib, desc(tokens=512, start_position=3584), pf) == (Status.OK, rec(18, 8))
+    # the second chunk (8 blocks): 2 parts; the first (4 blocks): too few for two parts of 4
+    assert ws(lib, desc(tokens=512, start_position=512), pf) == (Status.OK, rec(18, 2))
+    assert ws(lib, desc(tokens=512, start_position=0), pf) == (Status.OK, 0)
+    # f32 queries: their f16 staging comes first
+    assert ws(lib, desc(tokens=512, start_position=3584, q_dtype=int(DType.F32)), pf) == \
+        (Status.OK, 512 * 9 * 64 * 2 + rec(18, 8))
+    # three 256-token sequences at 3000 (26 blocks): 27 items, floor(148 / 27) = 5 parts; 6 would need a second wave
+    three = dict(n_seqs=3, tokens=256, start_position=3000, q_seq_stride=256 * 9 * 64, out_seq_stride=256 * 9 * 64,
+                 kv_seq_stride=3256 * 3 * 64)
+    assert ws(lib, desc(**three), pf) == (Status.OK, rec(27, 5))
+    # head_dim 128 (64-row KV blocks): 16 items, 38 blocks, 8 parts
+    d128 = dict(head_dim=128, n_heads=8, n_kv_heads=2, tokens=384, start_position=2000, q_token_stride=8 * 128,
+                out_token_stride=8 * 128, kv_row_stride=2 * 128)
+    assert ws(lib, desc(**d128), pf) == (Status.OK, rec(16, 8, 128))
+    # a whole 4096-token prompt: 144 items, floor(148 / 144) = 1, no split
+    assert ws(lib, desc(tokens=4096), pf) == (Status.OK, 0)
+
+
 def test_varlen_prefill_host_checks(lib):
     """The ragged prefill flag: AUTO picks the tensor-core prefill, the other kernels refuse it, the workspace holds
     the heaviest-first work list (16 bytes + 32 per unit of two 128-row tiles), the f16 staging of f32 queries and,
