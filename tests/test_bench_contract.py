@@ -43,3 +43,18 @@ def test_reference_arm_prints_the_contract_line():
     assert cpu["single_thread"]["cores"] == 1 and cpu["single_thread"]["value"] > 0
     assert line["e2e"] == {"value": line["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
     assert line["config"]["tokens"] == 512 and line["config"]["layers"] == 30
+
+
+def test_both_arms_draw_the_same_inputs_and_count_the_same_flops():
+    """The GPU arm's torch generator (synth_normal) and the reference arm's C generator (oracle.splitmix_normal) give
+    the same N(0,1) draws bit for bit, an odd count and a seed past 2^63 included, so both arms time the same
+    config-2 inputs. Config 2's step is 30 layers of 2 * 9 * 64 * T * (T + 1) FLOPs."""
+    import numpy as np
+
+    import oracle
+    sys.path.insert(0, str(ROOT))
+    import bench
+    for seed in (0, bench.SEED_CFG2, 2 ** 63 + 5):
+        a = bench.synth_normal(seed, (4097, 3)).numpy()
+        assert np.array_equal(a, oracle.splitmix_normal(seed, (4097, 3))), seed
+    assert bench.LAYERS * bench.flops_prefill(bench.T_PREFILL) == 579_962_142_720
