@@ -154,10 +154,11 @@ alpaca_cuda_status alpaca_attention(const alpaca_attn_desc* desc, alpaca_attn_ke
  * dealt to the SMs heaviest first across all sequences (the workspace then also holds that work list).
  * A call with fewer work items (sequences x heads x pairs of 128-query tiles; ragged: its bound, n_seqs x
  * ceil(tokens / 256) x heads) than SMs, such as one session's 512-token chunk at a moving start position
- * (MetalLlamaModel.swift:293-298) or a ragged step of a few sessions' chunks, splits each item's KV range into up to
- * 8 parts that run on their own SMs and merges them in a second kernel, when the workspace is at least
- * alpaca_attention_workspace_bytes (the parts' records live there). A ragged unit uses as many of the parts as its
- * own KV blocks allow (at least 4 blocks per part). Given only the minimum (0 bytes for f16 queries, the f32
+ * (MetalLlamaModel.swift:293-298) or a ragged step of a few sessions' chunks, splits each item's KV range into parts
+ * that run on their own SMs and merges them in a second kernel, when the workspace is at least
+ * alpaca_attention_workspace_bytes (the parts' records live there). Parts per item: min(8, floor(148 / items),
+ * KV blocks / 4), so all parts fit one wave and each holds at least 4 KV blocks. A ragged unit uses as many of the
+ * parts as its own KV blocks allow; a unit left whole writes its output directly. Given only the minimum (0 bytes for f16 queries, the f32
  * queries' staging otherwise, plus the ragged work list) the call runs unsplit. The results of the two agree to f32
  * rounding, but are not bit for bit equal. ALPACA_PREFILL_SPLITS=1 in the environment turns the split off. */
 alpaca_cuda_status alpaca_attn_prefill(const alpaca_attn_desc* desc, void* workspace, size_t workspace_bytes,
