@@ -118,7 +118,8 @@ def prefill_varlen(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch
                    flags: int = 0, workspace: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None,
                    block_table: torch.Tensor | None = None) -> AttnDesc:
     """Enqueue a ragged prefill (make_varlen_desc) on the tensor-core kernel; allocates the workspace (work list,
-    f16 staging of f32 queries) with torch when none is given."""
+    f16 staging of f32 queries and, for a call with fewer work items than SMs, the split-KV records) with torch
+    when none is given or the one given is smaller than the library asks for."""
     desc = make_varlen_desc(q, k, v, out, q_offsets, start_positions, max_tokens=max_tokens, max_ctx_len=max_ctx_len,
                             scale=scale, flags=flags, block_table=block_table)
     need = workspace_bytes(desc, Kernel.PREFILL_TC)
