@@ -105,9 +105,10 @@ struct PrefillArgs {
     float scale_log2;
     unsigned* err;
     unsigned flags;
-    // Split KV (uniform form, calls with fewer work items than SMs): each item's KV blocks are cut into kv_splits
-    // parts, each part an item of its own that leaves its unnormalised rows and their (max, sum) in `part`
-    // ([item][tile][row][D + 2] f32), and prefill_merge_kernel writes the output; kv_splits = 1 otherwise.
+    // Split KV (calls with fewer work items than SMs): each item's KV blocks are cut into kv_splits parts (a ragged
+    // unit into as many as its own blocks allow, unit_parts), each part an item of its own that leaves its
+    // unnormalised rows and their (max, sum) in `part` ([item][tile][row][D + 2] f32), and prefill_merge_kernel
+    // writes the output; a ragged unit left whole writes its output itself. kv_splits = 1 otherwise.
     int kv_splits;
     float* part;
     const int* block_table;  // paged cache: [seq][max_blocks] (null: contiguous caches)
